@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention path (one JSON line on stdout, rank 0).
+
+Workload (the configuration BASELINE.json's metric is quoted on): single-token
+gated GQA decode at 32k context, bf16 KV cache, Qwen3.5-4B shapes (16 query
+heads, 4 KV heads, head_dim 256), through the 8 full-attention layers of the
+stack.  A step is one token through those 8 layers: q/k norm + RoPE + KV
+append, split-KV attention over 32768 positions, merge + output gate.  Each
+layer has its own 128 MiB cache, so a step streams 1 GiB, eight times the
+126 MB L2: no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU; each GPU decodes its own
+sequence (sequence-partitioned decode, no collective), so per-GPU work is
+fixed as N grows ("scaling": "weak") and `value` aggregates over all GPUs.
+
+`--impl reference` times the reference's CPU implementation of the path (the
+C++ restatement in oracle/, all host threads, f32 cache) on the same workload
+and prints the same line with "impl": "reference"; under torchrun only rank 0
+runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rust-llm_b200"))
+
+CTX = 32768
+N_LAYERS = 8
+N_HEAD, N_KV, HD = 16, 4, 256
+KV_BYTES_PER_LAYER = 2 * N_KV * CTX * HD * 2          # K + V, bf16: 134,217,728 B
+METRIC = "decode attn µs/layer @32k ctx & HBM GB/s vs 8 TB/s; prefill attn TFLOPS"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_split_bf16_32k.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_baseline(seconds=12.0, max_reps=20):
+    """The oracle (C++ restatement of forward.rs) on one layer's decode at 32k,
+    f32 cache, all host threads; time per layer in µs."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as orc
+    threads = os.cpu_count() or 1
+    cfg = orc.qwen35_config(CTX)
+    r = orc.Rng(0)
+    kv = np.empty((2, N_KV, CTX, HD), np.float32)
+    kv[...] = r.normal(kv.shape)
+    qg = r.normal((1, N_HEAD * 2 * HD))
+    k = r.normal((1, N_KV * HD))
+    v = r.normal((1, N_KV * HD))
+    ones = np.ones(HD, np.float32)
+    orc.full_attn(cfg, CTX - 1, qg, k, v, kv, ones, ones, threads)  # warm
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < max_reps and (len(times) < 3 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        orc.full_attn(cfg, CTX - 1, qg, k, v, kv, ones, ones, threads)
+        times.append(time.perf_counter() - t0)
+    us = sum(times) / len(times) * 1e6
+    return us, threads, len(times)
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    us, threads, reps = cpu_baseline(seconds=max(10.0, min(60.0, 0.05 * args.steps)),
+                                     max_reps=max(3, args.steps))
+    sample = (f"{reps} single-layer decodes at position {CTX - 1} over a {CTX}-entry f32 "
+              f"cache (16/4 heads, hd 256), {threads} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": us, "unit": "us/layer",
+        "n_gpus": world, "steps": reps, "warmup": 1, "ms_per_step": us * N_LAYERS / 1e3,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1), seed 0",
+        "config": {"workload": "decode32k", "context": CTX, "layers": N_LAYERS,
+                   "heads": [N_HEAD, N_KV, HD], "kv_dtype": "f32"},
+        "cpu_baseline": {"value": us, "unit": "us/layer", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": us, "unit": "us/layer", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import rlcuda
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    cfg = rlcuda.qwen35_config(n_full=N_LAYERS, n_linear=0, context=CTX,
+                               kv_dtype=rlcuda.RL_KV_BF16, max_batch=1)
+    ctx = rlcuda.Context(cfg, device=local)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    for layer in range(N_LAYERS):
+        src = torch.randn((2, N_KV, CTX, HD), generator=gen, device=dev, dtype=torch.float32)
+        ctx.write_kv(layer, 0, src)
+        del src
+    torch.cuda.empty_cache()
+    qg = torch.randn((N_LAYERS, 1, N_HEAD * 2 * HD), generator=gen, device=dev)
+    kk = torch.randn((N_LAYERS, 1, N_KV * HD), generator=gen, device=dev)
+    vv = torch.randn((N_LAYERS, 1, N_KV * HD), generator=gen, device=dev)
+    out = torch.empty((N_LAYERS, 1, N_HEAD * HD), device=dev)
+    pos = CTX - 1
+
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+
+    def step():
+        for layer in range(N_LAYERS):
+            ctx.full_attn(layer, pos, 1, qg[layer], kk[layer], vv[layer], out[layer])
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- timed region: K graph replays of the 8-layer decode step
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        stream.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ctx.sync()
+    launches = args.steps * N_LAYERS * 3
+    layer_decodes = args.steps * N_LAYERS * world
+    us_per_layer = ms * 1e3 / layer_decodes
+    hbm_gbs = layer_decodes * KV_BYTES_PER_LAYER / (ms / 1e3) / 1e9
+
+    # ---- the dominant kernel alone: CUDA events around each decode_split
+    # launch on the library's stream, same workload, no graph
+    prof_steps = min(args.steps, 300)
+    ctx.profile_reset()
+    ctx.profile(True)
+    for _ in range(prof_steps):
+        step()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    dec_ms, dec_n = prof["decode"]
+    avg_us = dec_ms * 1e3 / max(dec_n, 1)
+    achieved = KV_BYTES_PER_LAYER / (avg_us * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+    shares = {k: round(v[0] / max(sum(x[0] for x in prof.values()), 1e-9), 4)
+              for k, v in prof.items() if v[1]}
+
+    # ---- end to end through the host entry point: pinned host inputs copied
+    # in and the result copied out inside the timed region, every layer
+    h_qg = torch.empty((N_LAYERS, 1, N_HEAD * 2 * HD), pin_memory=True)
+    h_k = torch.empty((N_LAYERS, 1, N_KV * HD), pin_memory=True)
+    h_v = torch.empty((N_LAYERS, 1, N_KV * HD), pin_memory=True)
+    h_qg.copy_(qg.cpu())
+    h_k.copy_(kk.cpu())
+    h_v.copy_(vv.cpu())
+    n_qg, n_k, n_v = h_qg.numpy(), h_k.numpy(), h_v.numpy()
+    e2e_steps = max(3, min(args.steps // 10, 500))
+    for layer in range(N_LAYERS):  # warm
+        ctx.full_attn_host(layer, pos, n_qg[layer], n_k[layer], n_v[layer])
+    barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    last = None
+    for _ in range(e2e_steps):
+        for layer in range(N_LAYERS):
+            last = ctx.full_attn_host(layer, pos, n_qg[layer], n_k[layer], n_v[layer])
+    e3.record(stream)
+    stream.synchronize()
+    e2e_ms = e2.elapsed_time(e3)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    assert last is not None and np.isfinite(last).all()
+    e2e_us = e2e_ms * 1e3 / (e2e_steps * N_LAYERS * world)
+    h2d = N_LAYERS * 4 * (N_HEAD * 2 * HD + 2 * N_KV * HD)
+    d2h = N_LAYERS * 4 * N_HEAD * HD
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        us, threads, reps = cpu_baseline()
+        cpu = {"value": us, "unit": "us/layer", "cores": threads, "kind": "port",
+               "sample": f"{reps} single-layer decodes at position {CTX - 1} over a "
+                         f"{CTX}-entry f32 cache (the reference has no bf16 cache), "
+                         f"C++ restatement of forward.rs, {threads} threads"}
+
+    traffic = ncu_traffic()
+    line = {
+        "metric": METRIC, "value": us_per_layer, "unit": "us/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) KV/q/k/v/gate, torch.Generator seed 1234+rank",
+        "config": {"workload": "decode32k", "context": CTX, "layers": N_LAYERS,
+                   "heads": [N_HEAD, N_KV, HD], "kv_dtype": "bf16", "rows": 1,
+                   "parallelism": f"sequence-partitioned x{world}, no collective",
+                   "l2": "inputs larger than L2: 8 layers x 128 MiB KV per step",
+                   "launch": "CUDA graph of the 8-layer step"},
+        "hbm_gbs": hbm_gbs,
+        "hbm_frac_of_8tbs": hbm_gbs / 8000.0,
+        "prefill_tflops": None,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "decode_split_kernel<bf16>",
+                     "peak_source": peak_kind,
+                     "avg_launch_us": avg_us, "launch_share": shares},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    graph.reset()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

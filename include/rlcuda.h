@@ -1,0 +1,194 @@
+/*
+ * rlcuda.h — C ABI of the B200 (sm_100a) attention path for the rust-llm
+ * Qwen3.5 hybrid runner.
+ *
+ * The library replaces the hot span of the reference's two attention
+ * methods and the caches they run on:
+ *   Exec::full_attn    crates/rust-llm/src/forward.rs:1220-1344 (span 1259-1340)
+ *   Exec::linear_attn  crates/rust-llm/src/forward.rs:1484-1663 (span 1530-1652)
+ *   Caches             crates/rust-llm/src/forward.rs:236-254, sized at :468-474
+ *   Runner::{reset, verify, accept, pos}  forward.rs:558-577, :641-650, :675-688, :553-555
+ * The projections on either side (forward.rs:1250, :1342, :1517, :1656) stay
+ * with the caller: a call takes the projection outputs and returns the
+ * `heads` buffer the output projection reads.
+ *
+ * Conventions
+ *   - Every function returns an rl_status (0 = ok, negative = error) unless
+ *     its comment says otherwise; rl_last_error() describes the last failure
+ *     on that context (or, for a NULL context, on the calling thread).
+ *   - A context is not thread-safe, like `&mut Runner`: one caller at a time.
+ *   - Device memory is owned by the context and freed by rl_ctx_destroy.
+ *   - Entry points named *_host take host pointers and return once the
+ *     result is in host memory.  The others take device pointers, are
+ *     enqueued on the context's stream and return immediately; rl_sync()
+ *     waits and reports any error a kernel flagged on the device.
+ *   - Arrays are f32, row-major, token-major, laid out as the reference's
+ *     buffers are (forward.rs:256-320).
+ */
+#ifndef RLCUDA_H
+#define RLCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    RL_OK = 0,
+    RL_EINVAL = -1,       /* bad argument: the reference's contract panics, forward.rs:811-820, :642-647, :676-681 */
+    RL_ECONTEXT = -2,     /* the batch does not fit the remaining context (forward.rs:815-820) */
+    RL_ECUDA = -3,        /* a CUDA runtime error */
+    RL_ENCCL = -4,        /* an NCCL error */
+    RL_ETIMEOUT = -5,     /* a bounded device-side wait gave up */
+    RL_EUNSUPPORTED = -6, /* a shape the kernels are not built for */
+    RL_ENOMEM = -7        /* device allocation failed */
+} rl_status;
+
+typedef enum { RL_KV_F32 = 0, RL_KV_BF16 = 1 } rl_kv_dtype;
+
+typedef struct rl_ctx rl_ctx;
+
+/* Shapes and sizes.  The model fields mirror Config (crates/rust-llm/src/
+ * model.rs:41-66); context and slots mirror Runner::with_speculation's
+ * `context` and `draft + 1` (forward.rs:445-491). */
+typedef struct {
+    int32_t n_full;      /* full-attention layers (KV caches) */
+    int32_t n_linear;    /* DeltaNet layers (conv + recurrent state rings) */
+    int32_t n_head;      /* 16 */
+    int32_t n_head_kv;   /* 4 */
+    int32_t head_dim;    /* 256 */
+    int32_t n_rot;       /* 64 */
+    float rope_theta;    /* 1e7 */
+    float rms_eps;       /* 1e-6 */
+    int32_t d_state;     /* 128 */
+    int32_t n_k_heads;   /* 16 */
+    int32_t n_v_heads;   /* 32 */
+    int32_t conv_kernel; /* 4 */
+    int32_t context;     /* positions per KV cache */
+    int32_t slots;       /* ring slots of the DeltaNet state: draft + 1 */
+    int32_t kv_dtype;    /* rl_kv_dtype */
+    int32_t max_batch;   /* most rows one call may carry (sizes the scratch) */
+} rl_config;
+
+/* Allocates the caches and scratch on `device` and zeroes them
+ * (Runner::with_speculation, forward.rs:445-491). */
+int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out);
+/* Frees everything the context owns.  NULL is a no-op. */
+void rl_ctx_destroy(rl_ctx *ctx);
+/* The last error on `ctx`, or on the calling thread if ctx is NULL.  Never NULL. */
+const char *rl_last_error(const rl_ctx *ctx);
+
+/* Enqueue on `stream` (a cudaStream_t) instead of the context's own stream. */
+int rl_set_stream(rl_ctx *ctx, void *stream);
+void *rl_get_stream(const rl_ctx *ctx);
+
+/* Zeroes the KV, conv and recurrent state and sets pos = live = 0
+ * (Runner::reset, forward.rs:558-577). */
+int rl_reset(rl_ctx *ctx);
+
+/* Per-layer weights, copied once from host memory.
+ * full:   q_norm, k_norm [head_dim] (FullBlock, model.rs:187-198)
+ * linear: conv1d [conv_dim][conv_kernel], ssm_a [n_v] (already -exp(A_log)),
+ *         dt_bias [n_v], norm [d_state] (LinearBlock, model.rs:200-216) */
+int rl_set_weights_full(rl_ctx *ctx, int layer, const float *q_norm, const float *k_norm);
+int rl_set_weights_linear(rl_ctx *ctx, int layer, const float *conv1d, const float *ssm_a,
+                          const float *dt_bias, const float *norm);
+
+/*
+ * Full attention for t rows at positions pos..pos+t-1 of full layer `layer`
+ * (Exec::full_attn's span forward.rs:1259-1340, called from Runner::run at
+ * forward.rs:850-855 with caches.pos): per-head q/k RMSNorm and RoPE, KV
+ * append, causal attention of row i over pos+i+1 positions, sigmoid output
+ * gate, transpose.
+ *   qg  [t][n_head][2*head_dim]  query | gate per head (the attn_q output)
+ *   k,v [t][n_head_kv][head_dim]
+ *   out [t][n_head*head_dim]     the `heads` buffer attn_output reads
+ * t = 1 runs split-KV flash decoding; larger t runs the same split-KV walk
+ * per row, or the tcgen05 prefill kernel from RL_OPT_PREFILL_ROWS rows on.
+ */
+int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const float *k,
+                 const float *v, float *out);
+int rl_full_attn_host(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const float *k,
+                      const float *v, float *out);
+
+/*
+ * Gated DeltaNet for t sequential rows of linear layer `layer`
+ * (Exec::linear_attn's span forward.rs:1530-1652, called at forward.rs:856-864
+ * with caches.live): row i reads ring slot (live+i)%slots and writes
+ * (live+i+1)%slots; with slots == 1 the state is updated in place.
+ *   qkv   [t][conv_dim]    conv_dim = 2*n_k*d_state + n_v*d_state
+ *   z     [t][n_v*d_state] output-gate logits
+ *   alpha [t][n_v]         raw, before softplus(alpha + dt_bias)*ssm_a
+ *   beta  [t][n_v]         raw, before the sigmoid
+ *   out   [t][n_v*d_state]
+ */
+int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, const float *z,
+                   const float *alpha, const float *beta, float *out);
+int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qkv,
+                        const float *z, const float *alpha, const float *beta, float *out);
+
+/* Commits `rows` >= 1 rows of the batch that just ran: pos += rows,
+ * live = (live + rows) % slots (Runner::accept, forward.rs:675-688). */
+int rl_accept(rl_ctx *ctx, int rows);
+/* Position of the next token (Runner::pos, forward.rs:553-555); -1 on NULL. */
+int rl_pos(const rl_ctx *ctx);
+/* Ring slot holding the committed state (Caches::live); -1 on NULL. */
+int rl_live(const rl_ctx *ctx);
+
+/* Waits for the context's stream; returns RL_ETIMEOUT / RL_EINVAL when a
+ * kernel flagged a bounded wait that gave up or a bad argument on the device. */
+int rl_sync(rl_ctx *ctx);
+
+/* Tuning and dispatch knobs (rl_set_option). */
+typedef enum {
+    RL_OPT_SPLITS = 0,        /* force the KV splits of the decode walk (0: automatic) */
+    RL_OPT_PREFILL_ROWS = 1,  /* rows from which full attention takes the tensor-core
+                                 prefill kernel (needs a bf16 cache); 0 disables */
+    RL_OPT_CHUNK_ROWS = 2     /* rows from which a DeltaNet call with slots == 1 takes
+                                 the chunked tensor-core kernel; 0 disables */
+} rl_option;
+int rl_set_option(rl_ctx *ctx, int option, int64_t value);
+int64_t rl_get_option(const rl_ctx *ctx, int option);
+
+/* ---- state access (tests, checkpoints, benchmark set-up) --------------
+ * `where`: 0 = host pointer, 1 = device pointer.  f32 in the reference's
+ * layouts (forward.rs:236-254):
+ *   KV   [2][n_head_kv][n][head_dim] for positions p0..p0+n-1 of `layer`
+ *   conv [slots][conv_dim][conv_kernel-1] of linear layer `layer`
+ *   ssm  [n_v][slots][d_state][d_state]   of linear layer `layer`  */
+int rl_write_kv(rl_ctx *ctx, int layer, int p0, int n, const float *src, int where);
+int rl_read_kv(rl_ctx *ctx, int layer, int p0, int n, float *dst, int where);
+int rl_write_conv(rl_ctx *ctx, int layer, const float *src, int where);
+int rl_read_conv(rl_ctx *ctx, int layer, float *dst, int where);
+int rl_write_ssm(rl_ctx *ctx, int layer, const float *src, int where);
+int rl_read_ssm(rl_ctx *ctx, int layer, float *dst, int where);
+
+/* ---- per-kernel timing (the device side of the reference's Profile,
+ * forward.rs:102-233) --------------------------------------------------
+ * Launch counts are always kept.  With timing on, every launch of a kernel
+ * is bracketed by CUDA events on the context's stream; rl_profile_read
+ * waits for the stream and returns the summed event time of the launches
+ * recorded since the last rl_profile_reset.  Do not enable it while the
+ * stream is being captured into a CUDA graph. */
+typedef enum {
+    RL_PROF_PROLOGUE = 0, /* q/k norm + RoPE + KV append */
+    RL_PROF_DECODE = 1,   /* split-KV attention walk */
+    RL_PROF_MERGE = 2,    /* split merge + output gate */
+    RL_PROF_DN_STEP = 3,  /* DeltaNet token-sequential step */
+    RL_PROF_PREFILL = 4,  /* tensor-core causal prefill attention */
+    RL_PROF_DN_CHUNK = 5, /* DeltaNet chunked prefill */
+    RL_PROF_KERNELS = 6
+} rl_prof_kernel;
+int rl_profile_enable(rl_ctx *ctx, int on);
+int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches);
+int rl_profile_reset(rl_ctx *ctx);
+
+/* Library version string; never NULL. */
+const char *rl_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RLCUDA_H */

@@ -1,0 +1,145 @@
+// Shared device helpers for the sm_100a attention kernels: bf16 unpacking,
+// mbarrier + bulk-copy (TMA) wrappers, bounded waits, block reductions.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rl {
+
+// Device status bits, OR-ed into the context's status word by a kernel that
+// had to give up; rl_sync() turns them into RL_ETIMEOUT / RL_EINVAL.
+constexpr int DEV_TIMEOUT = 1;
+constexpr int DEV_BAD_ARG = 2;
+
+// A bounded wait gives up after this many SM clocks (about a second at the
+// B200's 1.0-2.0 GHz), sets DEV_TIMEOUT and lets the kernel return.
+constexpr long long WAIT_LIMIT_CYCLES = 2000000000ll;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier -------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+// Makes initialised barriers visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete, for at most WAIT_LIMIT_CYCLES.
+// Returns false (and flags DEV_TIMEOUT) when it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - start > WAIT_LIMIT_CYCLES) {
+            atomicOr(status, DEV_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---- bulk copies (TMA, non-tensor) ---------------------------------------
+// One contiguous global -> shared copy completing on `bar`.  Both addresses
+// 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+        "[%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- bf16 ----------------------------------------------------------------
+// Eight bf16 in a 16-byte word, widened to f32 exactly.
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 &w, float *f) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(u[i] << 16);
+        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) {
+    return x;
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+    return __float2bfloat16_rn(x);
+}
+
+// ---- warp / block reductions ---------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum over the block in f64 (the reference accumulates squares in f64).
+// `red` holds blockDim.x/32 doubles.  Every thread gets the total.
+__device__ __forceinline__ double block_sum_d(double v, double *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum_d(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = -0.0;
+    for (int w = 0; w < nw; ++w) t += red[w];
+    return t;
+}
+
+// The reference's rms_scale (forward.rs:1697-1711) from an f64 sum of f32
+// squares: the mean rounded to f32, an f32 root and reciprocal.
+__device__ __forceinline__ float rms_scale_from_sum(double sum, int n, float eps) {
+    const float mean = static_cast<float>(sum / static_cast<double>(n));
+    return 1.0f / sqrtf(__fadd_rn(mean, eps));
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float softplusf_(float x) {
+    return x > 20.0f ? x : log1pf(expf(x));
+}
+
+}  // namespace rl

@@ -1,0 +1,62 @@
+// Internal launch interface between the C ABI (rlcuda.cu) and the kernels.
+// Every pointer here is device memory.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace rl {
+
+// One call of the full-attention path: t rows at positions pos..pos+t-1 of
+// one layer's cache.
+struct FullArgs {
+    const float *qg;       // [t][n_head][2*hd]  query | gate
+    const float *k, *v;    // [t][n_kv][hd]
+    const float *q_norm, *k_norm;  // [hd]
+    void *k_cache, *v_cache;       // [n_kv][context][hd], f32 or bf16
+    float *q_f32;                  // [t][n_head][hd] normalised, rotated queries
+    __nv_bfloat16 *q_bf16;         // same in bf16, or null when not needed
+    float *part_o, *part_ml;       // split-KV partials
+    float *out;                    // [t][n_head*hd]
+    int *status;
+    int t, pos, n_head, n_kv, hd, context, n_rot;
+    float theta_scale, eps;
+    bool kv_bf16;
+};
+
+cudaError_t init_full_attn_kernels();
+cudaError_t launch_full_prologue(const FullArgs &a, cudaStream_t st);
+cudaError_t launch_decode_split(const FullArgs &a, int chunk, int n_splits, cudaStream_t st);
+cudaError_t launch_decode_merge(const FullArgs &a, int n_splits, cudaStream_t st);
+int decode_tile_positions(bool kv_bf16);
+
+// One call of the Gated DeltaNet path: t sequential rows over ring slots
+// (live+i)%slots -> (live+i+1)%slots of one layer.
+struct LinArgs {
+    const float *qkv;     // [t][conv_dim]
+    const float *z;       // [t][n_v*s]
+    const float *alpha;   // [t][n_v] raw
+    const float *beta;    // [t][n_v] raw
+    float *conv_state;    // [slots][conv_dim][kernel-1]
+    float *ssm_state;     // [n_v][slots][s][s]
+    const float *conv1d;  // [conv_dim][kernel]
+    const float *ssm_a, *dt_bias;  // [n_v]
+    const float *norm;    // [s]
+    float *out;           // [t][n_v*s]
+    int *status;
+    int t, slots, live, s, n_k, n_v, kernel;
+    float eps;
+};
+
+cudaError_t init_dn_kernels();
+cudaError_t launch_dn_step(const LinArgs &a, cudaStream_t st);
+int dn_max_group();
+
+// KV cache fill from f32 (host-visible test and bench helper): positions
+// [p0, p0+n) of every KV head, src [2][n_kv][n][hd] f32 on the device.
+cudaError_t launch_kv_fill(void *k_cache, void *v_cache, const float *src, int n_kv,
+                           int context, int hd, int p0, int n, bool kv_bf16, cudaStream_t st);
+cudaError_t launch_kv_read(const void *k_cache, const void *v_cache, float *dst, int n_kv,
+                           int context, int hd, int p0, int n, bool kv_bf16, cudaStream_t st);
+
+}  // namespace rl

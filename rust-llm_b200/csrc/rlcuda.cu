@@ -1,0 +1,652 @@
+// The C ABI (include/rlcuda.h): the device context that owns the caches,
+// the scratch and the stream, argument checking with the reference's
+// contract, and dispatch to the kernels.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "rlcuda.h"
+
+#define RL_VERSION_STRING "rlcuda 0.1 (sm_100a)"
+
+struct rl_ctx {
+    rl_config cfg{};
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    // caches (forward.rs:236-254)
+    void *kv = nullptr;       // [n_full][2][n_kv][context][hd], f32 or bf16
+    float *conv = nullptr;    // [n_linear][slots][conv_dim][kernel-1]
+    float *ssm = nullptr;     // [n_linear][n_v][slots][s][s]
+    // weights
+    float *q_norm = nullptr, *k_norm = nullptr;              // [n_full][hd]
+    float *conv1d = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;
+    // scratch
+    float *q_f32 = nullptr;
+    __nv_bfloat16 *q_bf16 = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    int64_t part_rows = 0;    // (row, split) pairs the partial buffers hold
+    float *stage = nullptr;   // staging for the *_host entry points
+    size_t stage_floats = 0;
+    int *status = nullptr;    // device status word (rl::DEV_*)
+    int pos = 0, live = 0;
+    int64_t opt_splits = 0, opt_prefill_rows = 0, opt_chunk_rows = 0;
+    float theta_scale = 1.0f;
+    std::string err;
+    // per-kernel timing (rl_profile_*)
+    bool prof_on = false;
+    struct Pending {
+        int kernel;
+        cudaEvent_t a, b;
+    };
+    std::vector<cudaEvent_t> ev_pool;
+    std::vector<Pending> pending;
+    double prof_ms[RL_PROF_KERNELS] = {};
+    int64_t prof_launches[RL_PROF_KERNELS] = {};
+};
+
+namespace {
+
+thread_local std::string tl_err;
+
+int fail(rl_ctx *ctx, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    else tl_err = buf;
+    return code;
+}
+
+#define CK(ctx, call)                                                                      \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess)                                                             \
+            return fail((ctx), RL_ECUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_),  \
+                        __FILE__, __LINE__);                                               \
+    } while (0)
+
+size_t kv_elem(const rl_config &c) { return c.kv_dtype == RL_KV_BF16 ? 2 : 4; }
+size_t conv_dim(const rl_config &c) {
+    return (size_t)2 * c.n_k_heads * c.d_state + (size_t)c.n_v_heads * c.d_state;
+}
+size_t kv_layer_elems(const rl_config &c) {
+    return (size_t)2 * c.n_head_kv * c.context * c.head_dim;
+}
+size_t conv_layer_floats(const rl_config &c) {
+    return (size_t)c.slots * conv_dim(c) * (c.conv_kernel - 1);
+}
+size_t ssm_layer_floats(const rl_config &c) {
+    return (size_t)c.n_v_heads * c.slots * c.d_state * c.d_state;
+}
+
+void *kv_layer(rl_ctx *x, int layer) {
+    return (char *)x->kv + (size_t)layer * kv_layer_elems(x->cfg) * kv_elem(x->cfg);
+}
+
+cudaEvent_t take_event(rl_ctx *x) {
+    if (!x->ev_pool.empty()) {
+        cudaEvent_t e = x->ev_pool.back();
+        x->ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Brackets one kernel launch: counts it, and with timing on records an
+// event pair around it on the context's stream.
+struct ProfScope {
+    rl_ctx *x;
+    int k;
+    cudaEvent_t a = nullptr, b = nullptr;
+    ProfScope(rl_ctx *x_, int k_) : x(x_), k(k_) {
+        x->prof_launches[k] += 1;
+        if (x->prof_on) {
+            a = take_event(x);
+            b = take_event(x);
+            cudaEventRecord(a, x->stream);
+        }
+    }
+    ~ProfScope() {
+        if (a) {
+            cudaEventRecord(b, x->stream);
+            x->pending.push_back({k, a, b});
+        }
+    }
+};
+
+int drain_profile(rl_ctx *x) {
+    if (x->pending.empty()) return RL_OK;
+    cudaError_t e = cudaStreamSynchronize(x->stream);
+    for (auto &p : x->pending) {
+        float ms = 0.0f;
+        if (e == cudaSuccess && cudaEventElapsedTime(&ms, p.a, p.b) == cudaSuccess)
+            x->prof_ms[p.kernel] += ms;
+        x->ev_pool.push_back(p.a);
+        x->ev_pool.push_back(p.b);
+    }
+    x->pending.clear();
+    return e == cudaSuccess ? RL_OK : RL_ECUDA;
+}
+
+void free_all(rl_ctx *x) {
+    for (auto &p : x->pending) {
+        x->ev_pool.push_back(p.a);
+        x->ev_pool.push_back(p.b);
+    }
+    x->pending.clear();
+    for (cudaEvent_t e : x->ev_pool) cudaEventDestroy(e);
+    x->ev_pool.clear();
+    void *ps[] = {x->kv, x->conv, x->ssm, x->q_norm, x->k_norm, x->conv1d, x->ssm_a,
+                  x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->part_o, x->part_ml,
+                  x->stage, x->status};
+    for (void *p : ps)
+        if (p) cudaFree(p);
+    if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
+}
+
+template <typename T>
+int alloc(rl_ctx *x, T **p, size_t elems) {
+    if (elems == 0) elems = 1;
+    cudaError_t e = cudaMalloc((void **)p, elems * sizeof(T));
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        return fail(x, RL_ENOMEM, "cudaMalloc of %zu bytes: %s", elems * sizeof(T),
+                    cudaGetErrorString(e));
+    }
+    return RL_OK;
+}
+
+// Shapes the kernels are built for; anything else is refused up front.
+int check_shapes(rl_ctx *x, const rl_config &c) {
+    if (c.n_full < 0 || c.n_linear < 0 || c.context < 1 || c.slots < 1 || c.max_batch < 1)
+        return fail(x, RL_EINVAL, "n_full, n_linear >= 0; context, slots, max_batch >= 1");
+    if (c.kv_dtype != RL_KV_F32 && c.kv_dtype != RL_KV_BF16)
+        return fail(x, RL_EINVAL, "kv_dtype %d is neither RL_KV_F32 nor RL_KV_BF16", c.kv_dtype);
+    if (c.n_full > 0) {
+        if (c.head_dim != 256 || c.n_head_kv < 1 || c.n_head != 4 * c.n_head_kv)
+            return fail(x, RL_EUNSUPPORTED,
+                        "full attention is built for head_dim 256 and 4 query heads per KV "
+                        "head (got head_dim %d, %d/%d heads)",
+                        c.head_dim, c.n_head, c.n_head_kv);
+        if (c.n_rot < 0 || c.n_rot > c.head_dim || (c.n_rot & 1))
+            return fail(x, RL_EINVAL, "n_rot must be even and at most head_dim");
+    }
+    if (c.n_linear > 0) {
+        if (c.d_state != 128 || c.conv_kernel != 4 || c.n_k_heads < 1 ||
+            c.n_v_heads % c.n_k_heads != 0 || c.n_v_heads / c.n_k_heads > rl::dn_max_group())
+            return fail(x, RL_EUNSUPPORTED,
+                        "the DeltaNet kernels are built for d_state 128, conv_kernel 4 and "
+                        "n_v a multiple (at most %d) of n_k (got %d, %d, %d/%d)",
+                        rl::dn_max_group(), c.d_state, c.conv_kernel, c.n_v_heads, c.n_k_heads);
+    }
+    if (c.max_batch > c.context && c.n_full > 0)
+        return fail(x, RL_EINVAL, "max_batch %d exceeds the context %d", c.max_batch, c.context);
+    return RL_OK;
+}
+
+int check_status(rl_ctx *x) {
+    int st = 0;
+    CK(x, cudaMemcpyAsync(&st, x->status, sizeof(int), cudaMemcpyDeviceToHost, x->stream));
+    CK(x, cudaStreamSynchronize(x->stream));
+    if (st) {
+        CK(x, cudaMemsetAsync(x->status, 0, sizeof(int), x->stream));
+        if (st & rl::DEV_TIMEOUT)
+            return fail(x, RL_ETIMEOUT, "a kernel's bounded wait gave up (status %d)", st);
+        return fail(x, RL_EINVAL, "a kernel flagged a bad argument (status %d)", st);
+    }
+    return RL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *rl_version(void) { return RL_VERSION_STRING; }
+
+const char *rl_last_error(const rl_ctx *ctx) {
+    return ctx ? ctx->err.c_str() : tl_err.c_str();
+}
+
+int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
+    if (!cfg || !out) return fail(nullptr, RL_EINVAL, "cfg and out must not be NULL");
+    *out = nullptr;
+    int code = check_shapes(nullptr, *cfg);
+    if (code) return code;
+    CK((rl_ctx *)nullptr, cudaSetDevice(device));
+    rl_ctx *x = new rl_ctx();
+    x->cfg = *cfg;
+    x->device = device;
+    const rl_config &c = x->cfg;
+    auto bail = [&](int code) {
+        tl_err = x->err;
+        free_all(x);
+        delete x;
+        return code;
+    };
+    if (cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+        x->num_sms = 148;
+    if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(x, RL_ECUDA, "cudaStreamCreate failed"));
+    x->own_stream = true;
+    if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess)
+        return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
+    const size_t hd = c.head_dim, nh = c.n_head, cd = conv_dim(c), s = c.d_state;
+    const size_t mb = c.max_batch;
+    if ((code = alloc(x, (char **)&x->kv, (size_t)c.n_full * kv_layer_elems(c) * kv_elem(c))) ||
+        (code = alloc(x, &x->conv, (size_t)c.n_linear * conv_layer_floats(c))) ||
+        (code = alloc(x, &x->ssm, (size_t)c.n_linear * ssm_layer_floats(c))) ||
+        (code = alloc(x, &x->q_norm, (size_t)c.n_full * hd)) ||
+        (code = alloc(x, &x->k_norm, (size_t)c.n_full * hd)) ||
+        (code = alloc(x, &x->conv1d, (size_t)c.n_linear * cd * c.conv_kernel)) ||
+        (code = alloc(x, &x->ssm_a, (size_t)c.n_linear * c.n_v_heads)) ||
+        (code = alloc(x, &x->dt_bias, (size_t)c.n_linear * c.n_v_heads)) ||
+        (code = alloc(x, &x->ssm_norm, (size_t)c.n_linear * s)) ||
+        (code = alloc(x, &x->status, 1)))
+        return bail(code);
+    if (c.n_full > 0) {
+        x->part_rows = std::max<int64_t>(mb, 4 * (int64_t)x->num_sms);
+        if ((code = alloc(x, &x->q_f32, mb * nh * hd)) ||
+            (code = alloc(x, &x->q_bf16, mb * nh * hd)) ||
+            (code = alloc(x, &x->part_o, (size_t)x->part_rows * nh * hd)) ||
+            (code = alloc(x, &x->part_ml, (size_t)x->part_rows * nh * 2)))
+            return bail(code);
+    }
+    // staging for the host entry points: the larger of the two paths' in+out
+    const size_t full_io = mb * (2 * hd * nh + 2 * hd * c.n_head_kv + hd * nh);
+    const size_t lin_io = mb * (cd + 2 * s * c.n_v_heads + 2 * c.n_v_heads);
+    x->stage_floats = std::max(c.n_full ? full_io : 0, c.n_linear ? lin_io : 0);
+    if ((code = alloc(x, &x->stage, x->stage_floats))) return bail(code);
+    // theta_scale = theta^(-2/n_rot), computed on the host exactly as
+    // forward.rs:1853 does, so the device advances the same f32 angle
+    x->theta_scale = c.n_rot > 0 ? std::pow(c.rope_theta, -2.0f / (float)c.n_rot) : 1.0f;
+    if ((code = rl_reset(x))) return bail(code);
+    // unit norm weights until the caller sets its own
+    if (c.n_full > 0 || c.n_linear > 0) {
+        std::string ones;
+        const size_t n = std::max(hd, s);
+        float *h = new float[n];
+        for (size_t i = 0; i < n; ++i) h[i] = 1.0f;
+        for (int l = 0; l < c.n_full; ++l) {
+            cudaMemcpy(x->q_norm + l * hd, h, hd * 4, cudaMemcpyHostToDevice);
+            cudaMemcpy(x->k_norm + l * hd, h, hd * 4, cudaMemcpyHostToDevice);
+        }
+        for (int l = 0; l < c.n_linear; ++l)
+            cudaMemcpy(x->ssm_norm + l * s, h, s * 4, cudaMemcpyHostToDevice);
+        delete[] h;
+        cudaMemset(x->conv1d, 0, (size_t)c.n_linear * cd * c.conv_kernel * 4);
+        cudaMemset(x->ssm_a, 0, (size_t)c.n_linear * c.n_v_heads * 4);
+        cudaMemset(x->dt_bias, 0, (size_t)c.n_linear * c.n_v_heads * 4);
+        if (cudaDeviceSynchronize() != cudaSuccess)
+            return bail(fail(x, RL_ECUDA, "weight initialisation failed"));
+    }
+    *out = x;
+    return RL_OK;
+}
+
+void rl_ctx_destroy(rl_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    free_all(ctx);
+    delete ctx;
+}
+
+int rl_set_stream(rl_ctx *ctx, void *stream) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+    ctx->stream = (cudaStream_t)stream;
+    ctx->own_stream = false;
+    return RL_OK;
+}
+
+void *rl_get_stream(const rl_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+int rl_reset(rl_ctx *ctx) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaMemsetAsync(ctx->kv, 0, (size_t)c.n_full * kv_layer_elems(c) * kv_elem(c),
+                            ctx->stream));
+    CK(ctx, cudaMemsetAsync(ctx->conv, 0, (size_t)c.n_linear * conv_layer_floats(c) * 4,
+                            ctx->stream));
+    CK(ctx, cudaMemsetAsync(ctx->ssm, 0, (size_t)c.n_linear * ssm_layer_floats(c) * 4,
+                            ctx->stream));
+    CK(ctx, cudaMemsetAsync(ctx->status, 0, sizeof(int), ctx->stream));
+    ctx->pos = 0;
+    ctx->live = 0;
+    return RL_OK;
+}
+
+int rl_set_weights_full(rl_ctx *ctx, int layer, const float *q_norm, const float *k_norm) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (layer < 0 || layer >= ctx->cfg.n_full || !q_norm || !k_norm)
+        return fail(ctx, RL_EINVAL, "full layer %d of %d, or a NULL weight", layer, ctx->cfg.n_full);
+    const size_t hd = ctx->cfg.head_dim;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaMemcpy(ctx->q_norm + layer * hd, q_norm, hd * 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(ctx->k_norm + layer * hd, k_norm, hd * 4, cudaMemcpyHostToDevice));
+    return RL_OK;
+}
+
+int rl_set_weights_linear(rl_ctx *ctx, int layer, const float *conv1d, const float *ssm_a,
+                          const float *dt_bias, const float *norm) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_linear || !conv1d || !ssm_a || !dt_bias || !norm)
+        return fail(ctx, RL_EINVAL, "linear layer %d of %d, or a NULL weight", layer, c.n_linear);
+    const size_t cw = conv_dim(c) * c.conv_kernel, nv = c.n_v_heads, s = c.d_state;
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaMemcpy(ctx->conv1d + layer * cw, conv1d, cw * 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(ctx->ssm_a + layer * nv, ssm_a, nv * 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(ctx->dt_bias + layer * nv, dt_bias, nv * 4, cudaMemcpyHostToDevice));
+    CK(ctx, cudaMemcpy(ctx->ssm_norm + layer * s, norm, s * 4, cudaMemcpyHostToDevice));
+    return RL_OK;
+}
+
+int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const float *k,
+                 const float *v, float *out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_full)
+        return fail(ctx, RL_EINVAL, "full layer %d of %d", layer, c.n_full);
+    if (t < 1 || t > c.max_batch)
+        return fail(ctx, RL_EINVAL, "a batch of %d rows, but the scratch was sized for %d", t,
+                    c.max_batch);
+    if (pos < 0 || (int64_t)pos + t > c.context)
+        return fail(ctx, RL_ECONTEXT, "context of %d tokens holds %d and cannot take %d more",
+                    c.context, pos, t);
+    if (!qg || !k || !v || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const bool bf16 = c.kv_dtype == RL_KV_BF16;
+    const size_t half = (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
+    rl::FullArgs a{};
+    a.qg = qg;
+    a.k = k;
+    a.v = v;
+    a.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
+    a.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
+    a.k_cache = kv_layer(ctx, layer);
+    a.v_cache = (char *)a.k_cache + half;
+    a.q_f32 = ctx->q_f32;
+    a.q_bf16 = nullptr;
+    a.part_o = ctx->part_o;
+    a.part_ml = ctx->part_ml;
+    a.out = out;
+    a.status = ctx->status;
+    a.t = t;
+    a.pos = pos;
+    a.n_head = c.n_head;
+    a.n_kv = c.n_head_kv;
+    a.hd = c.head_dim;
+    a.context = c.context;
+    a.n_rot = c.n_rot;
+    a.theta_scale = ctx->theta_scale;
+    a.eps = c.rms_eps;
+    a.kv_bf16 = bf16;
+    {
+        ProfScope ps(ctx, RL_PROF_PROLOGUE);
+        CK(ctx, rl::launch_full_prologue(a, ctx->stream));
+    }
+    // split-KV walk: enough (split, KV head, row) CTAs for two per SM
+    const int64_t n_kv_max = (int64_t)pos + t;
+    const int P = rl::decode_tile_positions(bf16);
+    int64_t splits = ctx->opt_splits > 0
+                         ? ctx->opt_splits
+                         : (2 * (int64_t)ctx->num_sms + (int64_t)c.n_head_kv * t - 1) /
+                               ((int64_t)c.n_head_kv * t);
+    splits = std::max<int64_t>(1, std::min<int64_t>(splits, ctx->part_rows / t));
+    splits = std::min<int64_t>(splits, (n_kv_max + P - 1) / P);
+    int64_t chunk = (n_kv_max + splits - 1) / splits;
+    chunk = (chunk + P - 1) / P * P;
+    splits = (n_kv_max + chunk - 1) / chunk;
+    {
+        ProfScope ps(ctx, RL_PROF_DECODE);
+        CK(ctx, rl::launch_decode_split(a, (int)chunk, (int)splits, ctx->stream));
+    }
+    {
+        ProfScope ps(ctx, RL_PROF_MERGE);
+        CK(ctx, rl::launch_decode_merge(a, (int)splits, ctx->stream));
+    }
+    return RL_OK;
+}
+
+int rl_full_attn_host(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const float *k,
+                      const float *v, float *out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (t < 1 || t > c.max_batch)
+        return fail(ctx, RL_EINVAL, "a batch of %d rows, but the scratch was sized for %d", t,
+                    c.max_batch);
+    if (!qg || !k || !v || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t nqg = (size_t)t * 2 * c.head_dim * c.n_head;
+    const size_t nk = (size_t)t * c.head_dim * c.n_head_kv;
+    const size_t no = (size_t)t * c.head_dim * c.n_head;
+    float *dq = ctx->stage, *dk = dq + nqg, *dv = dk + nk, *dout = dv + nk;
+    CK(ctx, cudaMemcpyAsync(dq, qg, nqg * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+    int code = rl_full_attn(ctx, layer, pos, t, dq, dk, dv, dout);
+    if (code) return code;
+    CK(ctx, cudaMemcpyAsync(out, dout, no * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return check_status(ctx);
+}
+
+int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, const float *z,
+                   const float *alpha, const float *beta, float *out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_linear)
+        return fail(ctx, RL_EINVAL, "linear layer %d of %d", layer, c.n_linear);
+    if (t < 1 || t > c.max_batch)
+        return fail(ctx, RL_EINVAL, "a batch of %d rows, but the scratch was sized for %d", t,
+                    c.max_batch);
+    if (live < 0 || live >= c.slots)
+        return fail(ctx, RL_EINVAL, "live slot %d of a ring of %d", live, c.slots);
+    if (!qkv || !z || !alpha || !beta || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    CK(ctx, cudaSetDevice(ctx->device));
+    rl::LinArgs a{};
+    a.qkv = qkv;
+    a.z = z;
+    a.alpha = alpha;
+    a.beta = beta;
+    a.conv_state = ctx->conv + (size_t)layer * conv_layer_floats(c);
+    a.ssm_state = ctx->ssm + (size_t)layer * ssm_layer_floats(c);
+    a.conv1d = ctx->conv1d + (size_t)layer * conv_dim(c) * c.conv_kernel;
+    a.ssm_a = ctx->ssm_a + (size_t)layer * c.n_v_heads;
+    a.dt_bias = ctx->dt_bias + (size_t)layer * c.n_v_heads;
+    a.norm = ctx->ssm_norm + (size_t)layer * c.d_state;
+    a.out = out;
+    a.status = ctx->status;
+    a.t = t;
+    a.slots = c.slots;
+    a.live = live;
+    a.s = c.d_state;
+    a.n_k = c.n_k_heads;
+    a.n_v = c.n_v_heads;
+    a.kernel = c.conv_kernel;
+    a.eps = c.rms_eps;
+    {
+        ProfScope ps(ctx, RL_PROF_DN_STEP);
+        CK(ctx, rl::launch_dn_step(a, ctx->stream));
+    }
+    return RL_OK;
+}
+
+int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qkv,
+                        const float *z, const float *alpha, const float *beta, float *out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (t < 1 || t > c.max_batch)
+        return fail(ctx, RL_EINVAL, "a batch of %d rows, but the scratch was sized for %d", t,
+                    c.max_batch);
+    if (!qkv || !z || !alpha || !beta || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t nx = (size_t)t * conv_dim(c), nz = (size_t)t * c.n_v_heads * c.d_state;
+    const size_t ng = (size_t)t * c.n_v_heads;
+    float *dx = ctx->stage, *dz = dx + nx, *da = dz + nz, *db = da + ng, *dout = db + ng;
+    CK(ctx, cudaMemcpyAsync(dx, qkv, nx * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaMemcpyAsync(dz, z, nz * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaMemcpyAsync(da, alpha, ng * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CK(ctx, cudaMemcpyAsync(db, beta, ng * 4, cudaMemcpyHostToDevice, ctx->stream));
+    int code = rl_linear_attn(ctx, layer, live, t, dx, dz, da, db, dout);
+    if (code) return code;
+    CK(ctx, cudaMemcpyAsync(out, dout, nz * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return check_status(ctx);
+}
+
+int rl_accept(rl_ctx *ctx, int rows) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (rows < 1)
+        return fail(ctx, RL_EINVAL,
+                    "a batch commits at least its first row; accept(%d) would leave the last "
+                    "row of the batch live, not the state from before it",
+                    rows);
+    if ((int64_t)ctx->pos + rows > ctx->cfg.context)
+        return fail(ctx, RL_ECONTEXT, "accept(%d) at pos %d runs past the context of %d", rows,
+                    ctx->pos, ctx->cfg.context);
+    ctx->pos += rows;
+    ctx->live = (ctx->live + rows) % ctx->cfg.slots;
+    return RL_OK;
+}
+
+int rl_pos(const rl_ctx *ctx) { return ctx ? ctx->pos : -1; }
+int rl_live(const rl_ctx *ctx) { return ctx ? ctx->live : -1; }
+
+int rl_sync(rl_ctx *ctx) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    return check_status(ctx);
+}
+
+int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (value < 0) return fail(ctx, RL_EINVAL, "option values are >= 0");
+    switch (option) {
+    case RL_OPT_SPLITS: ctx->opt_splits = value; return RL_OK;
+    case RL_OPT_PREFILL_ROWS: ctx->opt_prefill_rows = value; return RL_OK;
+    case RL_OPT_CHUNK_ROWS: ctx->opt_chunk_rows = value; return RL_OK;
+    default: return fail(ctx, RL_EINVAL, "unknown option %d", option);
+    }
+}
+
+int64_t rl_get_option(const rl_ctx *ctx, int option) {
+    if (!ctx) return -1;
+    switch (option) {
+    case RL_OPT_SPLITS: return ctx->opt_splits;
+    case RL_OPT_PREFILL_ROWS: return ctx->opt_prefill_rows;
+    case RL_OPT_CHUNK_ROWS: return ctx->opt_chunk_rows;
+    default: return -1;
+    }
+}
+
+int rl_profile_enable(rl_ctx *ctx, int on) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    ctx->prof_on = on != 0;
+    return RL_OK;
+}
+
+int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (kernel < 0 || kernel >= RL_PROF_KERNELS)
+        return fail(ctx, RL_EINVAL, "unknown kernel %d", kernel);
+    CK(ctx, cudaSetDevice(ctx->device));
+    if (drain_profile(ctx)) return fail(ctx, RL_ECUDA, "profile events could not be read");
+    if (total_ms) *total_ms = ctx->prof_ms[kernel];
+    if (launches) *launches = ctx->prof_launches[kernel];
+    return RL_OK;
+}
+
+int rl_profile_reset(rl_ctx *ctx) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    CK(ctx, cudaSetDevice(ctx->device));
+    drain_profile(ctx);
+    for (int k = 0; k < RL_PROF_KERNELS; ++k) ctx->prof_ms[k] = 0.0, ctx->prof_launches[k] = 0;
+    return RL_OK;
+}
+
+// ---- state access ----------------------------------------------------------
+
+static int kv_io(rl_ctx *ctx, int layer, int p0, int n, float *buf, int where, bool write) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_full || p0 < 0 || n < 1 || (int64_t)p0 + n > c.context || !buf)
+        return fail(ctx, RL_EINVAL, "KV range %d+%d of layer %d is outside the cache", p0, n, layer);
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t elems = (size_t)2 * c.n_head_kv * n * c.head_dim;
+    float *dev = buf;
+    if (where == 0) CK(ctx, cudaMalloc(&dev, elems * 4));
+    auto done = [&](int code) {
+        if (where == 0) cudaFree(dev);
+        return code;
+    };
+    if (write && where == 0)
+        if (cudaMemcpy(dev, buf, elems * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return done(fail(ctx, RL_ECUDA, "copy of the KV rows failed"));
+    void *kc = kv_layer(ctx, layer);
+    void *vc = (char *)kc + (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
+    cudaError_t e = write ? rl::launch_kv_fill(kc, vc, dev, c.n_head_kv, c.context, c.head_dim,
+                                               p0, n, c.kv_dtype == RL_KV_BF16, ctx->stream)
+                          : rl::launch_kv_read(kc, vc, dev, c.n_head_kv, c.context, c.head_dim,
+                                               p0, n, c.kv_dtype == RL_KV_BF16, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess && !write && where == 0)
+        e = cudaMemcpy(buf, dev, elems * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return done(fail(ctx, RL_ECUDA, "KV access: %s", cudaGetErrorString(e)));
+    return done(RL_OK);
+}
+
+int rl_write_kv(rl_ctx *ctx, int layer, int p0, int n, const float *src, int where) {
+    return kv_io(ctx, layer, p0, n, (float *)src, where, true);
+}
+int rl_read_kv(rl_ctx *ctx, int layer, int p0, int n, float *dst, int where) {
+    return kv_io(ctx, layer, p0, n, dst, where, false);
+}
+
+static int state_io(rl_ctx *ctx, int layer, float *buf, int where, bool write, bool ssm) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_linear || !buf)
+        return fail(ctx, RL_EINVAL, "linear layer %d of %d", layer, c.n_linear);
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t n = ssm ? ssm_layer_floats(c) : conv_layer_floats(c);
+    float *dev = (ssm ? ctx->ssm : ctx->conv) + (size_t)layer * n;
+    const cudaMemcpyKind kind = write ? (where ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice)
+                                      : (where ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost);
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    CK(ctx, write ? cudaMemcpy(dev, buf, n * 4, kind) : cudaMemcpy(buf, dev, n * 4, kind));
+    return RL_OK;
+}
+
+int rl_write_conv(rl_ctx *ctx, int layer, const float *src, int where) {
+    return state_io(ctx, layer, (float *)src, where, true, false);
+}
+int rl_read_conv(rl_ctx *ctx, int layer, float *dst, int where) {
+    return state_io(ctx, layer, dst, where, false, false);
+}
+int rl_write_ssm(rl_ctx *ctx, int layer, const float *src, int where) {
+    return state_io(ctx, layer, (float *)src, where, true, true);
+}
+int rl_read_ssm(rl_ctx *ctx, int layer, float *dst, int where) {
+    return state_io(ctx, layer, dst, where, false, true);
+}
+
+}  // extern "C"

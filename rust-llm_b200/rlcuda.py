@@ -1,0 +1,294 @@
+"""Python host wrapper over the C ABI of librlcuda.so (include/rlcuda.h).
+
+It mirrors the reference's interface for the attention path: a context that
+owns the caches (``Caches``, crates/rust-llm/src/forward.rs:236-254), the two
+attention calls ``full_attn`` / ``linear_attn`` (forward.rs:1220, :1484) and
+the lifecycle ``reset`` / ``accept`` / ``pos`` (forward.rs:553-688).  Errors
+come back as :class:`RlError` carrying the library's status and message, the
+way the reference's contract violations panic.
+
+There is no fallback: if librlcuda.so is missing or cannot be loaded this
+module raises on import of the library.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librlcuda.so")
+
+RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED, RL_ENOMEM = (
+    0, -1, -2, -3, -4, -5, -6, -7)
+RL_KV_F32, RL_KV_BF16 = 0, 1
+RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS = 0, 1, 2
+PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk")
+HOST, DEVICE = 0, 1
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+
+
+class RlError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"rlcuda status {code}: {msg}")
+        self.code = code
+
+
+class Config(ctypes.Structure):
+    """rl_config (include/rlcuda.h)."""
+
+    _fields_ = [
+        ("n_full", ctypes.c_int32),
+        ("n_linear", ctypes.c_int32),
+        ("n_head", ctypes.c_int32),
+        ("n_head_kv", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("n_rot", ctypes.c_int32),
+        ("rope_theta", ctypes.c_float),
+        ("rms_eps", ctypes.c_float),
+        ("d_state", ctypes.c_int32),
+        ("n_k_heads", ctypes.c_int32),
+        ("n_v_heads", ctypes.c_int32),
+        ("conv_kernel", ctypes.c_int32),
+        ("context", ctypes.c_int32),
+        ("slots", ctypes.c_int32),
+        ("kv_dtype", ctypes.c_int32),
+        ("max_batch", ctypes.c_int32),
+    ]
+
+    @property
+    def conv_dim(self) -> int:
+        return 2 * self.n_k_heads * self.d_state + self.n_v_heads * self.d_state
+
+
+def qwen35_config(n_full=1, n_linear=1, context=2048, slots=1, kv_dtype=RL_KV_F32,
+                  max_batch=16) -> Config:
+    """The Qwen3.5-4B attention shapes (the reference's docs/models.md:100-105)."""
+    return Config(n_full, n_linear, 16, 4, 256, 64, 1e7, 1e-6, 128, 16, 32, 4, context, slots,
+                  kv_dtype, max_batch)
+
+
+# Every symbol include/rlcuda.h declares, with its ctypes signature.
+SIGNATURES = {
+    "rl_ctx_create": ([_i, ctypes.POINTER(Config), ctypes.POINTER(_vp)], _i),
+    "rl_ctx_destroy": ([_vp], None),
+    "rl_last_error": ([_vp], ctypes.c_char_p),
+    "rl_set_stream": ([_vp, _vp], _i),
+    "rl_get_stream": ([_vp], _vp),
+    "rl_reset": ([_vp], _i),
+    "rl_set_weights_full": ([_vp, _i, _f32p, _f32p], _i),
+    "rl_set_weights_linear": ([_vp, _i, _f32p, _f32p, _f32p, _f32p], _i),
+    "rl_full_attn": ([_vp, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
+    "rl_full_attn_host": ([_vp, _i, _i, _i, _f32p, _f32p, _f32p, _f32p], _i),
+    "rl_linear_attn": ([_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp], _i),
+    "rl_linear_attn_host": ([_vp, _i, _i, _i, _f32p, _f32p, _f32p, _f32p, _f32p], _i),
+    "rl_accept": ([_vp, _i], _i),
+    "rl_pos": ([_vp], _i),
+    "rl_live": ([_vp], _i),
+    "rl_sync": ([_vp], _i),
+    "rl_set_option": ([_vp, _i, ctypes.c_int64], _i),
+    "rl_get_option": ([_vp, _i], ctypes.c_int64),
+    "rl_write_kv": ([_vp, _i, _i, _i, _vp, _i], _i),
+    "rl_read_kv": ([_vp, _i, _i, _i, _vp, _i], _i),
+    "rl_write_conv": ([_vp, _i, _vp, _i], _i),
+    "rl_read_conv": ([_vp, _i, _vp, _i], _i),
+    "rl_write_ssm": ([_vp, _i, _vp, _i], _i),
+    "rl_read_ssm": ([_vp, _i, _vp, _i], _i),
+    "rl_profile_enable": ([_vp, _i], _i),
+    "rl_profile_read": ([_vp, _i, ctypes.POINTER(ctypes.c_double),
+                         ctypes.POINTER(ctypes.c_int64)], _i),
+    "rl_profile_reset": ([_vp], _i),
+    "rl_version": ([], ctypes.c_char_p),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads librlcuda.so, raising if it is absent: there is no CPU fallback."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python rust-llm_b200/build.py` "
+                "(nvcc, sm_100a); the attention path has no fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def _ptr(x) -> int:
+    """A device pointer: a torch tensor (its data_ptr) or an int."""
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    return int(x)
+
+
+class Context:
+    """One device's attention caches and the calls that run on them."""
+
+    def __init__(self, cfg: Config, device: int = 0):
+        self.cfg = cfg
+        self.device = device
+        h = _vp()
+        self._L = lib()
+        code = self._L.rl_ctx_create(device, ctypes.byref(cfg), ctypes.byref(h))
+        if code:
+            raise RlError(code, self._L.rl_last_error(None).decode())
+        self._h = h
+
+    # -- lifecycle -------------------------------------------------------
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.rl_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self, code: int):
+        if code:
+            raise RlError(code, self._L.rl_last_error(self._h).decode())
+
+    @property
+    def handle(self):
+        return self._h
+
+    def reset(self):
+        self._check(self._L.rl_reset(self._h))
+
+    def accept(self, rows: int):
+        self._check(self._L.rl_accept(self._h, rows))
+
+    @property
+    def pos(self) -> int:
+        return self._L.rl_pos(self._h)
+
+    @property
+    def live(self) -> int:
+        return self._L.rl_live(self._h)
+
+    def sync(self):
+        self._check(self._L.rl_sync(self._h))
+
+    def set_stream(self, stream_ptr: int):
+        self._check(self._L.rl_set_stream(self._h, stream_ptr))
+
+    def set_option(self, opt: int, value: int):
+        self._check(self._L.rl_set_option(self._h, opt, value))
+
+    # -- per-kernel timing -----------------------------------------------
+    def profile(self, on: bool):
+        self._check(self._L.rl_profile_enable(self._h, int(on)))
+
+    def profile_reset(self):
+        self._check(self._L.rl_profile_reset(self._h))
+
+    def profile_read(self) -> dict:
+        """{kernel: (total_ms, launches)} since the last reset."""
+        out = {}
+        for k, name in enumerate(PROF_KERNELS):
+            ms = ctypes.c_double()
+            n = ctypes.c_int64()
+            self._check(self._L.rl_profile_read(self._h, k, ctypes.byref(ms), ctypes.byref(n)))
+            out[name] = (ms.value, n.value)
+        return out
+
+    # -- weights ---------------------------------------------------------
+    def set_weights_full(self, layer, q_norm, k_norm):
+        q_norm = np.ascontiguousarray(q_norm, np.float32)
+        k_norm = np.ascontiguousarray(k_norm, np.float32)
+        self._check(self._L.rl_set_weights_full(self._h, layer, _p(q_norm), _p(k_norm)))
+
+    def set_weights_linear(self, layer, conv1d, ssm_a, dt_bias, norm):
+        a = [np.ascontiguousarray(x, np.float32) for x in (conv1d, ssm_a, dt_bias, norm)]
+        self._check(self._L.rl_set_weights_linear(self._h, layer, *(_p(x) for x in a)))
+
+    # -- the two attention calls ----------------------------------------
+    def full_attn_host(self, layer, pos, qg, k, v) -> np.ndarray:
+        """Host arrays in, host array out (the Runner drop-in path)."""
+        t = qg.shape[0]
+        qg, k, v = (np.ascontiguousarray(x, np.float32) for x in (qg, k, v))
+        out = np.empty((t, self.cfg.n_head * self.cfg.head_dim), np.float32)
+        self._check(self._L.rl_full_attn_host(self._h, layer, pos, t, _p(qg), _p(k), _p(v),
+                                              _p(out)))
+        return out
+
+    def full_attn(self, layer, pos, t, qg, k, v, out):
+        """Device pointers (torch tensors or ints); enqueued, not waited for."""
+        self._check(self._L.rl_full_attn(self._h, layer, pos, t, _ptr(qg), _ptr(k), _ptr(v),
+                                         _ptr(out)))
+
+    def linear_attn_host(self, layer, live, qkv, z, alpha, beta) -> np.ndarray:
+        t = qkv.shape[0]
+        qkv, z, alpha, beta = (np.ascontiguousarray(x, np.float32) for x in (qkv, z, alpha, beta))
+        out = np.empty((t, self.cfg.n_v_heads * self.cfg.d_state), np.float32)
+        self._check(self._L.rl_linear_attn_host(self._h, layer, live, t, _p(qkv), _p(z),
+                                                _p(alpha), _p(beta), _p(out)))
+        return out
+
+    def linear_attn(self, layer, live, t, qkv, z, alpha, beta, out):
+        self._check(self._L.rl_linear_attn(self._h, layer, live, t, _ptr(qkv), _ptr(z),
+                                           _ptr(alpha), _ptr(beta), _ptr(out)))
+
+    # -- state -----------------------------------------------------------
+    def write_kv(self, layer, p0, src):
+        """src [2][n_kv][n][hd] f32: a numpy array (host) or a torch CUDA tensor."""
+        n = src.shape[2]
+        if isinstance(src, np.ndarray):
+            src = np.ascontiguousarray(src, np.float32)
+            self._check(self._L.rl_write_kv(self._h, layer, p0, n, src.ctypes.data, HOST))
+        else:
+            self._check(self._L.rl_write_kv(self._h, layer, p0, n, src.data_ptr(), DEVICE))
+
+    def read_kv(self, layer, p0, n) -> np.ndarray:
+        c = self.cfg
+        out = np.empty((2, c.n_head_kv, n, c.head_dim), np.float32)
+        self._check(self._L.rl_read_kv(self._h, layer, p0, n, out.ctypes.data, HOST))
+        return out
+
+    def _state_shape(self, ssm: bool):
+        c = self.cfg
+        if ssm:
+            return (c.n_v_heads, c.slots, c.d_state, c.d_state)
+        return (c.slots, c.conv_dim, c.conv_kernel - 1)
+
+    def write_conv(self, layer, src):
+        src = np.ascontiguousarray(src, np.float32).reshape(self._state_shape(False))
+        self._check(self._L.rl_write_conv(self._h, layer, src.ctypes.data, HOST))
+
+    def read_conv(self, layer) -> np.ndarray:
+        out = np.empty(self._state_shape(False), np.float32)
+        self._check(self._L.rl_read_conv(self._h, layer, out.ctypes.data, HOST))
+        return out
+
+    def write_ssm(self, layer, src):
+        src = np.ascontiguousarray(src, np.float32).reshape(self._state_shape(True))
+        self._check(self._L.rl_write_ssm(self._h, layer, src.ctypes.data, HOST))
+
+    def read_ssm(self, layer) -> np.ndarray:
+        out = np.empty(self._state_shape(True), np.float32)
+        self._check(self._L.rl_read_ssm(self._h, layer, out.ctypes.data, HOST))
+        return out
