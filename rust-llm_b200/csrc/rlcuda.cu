@@ -194,9 +194,16 @@ int check_shapes(rl_ctx *x, const rl_config &c) {
                         "n_v a multiple (at most %d) of n_k (got %d, %d, %d/%d)",
                         rl::dn_max_group(), c.d_state, c.conv_kernel, c.n_v_heads, c.n_k_heads);
     }
-    if (c.max_batch > c.context && c.n_full > 0)
-        return fail(x, RL_EINVAL, "max_batch %d exceeds the context %d", c.max_batch, c.context);
     return RL_OK;
+}
+
+// Host -> device copy ordered on the context's stream and finished before
+// return (a synchronous cudaMemcpy runs on the legacy stream, which a
+// non-blocking stream does not wait for).
+cudaError_t h2d(rl_ctx *x, void *dst, const void *src, size_t bytes) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, x->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
+    return e;
 }
 
 int check_status(rl_ctx *x) {
@@ -230,6 +237,9 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     CK((rl_ctx *)nullptr, cudaSetDevice(device));
     rl_ctx *x = new rl_ctx();
     x->cfg = *cfg;
+    // a batch longer than the context could never run (forward.rs:461)
+    x->cfg.max_batch =
+        std::max(1, std::min(std::max(x->cfg.max_batch, x->cfg.slots), x->cfg.context));
     x->device = device;
     const rl_config &c = x->cfg;
     auto bail = [&](int code) {
@@ -340,8 +350,8 @@ int rl_set_weights_full(rl_ctx *ctx, int layer, const float *q_norm, const float
         return fail(ctx, RL_EINVAL, "full layer %d of %d, or a NULL weight", layer, ctx->cfg.n_full);
     const size_t hd = ctx->cfg.head_dim;
     CK(ctx, cudaSetDevice(ctx->device));
-    CK(ctx, cudaMemcpy(ctx->q_norm + layer * hd, q_norm, hd * 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(ctx->k_norm + layer * hd, k_norm, hd * 4, cudaMemcpyHostToDevice));
+    CK(ctx, h2d(ctx, ctx->q_norm + layer * hd, q_norm, hd * 4));
+    CK(ctx, h2d(ctx, ctx->k_norm + layer * hd, k_norm, hd * 4));
     return RL_OK;
 }
 
@@ -353,10 +363,10 @@ int rl_set_weights_linear(rl_ctx *ctx, int layer, const float *conv1d, const flo
         return fail(ctx, RL_EINVAL, "linear layer %d of %d, or a NULL weight", layer, c.n_linear);
     const size_t cw = conv_dim(c) * c.conv_kernel, nv = c.n_v_heads, s = c.d_state;
     CK(ctx, cudaSetDevice(ctx->device));
-    CK(ctx, cudaMemcpy(ctx->conv1d + layer * cw, conv1d, cw * 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(ctx->ssm_a + layer * nv, ssm_a, nv * 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(ctx->dt_bias + layer * nv, dt_bias, nv * 4, cudaMemcpyHostToDevice));
-    CK(ctx, cudaMemcpy(ctx->ssm_norm + layer * s, norm, s * 4, cudaMemcpyHostToDevice));
+    CK(ctx, h2d(ctx, ctx->conv1d + layer * cw, conv1d, cw * 4));
+    CK(ctx, h2d(ctx, ctx->ssm_a + layer * nv, ssm_a, nv * 4));
+    CK(ctx, h2d(ctx, ctx->dt_bias + layer * nv, dt_bias, nv * 4));
+    CK(ctx, h2d(ctx, ctx->ssm_norm + layer * s, norm, s * 4));
     return RL_OK;
 }
 
@@ -593,13 +603,16 @@ static int kv_io(rl_ctx *ctx, int layer, int p0, int n, float *buf, int where, b
     CK(ctx, cudaSetDevice(ctx->device));
     const size_t elems = (size_t)2 * c.n_head_kv * n * c.head_dim;
     float *dev = buf;
-    if (where == 0) CK(ctx, cudaMalloc(&dev, elems * 4));
+    if (where == 0) CK(ctx, cudaMallocAsync((void **)&dev, elems * 4, ctx->stream));
     auto done = [&](int code) {
-        if (where == 0) cudaFree(dev);
+        if (where == 0) {
+            cudaFreeAsync(dev, ctx->stream);
+            cudaStreamSynchronize(ctx->stream);
+        }
         return code;
     };
     if (write && where == 0)
-        if (cudaMemcpy(dev, buf, elems * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (h2d(ctx, dev, buf, elems * 4) != cudaSuccess)
             return done(fail(ctx, RL_ECUDA, "copy of the KV rows failed"));
     void *kc = kv_layer(ctx, layer);
     void *vc = (char *)kc + (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
@@ -608,8 +621,10 @@ static int kv_io(rl_ctx *ctx, int layer, int p0, int n, float *buf, int where, b
                           : rl::launch_kv_read(kc, vc, dev, c.n_head_kv, c.context, c.head_dim,
                                                p0, n, c.kv_dtype == RL_KV_BF16, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-    if (e == cudaSuccess && !write && where == 0)
-        e = cudaMemcpy(buf, dev, elems * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && !write && where == 0) {
+        e = cudaMemcpyAsync(buf, dev, elems * 4, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    }
     if (e != cudaSuccess) return done(fail(ctx, RL_ECUDA, "KV access: %s", cudaGetErrorString(e)));
     return done(RL_OK);
 }
@@ -631,8 +646,9 @@ static int state_io(rl_ctx *ctx, int layer, float *buf, int where, bool write, b
     float *dev = (ssm ? ctx->ssm : ctx->conv) + (size_t)layer * n;
     const cudaMemcpyKind kind = write ? (where ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice)
                                       : (where ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost);
+    CK(ctx, write ? cudaMemcpyAsync(dev, buf, n * 4, kind, ctx->stream)
+                  : cudaMemcpyAsync(buf, dev, n * 4, kind, ctx->stream));
     CK(ctx, cudaStreamSynchronize(ctx->stream));
-    CK(ctx, write ? cudaMemcpy(dev, buf, n * 4, kind) : cudaMemcpy(buf, dev, n * 4, kind));
     return RL_OK;
 }
 
