@@ -51,7 +51,7 @@ def peaks():
 
 def ncu_traffic():
     """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "decode_split_bf16_32k.txt")
+    path = os.path.join(ROOT, "profiles", "decode_bf16_32k.txt")
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_launch:"):
@@ -221,8 +221,11 @@ def run_ours(args):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    for _ in range(args.warmup):
-        graph.replay()
+    # replays run on the current stream: keep it the library's stream, which
+    # the timing events below are recorded on
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
     stream.synchronize()
 
     def barrier():
@@ -234,7 +237,7 @@ def run_ours(args):
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks, torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(args.steps):
             graph.replay()
@@ -247,18 +250,23 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ctx.sync()
-    launches = args.steps * N_LAYERS * 3
+    launches = args.steps * N_LAYERS  # one decode kernel per layer and token
     layer_decodes = args.steps * N_LAYERS * world
     us_per_layer = ms * 1e3 / layer_decodes
     hbm_gbs = layer_decodes * KV_BYTES_PER_LAYER / (ms / 1e3) / 1e9
 
-    # ---- the dominant kernel alone: CUDA events around each decode_split
-    # launch on the library's stream, same workload, no graph
+    # ---- the dominant kernel alone: CUDA events around each decode launch on
+    # the library's stream, same workload, no graph
+    # A sleep kernel first backs up the stream, so each event pair brackets
+    # the kernel alone and not the host's launch latency.
     prof_steps = min(args.steps, 300)
     ctx.profile_reset()
     ctx.profile(True)
-    for _ in range(prof_steps):
-        step()
+    with torch.cuda.stream(stream):
+        for b in range(0, prof_steps, 10):
+            torch.cuda._sleep(20_000_000)
+            for _ in range(min(10, prof_steps - b)):
+                step()
     prof = ctx.profile_read()
     ctx.profile(False)
     dec_ms, dec_n = prof["decode"]
@@ -324,7 +332,7 @@ def run_ours(args):
         "prefill_tflops": None,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "decode_split_kernel<bf16>",
+                     "kernel": "decode_kernel<bf16, fused>",
                      "peak_source": peak_kind,
                      "avg_launch_us": avg_us, "launch_share": shares},
         "cpu_baseline": cpu,
@@ -349,7 +357,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="full-attention layers per step (8 in the model; fewer only to "
+                         "keep a profiler capture small)")
     args = ap.parse_args()
+    globals()["N_LAYERS"] = args.layers
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -132,7 +132,10 @@ __device__ __forceinline__ double block_sum_d(double v, double *red) {
 // The reference's rms_scale (forward.rs:1697-1711) from an f64 sum of f32
 // squares: the mean rounded to f32, an f32 root and reciprocal.
 __device__ __forceinline__ float rms_scale_from_sum(double sum, int n, float eps) {
-    const float mean = static_cast<float>(sum / static_cast<double>(n));
+    // sum / n; for a power-of-two n the product with the exact reciprocal is
+    // the same rounding and avoids a double division
+    const double mean_d = (n & (n - 1)) == 0 ? sum * (1.0 / (double)n) : sum / (double)n;
+    const float mean = static_cast<float>(mean_d);
     return 1.0f / sqrtf(__fadd_rn(mean, eps));
 }
 

@@ -16,19 +16,37 @@ struct FullArgs {
     void *k_cache, *v_cache;       // [n_kv][context][hd], f32 or bf16
     float *q_f32;                  // [t][n_head][hd] normalised, rotated queries
     __nv_bfloat16 *q_bf16;         // same in bf16, or null when not needed
-    float *part_o, *part_ml;       // split-KV partials
-    float *out;                    // [t][n_head*hd]
-    int *status;
     int t, pos, n_head, n_kv, hd, context, n_rot;
     float theta_scale, eps;
     bool kv_bf16;
 };
 
+// One launch of the split-KV decode kernel (decode_attn.cu).
+struct DecodeArgs {
+    const float *qg;              // [t][n_head][2*hd] raw query | gate
+    const float *k_in, *v_in;     // [t][n_kv][hd] raw (fused path: appended here)
+    const float *q_f32;           // [t][n_head][hd] normalised queries (unfused path)
+    const float *q_norm, *k_norm;
+    const float *rope_cs, *rope_sn;  // [context][n_rot/2] cos, sin of the RoPE angles
+    void *k_cache_v, *v_cache_v;  // [n_kv][context][hd]
+    float *part_o, *part_ml;      // cross-cluster partials
+    int *counters;                // [rows][n_kv][8] arrival counters, zero between launches
+    float *out;                   // [t][n_head*hd]
+    int *status;
+    int pos, t, context, n_head, n_kv, chunk, n_splits, csize, n_rot;
+    float theta_scale, eps;
+    bool kv_bf16, fused;
+};
+cudaError_t init_decode_kernels();
+cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);
+int decode_positions_per_tile(bool kv_bf16);
+int decode_max_active_clusters(bool kv_bf16, bool fused, int csize);
+
 cudaError_t init_full_attn_kernels();
+// cos/sin of every position's RoPE angles, [context][n_rot/2] each
+cudaError_t launch_rope_table(float *cs, float *sn, int context, int n_rot, float theta_scale,
+                              cudaStream_t st);
 cudaError_t launch_full_prologue(const FullArgs &a, cudaStream_t st);
-cudaError_t launch_decode_split(const FullArgs &a, int chunk, int n_splits, cudaStream_t st);
-cudaError_t launch_decode_merge(const FullArgs &a, int n_splits, cudaStream_t st);
-int decode_tile_positions(bool kv_bf16);
 
 // One call of the Gated DeltaNet path: t sequential rows over ring slots
 // (live+i)%slots -> (live+i+1)%slots of one layer.

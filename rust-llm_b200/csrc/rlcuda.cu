@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdint>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -35,12 +36,16 @@ struct rl_ctx {
     float *q_f32 = nullptr;
     __nv_bfloat16 *q_bf16 = nullptr;
     float *part_o = nullptr, *part_ml = nullptr;
-    int64_t part_rows = 0;    // (row, split) pairs the partial buffers hold
+    int64_t part_rows = 0;    // (row, cluster) pairs the partial buffers hold
+    int *counters = nullptr;  // [max_batch][n_kv][8] decode arrival counters
+    float *rope_cs = nullptr, *rope_sn = nullptr;  // [context][n_rot/2]
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 0, opt_chunk_rows = 0;
+    // resident clusters of the decode kernel: [fused][log2 cluster size]
+    int max_clusters[2][4] = {};
     float theta_scale = 1.0f;
     std::string err;
     // per-kernel timing (rl_profile_*)
@@ -153,7 +158,7 @@ void free_all(rl_ctx *x) {
     x->ev_pool.clear();
     void *ps[] = {x->kv, x->conv, x->ssm, x->q_norm, x->k_norm, x->conv1d, x->ssm_a,
                   x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->part_o, x->part_ml,
-                  x->stage, x->status};
+                  x->counters, x->rope_cs, x->rope_sn, x->stage, x->status};
     for (void *p : ps)
         if (p) cudaFree(p);
     if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
@@ -253,8 +258,13 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "cudaStreamCreate failed"));
     x->own_stream = true;
-    if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess)
+    if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
+        rl::init_decode_kernels() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
+    for (int f = 0; f < 2; ++f)
+        for (int lc = 0; lc < 4; ++lc)
+            x->max_clusters[f][lc] =
+                rl::decode_max_active_clusters(cfg->kv_dtype == RL_KV_BF16, f == 1, 1 << lc);
     const size_t hd = c.head_dim, nh = c.n_head, cd = conv_dim(c), s = c.d_state;
     const size_t mb = c.max_batch;
     if ((code = alloc(x, (char **)&x->kv, (size_t)c.n_full * kv_layer_elems(c) * kv_elem(c))) ||
@@ -273,7 +283,14 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         if ((code = alloc(x, &x->q_f32, mb * nh * hd)) ||
             (code = alloc(x, &x->q_bf16, mb * nh * hd)) ||
             (code = alloc(x, &x->part_o, (size_t)x->part_rows * nh * hd)) ||
-            (code = alloc(x, &x->part_ml, (size_t)x->part_rows * nh * 2)))
+            (code = alloc(x, &x->part_ml, (size_t)x->part_rows * nh * 8 * 2)) ||
+            (code = alloc(x, &x->counters, (size_t)mb * c.n_head_kv * 8)))
+            return bail(code);
+        if (cudaMemset(x->counters, 0, (size_t)mb * c.n_head_kv * 8 * sizeof(int)) != cudaSuccess)
+            return bail(fail(x, RL_ECUDA, "counter initialisation failed"));
+        const size_t half = std::max(1, c.n_rot / 2);
+        if ((code = alloc(x, &x->rope_cs, (size_t)c.context * half)) ||
+            (code = alloc(x, &x->rope_sn, (size_t)c.context * half)))
             return bail(code);
     }
     // staging for the host entry points: the larger of the two paths' in+out
@@ -284,6 +301,12 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     // theta_scale = theta^(-2/n_rot), computed on the host exactly as
     // forward.rs:1853 does, so the device advances the same f32 angle
     x->theta_scale = c.n_rot > 0 ? std::pow(c.rope_theta, -2.0f / (float)c.n_rot) : 1.0f;
+    if (c.n_full > 0) {
+        if (rl::launch_rope_table(x->rope_cs, x->rope_sn, c.context, c.n_rot, x->theta_scale,
+                                  x->stream) != cudaSuccess ||
+            cudaStreamSynchronize(x->stream) != cudaSuccess)
+            return bail(fail(x, RL_ECUDA, "RoPE table set-up failed"));
+    }
     if ((code = rl_reset(x))) return bail(code);
     // unit norm weights until the caller sets its own
     if (c.n_full > 0 || c.n_linear > 0) {
@@ -383,56 +406,101 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         return fail(ctx, RL_ECONTEXT, "context of %d tokens holds %d and cannot take %d more",
                     c.context, pos, t);
     if (!qg || !k || !v || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    if (((uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15)
+        return fail(ctx, RL_EINVAL, "qg, k, v and out must be 16-byte aligned");
     CK(ctx, cudaSetDevice(ctx->device));
     const bool bf16 = c.kv_dtype == RL_KV_BF16;
     const size_t half = (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
-    rl::FullArgs a{};
-    a.qg = qg;
-    a.k = k;
-    a.v = v;
-    a.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
-    a.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
-    a.k_cache = kv_layer(ctx, layer);
-    a.v_cache = (char *)a.k_cache + half;
-    a.q_f32 = ctx->q_f32;
-    a.q_bf16 = nullptr;
-    a.part_o = ctx->part_o;
-    a.part_ml = ctx->part_ml;
-    a.out = out;
-    a.status = ctx->status;
-    a.t = t;
-    a.pos = pos;
-    a.n_head = c.n_head;
-    a.n_kv = c.n_head_kv;
-    a.hd = c.head_dim;
-    a.context = c.context;
-    a.n_rot = c.n_rot;
-    a.theta_scale = ctx->theta_scale;
-    a.eps = c.rms_eps;
-    a.kv_bf16 = bf16;
-    {
+    void *k_cache = kv_layer(ctx, layer);
+    void *v_cache = (char *)k_cache + half;
+    const bool fused = t == 1;
+    if (!fused) {
+        // rows of a batch attend to each other's keys: append them all first
+        rl::FullArgs a{};
+        a.qg = qg;
+        a.k = k;
+        a.v = v;
+        a.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
+        a.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
+        a.k_cache = k_cache;
+        a.v_cache = v_cache;
+        a.q_f32 = ctx->q_f32;
+        a.q_bf16 = nullptr;
+        a.t = t;
+        a.pos = pos;
+        a.n_head = c.n_head;
+        a.n_kv = c.n_head_kv;
+        a.hd = c.head_dim;
+        a.context = c.context;
+        a.n_rot = c.n_rot;
+        a.theta_scale = ctx->theta_scale;
+        a.eps = c.rms_eps;
+        a.kv_bf16 = bf16;
         ProfScope ps(ctx, RL_PROF_PROLOGUE);
         CK(ctx, rl::launch_full_prologue(a, ctx->stream));
     }
-    // split-KV walk: enough (split, KV head, row) CTAs for two per SM
+    // Split-KV walk.  The (split, KV head, row) CTAs of one launch must all be
+    // resident at once (one wave); the splits of a (row, KV head) form
+    // clusters of csize CTAs.  Among cluster sizes 8, 4, 2, 1, take the one
+    // that keeps the most CTAs resident, the larger size on a tie (fewer
+    // partials for the cross-cluster merge).
     const int64_t n_kv_max = (int64_t)pos + t;
-    const int P = rl::decode_tile_positions(bf16);
-    int64_t splits = ctx->opt_splits > 0
-                         ? ctx->opt_splits
-                         : (2 * (int64_t)ctx->num_sms + (int64_t)c.n_head_kv * t - 1) /
-                               ((int64_t)c.n_head_kv * t);
-    splits = std::max<int64_t>(1, std::min<int64_t>(splits, ctx->part_rows / t));
-    splits = std::min<int64_t>(splits, (n_kv_max + P - 1) / P);
+    const int P = rl::decode_positions_per_tile(bf16);
+    const int64_t tiles = (n_kv_max + P - 1) / P;
+    const int64_t groups = (int64_t)c.n_head_kv * t;  // (KV head, row) pairs
+    int64_t splits = 0;
+    int csize = 1;
+    for (int lc = 3; lc >= 0; --lc) {
+        const int cs = 1 << lc;
+        int64_t per = (int64_t)ctx->max_clusters[fused ? 1 : 0][lc] / groups * cs;
+        if (ctx->opt_splits > 0) per = std::min<int64_t>(per, ctx->opt_splits);
+        per = std::min<int64_t>(per, (tiles + cs - 1) / cs * cs);
+        per = std::min<int64_t>(per, (int64_t)cs * std::max<int64_t>(1, ctx->part_rows / t));
+        per = std::min<int64_t>(per, (int64_t)cs * 64);  // the final merge holds 64 clusters
+        per = per / cs * cs;
+        // a smaller cluster only if it keeps at least 1/8 more CTAs resident:
+        // larger clusters leave fewer partials for the cross-cluster merge
+        if (per * 8 > splits * 9) splits = per, csize = cs;
+    }
+    if (splits < 1) {
+        // more (KV head, row) pairs than resident CTAs: one split each, in waves
+        splits = 1;
+        csize = 1;
+    }
     int64_t chunk = (n_kv_max + splits - 1) / splits;
     chunk = (chunk + P - 1) / P * P;
-    splits = (n_kv_max + chunk - 1) / chunk;
+    rl::DecodeArgs d{};
+    d.qg = qg;
+    d.k_in = k;
+    d.v_in = v;
+    d.q_f32 = ctx->q_f32;
+    d.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
+    d.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
+    d.rope_cs = ctx->rope_cs;
+    d.rope_sn = ctx->rope_sn;
+    d.k_cache_v = k_cache;
+    d.v_cache_v = v_cache;
+    d.part_o = ctx->part_o;
+    d.part_ml = ctx->part_ml;
+    d.counters = ctx->counters;
+    d.out = out;
+    d.status = ctx->status;
+    d.pos = pos;
+    d.t = t;
+    d.context = c.context;
+    d.n_head = c.n_head;
+    d.n_kv = c.n_head_kv;
+    d.chunk = (int)chunk;
+    d.n_splits = (int)splits;
+    d.csize = csize;
+    d.n_rot = c.n_rot;
+    d.theta_scale = ctx->theta_scale;
+    d.eps = c.rms_eps;
+    d.kv_bf16 = bf16;
+    d.fused = fused;
     {
         ProfScope ps(ctx, RL_PROF_DECODE);
-        CK(ctx, rl::launch_decode_split(a, (int)chunk, (int)splits, ctx->stream));
-    }
-    {
-        ProfScope ps(ctx, RL_PROF_MERGE);
-        CK(ctx, rl::launch_decode_merge(a, (int)splits, ctx->stream));
+        CK(ctx, rl::launch_decode(d, ctx->stream));
     }
     return RL_OK;
 }

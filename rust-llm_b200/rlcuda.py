@@ -18,7 +18,8 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "librlcuda.so")
+# RLCUDA_LIB points at a library built elsewhere (default: the in-tree build)
+LIB_PATH = os.environ.get("RLCUDA_LIB") or os.path.join(HERE, "librlcuda.so")
 
 RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED, RL_ENOMEM = (
     0, -1, -2, -3, -4, -5, -6, -7)
