@@ -185,6 +185,37 @@ int rl_profile_enable(rl_ctx *ctx, int on);
 int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches);
 int rl_profile_reset(rl_ctx *ctx);
 
+/* ---- full attention without allocation ---------------------------------
+ * No counterpart in the reference: its runner owns all of its memory, so it
+ * never needed one.  Some callers of this library cannot allocate device
+ * memory or hold an rl_ctx: a serving loop that plans every byte up front and
+ * must not allocate once tokens are flowing (the reference runner's own
+ * "the pass allocates nothing" rule), or a plug-in living inside another
+ * framework's memory budget.  This entry point allocates nothing.  The
+ * caller passes its own KV cache for one layer (k_cache, v_cache:
+ * [n_head_kv][context][head_dim] of cfg->kv_dtype), the layer's q_norm and
+ * k_norm ([head_dim], device), the inputs and the output, all device
+ * pointers with the layouts of rl_full_attn; only cfg's full-attention
+ * fields (n_head, n_head_kv, head_dim, n_rot, rope_theta, rms_eps, context,
+ * kv_dtype) are read.  The work is enqueued on `stream` of the current
+ * device; the call returns without waiting.
+ *
+ * Scratch lives in one static device array of RL_NOALLOC_SCRATCH_BYTES per
+ * GPU that loads the library, held until the process exits.  A call whose
+ * scratch would not fit (many rows at long context) is refused with
+ * RL_EINVAL.  Every call shares that array and it keeps the last call's
+ * contents (the call clears what must start at zero itself), so calls whose
+ * work overlaps on the GPU (other streams, other host threads) race: run them
+ * one after another.  The first call on a device, with that device current,
+ * resolves the array's device address and the kernels' launch limits; make
+ * that first call before any stream capture.  A device-side wait that gives
+ * up leaves `out` unwritten; there is no status channel beyond the return
+ * code, which covers argument and launch errors. */
+#define RL_NOALLOC_SCRATCH_BYTES (4u << 20)
+int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_cache, void *v_cache,
+                         const float *q_norm, const float *k_norm, int pos, int t,
+                         const float *qg, const float *k, const float *v, float *out);
+
 /* Library version string; never NULL. */
 const char *rl_version(void);
 

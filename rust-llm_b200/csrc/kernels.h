@@ -77,4 +77,7 @@ cudaError_t launch_kv_fill(void *k_cache, void *v_cache, const float *src, int n
 cudaError_t launch_kv_read(const void *k_cache, const void *v_cache, float *dst, int n_kv,
                            int context, int hd, int p0, int n, bool kv_bf16, cudaStream_t st);
 
+// Sets the calling thread's message for rl_last_error(NULL).
+void set_thread_error(const char *msg);
+
 }  // namespace rl

@@ -226,6 +226,8 @@ int check_status(rl_ctx *x) {
 
 }  // namespace
 
+void rl::set_thread_error(const char *msg) { tl_err = msg; }
+
 extern "C" {
 
 const char *rl_version(void) { return RL_VERSION_STRING; }

@@ -103,6 +103,8 @@ SIGNATURES = {
     "rl_profile_read": ([_vp, _i, ctypes.POINTER(ctypes.c_double),
                          ctypes.POINTER(ctypes.c_int64)], _i),
     "rl_profile_reset": ([_vp], _i),
+    "rl_full_attn_noalloc": ([ctypes.POINTER(Config), _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp,
+                              _vp, _vp], _i),
     "rl_version": ([], ctypes.c_char_p),
 }
 
