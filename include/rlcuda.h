@@ -146,8 +146,10 @@ typedef enum {
     RL_OPT_SPLITS = 0,        /* force the KV splits of the decode walk (0: automatic) */
     RL_OPT_PREFILL_ROWS = 1,  /* rows from which full attention takes the tensor-core
                                  prefill kernel (needs a bf16 cache); 0 disables */
-    RL_OPT_CHUNK_ROWS = 2     /* rows from which a DeltaNet call with slots == 1 takes
+    RL_OPT_CHUNK_ROWS = 2,    /* rows from which a DeltaNet call with slots == 1 takes
                                  the chunked tensor-core kernel; 0 disables */
+    RL_OPT_CLUSTER = 3        /* force the cluster size (1, 2, 4, 8) of the decode walk's
+                                 splits (0: automatic) */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);

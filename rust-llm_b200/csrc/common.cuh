@@ -65,6 +65,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     return true;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier 1 over the 128 threads of warps 0-3 (the consumer warps of
+// the decode kernels; their producer warp does not take part).
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 // ---- bulk copies (TMA, non-tensor) ---------------------------------------
 // One contiguous global -> shared copy completing on `bar`.  Both addresses
 // 16-byte aligned, bytes a multiple of 16.  No multicast.
@@ -75,6 +83,30 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "[%3];" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// ---- tensor copies (TMA, tiled) --------------------------------------------
+// One box of a 2-D tensor map, global -> shared, completing on `bar`.  The
+// map is a __grid_constant__ kernel parameter.  x (the innermost
+// coordinate, in elements) must keep x * element size a multiple of 16
+// bytes; y may be any row.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a box written
+// with the 128-byte swizzle (rows of 128 bytes, box base 1024-byte aligned).
+__device__ __forceinline__ uint32_t swz128(int r, int c) {
+    return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
 // ---- bf16 ----------------------------------------------------------------

@@ -28,6 +28,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "decode_merge.cuh"
 #include "kernels.h"
 
 namespace cg = cooperative_groups;
@@ -76,45 +77,6 @@ __device__ __forceinline__ void chunk_to_f2(const uint4 &w, float2 *f, const flo
     f[1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
 }
 
-__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// RMSNorm (f64 sum of f32 squares, forward.rs:1697-1711) and partial RoPE
-// from the angle table of one 256-wide head by one warp; the result lands in
-// `dst` (shared).  x holds the lane's 8 consecutive inputs.
-__device__ __forceinline__ void warp_norm_rope(const float *x, const float *w, float *dst,
-                                               const float *cs, const float *sn, int n_rot,
-                                               float eps, int lane) {
-    double sq = 0.0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sq += (double)__fmul_rn(x[e], x[e]);
-    sq = warp_sum_d(sq);
-    const float scale = rms_scale_from_sum(sq, dec2::HD, eps);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) dst[lane * 8 + e] = __fmul_rn(__fmul_rn(x[e], scale), w[lane * 8 + e]);
-    __syncwarp();
-    const int half = n_rot / 2;
-    float y[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const int d = lane * 8 + e;
-        y[e] = dst[d];
-        if (d < n_rot) {
-            const int pr = d < half ? d : d - half;
-            const float c = cs[pr], s = sn[pr];
-            const float x0 = dst[pr], x1 = dst[pr + half];
-            y[e] = d < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
-                            : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-        }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < 8; ++e) dst[lane * 8 + e] = y[e];
-    __syncwarp();
-}
 
 template <typename KV, bool FUSED>
 __global__ void __launch_bounds__(dec2::THREADS, 2) decode_kernel(const DecodeArgs a) {
@@ -210,7 +172,7 @@ __global__ void __launch_bounds__(dec2::THREADS, 2) decode_kernel(const DecodeAr
                 rope_sn[i] = a.rope_sn[(size_t)pos_row * half + i];
             }
             consumer_bar();
-            warp_norm_rope(x, a.q_norm, q_s[warp], rope_cs, rope_sn, a.n_rot, a.eps, lane);
+            warp_norm_rope<dec2::HD>(x, a.q_norm, q_s[warp], rope_cs, rope_sn, a.n_rot, a.eps, lane);
             if (covers_new && warp < 2) {
                 // warp 0: the new key (normed, rotated); warp 1: the new value.
                 // Both are rounded to the cache's type, stored to the cache
@@ -224,7 +186,7 @@ __global__ void __launch_bounds__(dec2::THREADS, 2) decode_kernel(const DecodeAr
                 }
                 float y[8];
                 if (warp == 0) {
-                    warp_norm_rope(x, a.k_norm, kf_s, rope_cs, rope_sn, a.n_rot, a.eps, lane);
+                    warp_norm_rope<dec2::HD>(x, a.k_norm, kf_s, rope_cs, rope_sn, a.n_rot, a.eps, lane);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) y[e] = kf_s[lane * 8 + e];
                 } else {
@@ -388,143 +350,8 @@ __global__ void __launch_bounds__(dec2::THREADS, 2) decode_kernel(const DecodeAr
         }
     }
     __syncthreads();
-    __shared__ float wscale[CWARPS][GROUP];
-    if (tid < GROUP) {
-        float M = -INFINITY;
-        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, red_ml[(w * GROUP + tid) * 2]);
-        float L = 0.0f;
-        for (int w = 0; w < CWARPS; ++w) {
-            const float mw = red_ml[(w * GROUP + tid) * 2];
-            const float sc = mw == -INFINITY ? 0.0f : exp2f(mw - M);
-            wscale[w][tid] = sc;
-            L = fmaf(red_ml[(w * GROUP + tid) * 2 + 1], sc, L);
-        }
-        cta_m[tid] = M;
-        cta_l[tid] = L;
-    }
-    __syncthreads();
-    for (int e4 = tid; e4 < GROUP * HD / 4; e4 += THREADS) {
-        const int h = e4 / (HD / 4);
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int w = 0; w < CWARPS; ++w) {
-            const float sc = wscale[w][h];
-            const float4 r = reinterpret_cast<const float4 *>(red_o)[w * GROUP * HD / 4 + e4];
-            o.x = fmaf(r.x, sc, o.x), o.y = fmaf(r.y, sc, o.y);
-            o.z = fmaf(r.z, sc, o.z), o.w = fmaf(r.w, sc, o.w);
-        }
-        reinterpret_cast<float4 *>(cta_o)[e4] = o;
-    }
-
-    // ---------------- merge the cluster's splits through DSMEM ----------------
-    cluster.sync();
-    const int ds = HD / C;          // this rank's slice of the head dimension
-    const int d0 = crank * ds;
-    float *gout_o = a.part_o;       // [row][head][cluster][HD]
-    float *gout_ml = a.part_ml;     // [row][head][cluster][C][2]
-    __shared__ float rscale[8][GROUP], cl_M[GROUP], cl_L[GROUP];
-    if (tid < GROUP) {
-        float mr[8], lr[8];
-        float M = -INFINITY;
-        for (int r = 0; r < C; ++r) {
-            mr[r] = *cluster.map_shared_rank(&cta_m[tid], r);
-            lr[r] = *cluster.map_shared_rank(&cta_l[tid], r);
-            M = fmaxf(M, mr[r]);
-        }
-        float L = 0.0f;
-        for (int r = 0; r < C; ++r) {
-            const float sc = mr[r] == -INFINITY ? 0.0f : exp2f(mr[r] - M);
-            rscale[r][tid] = sc;
-            L = fmaf(lr[r], sc, L);
-        }
-        cl_M[tid] = M;
-        cl_L[tid] = L;
-    }
-    __syncthreads();
-    for (int e4 = tid; e4 < GROUP * ds / 4; e4 += THREADS) {
-        const int h = e4 / (ds / 4), d = d0 + (e4 % (ds / 4)) * 4;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < C; ++r) {
-            const float sc = rscale[r][h];
-            const float4 v = *reinterpret_cast<const float4 *>(
-                cluster.map_shared_rank(&cta_o[h * HD + d], r));
-            o.x = fmaf(v.x, sc, o.x), o.y = fmaf(v.y, sc, o.y);
-            o.z = fmaf(v.z, sc, o.z), o.w = fmaf(v.w, sc, o.w);
-        }
-        const int hh = head0 + h;  // (row, query head)
-        if (n_cl == 1) {
-            const float L = cl_L[h];
-            const float *g = a.qg + (size_t)hh * 2 * HD + HD + d;
-            float *dst = a.out + (size_t)hh * HD + d;
-            dst[0] = (o.x / L) * sigmoidf_(g[0]);
-            dst[1] = (o.y / L) * sigmoidf_(g[1]);
-            dst[2] = (o.z / L) * sigmoidf_(g[2]);
-            dst[3] = (o.w / L) * sigmoidf_(g[3]);
-        } else {
-            *reinterpret_cast<float4 *>(&gout_o[((size_t)hh * n_cl + cl) * HD + d]) = o;
-            if (e4 % (ds / 4) == 0) {
-                gout_ml[(((size_t)hh * n_cl + cl) * C + crank) * 2] = cl_M[h];
-                gout_ml[(((size_t)hh * n_cl + cl) * C + crank) * 2 + 1] = cl_L[h];
-            }
-        }
-    }
-    cluster.sync();  // peers are done reading this CTA's shared memory
-    if (n_cl == 1) {
-        if (flag_s && tid == 0) atomicOr(a.status, DEV_TIMEOUT);
-        return;
-    }
-
-    // ---------------- last cluster to finish a slice merges it ----------------
-    __threadfence();
-    __syncthreads();
-    __shared__ int last_s;
-    int *counter = a.counters + ((size_t)row * a.n_kv + kh) * 8 + crank;
-    if (tid == 0) last_s = atomicAdd(counter, 1) == n_cl - 1;
-    __syncthreads();
-    if (!last_s) return;
-    __threadfence();
-    // one thread per (head, 4 dims) of the slice; every load below is
-    // independent of the others, so they are all in flight at once
-    __shared__ float fscale[GROUP][64];  // per-cluster weights, n_cl <= 64
-    __shared__ float fL[GROUP];
-    if (tid < GROUP) {
-        const float *ml = gout_ml + (size_t)(head0 + tid) * n_cl * C * 2 + crank * 2;
-        float M = -INFINITY;
-        for (int c = 0; c < n_cl; ++c) M = fmaxf(M, __ldcg(ml + (size_t)c * C * 2));
-        float L = 0.0f;
-        for (int c = 0; c < n_cl; ++c) {
-            const float mc = __ldcg(ml + (size_t)c * C * 2);
-            const float sc = mc == -INFINITY ? 0.0f : exp2f(mc - M);
-            fscale[tid][c] = sc;
-            L = fmaf(__ldcg(ml + (size_t)c * C * 2 + 1), sc, L);
-        }
-        fL[tid] = L;
-    }
-    __syncthreads();
-    for (int e4 = tid; e4 < GROUP * ds / 4; e4 += THREADS) {
-        const int h = e4 / (ds / 4), d = d0 + (e4 % (ds / 4)) * 4;
-        const int hh = head0 + h;
-        const float4 *src = reinterpret_cast<const float4 *>(gout_o + (size_t)hh * n_cl * HD + d);
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-        for (int c = 0; c < n_cl; ++c) {
-            const float4 v = __ldcg(src + (size_t)c * HD / 4);
-            const float sc = fscale[h][c];
-            o.x = fmaf(v.x, sc, o.x), o.y = fmaf(v.y, sc, o.y);
-            o.z = fmaf(v.z, sc, o.z), o.w = fmaf(v.w, sc, o.w);
-        }
-        const float L = fL[h];
-        const float *g = a.qg + (size_t)hh * 2 * HD + HD + d;
-        float *dst = a.out + (size_t)hh * HD + d;
-        dst[0] = (o.x / L) * sigmoidf_(g[0]);
-        dst[1] = (o.y / L) * sigmoidf_(g[1]);
-        dst[2] = (o.z / L) * sigmoidf_(g[2]);
-        dst[3] = (o.w / L) * sigmoidf_(g[3]);
-    }
-    if (tid == 0) {
-        *counter = 0;  // ready for the next launch (and the next graph replay)
-        if (flag_s) atomicOr(a.status, DEV_TIMEOUT);
-    }
+    decode_merge<HD, GROUP, CWARPS, THREADS>(cluster, a, red_o, red_ml, cta_o, cta_m, cta_l,
+                                             flag_s, head0, kh, row, crank, cl, n_cl, C, tid);
 }
 
 template <typename KV, bool FUSED>

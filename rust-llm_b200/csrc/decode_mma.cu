@@ -1,0 +1,481 @@
+// Split-KV flash decoding over a bf16 KV cache, sm_100a: K/V tiles staged by
+// TMA tensor copies, both dot products on the tensor cores (mma.sync
+// m16n8k16, bf16 in, f32 accumulate).
+//
+// The step is bound by HBM: every cached position is read once (1 KiB of K
+// and V per KV head) and used by the four query heads of its group.  What
+// keeps it at the memory roofline:
+//   - copies are TMA boxes of 64 positions x 64 dims (8 KiB, 128-byte
+//     swizzle): one tile of 64 positions is 4 K boxes + 4 V boxes, 64 KiB,
+//     in a 3-deep ring per CTA.  Row-sized (512 B) bulk copies issue too
+//     slowly to keep one SM's share of HBM in flight;
+//   - the swizzle puts the 8 rows an ldmatrix reads in 8 different bank
+//     groups, so the stage needs no padding and one copy fills it;
+//   - the two dot products are m16n8k16 chains (~2 instructions per
+//     position and head instead of ~25 on the CUDA cores), leaving the
+//     consumer warps idle most of the time;
+//   - the fused prologue issues all of its small loads (query, gate, norm
+//     weights, RoPE row) before using any of them.
+//
+// Precision: the queries and the softmax weights enter the MMAs as a bf16
+// pair hi + lo (hi = bf16(x), lo = bf16(x - hi)), a 16-bit mantissa; keys and
+// values are already bf16 in the cache.  So S^T = K [q_hi | q_lo]^T and
+// O^T = V^T [p_hi | p_lo]^T are each one m16n8k16 chain whose 8 columns hold
+// the 4 heads' hi parts and lo parts, summed afterwards.  Residual error is
+// ~1e-5 relative, inside the 1e-4 bar.
+//
+// Shape of the work: one CTA per (KV split, KV head, query row), one CTA per
+// SM; a tile is 64 positions, 16 per consumer warp (the M of S^T).  A single
+// producer lane keeps STAGES tiles in flight behind full/empty mbarriers.
+// The cross-split merge, the output gate and (for one decode row) the fused
+// q/k norm, RoPE and KV append are shared with decode_attn.cu.
+//
+// Reference: attend_batch / softmax of Exec::full_attn
+// (crates/rust-llm/src/forward.rs:1783-1842) and its gate (:1327-1340).
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "decode_merge.cuh"
+#include "kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace rl {
+namespace dm {
+constexpr int HD = 256;
+constexpr int GROUP = 4;
+constexpr int CWARPS = 4;
+constexpr int THREADS = (CWARPS + 1) * 32;
+constexpr int STAGES = 3;
+constexpr int P = 16 * CWARPS;                  // positions per tile
+constexpr int BOX_COLS = kDecodeBoxCols;        // dims per box (128 bytes)
+constexpr int NBOX = HD / BOX_COLS;             // boxes per 256-dim row block
+constexpr int BOX_BYTES = P * BOX_COLS * 2;     // 8 KiB
+constexpr int HALF_BYTES = NBOX * BOX_BYTES;    // K (or V) part of a stage
+constexpr int STAGE_BYTES = 2 * HALF_BYTES;     // 64 KiB
+constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr float LOG2E = 1.4426950408889634f;
+static_assert(kDecodeBoxRows == P, "one box row per tile position");
+static_assert((size_t)STAGES * STAGE_BYTES >=
+                  (size_t)(CWARPS * GROUP * HD + CWARPS * GROUP * 2 + GROUP * HD) * 4,
+              "the merge scratch reuses the stage ring");
+}  // namespace dm
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// d += a (16x16, row) * b (16x8, col), bf16 in, f32 accumulate
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+// The bf16 pair (hi, lo) of x: hi = bf16(x), lo = bf16(x - hi).
+__device__ __forceinline__ float bf16_hi(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// One lane's share (8 consecutive dims) of a 256-wide head before RMSNorm
+// and RoPE, with every global load issued before any is used.
+struct LaneHead {
+    float x[8], w[8], c[8], s[8];
+};
+
+__device__ __forceinline__ void load4(float *dst, const float *src) {
+    const float4 f = *reinterpret_cast<const float4 *>(src);
+    dst[0] = f.x, dst[1] = f.y, dst[2] = f.z, dst[3] = f.w;
+}
+
+__device__ __forceinline__ void load_lane_head(LaneHead &h, const float *x, const float *w,
+                                               const float *cs_row, const float *sn_row,
+                                               int n_rot, int lane) {
+    load4(h.x, x + lane * 8);
+    load4(h.x + 4, x + lane * 8 + 4);
+    load4(h.w, w + lane * 8);
+    load4(h.w + 4, w + lane * 8 + 4);
+    const int half = n_rot / 2;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
+        const int pr = d < half ? d : d - half;
+        h.c[e] = d < n_rot ? cs_row[pr] : 1.0f;
+        h.s[e] = d < n_rot ? sn_row[pr] : 0.0f;
+    }
+}
+
+// RMSNorm (f64 sum of f32 squares, forward.rs:1697-1711) then partial RoPE
+// (forward.rs:1851-1862) of one head by one warp; the result lands in `dst`
+// (shared, 256 floats).
+__device__ __forceinline__ void lane_norm_rope(const LaneHead &h, float *dst, int n_rot, float eps,
+                                               int lane) {
+    double sq = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sq += (double)__fmul_rn(h.x[e], h.x[e]);
+    sq = warp_sum_d(sq);
+    const float scale = rms_scale_from_sum(sq, dm::HD, eps);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dst[lane * 8 + e] = __fmul_rn(__fmul_rn(h.x[e], scale), h.w[e]);
+    __syncwarp();
+    const int half = n_rot / 2;
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
+        y[e] = dst[d];
+        if (d < n_rot) {
+            const int pr = d < half ? d : d - half;
+            const float x0 = dst[pr], x1 = dst[pr + half];
+            y[e] = d < half ? __fsub_rn(__fmul_rn(x0, h.c[e]), __fmul_rn(x1, h.s[e]))
+                            : __fadd_rn(__fmul_rn(x0, h.s[e]), __fmul_rn(x1, h.c[e]));
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dst[lane * 8 + e] = y[e];
+    __syncwarp();
+}
+
+template <bool FUSED>
+__global__ void __launch_bounds__(dm::THREADS, 1)
+    decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ CUtensorMap kv_map) {
+    using namespace dm;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+    __shared__ __align__(16) float q_s[GROUP][HD];
+    __shared__ __align__(16) __nv_bfloat16 newk_s[HD], newv_s[HD];
+    __shared__ __align__(16) float kf_s[HD];
+    __shared__ __align__(16) __nv_bfloat16 pbuf[CWARPS][8][16];  // P^T per warp: [col][pos]
+    __shared__ float cta_m[GROUP], cta_l[GROUP];
+    __shared__ int flag_s;
+
+    // the swizzled boxes want a 1024-byte aligned base
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
+    const int C = a.csize;
+    const int crank = split % C, cl = split / C, n_cl = a.n_splits / C;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int pos_row = a.pos + row;
+    const int n_kv = pos_row + 1;
+    const int p_begin = split * a.chunk;
+    const int p_end = min(p_begin + a.chunk, n_kv);
+    const int n_tiles = p_end > p_begin ? (p_end - p_begin + P - 1) / P : 0;
+    const int head0 = row * a.n_head + kh * GROUP;
+    __nv_bfloat16 *const k_cache = static_cast<__nv_bfloat16 *>(a.k_cache_v);
+    __nv_bfloat16 *const v_cache = static_cast<__nv_bfloat16 *>(a.v_cache_v);
+    const bool covers_new = FUSED && p_begin <= pos_row && pos_row < p_end;
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], CWARPS);
+        }
+        flag_s = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    // per-lane softmax state for heads hb, hb+1 (hb = (lane & 1) * 2)
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+    float o[16][4];
+#pragma unroll
+    for (int mt = 0; mt < 16; ++mt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[mt][c] = 0.0f;
+    bool ok = true;
+
+    if (warp == CWARPS) {
+        // ---------------- producer: one lane, 8 tensor boxes per tile ----------------
+        if (lane == 0) {
+            prefetch_tensormap(&kv_map);
+            const int krow = a.k_row0 + kh * a.context + p_begin;
+            const int vrow = a.v_row0 + kh * a.context + p_begin;
+            int issued = 0;
+            for (int j = 0; j < n_tiles; ++j) {
+                const int s = j % STAGES;
+                if (j >= STAGES && !mbar_wait(&empty_bar[s], ((j / STAGES) - 1) & 1, a.status)) {
+                    flag_s = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+                unsigned char *st = smem + (size_t)s * STAGE_BYTES;
+#pragma unroll
+                for (int b = 0; b < NBOX; ++b) {
+                    tma_load_2d(st + b * BOX_BYTES, &kv_map, b * BOX_COLS, krow + j * P, &full_bar[s]);
+                    tma_load_2d(st + HALF_BYTES + b * BOX_BYTES, &kv_map, b * BOX_COLS, vrow + j * P,
+                                &full_bar[s]);
+                }
+                issued = j + 1;
+            }
+            // every copy this CTA started has landed before its shared memory
+            // is reused or released (a no-op unless a consumer gave up early)
+            for (int j = max(0, issued - STAGES); j < issued; ++j)
+                mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, a.status);
+        }
+    } else {
+        // ---------------- consumers ----------------
+        if (FUSED) {
+            const int half = a.n_rot / 2;
+            const float *cs_row = a.rope_cs + (size_t)pos_row * half;
+            const float *sn_row = a.rope_sn + (size_t)pos_row * half;
+            LaneHead hq, hk;
+            load_lane_head(hq, a.qg + (size_t)(head0 + warp) * 2 * HD, a.q_norm, cs_row, sn_row,
+                           a.n_rot, lane);
+            const float *kv_in = (warp == 0 ? a.k_in : a.v_in) + (size_t)row * a.n_kv * HD +
+                                 (size_t)kh * HD;
+            if (covers_new && warp < 2)
+                load_lane_head(hk, kv_in, a.k_norm, cs_row, sn_row, a.n_rot, lane);
+            lane_norm_rope(hq, q_s[warp], a.n_rot, a.eps, lane);
+            if (covers_new && warp < 2) {
+                float y[8];
+                if (warp == 0) {
+                    lane_norm_rope(hk, kf_s, a.n_rot, a.eps, lane);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) y[e] = kf_s[lane * 8 + e];
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) y[e] = hk.x[e];
+                }
+                __nv_bfloat16 *cache = (warp == 0 ? k_cache : v_cache) +
+                                       ((size_t)kh * a.context + pos_row) * HD + lane * 8;
+                __nv_bfloat16 *keep = (warp == 0 ? newk_s : newv_s) + lane * 8;
+                uint4 packed;
+                packed.x = pack_bf16(y[0], y[1]);
+                packed.y = pack_bf16(y[2], y[3]);
+                packed.z = pack_bf16(y[4], y[5]);
+                packed.w = pack_bf16(y[6], y[7]);
+                *reinterpret_cast<uint4 *>(cache) = packed;
+                *reinterpret_cast<uint4 *>(keep) = packed;
+            }
+            consumer_bar();
+        }
+        // B fragments of [q_hi | q_lo]^T: column n = lane/4 (heads 0-3 hi,
+        // 4-7 lo), rows (dims) ks*16 + (lane%4)*2 + {0, 1} and + 8
+        uint32_t qf[16][2];
+        {
+            const int n = lane >> 2, kb = (lane & 3) * 2, hq = n & 3;
+            const bool lo = n >= 4;
+            const float *qrow = FUSED ? q_s[hq] : a.q_f32 + (size_t)(head0 + hq) * HD;
+#pragma unroll
+            for (int ks = 0; ks < 16; ++ks)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int d = ks * 16 + hf * 8 + kb;
+                    const float2 xv = *reinterpret_cast<const float2 *>(qrow + d);
+                    float x0 = xv.x, x1 = xv.y;
+                    if (lo) x0 = x0 - bf16_hi(x0), x1 = x1 - bf16_hi(x1);
+                    qf[ks][hf] = pack_bf16(x0, x1);
+                }
+        }
+        const float qk_scale = (1.0f / 16.0f) * LOG2E;  // 1/sqrt(256), in log2 units
+        const int wrow0 = warp * 16;                      // this warp's rows of a tile
+        const uint32_t smem0 = smem_u32(smem);
+        // ldmatrix rows: K (A = K rows, chunk k_c of each 16-dim step) and
+        // V^T (A = V rows transposed)
+        const int k_r = (lane & 7) + ((lane >> 3) & 1) * 8, k_c = lane >> 4;
+        const int v_r = (lane >> 4) * 8 + (lane & 7), v_c = (lane >> 3) & 1;
+
+        for (int j = 0; j < n_tiles; ++j) {
+            const int s = j % STAGES;
+            if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[s], (j / STAGES) & 1, a.status))) {
+                ok = false;
+                break;
+            }
+            const int base = p_begin + j * P;
+            const int vw = max(0, min(16, p_end - base - wrow0));  // valid rows of this warp
+            const uint32_t kst = smem0 + s * STAGE_BYTES;
+            const uint32_t vst = kst + HALF_BYTES;
+            bool patched = false;
+            if (FUSED && covers_new && pos_row >= base + wrow0 && pos_row < base + wrow0 + 16) {
+                // the appended row is in this warp's block: the copy may have
+                // read it before it was written, so put the fresh one in place
+                const int r = pos_row - base;
+                const int b = lane >> 3, c = lane & 7;
+                unsigned char *st = smem + (size_t)s * STAGE_BYTES;
+                *reinterpret_cast<uint4 *>(st + b * BOX_BYTES + swz128(r, c)) =
+                    reinterpret_cast<const uint4 *>(newk_s)[lane];
+                *reinterpret_cast<uint4 *>(st + HALF_BYTES + b * BOX_BYTES + swz128(r, c)) =
+                    reinterpret_cast<const uint4 *>(newv_s)[lane];
+                __syncwarp();
+                patched = true;
+            }
+            if (vw > 0) {
+                // ---- S^T = K q^T over 16 dims per MMA; rows past vw read row 0
+                float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const int kr = wrow0 + (k_r < vw ? k_r : 0);
+#pragma unroll
+                for (int ks = 0; ks < 16; ++ks) {
+                    const int ch = 2 * ks + k_c;  // 16-byte chunk of the 512-byte row
+                    uint32_t fa[4];
+                    ldsm_x4(kst + (ch >> 3) * BOX_BYTES + swz128(kr, ch & 7), fa);
+                    mma_16816(sacc, fa, qf[ks][0], qf[ks][1]);
+                }
+                // hi + lo columns: lane^2 holds the other half of the same heads
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sacc[c] += __shfl_xor_sync(0xffffffffu, sacc[c], 2);
+                const int p0 = lane >> 2, p1 = p0 + 8;
+                float sv[4];
+                sv[0] = p0 < vw ? sacc[0] * qk_scale : -INFINITY;
+                sv[1] = p0 < vw ? sacc[1] * qk_scale : -INFINITY;
+                sv[2] = p1 < vw ? sacc[2] * qk_scale : -INFINITY;
+                sv[3] = p1 < vw ? sacc[3] * qk_scale : -INFINITY;
+                // ---- online softmax over the warp's 16 positions, heads hb, hb+1
+                float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                }
+                const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+                const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
+                const float pv0 = exp2f(sv[0] - mn0), pv1 = exp2f(sv[1] - mn1);
+                const float pv2 = exp2f(sv[2] - mn0), pv3 = exp2f(sv[3] - mn1);
+                l_run[0] = fmaf(l_run[0], al0, pv0 + pv2);
+                l_run[1] = fmaf(l_run[1], al1, pv1 + pv3);
+                m_run[0] = mn0;
+                m_run[1] = mn1;
+                // ---- P^T as the B operand of the second MMA, through shared
+                if ((lane & 2) == 0) {
+                    const int hb = (lane & 1) * 2;
+                    __nv_bfloat16 *pb = &pbuf[warp][0][0];
+                    const float pv[4] = {pv0, pv1, pv2, pv3};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int h = hb + (c & 1), p = (c < 2) ? p0 : p1;
+                        const float hi = bf16_hi(pv[c]);
+                        pb[h * 16 + p] = __float2bfloat16_rn(pv[c]);
+                        pb[(h + 4) * 16 + p] = __float2bfloat16_rn(pv[c] - hi);
+                    }
+                }
+                __syncwarp();
+                const uint32_t b0 =
+                    *reinterpret_cast<const uint32_t *>(&pbuf[warp][lane >> 2][(lane & 3) * 2]);
+                const uint32_t b1 =
+                    *reinterpret_cast<const uint32_t *>(&pbuf[warp][lane >> 2][(lane & 3) * 2 + 8]);
+                // ---- rescale, then O^T += V^T P^T, 16 dims per MMA
+                if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+                    for (int mt = 0; mt < 16; ++mt) {
+                        o[mt][0] *= al0, o[mt][1] *= al1;
+                        o[mt][2] *= al0, o[mt][3] *= al1;
+                    }
+                }
+                const int vr = wrow0 + (v_r < vw ? v_r : 0);
+#pragma unroll
+                for (int mt = 0; mt < 16; ++mt) {
+                    const int ch = 2 * mt + v_c;
+                    uint32_t fa[4];
+                    ldsm_x4_t(vst + (ch >> 3) * BOX_BYTES + swz128(vr, ch & 7), fa);
+                    mma_16816(o[mt], fa, b0, b1);
+                }
+                __syncwarp();
+            }
+            if (patched) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[s]);
+        }
+    }
+
+    // ---------------- hand the warps' states to the shared merge ----------------
+    __syncthreads();  // every tile consumed: the stage ring is free
+    if (!ok) atomicOr(&flag_s, 1);
+    float *red_o = reinterpret_cast<float *>(smem);   // [CWARPS][GROUP][HD]
+    float *red_ml = red_o + CWARPS * GROUP * HD;      // [CWARPS][GROUP][2]
+    float *cta_o = red_ml + CWARPS * GROUP * 2;       // [GROUP][HD]
+    if (warp < CWARPS) {
+        // l: sum the lanes' partial sums over positions (lanes with the same
+        // lane & 3); O: hi column + lo column (lane ^ 2)
+        float l0 = l_run[0], l1 = l_run[1];
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 16; ++mt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[mt][c] += __shfl_xor_sync(0xffffffffu, o[mt][c], 2);
+        if ((lane & 2) == 0) {
+            const int hb = (lane & 1) * 2, dr = lane >> 2;
+#pragma unroll
+            for (int mt = 0; mt < 16; ++mt) {
+                red_o[(warp * GROUP + hb) * HD + mt * 16 + dr] = o[mt][0];
+                red_o[(warp * GROUP + hb + 1) * HD + mt * 16 + dr] = o[mt][1];
+                red_o[(warp * GROUP + hb) * HD + mt * 16 + dr + 8] = o[mt][2];
+                red_o[(warp * GROUP + hb + 1) * HD + mt * 16 + dr + 8] = o[mt][3];
+            }
+            if (lane < 2) {
+                red_ml[(warp * GROUP + hb) * 2] = m_run[0];
+                red_ml[(warp * GROUP + hb) * 2 + 1] = l0;
+                red_ml[(warp * GROUP + hb + 1) * 2] = m_run[1];
+                red_ml[(warp * GROUP + hb + 1) * 2 + 1] = l1;
+            }
+        }
+    }
+    __syncthreads();
+    decode_merge<HD, GROUP, CWARPS, THREADS>(cluster, a, red_o, red_ml, cta_o, cta_m, cta_l,
+                                             flag_s, head0, kh, row, crank, cl, n_cl, C, tid);
+}
+
+template <bool FUSED>
+static cudaError_t launch_mma_t(const DecodeArgs &a, const CUtensorMap &map, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_splits, a.n_kv, a.t);
+    cfg.blockDim = dim3(dm::THREADS);
+    cfg.dynamicSmemBytes = dm::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_mma_kernel<FUSED>, a, map);
+}
+
+cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st) {
+    return a.fused ? launch_mma_t<true>(a, kv_map, st) : launch_mma_t<false>(a, kv_map, st);
+}
+
+cudaError_t init_decode_mma_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dm::SMEM);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(decode_mma_kernel<false>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dm::SMEM);
+}
+
+int decode_mma_max_active_clusters(bool fused, int csize) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(csize * 64, 1, 1);
+    cfg.blockDim = dim3(dm::THREADS);
+    cfg.dynamicSmemBytes = dm::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    cudaError_t e = fused ? cudaOccupancyMaxActiveClusters(&n, decode_mma_kernel<true>, &cfg)
+                          : cudaOccupancyMaxActiveClusters(&n, decode_mma_kernel<false>, &cfg);
+    return e == cudaSuccess ? n : 0;
+}
+
+int decode_mma_positions_per_tile() { return dm::P; }
+
+}  // namespace rl

@@ -2,6 +2,7 @@
 // Every pointer here is device memory.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -36,11 +37,22 @@ struct DecodeArgs {
     int pos, t, context, n_head, n_kv, chunk, n_splits, csize, n_rot;
     float theta_scale, eps;
     bool kv_bf16, fused;
+    // tensor-map rows of this layer's K and V caches (bf16 tensor-core
+    // kernel): row of (KV head kh, position p) = k_row0 + kh * context + p
+    int k_row0, v_row0;
 };
 cudaError_t init_decode_kernels();
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);
 int decode_positions_per_tile(bool kv_bf16);
 int decode_max_active_clusters(bool kv_bf16, bool fused, int csize);
+// bf16 caches: the same step with K/V tiles staged by TMA tensor copies and
+// both dot products on mma.sync (decode_mma.cu).  `kv_map` covers the
+// whole KV allocation as rows of head_dim bf16, in boxes of 64 x 64.
+cudaError_t init_decode_mma_kernels();
+cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st);
+constexpr int kDecodeBoxRows = 64, kDecodeBoxCols = 64;
+int decode_mma_max_active_clusters(bool fused, int csize);
+int decode_mma_positions_per_tile();
 
 cudaError_t init_full_attn_kernels();
 // cos/sin of every position's RoPE angles, [context][n_rot/2] each

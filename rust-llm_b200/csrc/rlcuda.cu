@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "rlcuda.h"
+#include "tmap.h"
 
 #define RL_VERSION_STRING "rlcuda 0.1 (sm_100a)"
 
@@ -39,11 +40,13 @@ struct rl_ctx {
     int64_t part_rows = 0;    // (row, cluster) pairs the partial buffers hold
     int *counters = nullptr;  // [max_batch][n_kv][8] decode arrival counters
     float *rope_cs = nullptr, *rope_sn = nullptr;  // [context][n_rot/2]
+    // bf16 caches: TMA map of the whole KV allocation as rows of head_dim
+    CUtensorMap kv_map{};
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
-    int64_t opt_splits = 0, opt_prefill_rows = 0, opt_chunk_rows = 0;
+    int64_t opt_splits = 0, opt_prefill_rows = 0, opt_chunk_rows = 0, opt_cluster = 0;
     // resident clusters of the decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
     float theta_scale = 1.0f;
@@ -261,12 +264,14 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         return bail(fail(x, RL_ECUDA, "cudaStreamCreate failed"));
     x->own_stream = true;
     if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
-        rl::init_decode_kernels() != cudaSuccess)
+        rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
     for (int f = 0; f < 2; ++f)
         for (int lc = 0; lc < 4; ++lc)
             x->max_clusters[f][lc] =
-                rl::decode_max_active_clusters(cfg->kv_dtype == RL_KV_BF16, f == 1, 1 << lc);
+                cfg->kv_dtype == RL_KV_BF16
+                    ? rl::decode_mma_max_active_clusters(f == 1, 1 << lc)
+                    : rl::decode_max_active_clusters(false, f == 1, 1 << lc);
     const size_t hd = c.head_dim, nh = c.n_head, cd = conv_dim(c), s = c.d_state;
     const size_t mb = c.max_batch;
     if ((code = alloc(x, (char **)&x->kv, (size_t)c.n_full * kv_layer_elems(c) * kv_elem(c))) ||
@@ -294,6 +299,15 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         if ((code = alloc(x, &x->rope_cs, (size_t)c.context * half)) ||
             (code = alloc(x, &x->rope_sn, (size_t)c.context * half)))
             return bail(code);
+        if (c.kv_dtype == RL_KV_BF16) {
+            const uint64_t rows = (uint64_t)c.n_full * 2 * c.n_head_kv * c.context;
+            if (rows >= (1ull << 31))
+                return bail(fail(x, RL_EUNSUPPORTED, "a bf16 KV cache of %llu rows exceeds 2^31",
+                                 (unsigned long long)rows));
+            if (rl::encode_bf16_2d(&x->kv_map, x->kv, rows, c.head_dim, (uint64_t)c.head_dim * 2,
+                                   rl::kDecodeBoxRows, rl::kDecodeBoxCols) != cudaSuccess)
+                return bail(fail(x, RL_ECUDA, "encoding the KV tensor map failed"));
+        }
     }
     // staging for the host entry points: the larger of the two paths' in+out
     const size_t full_io = mb * (2 * hd * nh + 2 * hd * c.n_head_kv + hd * nh);
@@ -447,13 +461,15 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     // that keeps the most CTAs resident, the larger size on a tie (fewer
     // partials for the cross-cluster merge).
     const int64_t n_kv_max = (int64_t)pos + t;
-    const int P = rl::decode_positions_per_tile(bf16);
+    // bf16 caches run the tensor-core kernel, f32 caches the CUDA-core one
+    const int P = bf16 ? rl::decode_mma_positions_per_tile() : rl::decode_positions_per_tile(false);
     const int64_t tiles = (n_kv_max + P - 1) / P;
     const int64_t groups = (int64_t)c.n_head_kv * t;  // (KV head, row) pairs
     int64_t splits = 0;
     int csize = 1;
     for (int lc = 3; lc >= 0; --lc) {
         const int cs = 1 << lc;
+        if (ctx->opt_cluster > 0 && cs != ctx->opt_cluster) continue;
         int64_t per = (int64_t)ctx->max_clusters[fused ? 1 : 0][lc] / groups * cs;
         if (ctx->opt_splits > 0) per = std::min<int64_t>(per, ctx->opt_splits);
         per = std::min<int64_t>(per, (tiles + cs - 1) / cs * cs);
@@ -500,9 +516,12 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     d.eps = c.rms_eps;
     d.kv_bf16 = bf16;
     d.fused = fused;
+    d.k_row0 = layer * 2 * c.n_head_kv * c.context;
+    d.v_row0 = d.k_row0 + c.n_head_kv * c.context;
     {
         ProfScope ps(ctx, RL_PROF_DECODE);
-        CK(ctx, rl::launch_decode(d, ctx->stream));
+        CK(ctx, bf16 ? rl::launch_decode_mma(d, ctx->kv_map, ctx->stream)
+                     : rl::launch_decode(d, ctx->stream));
     }
     return RL_OK;
 }
@@ -624,6 +643,11 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
     case RL_OPT_SPLITS: ctx->opt_splits = value; return RL_OK;
     case RL_OPT_PREFILL_ROWS: ctx->opt_prefill_rows = value; return RL_OK;
     case RL_OPT_CHUNK_ROWS: ctx->opt_chunk_rows = value; return RL_OK;
+    case RL_OPT_CLUSTER:
+        if (value != 0 && value != 1 && value != 2 && value != 4 && value != 8)
+            return fail(ctx, RL_EINVAL, "cluster size must be 0 (automatic), 1, 2, 4 or 8");
+        ctx->opt_cluster = value;
+        return RL_OK;
     default: return fail(ctx, RL_EINVAL, "unknown option %d", option);
     }
 }
@@ -634,6 +658,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_SPLITS: return ctx->opt_splits;
     case RL_OPT_PREFILL_ROWS: return ctx->opt_prefill_rows;
     case RL_OPT_CHUNK_ROWS: return ctx->opt_chunk_rows;
+    case RL_OPT_CLUSTER: return ctx->opt_cluster;
     default: return -1;
     }
 }

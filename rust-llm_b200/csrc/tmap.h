@@ -1,0 +1,19 @@
+// Tensor maps (TMA descriptors) for the caches, encoded on the host through
+// the driver entry point the runtime hands out, so the library does not link
+// libcuda directly.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rl {
+
+// A 2-D bf16 tensor of `rows` rows of `cols` elements (row pitch
+// `row_bytes`, a multiple of 16), read in boxes of box_rows x box_cols with
+// the 128-byte swizzle (box_cols * 2 <= 128).  Returns cudaErrorInvalidValue
+// when the driver refuses the encoding.
+cudaError_t encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                           uint64_t row_bytes, uint32_t box_rows, uint32_t box_cols);
+
+}  // namespace rl
