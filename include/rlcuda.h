@@ -148,8 +148,10 @@ typedef enum {
                                  prefill kernel (needs a bf16 cache); 0 disables */
     RL_OPT_CHUNK_ROWS = 2,    /* rows from which a DeltaNet call with slots == 1 takes
                                  the chunked tensor-core kernel; 0 disables */
-    RL_OPT_CLUSTER = 3        /* force the cluster size (1, 2, 4, 8) of the decode walk's
-                                 splits (0: automatic) */
+    RL_OPT_CLUSTER = 3,       /* force the cluster size (1, 2, 4, 8) of the f32 decode
+                                 walk's splits (0: automatic) */
+    RL_OPT_EARLY_TILES = 4    /* bf16 decode: 64-position tiles a walk CTA streams before
+                                 its inputs are loaded (1..3, default 2) */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);

@@ -25,23 +25,31 @@
 // ~1e-5 relative, inside the 1e-4 bar.
 //
 // Shape of the work: one CTA per (KV split, KV head, query row), one CTA per
-// SM; a tile is 64 positions, 16 per consumer warp (the M of S^T).  A single
-// producer lane keeps STAGES tiles in flight behind full/empty mbarriers.
-// The cross-split merge, the output gate and (for one decode row) the fused
-// q/k norm, RoPE and KV append are shared with decode_attn.cu.
+// SM, one wave; a tile is 64 positions, 16 per consumer warp (the M of
+// S^T).  A single producer lane keeps STAGES tiles in flight behind
+// full/empty mbarriers.  Each CTA merges its four warps and writes one
+// partial (max, sum, unnormalised output) per query head; a second small
+// kernel (decode_combine_kernel) merges the splits and applies the sigmoid
+// output gate.  For one decode row the q/k norm, RoPE and KV append are fused
+// into the walk.
+//
+// Both kernels are launched as programmatic dependents of the kernel before
+// them (PDL).  The walk's producer may start streaming this layer's cache
+// before the previous kernel has finished (`early_kv`, set by the host when
+// nothing since the last decode wrote the cache other than decode appends,
+// which are fenced before the trigger); every read of the step's inputs and
+// every global write waits for the previous grid first.  The combine kernel
+// lets the next walk be scheduled as soon as it starts, so one layer's merge
+// tail overlaps the next layer's first tiles.
 //
 // Reference: attend_batch / softmax of Exec::full_attn
 // (crates/rust-llm/src/forward.rs:1783-1842) and its gate (:1327-1340).
-#include <cooperative_groups.h>
-
 #include "common.cuh"
-#include "decode_merge.cuh"
 #include "kernels.h"
-
-namespace cg = cooperative_groups;
 
 namespace rl {
 namespace dm {
+constexpr int kStaticRounds = 2;  // tiles per CTA dealt by index before the counter
 constexpr int HD = 256;
 constexpr int GROUP = 4;
 constexpr int CWARPS = 4;
@@ -147,41 +155,64 @@ __device__ __forceinline__ void lane_norm_rope(const LaneHead &h, float *dst, in
     __syncwarp();
 }
 
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <bool FUSED>
 __global__ void __launch_bounds__(dm::THREADS, 1)
     decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ CUtensorMap kv_map) {
     using namespace dm;
-    cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], ready_bar;
     __shared__ __align__(16) float q_s[GROUP][HD];
     __shared__ __align__(16) __nv_bfloat16 newk_s[HD], newv_s[HD];
     __shared__ __align__(16) float kf_s[HD];
     __shared__ __align__(16) __nv_bfloat16 pbuf[CWARPS][8][16];  // P^T per warp: [col][pos]
-    __shared__ float cta_m[GROUP], cta_l[GROUP];
     __shared__ int flag_s;
+    __shared__ int tile_s[STAGES];  // tile index in each stage, -1: no more tiles
 
     // the swizzled boxes want a 1024-byte aligned base
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
-    const int C = a.csize;
-    const int crank = split % C, cl = split / C, n_cl = a.n_splits / C;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int pos_row = a.pos + row;
     const int n_kv = pos_row + 1;
-    const int p_begin = split * a.chunk;
-    const int p_end = min(p_begin + a.chunk, n_kv);
-    const int n_tiles = p_end > p_begin ? (p_end - p_begin + P - 1) / P : 0;
+    const int n_all = (n_kv + P - 1) / P;   // tiles of this row
+    const int n_split = a.n_splits;          // CTAs sharing them
     const int head0 = row * a.n_head + kh * GROUP;
     __nv_bfloat16 *const k_cache = static_cast<__nv_bfloat16 *>(a.k_cache_v);
     __nv_bfloat16 *const v_cache = static_cast<__nv_bfloat16 *>(a.v_cache_v);
-    const bool covers_new = FUSED && p_begin <= pos_row && pos_row < p_end;
+    // every CTA of a KV head builds the appended row (any of them may draw
+    // the tile holding it); split 0 writes it to the cache
+    const bool builds_new = FUSED;
+    const bool writes_new = FUSED && split == 0;
+    const float *cs_row = a.rope_cs + (size_t)pos_row * (a.n_rot / 2);
+    const float *sn_row = a.rope_sn + (size_t)pos_row * (a.n_rot / 2);
+    const float *kv_in = (warp == 0 ? a.k_in : a.v_in) + (size_t)row * a.n_kv * HD + (size_t)kh * HD;
+    if (FUSED && warp < CWARPS && lane < 8) {
+        // warm L2 with this step's small inputs while the previous grid
+        // finishes; the values themselves are read after the wait
+        const float *q = a.qg + (size_t)(head0 + warp) * 2 * HD;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(q + lane * 32));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.q_norm + lane * 32));
+        if (warp < 2) asm volatile("prefetch.global.L2 [%0];" ::"l"(kv_in + lane * 32));
+        if (warp == 0 && lane == 0) {
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(cs_row));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(sn_row));
+        }
+        if (warp == 1) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.k_norm + lane * 32));
+    }
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], CWARPS);
         }
+        mbar_init(&ready_bar, CWARPS);
         flag_s = 0;
         fence_barrier_init();
     }
@@ -198,47 +229,79 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
 
     if (warp == CWARPS) {
         // ---------------- producer: one lane, 8 tensor boxes per tile ----------------
+        // Tiles are dealt to the row's CTAs: the first kStaticRounds rounds
+        // by index (split, split + n_split, ...), the rest from an atomic
+        // counter, so the CTAs finish within about one tile of each other
+        // whatever bandwidth each SM gets.  Every CTA ends with exactly one
+        // draw past the end; the last such draw resets the counter for the
+        // next launch.
         if (lane == 0) {
             prefetch_tensormap(&kv_map);
-            const int krow = a.k_row0 + kh * a.context + p_begin;
-            const int vrow = a.v_row0 + kh * a.context + p_begin;
-            int issued = 0;
-            for (int j = 0; j < n_tiles; ++j) {
-                const int s = j % STAGES;
-                if (j >= STAGES && !mbar_wait(&empty_bar[s], ((j / STAGES) - 1) & 1, a.status)) {
+            if (!a.early_kv) grid_dep_wait();
+            int *counter = a.counters + ((size_t)row * a.n_kv + kh) * 8;
+            const int n_dyn = max(0, n_all - kStaticRounds * n_split);
+            const int krow = a.k_row0 + kh * a.context;
+            const int vrow = a.v_row0 + kh * a.context;
+            const int early = max(1, min(a.early_tiles, STAGES));
+            int issued = 0, round = 0, tile = split;
+            bool stopped = false;
+            while (true) {
+                if (round >= kStaticRounds || tile >= n_all) {
+                    const int t = atomicAdd(counter, 1);
+                    if (t >= n_dyn) {
+                        if (t == n_dyn + n_split - 1) atomicExch(counter, 0);
+                        break;
+                    }
+                    tile = kStaticRounds * n_split + t;
+                }
+                const int s = issued % STAGES;
+                if ((issued == early && !mbar_wait(&ready_bar, 0, a.status)) ||
+                    (issued >= STAGES &&
+                     !mbar_wait(&empty_bar[s], ((issued / STAGES) - 1) & 1, a.status))) {
                     flag_s = 1;
+                    stopped = true;
                     break;
                 }
+                tile_s[s] = tile;
                 mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
                 unsigned char *st = smem + (size_t)s * STAGE_BYTES;
 #pragma unroll
                 for (int b = 0; b < NBOX; ++b) {
-                    tma_load_2d(st + b * BOX_BYTES, &kv_map, b * BOX_COLS, krow + j * P, &full_bar[s]);
-                    tma_load_2d(st + HALF_BYTES + b * BOX_BYTES, &kv_map, b * BOX_COLS, vrow + j * P,
+                    tma_load_2d(st + b * BOX_BYTES, &kv_map, b * BOX_COLS, krow + tile * P,
                                 &full_bar[s]);
+                    tma_load_2d(st + HALF_BYTES + b * BOX_BYTES, &kv_map, b * BOX_COLS,
+                                vrow + tile * P, &full_bar[s]);
                 }
-                issued = j + 1;
+                ++issued;
+                ++round;
+                tile += n_split;
             }
-            // every copy this CTA started has landed before its shared memory
-            // is reused or released (a no-op unless a consumer gave up early)
-            for (int j = max(0, issued - STAGES); j < issued; ++j)
-                mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, a.status);
+            // tell the consumers there is nothing more: an arrival without
+            // bytes on the next stage, whose tile index reads -1
+            const int s = issued % STAGES;
+            if (!stopped && (issued < STAGES ||
+                             mbar_wait(&empty_bar[s], ((issued / STAGES) - 1) & 1, a.status))) {
+                tile_s[s] = -1;
+                mbar_arrive(&full_bar[s]);
+            } else {
+                flag_s = 1;
+                // a consumer gave up: every copy this CTA started lands before
+                // its shared memory is released
+                for (int j = max(0, issued - STAGES); j < issued; ++j)
+                    mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, a.status);
+            }
         }
     } else {
         // ---------------- consumers ----------------
+        grid_dep_wait();  // the step's inputs come from the kernel before
         if (FUSED) {
-            const int half = a.n_rot / 2;
-            const float *cs_row = a.rope_cs + (size_t)pos_row * half;
-            const float *sn_row = a.rope_sn + (size_t)pos_row * half;
             LaneHead hq, hk;
             load_lane_head(hq, a.qg + (size_t)(head0 + warp) * 2 * HD, a.q_norm, cs_row, sn_row,
                            a.n_rot, lane);
-            const float *kv_in = (warp == 0 ? a.k_in : a.v_in) + (size_t)row * a.n_kv * HD +
-                                 (size_t)kh * HD;
-            if (covers_new && warp < 2)
+            if (builds_new && warp < 2)
                 load_lane_head(hk, kv_in, a.k_norm, cs_row, sn_row, a.n_rot, lane);
             lane_norm_rope(hq, q_s[warp], a.n_rot, a.eps, lane);
-            if (covers_new && warp < 2) {
+            if (builds_new && warp < 2) {
                 float y[8];
                 if (warp == 0) {
                     lane_norm_rope(hk, kf_s, a.n_rot, a.eps, lane);
@@ -256,8 +319,13 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
                 packed.y = pack_bf16(y[2], y[3]);
                 packed.z = pack_bf16(y[4], y[5]);
                 packed.w = pack_bf16(y[6], y[7]);
-                *reinterpret_cast<uint4 *>(cache) = packed;
                 *reinterpret_cast<uint4 *>(keep) = packed;
+                if (writes_new) {
+                    *reinterpret_cast<uint4 *>(cache) = packed;
+                    // visible GPU-wide before this grid's trigger, so a later
+                    // walk that streams early reads the appended row
+                    __threadfence();
+                }
             }
             consumer_bar();
         }
@@ -279,6 +347,8 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
                     qf[ks][hf] = pack_bf16(x0, x1);
                 }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready_bar);           // inputs consumed
         const float qk_scale = (1.0f / 16.0f) * LOG2E;  // 1/sqrt(256), in log2 units
         const int wrow0 = warp * 16;                      // this warp's rows of a tile
         const uint32_t smem0 = smem_u32(smem);
@@ -287,18 +357,20 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
         const int k_r = (lane & 7) + ((lane >> 3) & 1) * 8, k_c = lane >> 4;
         const int v_r = (lane >> 4) * 8 + (lane & 7), v_c = (lane >> 3) & 1;
 
-        for (int j = 0; j < n_tiles; ++j) {
+        for (int j = 0;; ++j) {
             const int s = j % STAGES;
             if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[s], (j / STAGES) & 1, a.status))) {
                 ok = false;
                 break;
             }
-            const int base = p_begin + j * P;
-            const int vw = max(0, min(16, p_end - base - wrow0));  // valid rows of this warp
+            const int tile = tile_s[s];
+            if (tile < 0) break;
+            const int base = tile * P;
+            const int vw = max(0, min(16, n_kv - base - wrow0));  // valid rows of this warp
             const uint32_t kst = smem0 + s * STAGE_BYTES;
             const uint32_t vst = kst + HALF_BYTES;
             bool patched = false;
-            if (FUSED && covers_new && pos_row >= base + wrow0 && pos_row < base + wrow0 + 16) {
+            if (FUSED && pos_row >= base + wrow0 && pos_row < base + wrow0 + 16) {
                 // the appended row is in this warp's block: the copy may have
                 // read it before it was written, so put the fresh one in place
                 const int r = pos_row - base;
@@ -388,12 +460,11 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
         }
     }
 
-    // ---------------- hand the warps' states to the shared merge ----------------
+    // ---------------- merge the four warps, write this split's partial ----------------
     __syncthreads();  // every tile consumed: the stage ring is free
     if (!ok) atomicOr(&flag_s, 1);
     float *red_o = reinterpret_cast<float *>(smem);   // [CWARPS][GROUP][HD]
     float *red_ml = red_o + CWARPS * GROUP * HD;      // [CWARPS][GROUP][2]
-    float *cta_o = red_ml + CWARPS * GROUP * 2;       // [GROUP][HD]
     if (warp < CWARPS) {
         // l: sum the lanes' partial sums over positions (lanes with the same
         // lane & 3); O: hi column + lo column (lane ^ 2)
@@ -425,8 +496,108 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
         }
     }
     __syncthreads();
-    decode_merge<HD, GROUP, CWARPS, THREADS>(cluster, a, red_o, red_ml, cta_o, cta_m, cta_l,
-                                             flag_s, head0, kh, row, crank, cl, n_cl, C, tid);
+    __shared__ float wscale[CWARPS][GROUP];
+    if (tid < GROUP) {
+        float M = -INFINITY;
+        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, red_ml[(w * GROUP + tid) * 2]);
+        float L = 0.0f;
+        for (int w = 0; w < CWARPS; ++w) {
+            const float mw = red_ml[(w * GROUP + tid) * 2];
+            const float sc = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+            wscale[w][tid] = sc;
+            L = fmaf(red_ml[(w * GROUP + tid) * 2 + 1], sc, L);
+        }
+        // partial (max, sum) of query head head0 + tid for this split
+        float2 *pml = reinterpret_cast<float2 *>(a.part_ml);
+        pml[(size_t)(head0 + tid) * a.n_splits + split] = make_float2(M, L);
+    }
+    __syncthreads();
+    for (int e4 = tid; e4 < GROUP * HD / 4; e4 += THREADS) {
+        const int h = e4 / (HD / 4), d4 = e4 % (HD / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) {
+            const float sc = wscale[w][h];
+            const float4 r = reinterpret_cast<const float4 *>(red_o)[w * GROUP * HD / 4 + e4];
+            acc.x = fmaf(r.x, sc, acc.x), acc.y = fmaf(r.y, sc, acc.y);
+            acc.z = fmaf(r.z, sc, acc.z), acc.w = fmaf(r.w, sc, acc.w);
+        }
+        reinterpret_cast<float4 *>(a.part_o + ((size_t)(head0 + h) * a.n_splits + split) * HD)[d4] =
+            acc;
+    }
+    if (tid == 0 && flag_s) atomicOr(a.status, DEV_TIMEOUT);
+    __syncthreads();
+    grid_dep_launch();
+}
+
+// Merges the splits of one (row, query head) for a 64-dim slice and applies
+// the sigmoid output gate (forward.rs:1327-1340).  Block: 64 dims x 8 split
+// lanes; each thread issues its partial loads in predicated batches of 8, so
+// a merge of up to 64 splits is one round trip to L2.
+constexpr int kCombineDims = 64, kCombineLanes = 8, kCombineBatch = 8, kCombineMaxSplits = 512;
+__global__ void __launch_bounds__(kCombineDims *kCombineLanes)
+    decode_combine_kernel(const __grid_constant__ DecodeArgs a) {
+    grid_dep_launch();  // the next walk may be scheduled while this merge runs
+    grid_dep_wait();    // the walk's partials are complete and visible
+    __shared__ float sc_s[kCombineMaxSplits], m_s[kCombineMaxSplits], l_s[kCombineMaxSplits];
+    __shared__ float red[kCombineLanes][kCombineDims];
+    __shared__ float L_s;
+    const int hh = blockIdx.x;  // row * n_head + head
+    const int tx = threadIdx.x % kCombineDims, ty = threadIdx.x / kCombineDims;
+    const int d = blockIdx.y * kCombineDims + tx;
+    const int S = a.n_splits;
+    const float gate = a.qg[(size_t)hh * 2 * dm::HD + dm::HD + d];
+    const float2 *ml = reinterpret_cast<const float2 *>(a.part_ml) + (size_t)hh * S;
+    const float *po = a.part_o + (size_t)hh * S * dm::HD + d;
+    // the first batch of partials goes out with the (max, sum) loads
+    float v[kCombineBatch];
+#pragma unroll
+    for (int i = 0; i < kCombineBatch; ++i) {
+        const int s = ty + i * kCombineLanes;
+        v[i] = s < S ? __ldcg(po + (size_t)s * dm::HD) : 0.0f;
+    }
+    for (int s = threadIdx.x; s < S; s += blockDim.x) {
+        const float2 x = __ldcg(&ml[s]);
+        m_s[s] = x.x;
+        l_s[s] = x.y;
+    }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, m_s[s]);
+    for (int s = threadIdx.x; s < S; s += blockDim.x)
+        sc_s[s] = m_s[s] == -INFINITY ? 0.0f : exp2f(m_s[s] - M);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float L = 0.0f;
+        for (int s = 0; s < S; ++s) L = fmaf(l_s[s], sc_s[s], L);
+        L_s = L;
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kCombineBatch; ++i) {
+        const int s = ty + i * kCombineLanes;
+        if (s < S) acc = fmaf(v[i], sc_s[s], acc);
+    }
+    for (int s0 = kCombineBatch * kCombineLanes; s0 < S; s0 += kCombineBatch * kCombineLanes) {
+#pragma unroll
+        for (int i = 0; i < kCombineBatch; ++i) {
+            const int s = s0 + ty + i * kCombineLanes;
+            v[i] = s < S ? __ldcg(po + (size_t)s * dm::HD) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kCombineBatch; ++i) {
+            const int s = s0 + ty + i * kCombineLanes;
+            if (s < S) acc = fmaf(v[i], sc_s[s], acc);
+        }
+    }
+    red[ty][tx] = acc;
+    __syncthreads();
+    if (ty == 0) {
+        float o = 0.0f;
+#pragma unroll
+        for (int y = 0; y < kCombineLanes; ++y) o += red[y][tx];
+        a.out[(size_t)hh * dm::HD + d] = (o / L_s) * sigmoidf_(gate);
+    }
 }
 
 template <bool FUSED>
@@ -437,43 +608,53 @@ static cudaError_t launch_mma_t(const DecodeArgs &a, const CUtensorMap &map, cud
     cfg.dynamicSmemBytes = dm::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = a.csize;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, decode_mma_kernel<FUSED>, a, map);
 }
 
 cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st) {
+    if (a.n_splits > kCombineMaxSplits) return cudaErrorInvalidValue;
     return a.fused ? launch_mma_t<true>(a, kv_map, st) : launch_mma_t<false>(a, kv_map, st);
+}
+
+cudaError_t launch_decode_combine(const DecodeArgs &a, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_head * a.t, dm::HD / kCombineDims);
+    cfg.blockDim = dim3(kCombineDims * kCombineLanes);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_combine_kernel, a);
 }
 
 cudaError_t init_decode_mma_kernels() {
     cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dm::SMEM);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(decode_mma_kernel<false>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dm::SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(decode_mma_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dm::SMEM);
+    // the merge asks for the walk's shared-memory split, so a walk CTA of the
+    // next layer can join it on the same SM without reconfiguring the SM
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(decode_combine_kernel,
+                                 cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    return e;
 }
 
-int decode_mma_max_active_clusters(bool fused, int csize) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(csize * 64, 1, 1);
-    cfg.blockDim = dim3(dm::THREADS);
-    cfg.dynamicSmemBytes = dm::SMEM;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = csize;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    cudaError_t e = fused ? cudaOccupancyMaxActiveClusters(&n, decode_mma_kernel<true>, &cfg)
-                          : cudaOccupancyMaxActiveClusters(&n, decode_mma_kernel<false>, &cfg);
-    return e == cudaSuccess ? n : 0;
+int decode_mma_max_active_ctas(bool fused) {
+    int per_sm = 0;
+    const cudaError_t e =
+        fused ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mma_kernel<true>,
+                                                              dm::THREADS, dm::SMEM)
+              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mma_kernel<false>,
+                                                              dm::THREADS, dm::SMEM);
+    return e == cudaSuccess ? per_sm : 0;
 }
 
 int decode_mma_positions_per_tile() { return dm::P; }

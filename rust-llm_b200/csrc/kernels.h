@@ -40,6 +40,11 @@ struct DecodeArgs {
     // tensor-map rows of this layer's K and V caches (bf16 tensor-core
     // kernel): row of (KV head kh, position p) = k_row0 + kh * context + p
     int k_row0, v_row0;
+    // bf16 walk: the producer may stream the cache before the previous
+    // grid completes (nothing since the last decode wrote the cache)
+    bool early_kv;
+    // bf16 walk: tiles streamed before the consumers hold their inputs
+    int early_tiles;
 };
 cudaError_t init_decode_kernels();
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);
@@ -48,10 +53,14 @@ int decode_max_active_clusters(bool kv_bf16, bool fused, int csize);
 // bf16 caches: the same step with K/V tiles staged by TMA tensor copies and
 // both dot products on mma.sync (decode_mma.cu).  `kv_map` covers the
 // whole KV allocation as rows of head_dim bf16, in boxes of 64 x 64.
+// The walk writes one partial per (row, query head, split) into part_o
+// [t][n_head][n_splits][hd] and part_ml [t][n_head][n_splits][2];
+// launch_decode_combine merges them and applies the output gate.
 cudaError_t init_decode_mma_kernels();
 cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st);
+cudaError_t launch_decode_combine(const DecodeArgs &a, cudaStream_t st);
 constexpr int kDecodeBoxRows = 64, kDecodeBoxCols = 64;
-int decode_mma_max_active_clusters(bool fused, int csize);
+int decode_mma_max_active_ctas(bool fused);  // resident walk CTAs per SM
 int decode_mma_positions_per_tile();
 
 cudaError_t init_full_attn_kernels();

@@ -47,8 +47,14 @@ struct rl_ctx {
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 0, opt_chunk_rows = 0, opt_cluster = 0;
-    // resident clusters of the decode kernel: [fused][log2 cluster size]
+    int64_t opt_early_tiles = 2;
+    // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
+    // resident CTAs per SM of the bf16 walk: [fused]
+    int mma_per_sm[2] = {};
+    // the next bf16 decode may stream the cache early: nothing but decode
+    // appends (fenced before their grid's trigger) wrote it since the last one
+    bool early_ok = false;
     float theta_scale = 1.0f;
     std::string err;
     // per-kernel timing (rl_profile_*)
@@ -266,12 +272,11 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
         rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
-    for (int f = 0; f < 2; ++f)
+    for (int f = 0; f < 2; ++f) {
         for (int lc = 0; lc < 4; ++lc)
-            x->max_clusters[f][lc] =
-                cfg->kv_dtype == RL_KV_BF16
-                    ? rl::decode_mma_max_active_clusters(f == 1, 1 << lc)
-                    : rl::decode_max_active_clusters(false, f == 1, 1 << lc);
+            x->max_clusters[f][lc] = rl::decode_max_active_clusters(false, f == 1, 1 << lc);
+        x->mma_per_sm[f] = rl::decode_mma_max_active_ctas(f == 1);
+    }
     const size_t hd = c.head_dim, nh = c.n_head, cd = conv_dim(c), s = c.d_state;
     const size_t mb = c.max_batch;
     if ((code = alloc(x, (char **)&x->kv, (size_t)c.n_full * kv_layer_elems(c) * kv_elem(c))) ||
@@ -362,6 +367,7 @@ int rl_set_stream(rl_ctx *ctx, void *stream) {
     if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     ctx->stream = (cudaStream_t)stream;
     ctx->own_stream = false;
+    ctx->early_ok = false;
     return RL_OK;
 }
 
@@ -378,8 +384,12 @@ int rl_reset(rl_ctx *ctx) {
     CK(ctx, cudaMemsetAsync(ctx->ssm, 0, (size_t)c.n_linear * ssm_layer_floats(c) * 4,
                             ctx->stream));
     CK(ctx, cudaMemsetAsync(ctx->status, 0, sizeof(int), ctx->stream));
+    if (ctx->counters)
+        CK(ctx, cudaMemsetAsync(ctx->counters, 0,
+                                (size_t)c.max_batch * c.n_head_kv * 8 * sizeof(int), ctx->stream));
     ctx->pos = 0;
     ctx->live = 0;
+    ctx->early_ok = false;
     return RL_OK;
 }
 
@@ -455,16 +465,74 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         ProfScope ps(ctx, RL_PROF_PROLOGUE);
         CK(ctx, rl::launch_full_prologue(a, ctx->stream));
     }
-    // Split-KV walk.  The (split, KV head, row) CTAs of one launch must all be
-    // resident at once (one wave); the splits of a (row, KV head) form
-    // clusters of csize CTAs.  Among cluster sizes 8, 4, 2, 1, take the one
-    // that keeps the most CTAs resident, the larger size on a tie (fewer
-    // partials for the cross-cluster merge).
     const int64_t n_kv_max = (int64_t)pos + t;
-    // bf16 caches run the tensor-core kernel, f32 caches the CUDA-core one
-    const int P = bf16 ? rl::decode_mma_positions_per_tile() : rl::decode_positions_per_tile(false);
-    const int64_t tiles = (n_kv_max + P - 1) / P;
     const int64_t groups = (int64_t)c.n_head_kv * t;  // (KV head, row) pairs
+    rl::DecodeArgs d{};
+    d.qg = qg;
+    d.k_in = k;
+    d.v_in = v;
+    d.q_f32 = ctx->q_f32;
+    d.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
+    d.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
+    d.rope_cs = ctx->rope_cs;
+    d.rope_sn = ctx->rope_sn;
+    d.k_cache_v = k_cache;
+    d.v_cache_v = v_cache;
+    d.part_o = ctx->part_o;
+    d.part_ml = ctx->part_ml;
+    d.counters = ctx->counters;
+    d.out = out;
+    d.status = ctx->status;
+    d.pos = pos;
+    d.t = t;
+    d.context = c.context;
+    d.n_head = c.n_head;
+    d.n_kv = c.n_head_kv;
+    d.n_rot = c.n_rot;
+    d.theta_scale = ctx->theta_scale;
+    d.eps = c.rms_eps;
+    d.kv_bf16 = bf16;
+    d.fused = fused;
+    d.k_row0 = layer * 2 * c.n_head_kv * c.context;
+    d.v_row0 = d.k_row0 + c.n_head_kv * c.context;
+
+    if (bf16) {
+        // One wave of walk CTAs: as many splits per (KV head, row) as keep
+        // every resident slot busy, each a whole number of 64-position tiles.
+        const int P = rl::decode_mma_positions_per_tile();
+        const int64_t tiles = (n_kv_max + P - 1) / P;
+        const int64_t resident = (int64_t)std::max(1, ctx->mma_per_sm[fused ? 1 : 0]) * ctx->num_sms;
+        int64_t splits = std::max<int64_t>(1, resident / groups);
+        if (ctx->opt_splits > 0) splits = std::min<int64_t>(splits, ctx->opt_splits);
+        splits = std::min<int64_t>(splits, tiles);
+        splits = std::min<int64_t>(splits, std::max<int64_t>(1, ctx->part_rows / t));
+        splits = std::min<int64_t>(splits, 512);
+        int64_t chunk = (tiles + splits - 1) / splits * P;  // positions per split
+        splits = (n_kv_max + chunk - 1) / chunk;
+        d.chunk = (int)chunk;
+        d.n_splits = (int)splits;
+        d.csize = 1;
+        d.early_kv = fused && ctx->early_ok;
+        d.early_tiles = (int)ctx->opt_early_tiles;
+        {
+            ProfScope ps(ctx, RL_PROF_DECODE);
+            CK(ctx, rl::launch_decode_mma(d, ctx->kv_map, ctx->stream));
+        }
+        {
+            ProfScope ps(ctx, RL_PROF_MERGE);
+            CK(ctx, rl::launch_decode_combine(d, ctx->stream));
+        }
+        ctx->early_ok = fused;
+        return RL_OK;
+    }
+
+    // f32 caches: split-KV walk on the CUDA cores.  The (split, KV head, row)
+    // CTAs of one launch must all be resident at once (one wave); the splits
+    // of a (row, KV head) form clusters of csize CTAs.  Among cluster sizes
+    // 8, 4, 2, 1, take the one that keeps the most CTAs resident, the larger
+    // size on a tie (fewer partials for the cross-cluster merge).
+    const int P = rl::decode_positions_per_tile(false);
+    const int64_t tiles = (n_kv_max + P - 1) / P;
     int64_t splits = 0;
     int csize = 1;
     for (int lc = 3; lc >= 0; --lc) {
@@ -487,42 +555,15 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     }
     int64_t chunk = (n_kv_max + splits - 1) / splits;
     chunk = (chunk + P - 1) / P * P;
-    rl::DecodeArgs d{};
-    d.qg = qg;
-    d.k_in = k;
-    d.v_in = v;
-    d.q_f32 = ctx->q_f32;
-    d.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
-    d.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
-    d.rope_cs = ctx->rope_cs;
-    d.rope_sn = ctx->rope_sn;
-    d.k_cache_v = k_cache;
-    d.v_cache_v = v_cache;
-    d.part_o = ctx->part_o;
-    d.part_ml = ctx->part_ml;
-    d.counters = ctx->counters;
-    d.out = out;
-    d.status = ctx->status;
-    d.pos = pos;
-    d.t = t;
-    d.context = c.context;
-    d.n_head = c.n_head;
-    d.n_kv = c.n_head_kv;
     d.chunk = (int)chunk;
     d.n_splits = (int)splits;
     d.csize = csize;
-    d.n_rot = c.n_rot;
-    d.theta_scale = ctx->theta_scale;
-    d.eps = c.rms_eps;
-    d.kv_bf16 = bf16;
-    d.fused = fused;
-    d.k_row0 = layer * 2 * c.n_head_kv * c.context;
-    d.v_row0 = d.k_row0 + c.n_head_kv * c.context;
+    d.early_kv = false;
     {
         ProfScope ps(ctx, RL_PROF_DECODE);
-        CK(ctx, bf16 ? rl::launch_decode_mma(d, ctx->kv_map, ctx->stream)
-                     : rl::launch_decode(d, ctx->stream));
+        CK(ctx, rl::launch_decode(d, ctx->stream));
     }
+    ctx->early_ok = false;
     return RL_OK;
 }
 
@@ -643,6 +684,10 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
     case RL_OPT_SPLITS: ctx->opt_splits = value; return RL_OK;
     case RL_OPT_PREFILL_ROWS: ctx->opt_prefill_rows = value; return RL_OK;
     case RL_OPT_CHUNK_ROWS: ctx->opt_chunk_rows = value; return RL_OK;
+    case RL_OPT_EARLY_TILES:
+        if (value < 1 || value > 3) return fail(ctx, RL_EINVAL, "early tiles must be 1, 2 or 3");
+        ctx->opt_early_tiles = value;
+        return RL_OK;
     case RL_OPT_CLUSTER:
         if (value != 0 && value != 1 && value != 2 && value != 4 && value != 8)
             return fail(ctx, RL_EINVAL, "cluster size must be 0 (automatic), 1, 2, 4 or 8");
@@ -659,6 +704,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_PREFILL_ROWS: return ctx->opt_prefill_rows;
     case RL_OPT_CHUNK_ROWS: return ctx->opt_chunk_rows;
     case RL_OPT_CLUSTER: return ctx->opt_cluster;
+    case RL_OPT_EARLY_TILES: return ctx->opt_early_tiles;
     default: return -1;
     }
 }
@@ -711,6 +757,7 @@ static int kv_io(rl_ctx *ctx, int layer, int p0, int n, float *buf, int where, b
             return done(fail(ctx, RL_ECUDA, "copy of the KV rows failed"));
     void *kc = kv_layer(ctx, layer);
     void *vc = (char *)kc + (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
+    if (write) ctx->early_ok = false;
     cudaError_t e = write ? rl::launch_kv_fill(kc, vc, dev, c.n_head_kv, c.context, c.head_dim,
                                                p0, n, c.kv_dtype == RL_KV_BF16, ctx->stream)
                           : rl::launch_kv_read(kc, vc, dev, c.n_head_kv, c.context, c.head_dim,
