@@ -562,16 +562,22 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
         l_s[s] = x.y;
     }
     __syncthreads();
-    float M = -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, m_s[s]);
-    for (int s = threadIdx.x; s < S; s += blockDim.x)
-        sc_s[s] = m_s[s] == -INFINITY ? 0.0f : exp2f(m_s[s] - M);
-    __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {
+        // one warp: the max over the splits, each split's weight, the sum
+        const int lane = threadIdx.x;
+        float M = -INFINITY;
+        for (int s = lane; s < S; s += 32) M = fmaxf(M, m_s[s]);
+        M = warp_max(M);
         float L = 0.0f;
-        for (int s = 0; s < S; ++s) L = fmaf(l_s[s], sc_s[s], L);
-        L_s = L;
+        for (int s = lane; s < S; s += 32) {
+            const float sc = m_s[s] == -INFINITY ? 0.0f : exp2f(m_s[s] - M);
+            sc_s[s] = sc;
+            L = fmaf(l_s[s], sc, L);
+        }
+        L = warp_sum(L);
+        if (lane == 0) L_s = L;
     }
+    __syncthreads();
     float acc = 0.0f;
 #pragma unroll
     for (int i = 0; i < kCombineBatch; ++i) {
