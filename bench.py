@@ -177,6 +177,82 @@ def run_reference(args):
     return 0
 
 
+DN_LAYERS = 72  # 3 x the stack's 24: 144 MiB of distinct state per step, more than L2
+DN_BYTES_PER_LAYER = (2 * 32 * 128 * 128 * 4      # recurrent state read + write
+                      + 2 * 8192 * 3 * 4          # conv history read + write
+                      + 8192 * 4 * 4              # conv weights
+                      + 4 * (8192 + 2 * 4096 + 2 * 32))  # qkv, z, out, alpha, beta
+
+
+def dn_step_bench(args, dev, stream, rlcuda, torch):
+    """Config 1 shapes: one Gated DeltaNet decode step per layer over 72 layers
+    (three times the stack's 24, each with its own 2 MiB state, so a step moves
+    144 MiB of distinct state and L2 cannot hold it), CUDA-graph captured;
+    returns µs per layer and the HBM rate of the algorithmic bytes."""
+    cfg = rlcuda.qwen35_config(n_full=0, n_linear=DN_LAYERS, context=16, max_batch=1)
+    ctx = rlcuda.Context(cfg, device=dev.index)
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    import numpy as np
+    r = np.random.default_rng(1)
+    for layer in range(DN_LAYERS):
+        ctx.set_weights_linear(layer, r.normal(0, 0.5, (8192, 4)).astype(np.float32),
+                               -np.exp(r.uniform(0, np.log(16), 32)).astype(np.float32),
+                               r.normal(0, 0.1, 32).astype(np.float32), np.ones(128, np.float32))
+        ctx.write_conv(layer, r.normal(0, 0.5, (1, 8192, 3)).astype(np.float32))
+        ctx.write_ssm(layer, r.normal(0, 0.1, (32, 1, 128, 128)).astype(np.float32))
+    qkv = torch.randn((DN_LAYERS, 8192), generator=gen, device=dev)
+    z = torch.randn((DN_LAYERS, 4096), generator=gen, device=dev)
+    al = torch.randn((DN_LAYERS, 32), generator=gen, device=dev)
+    be = torch.randn((DN_LAYERS, 32), generator=gen, device=dev)
+    out = torch.empty((DN_LAYERS, 4096), device=dev)
+
+    def step():
+        for layer in range(DN_LAYERS):
+            ctx.linear_attn(layer, 0, 1, qkv[layer], z[layer], al[layer], be[layer], out[layer])
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    steps = max(20, min(args.steps, 2000))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ctx.sync()
+    us = e0.elapsed_time(e1) * 1e3 / (steps * DN_LAYERS)
+    # one launch alone, events around it (sleep first so the host is ahead)
+    ctx.profile_reset()
+    ctx.profile(True)
+    with torch.cuda.stream(stream):
+        for b in range(10):
+            torch.cuda._sleep(5_000_000)
+            step()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    ms, n = prof["dn_step"]
+    graph.reset()
+    ctx.close()
+    peak, _ = peaks()
+    gbs = DN_BYTES_PER_LAYER / (us * 1e-6) / 1e9
+    return {"workload": "config 1 DeltaNet decode step, 72 layers per graph step",
+            "us_per_layer": us, "bytes_per_layer": DN_BYTES_PER_LAYER, "gbs": gbs,
+            "frac_of_measured_hbm": gbs / peak, "frac_of_8tbs": gbs / 8000.0,
+            "avg_launch_us_alone": ms * 1e3 / max(n, 1),
+            "l2": "72 x 2 MiB of state per step, more than the 126 MB L2"}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -309,6 +385,8 @@ def run_ours(args):
     h2d = N_LAYERS * 4 * (N_HEAD * 2 * HD + 2 * N_KV * HD)
     d2h = N_LAYERS * 4 * N_HEAD * HD
 
+    dn = dn_step_bench(args, dev, stream, rlcuda, torch) if not args.no_dn else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         us, threads, reps = cpu_baseline()
@@ -331,6 +409,7 @@ def run_ours(args):
         "hbm_gbs": hbm_gbs,
         "hbm_frac_of_8tbs": hbm_gbs / 8000.0,
         "prefill_tflops": None,
+        "dn_step": dn,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "kernel": "decode_mma_kernel<fused> (split-KV walk)",
@@ -358,6 +437,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-dn", action="store_true", help="skip the DeltaNet step section")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="full-attention layers per step (8 in the model; fewer only to "
                          "keep a profiler capture small)")

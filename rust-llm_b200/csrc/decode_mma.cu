@@ -34,13 +34,14 @@
 // into the walk.
 //
 // Both kernels are launched as programmatic dependents of the kernel before
-// them (PDL).  The walk's producer may start streaming this layer's cache
-// before the previous kernel has finished (`early_kv`, set by the host when
-// nothing since the last decode wrote the cache other than decode appends,
-// which are fenced before the trigger); every read of the step's inputs and
-// every global write waits for the previous grid first.  The combine kernel
-// lets the next walk be scheduled as soon as it starts, so one layer's merge
-// tail overlaps the next layer's first tiles.
+// them (PDL), and each triggers its own dependents only after its grid-
+// dependency wait has returned (the merge right after it, the walk at its
+// end).  So when a kernel starts, every kernel but the one just ahead of it
+// has completed, and the one just ahead has passed its wait.  The walk's producer may start streaming this layer's cache before
+// the previous kernel has finished (`early_kv`, set by the host when the
+// kernel just ahead cannot be writing this cache: a merge, a DeltaNet step,
+// or nothing since a synchronous write); every read of the step's inputs and
+// every global write waits for the previous grid first.
 //
 // Reference: attend_batch / softmax of Exec::full_attn
 // (crates/rust-llm/src/forward.rs:1783-1842) and its gate (:1327-1340).
@@ -526,6 +527,7 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
             acc;
     }
     if (tid == 0 && flag_s) atomicOr(a.status, DEV_TIMEOUT);
+    // triggered last: a merge resident for the whole walk slowed it down
     __syncthreads();
     grid_dep_launch();
 }
@@ -537,8 +539,8 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
 constexpr int kCombineDims = 64, kCombineLanes = 8, kCombineBatch = 8, kCombineMaxSplits = 512;
 __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
     decode_combine_kernel(const __grid_constant__ DecodeArgs a) {
-    grid_dep_launch();  // the next walk may be scheduled while this merge runs
     grid_dep_wait();    // the walk's partials are complete and visible
+    grid_dep_launch();  // the next kernel may be scheduled while this merge runs
     __shared__ float sc_s[kCombineMaxSplits], m_s[kCombineMaxSplits], l_s[kCombineMaxSplits];
     __shared__ float red[kCombineLanes][kCombineDims];
     __shared__ float L_s;

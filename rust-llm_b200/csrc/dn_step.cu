@@ -20,6 +20,16 @@
 // over j, is exchanged through distributed shared memory, and one cluster
 // barrier after the history is read lets the key head's single writer update
 // the shared q/k conv history without racing the CTAs that read it.
+//
+// The kernel is launched as a programmatic dependent (PDL) of the kernel
+// before it and triggers its own dependents as soon as its grid-dependency
+// wait returns, so when a kernel starts, every kernel before the one just
+// ahead of it has completed.  What the context owns and only this kernel
+// writes (the state block and conv history of this layer) is therefore safe
+// to load before the wait unless the kernel just ahead is a step of the same
+// layer; the host passes `early_state` accordingly.  The conv weights and
+// gate constants are loaded before the wait always (set once, synchronously);
+// the row inputs are read, and every global write is made, after it.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -57,13 +67,6 @@ __global__ void __launch_bounds__(dn::THREADS, 1) dn_step_kernel(const LinArgs a
     const float shrink = 1.0f / sqrtf((float)S);
     const float l2_eps = a.eps / (float)S;
 
-    // state block, rows warp*RPW .. +RPW, column j, read from slot `live`
-    float st[RPW];
-    {
-        const float *src = a.ssm_state + ((size_t)(vh * slots + a.live) * S) * S + j;
-#pragma unroll
-        for (int ii = 0; ii < RPW; ++ii) st[ii] = src[(size_t)(warp * RPW + ii) * S];
-    }
     // channels: thread tid convolves q (tid < S) or k (tid >= S) channel of
     // key head kh; threads tid < JC also take value channel j0 + tid
     const int ch0 = tid < S ? kh * S + tid : key_dim + kh * S + (tid - S);
@@ -73,17 +76,32 @@ __global__ void __launch_bounds__(dn::THREADS, 1) dn_step_kernel(const LinArgs a
     float w0[4], h0[HIST], w1[4] = {0, 0, 0, 0}, h1[HIST] = {0, 0, 0};
 #pragma unroll
     for (int e = 0; e < 4; ++e) w0[e] = a.conv1d[(size_t)ch0 * 4 + e];
-    const float *hist_live = a.conv_state + (size_t)a.live * conv_dim * HIST;
-#pragma unroll
-    for (int e = 0; e < HIST; ++e) h0[e] = hist_live[(size_t)ch0 * HIST + e];
     if (has_v) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) w1[e] = a.conv1d[(size_t)ch1 * 4 + e];
-#pragma unroll
-        for (int e = 0; e < HIST; ++e) h1[e] = hist_live[(size_t)ch1 * HIST + e];
     }
     const float dt_bias = a.dt_bias[vh], ssm_a = a.ssm_a[vh];
     const float wnorm = a.norm[j];
+    // state block, rows warp*RPW .. +RPW, column j, and the conv history,
+    // both read from slot `live`
+    float st[RPW];
+    const float *hist_live = a.conv_state + (size_t)a.live * conv_dim * HIST;
+    auto load_state = [&]() {
+        const float *src = a.ssm_state + ((size_t)(vh * slots + a.live) * S) * S + j;
+#pragma unroll
+        for (int ii = 0; ii < RPW; ++ii) st[ii] = src[(size_t)(warp * RPW + ii) * S];
+#pragma unroll
+        for (int e = 0; e < HIST; ++e) h0[e] = hist_live[(size_t)ch0 * HIST + e];
+        if (has_v) {
+#pragma unroll
+            for (int e = 0; e < HIST; ++e) h1[e] = hist_live[(size_t)ch1 * HIST + e];
+        }
+    };
+    if (a.early_state) load_state();
+    // the row inputs come from the kernel before; so does the right to write
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!a.early_state) load_state();
     // every CTA of the cluster holds the history it read; only now may the
     // writer overwrite slot `live` (slots == 1, or a batch that wraps the ring)
     cluster.sync();
@@ -213,13 +231,15 @@ cudaError_t launch_dn_step(const LinArgs &a, cudaStream_t st) {
     cfg.blockDim = dim3(dn::THREADS);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = dn::CL * gv;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, dn_step_kernel, a);
 }
 

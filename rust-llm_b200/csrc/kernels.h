@@ -85,6 +85,9 @@ struct LinArgs {
     int *status;
     int t, slots, live, s, n_k, n_v, kernel;
     float eps;
+    // the state and conv history may be read before the grid-dependency
+    // wait: the kernel just ahead on the stream is not a step of this layer
+    bool early_state;
 };
 
 cudaError_t init_dn_kernels();

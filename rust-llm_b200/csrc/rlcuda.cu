@@ -52,9 +52,13 @@ struct rl_ctx {
     int max_clusters[2][4] = {};
     // resident CTAs per SM of the bf16 walk: [fused]
     int mma_per_sm[2] = {};
-    // the next bf16 decode may stream the cache early: nothing but decode
-    // appends (fenced before their grid's trigger) wrote it since the last one
+    // the next bf16 decode may stream the cache early: the kernel just ahead
+    // on the stream cannot be writing it
     bool early_ok = false;
+    // the library kernel launched last on the stream: 1 = DeltaNet step of
+    // layer prev_layer (its successor must not read that layer's state before
+    // its grid-dependency wait), 0 = anything else
+    int prev_dn = 0, prev_layer = -1;
     float theta_scale = 1.0f;
     std::string err;
     // per-kernel timing (rl_profile_*)
@@ -523,6 +527,7 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
             CK(ctx, rl::launch_decode_combine(d, ctx->stream));
         }
         ctx->early_ok = fused;
+        ctx->prev_dn = 0;
         return RL_OK;
     }
 
@@ -564,6 +569,7 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         CK(ctx, rl::launch_decode(d, ctx->stream));
     }
     ctx->early_ok = false;
+    ctx->prev_dn = 0;
     return RL_OK;
 }
 
@@ -623,10 +629,13 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
     a.n_v = c.n_v_heads;
     a.kernel = c.conv_kernel;
     a.eps = c.rms_eps;
+    a.early_state = !(ctx->prev_dn && ctx->prev_layer == layer);
     {
         ProfScope ps(ctx, RL_PROF_DN_STEP);
         CK(ctx, rl::launch_dn_step(a, ctx->stream));
     }
+    ctx->prev_dn = 1;
+    ctx->prev_layer = layer;
     return RL_OK;
 }
 
