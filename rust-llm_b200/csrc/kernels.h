@@ -63,6 +63,21 @@ constexpr int kDecodeBoxRows = 64, kDecodeBoxCols = 64;
 int decode_mma_max_active_ctas(bool fused);  // resident walk CTAs per SM
 int decode_mma_positions_per_tile();
 
+// One call of the tcgen05 causal prefill (prefill.cu): t rows at positions
+// pos..pos+t-1 whose queries the prologue staged in bf16 (q_map: [t][n_head]
+// [hd] in boxes of 128 rows x 64 dims) and whose keys and values it appended
+// to the bf16 cache (kv_map, as for the decode walk).
+struct PrefillArgs {
+    const float *qg;  // [t][n_head][2*hd]: the gate half is read here
+    float *out;       // [t][n_head*hd]
+    int *status;
+    int t, pos, n_head, n_kv, context, k_row0, v_row0;
+};
+cudaError_t init_prefill_kernels();
+cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
+                           const CUtensorMap &kv_map, cudaStream_t st);
+constexpr int kPrefillQBoxRows = 128;
+
 cudaError_t init_full_attn_kernels();
 // cos/sin of every position's RoPE angles, [context][n_rot/2] each
 cudaError_t launch_rope_table(float *cs, float *sn, int context, int n_rot, float theta_scale,

@@ -1,0 +1,309 @@
+// Causal prefill attention for the gated GQA layers on the fifth-generation
+// tensor cores (tcgen05 + tensor memory), bf16 in, f32 accumulate, sm_100a.
+//
+// One CTA per (128-row query tile, query head).  Warp roles:
+//   warp 0      TMA producer: the query tile once (4 boxes of 128 rows x 64
+//               dims), then K and V tiles of 64 positions (4 + 4 boxes of
+//               64 x 64) into a 2-stage ring; 128-byte swizzle throughout
+//   warp 1      tensor-memory allocator and the single MMA-issuing thread:
+//               S_j = Q K_j^T (M 128, N 64, K 256: 16 MMAs) into one of two
+//               S buffers, then O += P_{j-1} V_{j-1} (M 128, N 256, K 64: 4
+//               MMAs) with P read from tensor memory, so the next tile's
+//               Q K^T runs while the softmax works on this one
+//   warps 2-5   softmax and epilogue, one query row per thread: S row from
+//               tensor memory, causal mask, online softmax in log2 units with
+//               a lazy rescale (O is corrected only when a row's max grows by
+//               more than 2^8), P written back as bf16 over the S buffer; at
+//               the end O / l times the sigmoid output gate, to global memory
+// Tensor memory (512 columns): O in columns 0-255, S buffers at 256 and 320;
+// P_j aliases the first 32 columns of its S buffer.  MMAs of one thread run
+// in issue order, so Q K^T of tile j+2 (same S buffer) cannot overtake the
+// P V of tile j that reads P_j.
+//
+// Reference: attend_batch / softmax over the causal prefix
+// (crates/rust-llm/src/forward.rs:1783-1842) and the gate (:1327-1340); the
+// queries and the appended keys come from the multi-row prologue
+// (full_attn.cu), which applies the norms and RoPE (:1259-1292).
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace rl {
+namespace pf {
+constexpr int HD = 256;
+constexpr int BM = 128;          // query rows per CTA
+constexpr int BN = 64;           // key positions per tile
+constexpr int THREADS = 192;     // 6 warps
+constexpr int Q_BOX = BM * 128;  // 16 KiB: 128 rows x 64 dims
+constexpr int KV_BOX = BN * 128; // 8 KiB: 64 rows x 64 dims
+constexpr int Q_BYTES = 4 * Q_BOX;
+constexpr int KV_HALF = 4 * KV_BOX;  // K (or V) of one tile
+constexpr int STAGE = 2 * KV_HALF;
+constexpr int SMEM = Q_BYTES + 2 * STAGE + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t O_COL = 0, S_COL = 256;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_LOG2 = 8.0f;
+}  // namespace pf
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y,
+                                            int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__global__ void __launch_bounds__(pf::THREADS, 1)
+    prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap q_map,
+                   const __grid_constant__ CUtensorMap kv_map) {
+    using namespace pf;
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2],
+        p_full[2], o_ready, o_final;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int flag_s;
+
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // heaviest query tiles first: they have the most key tiles
+    const int n_qt = (a.t + BM - 1) / BM;
+    const int qt = n_qt - 1 - (int)(blockIdx.x / a.n_head);
+    const int head = blockIdx.x % a.n_head;
+    const int kh = head / (a.n_head / a.n_kv);
+    const int q0 = qt * BM;
+    const int q_last = min(a.t, q0 + BM) - 1;              // last valid row of the tile
+    const int n_kt = (a.pos + q_last) / BN + 1;             // key tiles the tile needs
+    const uint32_t sbase = smem_u32(smem);
+
+    if (tid == 0) {
+        mbar_init(&q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+            mbar_init(&p_full[s], 4);
+        }
+        mbar_init(&o_ready, 1);
+        mbar_init(&o_final, 1);
+        flag_s = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&tmem_base_s, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tensormap(&q_map);
+            prefetch_tensormap(&kv_map);
+            mbar_arrive_expect_tx(&q_full, Q_BYTES);
+            for (int b = 0; b < 4; ++b)
+                tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
+            const int krow = a.k_row0 + kh * a.context, vrow = a.v_row0 + kh * a.context;
+            int issued = 0;
+            for (int j = 0; j < n_kt; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, a.status)) {
+                    flag_s = 1;
+                    break;
+                }
+                unsigned char *st = smem + Q_BYTES + s * STAGE;
+                mbar_arrive_expect_tx(&k_full[s], KV_HALF);
+                for (int b = 0; b < 4; ++b)
+                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, krow + j * BN, &k_full[s]);
+                mbar_arrive_expect_tx(&v_full[s], KV_HALF);
+                for (int b = 0; b < 4; ++b)
+                    tma_load_2d(st + KV_HALF + b * KV_BOX, &kv_map, b * 64, vrow + j * BN,
+                                &v_full[s]);
+                issued = j + 1;
+            }
+            // everything started has landed before the CTA releases its memory
+            mbar_wait(&q_full, 0, a.status);
+            for (int j = max(0, issued - 2); j < issued; ++j) {
+                mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status);
+                mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.status);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t id_qk = tc::idesc_bf16(BM, BN, false);
+            constexpr uint32_t id_pv = tc::idesc_bf16(BM, HD, true);
+            bool ok = mbar_wait(&q_full, 0, a.status);
+            tc::fence_after_sync();
+            for (int j = 0; ok && j <= n_kt; ++j) {
+                if (j < n_kt) {
+                    const int s = j & 1;
+                    if (!mbar_wait(&k_full[s], (j >> 1) & 1, a.status)) { ok = false; break; }
+                    tc::fence_after_sync();
+                    const uint32_t kst = sbase + Q_BYTES + s * STAGE;
+                    const uint32_t d = tmem + S_COL + s * BN;
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint32_t off = (kk & 3) * 32;  // 16 dims inside a 64-dim box
+                        const uint64_t da = tc::smem_desc(sbase + (kk >> 2) * Q_BOX + off, 16, 1024);
+                        const uint64_t db = tc::smem_desc(kst + (kk >> 2) * KV_BOX + off, 16, 1024);
+                        tc::mma_ss(d, da, db, id_qk, kk > 0);
+                    }
+                    tc::commit(&s_full[s]);
+                }
+                if (j >= 1) {
+                    const int jj = j - 1, s = jj & 1;
+                    if (!mbar_wait(&p_full[s], (jj >> 1) & 1, a.status) ||
+                        !mbar_wait(&v_full[s], (jj >> 1) & 1, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t vst = sbase + Q_BYTES + s * STAGE + KV_HALF;
+                    const uint32_t p = tmem + S_COL + s * BN;
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk) {
+                        const uint64_t db = tc::smem_desc(vst + kk * 16 * 128, KV_BOX, 1024);
+                        tc::mma_ts(tmem + O_COL, p + kk * 8, db, id_pv, jj > 0 || kk > 0);
+                    }
+                    tc::commit(&kv_empty[s]);
+                    tc::commit(&o_ready);
+                }
+            }
+            if (!ok) flag_s = 1;
+            // o_final completes when every MMA issued above is done; the
+            // tensor memory is not released before that
+            tc::commit(&o_final);
+            mbar_wait(&o_final, 0, a.status);
+        }
+    } else {
+        // ---------------- softmax + epilogue: one query row per thread ----------------
+        const int quarter = warp & 3;  // tensor-memory lanes 32*quarter.. this warp may touch
+        const int r = quarter * 32 + lane;
+        const int qa = a.pos + q0 + r;  // absolute position of this row
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        const float scale = (1.0f / 16.0f) * LOG2E;
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < n_kt; ++j) {
+            const int s = j & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, a.status))) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            const uint32_t sc = tmem + lane_off + S_COL + s * BN;
+            uint32_t u0[32], u1[32];
+            tc::ld32(sc, u0);
+            tc::ld32(sc + 32, u1);
+            tc::wait_ld();
+            float x[64];
+            const int kv0 = j * BN;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float v0 = kv0 + c <= qa ? __uint_as_float(u0[c]) * scale : -INFINITY;
+                const float v1 = kv0 + 32 + c <= qa ? __uint_as_float(u1[c]) * scale : -INFINITY;
+                x[c] = v0;
+                x[32 + c] = v1;
+                mt = fmaxf(mt, fmaxf(v0, v1));
+            }
+            const bool grow = mt > m_run + RESCALE_LOG2;
+            if (__any_sync(0xffffffffu, grow)) {
+                const float m_new = grow ? mt : m_run;
+                const float corr = m_run == -INFINITY ? 0.0f : exp2f(m_run - m_new);
+                if (j > 0) {
+                    // O holds tiles < j: wait for the last P V, then correct it
+                    if (!__all_sync(0xffffffffu, mbar_wait(&o_ready, (j - 1) & 1, a.status))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t oc = tmem + lane_off + O_COL;
+#pragma unroll 1
+                    for (int c = 0; c < HD / 32; ++c) {
+                        uint32_t o[32];
+                        tc::ld32(oc + c * 32, o);
+                        tc::wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                        tc::st32(oc + c * 32, o);
+                    }
+                    tc::wait_st();
+                }
+                l_run *= corr;
+                m_run = m_new;
+            }
+            uint32_t pk[32];
+            float ps = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float p0 = exp2f(x[2 * c] - m_run), p1 = exp2f(x[2 * c + 1] - m_run);
+                ps += p0 + p1;
+                __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+                pk[c] = *reinterpret_cast<uint32_t *>(&h);
+            }
+            l_run += ps;
+            tc::st32(sc, pk);
+            tc::wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[s]);
+        }
+        // ---- epilogue: O / l * sigmoid(gate)
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(&o_final, 0, a.status))) ok = false;
+        if (!ok) flag_s = 1;
+        tc::fence_after_sync();
+        const int row = q0 + r;
+        const float inv_l = 1.0f / l_run;
+        const uint32_t oc = tmem + lane_off + O_COL;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tc::ld32(oc + c * 32, o);
+            tc::wait_ld();
+            if (ok && row < a.t) {
+                const float *g = a.qg + ((size_t)row * a.n_head + head) * 2 * HD + HD + c * 32;
+                float *dst = a.out + ((size_t)row * a.n_head + head) * HD + c * 32;
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const float4 gv = *reinterpret_cast<const float4 *>(g + e);
+                    float4 y;
+                    y.x = __uint_as_float(o[e]) * inv_l * sigmoidf_(gv.x);
+                    y.y = __uint_as_float(o[e + 1]) * inv_l * sigmoidf_(gv.y);
+                    y.z = __uint_as_float(o[e + 2]) * inv_l * sigmoidf_(gv.z);
+                    y.w = __uint_as_float(o[e + 3]) * inv_l * sigmoidf_(gv.w);
+                    *reinterpret_cast<float4 *>(dst + e) = y;
+                }
+            }
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+    if (tid == 0 && flag_s) atomicOr(a.status, DEV_TIMEOUT);
+}
+
+cudaError_t init_prefill_kernels() {
+    return cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                pf::SMEM);
+}
+
+cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
+                           const CUtensorMap &kv_map, cudaStream_t st) {
+    const int n_qt = (a.t + pf::BM - 1) / pf::BM;
+    prefill_kernel<<<n_qt * a.n_head, pf::THREADS, pf::SMEM, st>>>(a, q_map, kv_map);
+    return cudaGetLastError();
+}
+
+}  // namespace rl

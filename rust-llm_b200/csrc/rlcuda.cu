@@ -42,11 +42,13 @@ struct rl_ctx {
     float *rope_cs = nullptr, *rope_sn = nullptr;  // [context][n_rot/2]
     // bf16 caches: TMA map of the whole KV allocation as rows of head_dim
     CUtensorMap kv_map{};
+    // bf16 caches: TMA map of the staged bf16 queries [max_batch][n_head][hd]
+    CUtensorMap q_map{};
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
-    int64_t opt_splits = 0, opt_prefill_rows = 0, opt_chunk_rows = 0, opt_cluster = 0;
+    int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 0, opt_cluster = 0;
     int64_t opt_early_tiles = 2;
     // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
@@ -274,7 +276,8 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         return bail(fail(x, RL_ECUDA, "cudaStreamCreate failed"));
     x->own_stream = true;
     if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
-        rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess)
+        rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess ||
+        rl::init_prefill_kernels() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
     for (int f = 0; f < 2; ++f) {
         for (int lc = 0; lc < 4; ++lc)
@@ -316,6 +319,10 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
             if (rl::encode_bf16_2d(&x->kv_map, x->kv, rows, c.head_dim, (uint64_t)c.head_dim * 2,
                                    rl::kDecodeBoxRows, rl::kDecodeBoxCols) != cudaSuccess)
                 return bail(fail(x, RL_ECUDA, "encoding the KV tensor map failed"));
+            if (rl::encode_bf16_3d(&x->q_map, x->q_bf16, c.head_dim, c.n_head, mb,
+                                   (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
+                                   64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
+                return bail(fail(x, RL_ECUDA, "encoding the query tensor map failed"));
         }
     }
     // staging for the host entry points: the larger of the two paths' in+out
@@ -444,6 +451,7 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     void *k_cache = kv_layer(ctx, layer);
     void *v_cache = (char *)k_cache + half;
     const bool fused = t == 1;
+    const bool prefill = bf16 && ctx->opt_prefill_rows > 0 && t >= ctx->opt_prefill_rows;
     if (!fused) {
         // rows of a batch attend to each other's keys: append them all first
         rl::FullArgs a{};
@@ -455,7 +463,7 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         a.k_cache = k_cache;
         a.v_cache = v_cache;
         a.q_f32 = ctx->q_f32;
-        a.q_bf16 = nullptr;
+        a.q_bf16 = prefill ? ctx->q_bf16 : nullptr;
         a.t = t;
         a.pos = pos;
         a.n_head = c.n_head;
@@ -466,8 +474,30 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         a.theta_scale = ctx->theta_scale;
         a.eps = c.rms_eps;
         a.kv_bf16 = bf16;
-        ProfScope ps(ctx, RL_PROF_PROLOGUE);
-        CK(ctx, rl::launch_full_prologue(a, ctx->stream));
+        {
+            ProfScope ps(ctx, RL_PROF_PROLOGUE);
+            CK(ctx, rl::launch_full_prologue(a, ctx->stream));
+        }
+        if (prefill) {
+            rl::PrefillArgs pa{};
+            pa.qg = qg;
+            pa.out = out;
+            pa.status = ctx->status;
+            pa.t = t;
+            pa.pos = pos;
+            pa.n_head = c.n_head;
+            pa.n_kv = c.n_head_kv;
+            pa.context = c.context;
+            pa.k_row0 = layer * 2 * c.n_head_kv * c.context;
+            pa.v_row0 = pa.k_row0 + c.n_head_kv * c.context;
+            {
+                ProfScope ps(ctx, RL_PROF_PREFILL);
+                CK(ctx, rl::launch_prefill(pa, ctx->q_map, ctx->kv_map, ctx->stream));
+            }
+            ctx->early_ok = false;
+            ctx->prev_dn = 0;
+            return RL_OK;
+        }
     }
     const int64_t n_kv_max = (int64_t)pos + t;
     const int64_t groups = (int64_t)c.n_head_kv * t;  // (KV head, row) pairs

@@ -38,4 +38,20 @@ cudaError_t encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, ui
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t encode_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1,
+                           uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                           uint32_t b0, uint32_t b1, uint32_t b2) {
+    std::call_once(g_once, resolve);
+    if (!g_encode) return cudaErrorNotSupported;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base),
+                                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace rl

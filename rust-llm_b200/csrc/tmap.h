@@ -16,4 +16,11 @@ namespace rl {
 cudaError_t encode_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
                            uint64_t row_bytes, uint32_t box_rows, uint32_t box_cols);
 
+// A 3-D bf16 tensor [d2][d1][d0] (d0 contiguous, strides in bytes for d1 and
+// d2, multiples of 16), read in boxes of b2 x b1 x b0 with the 128-byte
+// swizzle (b0 * 2 <= 128).
+cudaError_t encode_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1,
+                           uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                           uint32_t b0, uint32_t b1, uint32_t b2);
+
 }  // namespace rl

@@ -202,6 +202,9 @@ class Context:
     def set_option(self, opt: int, value: int):
         self._check(self._L.rl_set_option(self._h, opt, value))
 
+    def get_option(self, opt: int) -> int:
+        return int(self._L.rl_get_option(self._h, opt))
+
     # -- per-kernel timing -----------------------------------------------
     def profile(self, on: bool):
         self._check(self._L.rl_profile_enable(self._h, int(on)))
