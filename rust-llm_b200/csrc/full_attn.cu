@@ -1,7 +1,7 @@
 // Gated GQA full attention: the prologue of a multi-row call.
 //
 //   full_prologue_kernel   per-head q/k RMSNorm + partial RoPE, KV append of
-//                          all t rows, f32 (and optional bf16) staging of the
+//                          all t rows, f32 and/or bf16 staging of the
 //                          queries, before the attention kernels read them
 //
 // Reference: the first half of Exec::full_attn's span
@@ -14,69 +14,112 @@
 namespace rl {
 
 // ---------------------------------------------------------------------------
-// Prologue.  Block (head, row): heads [0, n_head) are queries, read from the
-// query half of qg; heads [n_head, n_head + n_kv) are keys.  One thread per
-// dimension.
+// Prologue.  One warp per (row, head): heads [0, n_head) are queries, read
+// from the query half of qg; heads [n_head, n_head + n_kv) are keys, whose
+// warp also appends the value row.  Each lane holds 8 consecutive dims; the
+// RMSNorm's sum of squares is an f64 warp sum (forward.rs:1697-1711) and the
+// RoPE angles come from the per-context table, whose angles are advanced by
+// repeated f32 multiplication as forward.rs:1855-1861 does.
 template <typename KV>
-__global__ void full_prologue_kernel(const float *__restrict__ qg, const float *__restrict__ k,
-                                     const float *__restrict__ v,
-                                     const float *__restrict__ q_norm,
-                                     const float *__restrict__ k_norm, KV *__restrict__ k_cache,
-                                     KV *__restrict__ v_cache, float *__restrict__ q_out,
-                                     __nv_bfloat16 *__restrict__ q_out_bf16, int pos, int n_head,
-                                     int n_kv, int context, int n_rot, float theta_scale,
-                                     float eps) {
-    extern __shared__ float buf[];  // hd floats
-    __shared__ double red[32];
-    const int hd = blockDim.x, d = threadIdx.x;
-    const int hh = blockIdx.x, i = blockIdx.y, p = pos + i;
-    const bool is_q = hh < n_head;
-    const float x = is_q ? qg[(size_t)i * 2 * hd * n_head + (size_t)hh * 2 * hd + d]
-                         : k[(size_t)i * hd * n_kv + (size_t)(hh - n_head) * hd + d];
-    const double sum = block_sum_d((double)__fmul_rn(x, x), red);
-    const float scale = rms_scale_from_sum(sum, hd, eps);
-    const float w = is_q ? q_norm[d] : k_norm[d];
-    buf[d] = __fmul_rn(__fmul_rn(x, scale), w);
-    __syncthreads();
-    float y = buf[d];
-    const int half = n_rot / 2;
-    if (d < n_rot) {
-        // the angle of pair (d mod half), advanced by repeated f32
-        // multiplication exactly as forward.rs:1855-1861 does
+__global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_heads = a.n_head + a.n_kv;
+    const int64_t item = (int64_t)blockIdx.x * 8 + warp;
+    if (item >= (int64_t)a.t * n_heads) return;
+    const int i = (int)(item / n_heads), hh = (int)(item % n_heads), p = a.pos + i;
+    const bool is_q = hh < a.n_head;
+    constexpr int HD = 256;
+    const float *src = is_q ? a.qg + ((size_t)i * a.n_head + hh) * 2 * HD
+                            : a.k + ((size_t)i * a.n_kv + (hh - a.n_head)) * HD;
+    const float *w = is_q ? a.q_norm : a.k_norm;
+    const int half = a.n_rot / 2;
+    const float *cs_row = a.rope_cs ? a.rope_cs + (size_t)p * half : nullptr;
+    const float *sn_row = a.rope_sn ? a.rope_sn + (size_t)p * half : nullptr;
+    float x[8], wv[8], c[8], sn[8];
+    *reinterpret_cast<float4 *>(x) = *reinterpret_cast<const float4 *>(src + lane * 8);
+    *reinterpret_cast<float4 *>(x + 4) = *reinterpret_cast<const float4 *>(src + lane * 8 + 4);
+    *reinterpret_cast<float4 *>(wv) = *reinterpret_cast<const float4 *>(w + lane * 8);
+    *reinterpret_cast<float4 *>(wv + 4) = *reinterpret_cast<const float4 *>(w + lane * 8 + 4);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
         const int pr = d < half ? d : d - half;
-        float theta = (float)p;
-        for (int j = 0; j < pr; ++j) theta = __fmul_rn(theta, theta_scale);
-        const float c = cosf(theta), s = sinf(theta);
-        const float x0 = buf[pr], x1 = buf[pr + half];
-        y = d < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
-                     : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        c[e] = 1.0f;
+        sn[e] = 0.0f;
+        if (d < a.n_rot) {
+            if (a.rope_cs) {
+                c[e] = cs_row[pr];
+                sn[e] = sn_row[pr];
+            } else {
+                // no table (callers without a context): the same angle,
+                // advanced by repeated f32 multiplication from theta = p
+                float theta = (float)p;
+                for (int jj = 0; jj < pr; ++jj) theta = __fmul_rn(theta, a.theta_scale);
+                c[e] = cosf(theta);
+                sn[e] = sinf(theta);
+            }
+        }
+    }
+    double sq = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sq += (double)__fmul_rn(x[e], x[e]);
+    sq = warp_sum_d(sq);
+    const float scale = rms_scale_from_sum(sq, HD, a.eps);
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = __fmul_rn(__fmul_rn(x[e], scale), wv[e]);
+    // RoPE pairs dim d with d +- half: fetch the partner from the lane that
+    // holds it (half is a multiple of 8, so the partner sits at the same e)
+    const int lane_shift = half / 8;
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int d = lane * 8 + e;
+        const bool lo = d < half;
+        const float up = __shfl_down_sync(0xffffffffu, y[e], lane_shift > 0 ? lane_shift : 1);
+        const float dn = __shfl_up_sync(0xffffffffu, y[e], lane_shift > 0 ? lane_shift : 1);
+        r[e] = y[e];
+        if (d < a.n_rot)
+            r[e] = lo ? __fsub_rn(__fmul_rn(y[e], c[e]), __fmul_rn(up, sn[e]))
+                      : __fadd_rn(__fmul_rn(dn, sn[e]), __fmul_rn(y[e], c[e]));
     }
     if (is_q) {
-        const size_t o = ((size_t)i * n_head + hh) * hd + d;
-        q_out[o] = y;
-        if (q_out_bf16) q_out_bf16[o] = __float2bfloat16_rn(y);
+        const size_t o = ((size_t)i * a.n_head + hh) * HD + lane * 8;
+        if (a.q_f32) {
+            *reinterpret_cast<float4 *>(a.q_f32 + o) = make_float4(r[0], r[1], r[2], r[3]);
+            *reinterpret_cast<float4 *>(a.q_f32 + o + 4) = make_float4(r[4], r[5], r[6], r[7]);
+        }
+        if (a.q_bf16) {
+            __nv_bfloat162 b[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) b[e] = __floats2bfloat162_rn(r[2 * e], r[2 * e + 1]);
+            *reinterpret_cast<uint4 *>(a.q_bf16 + o) = *reinterpret_cast<uint4 *>(b);
+        }
     } else {
-        const int kh = hh - n_head;
-        const size_t to = ((size_t)kh * context + p) * hd + d;
-        k_cache[to] = from_f32<KV>(y);
-        v_cache[to] = from_f32<KV>(v[(size_t)i * hd * n_kv + (size_t)kh * hd + d]);
+        const int kh = hh - a.n_head;
+        const size_t to = ((size_t)kh * a.context + p) * HD + lane * 8;
+        KV *kc = static_cast<KV *>(a.k_cache), *vc = static_cast<KV *>(a.v_cache);
+        const float *vsrc = a.v + ((size_t)i * a.n_kv + kh) * HD + lane * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            kc[to + e] = from_f32<KV>(r[e]);
+            vc[to + e] = from_f32<KV>(vsrc[e]);
+        }
     }
 }
 
 // ---------------------------------------------------------------------------
 // Host launchers.
 
-template <typename KV>
-static cudaError_t launch_prologue_t(const FullArgs &a, cudaStream_t st) {
-    dim3 grid(a.n_head + a.n_kv, a.t);
-    full_prologue_kernel<KV><<<grid, a.hd, a.hd * sizeof(float), st>>>(
-        a.qg, a.k, a.v, a.q_norm, a.k_norm, (KV *)a.k_cache, (KV *)a.v_cache, a.q_f32, a.q_bf16,
-        a.pos, a.n_head, a.n_kv, a.context, a.n_rot, a.theta_scale, a.eps);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_full_prologue(const FullArgs &a, cudaStream_t st) {
-    return a.kv_bf16 ? launch_prologue_t<__nv_bfloat16>(a, st) : launch_prologue_t<float>(a, st);
+    if (a.hd != 256 || (a.n_rot % 16) != 0) return cudaErrorInvalidValue;
+    const int64_t items = (int64_t)a.t * (a.n_head + a.n_kv);
+    const unsigned blocks = (unsigned)((items + 7) / 8);
+    if (a.kv_bf16)
+        full_prologue_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);
+    else
+        full_prologue_kernel<float><<<blocks, 256, 0, st>>>(a);
+    return cudaGetLastError();
 }
 
 cudaError_t init_full_attn_kernels() { return cudaSuccess; }

@@ -14,8 +14,9 @@ struct FullArgs {
     const float *qg;       // [t][n_head][2*hd]  query | gate
     const float *k, *v;    // [t][n_kv][hd]
     const float *q_norm, *k_norm;  // [hd]
+    const float *rope_cs, *rope_sn;  // [context][n_rot/2] cos, sin of the RoPE angles
     void *k_cache, *v_cache;       // [n_kv][context][hd], f32 or bf16
-    float *q_f32;                  // [t][n_head][hd] normalised, rotated queries
+    float *q_f32;                  // [t][n_head][hd] normalised, rotated queries, or null
     __nv_bfloat16 *q_bf16;         // same in bf16, or null when not needed
     int t, pos, n_head, n_kv, hd, context, n_rot;
     float theta_scale, eps;

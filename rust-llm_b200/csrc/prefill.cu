@@ -10,11 +10,13 @@
 //               S buffers, then O += P_{j-1} V_{j-1} (M 128, N 256, K 64: 4
 //               MMAs) with P read from tensor memory, so the next tile's
 //               Q K^T runs while the softmax works on this one
-//   warps 2-5   softmax and epilogue, one query row per thread: S row from
-//               tensor memory, causal mask, online softmax in log2 units with
-//               a lazy rescale (O is corrected only when a row's max grows by
-//               more than 2^8), P written back as bf16 over the S buffer; at
-//               the end O / l times the sigmoid output gate, to global memory
+//   warps 2-9   softmax and epilogue, two threads per query row (each half
+//               of the tile's columns and of O): S from tensor memory, causal
+//               mask on the diagonal tiles, the row max exchanged through
+//               shared memory, online softmax in log2 units with a lazy
+//               rescale (O is corrected only when a row's max grows by more
+//               than 2^8), P written back as bf16 over the S buffer; at the
+//               end O / l times the sigmoid output gate, to global memory
 // Tensor memory (512 columns): O in columns 0-255, S buffers at 256 and 320;
 // P_j aliases the first 32 columns of its S buffer.  MMAs of one thread run
 // in issue order, so Q K^T of tile j+2 (same S buffer) cannot overtake the
@@ -33,7 +35,7 @@ namespace pf {
 constexpr int HD = 256;
 constexpr int BM = 128;          // query rows per CTA
 constexpr int BN = 64;           // key positions per tile
-constexpr int THREADS = 192;     // 6 warps
+constexpr int THREADS = 320;     // 10 warps
 constexpr int Q_BOX = BM * 128;  // 16 KiB: 128 rows x 64 dims
 constexpr int KV_BOX = BN * 128; // 8 KiB: 64 rows x 64 dims
 constexpr int Q_BYTES = 4 * Q_BOX;
@@ -45,6 +47,12 @@ constexpr uint32_t O_COL = 0, S_COL = 256;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_LOG2 = 8.0f;
 }  // namespace pf
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y,
                                             int z, uint64_t *bar) {
@@ -64,6 +72,10 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         p_full[2], o_ready, o_final;
     __shared__ uint32_t tmem_base_s;
     __shared__ int flag_s;
+    __shared__ float red_m[2][2][BM], red_l[2][BM];  // the two halves of each row
+    // the halves meet on mbarriers (bounded waits), not named barriers, so a
+    // warp that gives up cannot leave its partner waiting for good
+    __shared__ __align__(8) uint64_t mx_bar[2], l_bar;
 
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -84,10 +96,13 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             mbar_init(&v_full[s], 1);
             mbar_init(&kv_empty[s], 1);
             mbar_init(&s_full[s], 1);
-            mbar_init(&p_full[s], 4);
+            mbar_init(&p_full[s], 8);
         }
         mbar_init(&o_ready, 1);
         mbar_init(&o_final, 1);
+        mbar_init(&mx_bar[0], 256);
+        mbar_init(&mx_bar[1], 256);
+        mbar_init(&l_bar, 256);
         flag_s = 0;
         fence_barrier_init();
     }
@@ -182,12 +197,17 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             mbar_wait(&o_final, 0, a.status);
         }
     } else {
-        // ---------------- softmax + epilogue: one query row per thread ----------------
-        const int quarter = warp & 3;  // tensor-memory lanes 32*quarter.. this warp may touch
+        // ---------------- softmax + epilogue: two threads per query row ----------------
+        // warps 2-5 take S columns 0-31 of each tile and O columns 0-127,
+        // warps 6-9 columns 32-63 and O columns 128-255; warps w and w+4 share
+        // the tensor-memory lane quarter w % 4, i.e. the same 32 rows
+        const int quarter = warp & 3;
+        const int h = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;
         const int qa = a.pos + q0 + r;  // absolute position of this row
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         const float scale = (1.0f / 16.0f) * LOG2E;
+        const int first_masked = (a.pos + q0) / BN;  // earliest tile a row of the CTA masks
         float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
         for (int j = 0; j < n_kt; ++j) {
@@ -198,35 +218,44 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             }
             tc::fence_after_sync();
             const uint32_t sc = tmem + lane_off + S_COL + s * BN;
-            uint32_t u0[32], u1[32];
-            tc::ld32(sc, u0);
-            tc::ld32(sc + 32, u1);
+            uint32_t u[32];
+            tc::ld32(sc + 32 * h, u);
             tc::wait_ld();
-            float x[64];
-            const int kv0 = j * BN;
-            float mt = -INFINITY;
+            const int kv0 = j * BN + 32 * h;
+            if (j >= first_masked) {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const float v0 = kv0 + c <= qa ? __uint_as_float(u0[c]) * scale : -INFINITY;
-                const float v1 = kv0 + 32 + c <= qa ? __uint_as_float(u1[c]) * scale : -INFINITY;
-                x[c] = v0;
-                x[32 + c] = v1;
-                mt = fmaxf(mt, fmaxf(v0, v1));
+                for (int c = 0; c < 32; ++c)
+                    if (kv0 + c > qa) u[c] = __float_as_uint(-INFINITY);
             }
+            float mx0 = __uint_as_float(u[0]), mx1 = __uint_as_float(u[1]);
+#pragma unroll
+            for (int c = 2; c < 32; c += 2) {
+                mx0 = fmaxf(mx0, __uint_as_float(u[c]));
+                mx1 = fmaxf(mx1, __uint_as_float(u[c + 1]));
+            }
+            // the row's max over both halves (scores scale by a positive constant)
+            red_m[j & 1][h][r] = fmaxf(mx0, mx1);
+            mbar_arrive(&mx_bar[j & 1]);
+            if (!__all_sync(0xffffffffu, mbar_wait(&mx_bar[j & 1], (j >> 1) & 1, a.status))) {
+                ok = false;
+                break;
+            }
+            const float mt = fmaxf(red_m[j & 1][0][r], red_m[j & 1][1][r]) * scale;
             const bool grow = mt > m_run + RESCALE_LOG2;
             if (__any_sync(0xffffffffu, grow)) {
                 const float m_new = grow ? mt : m_run;
                 const float corr = m_run == -INFINITY ? 0.0f : exp2f(m_run - m_new);
                 if (j > 0) {
-                    // O holds tiles < j: wait for the last P V, then correct it
+                    // O holds tiles < j: wait for the last P V, then correct
+                    // this thread's half of the row
                     if (!__all_sync(0xffffffffu, mbar_wait(&o_ready, (j - 1) & 1, a.status))) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t oc = tmem + lane_off + O_COL;
+                    const uint32_t oc = tmem + lane_off + O_COL + 128 * h;
 #pragma unroll 1
-                    for (int c = 0; c < HD / 32; ++c) {
+                    for (int c = 0; c < 4; ++c) {
                         uint32_t o[32];
                         tc::ld32(oc + c * 32, o);
                         tc::wait_ld();
@@ -240,37 +269,44 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 l_run *= corr;
                 m_run = m_new;
             }
-            uint32_t pk[32];
-            float ps = 0.0f;
+            uint32_t pk[16];
+            float ps0 = 0.0f, ps1 = 0.0f;
+            const float neg_m = -m_run;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const float p0 = exp2f(x[2 * c] - m_run), p1 = exp2f(x[2 * c + 1] - m_run);
-                ps += p0 + p1;
-                __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-                pk[c] = *reinterpret_cast<uint32_t *>(&h);
+            for (int c = 0; c < 16; ++c) {
+                const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * c]), scale, neg_m));
+                const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * c + 1]), scale, neg_m));
+                ps0 += p0;
+                ps1 += p1;
+                __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
+                pk[c] = *reinterpret_cast<uint32_t *>(&hh);
             }
-            l_run += ps;
-            tc::st32(sc, pk);
+            l_run += ps0 + ps1;
+            tc::st16(sc + 16 * h, pk);
             tc::wait_st();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[s]);
         }
-        // ---- epilogue: O / l * sigmoid(gate)
+        // ---- epilogue: O / l * sigmoid(gate), this thread's 128 columns
         if (ok && !__all_sync(0xffffffffu, mbar_wait(&o_final, 0, a.status))) ok = false;
         if (!ok) flag_s = 1;
+        red_l[h][r] = l_run;
+        mbar_arrive(&l_bar);
+        if (!__all_sync(0xffffffffu, mbar_wait(&l_bar, 0, a.status))) ok = false;
         tc::fence_after_sync();
         const int row = q0 + r;
-        const float inv_l = 1.0f / l_run;
-        const uint32_t oc = tmem + lane_off + O_COL;
+        const float inv_l = 1.0f / (red_l[0][r] + red_l[1][r]);
+        const uint32_t oc = tmem + lane_off + O_COL + 128 * h;
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
             tc::ld32(oc + c * 32, o);
             tc::wait_ld();
             if (ok && row < a.t) {
-                const float *g = a.qg + ((size_t)row * a.n_head + head) * 2 * HD + HD + c * 32;
-                float *dst = a.out + ((size_t)row * a.n_head + head) * HD + c * 32;
+                const int d0 = 128 * h + c * 32;
+                const float *g = a.qg + ((size_t)row * a.n_head + head) * 2 * HD + HD + d0;
+                float *dst = a.out + ((size_t)row * a.n_head + head) * HD + d0;
 #pragma unroll
                 for (int e = 0; e < 32; e += 4) {
                     const float4 gv = *reinterpret_cast<const float4 *>(g + e);

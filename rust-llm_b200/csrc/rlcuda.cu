@@ -205,6 +205,10 @@ int check_shapes(rl_ctx *x, const rl_config &c) {
                         c.head_dim, c.n_head, c.n_head_kv);
         if (c.n_rot < 0 || c.n_rot > c.head_dim || (c.n_rot & 1))
             return fail(x, RL_EINVAL, "n_rot must be even and at most head_dim");
+        if (c.n_rot % 16)
+            return fail(x, RL_EUNSUPPORTED,
+                        "the kernels rotate whole 8-dim lanes: n_rot must be a multiple of 16 "
+                        "(got %d)", c.n_rot);
     }
     if (c.n_linear > 0) {
         if (c.d_state != 128 || c.conv_kernel != 4 || c.n_k_heads < 1 ||
@@ -462,7 +466,9 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         a.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
         a.k_cache = k_cache;
         a.v_cache = v_cache;
-        a.q_f32 = ctx->q_f32;
+        a.rope_cs = ctx->rope_cs;
+        a.rope_sn = ctx->rope_sn;
+        a.q_f32 = prefill ? nullptr : ctx->q_f32;
         a.q_bf16 = prefill ? ctx->q_bf16 : nullptr;
         a.t = t;
         a.pos = pos;

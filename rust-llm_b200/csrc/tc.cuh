@@ -113,6 +113,13 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
         RL_W8(0), RL_W8(8), RL_W8(16), RL_W8(24)
         : "memory");
 }
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
+        "%10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        RL_W8(0), RL_W8(8)
+        : "memory");
+}
 #undef RL_W8
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
