@@ -95,6 +95,19 @@ __global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
             for (int e = 0; e < 4; ++e) b[e] = __floats2bfloat162_rn(r[2 * e], r[2 * e + 1]);
             *reinterpret_cast<uint4 *>(a.q_bf16 + o) = *reinterpret_cast<uint4 *>(b);
         }
+        if (a.gate_bf16) {
+            // the output gate, sigmoid(g) (forward.rs:1327-1340), staged in
+            // bf16 for the prefill kernel's epilogue
+            float g[8];
+            *reinterpret_cast<float4 *>(g) = *reinterpret_cast<const float4 *>(src + HD + lane * 8);
+            *reinterpret_cast<float4 *>(g + 4) =
+                *reinterpret_cast<const float4 *>(src + HD + lane * 8 + 4);
+            __nv_bfloat162 b[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                b[e] = __floats2bfloat162_rn(sigmoidf_(g[2 * e]), sigmoidf_(g[2 * e + 1]));
+            *reinterpret_cast<uint4 *>(a.gate_bf16 + o) = *reinterpret_cast<uint4 *>(b);
+        }
     } else {
         const int kh = hh - a.n_head;
         const size_t to = ((size_t)kh * a.context + p) * HD + lane * 8;

@@ -18,6 +18,7 @@ struct FullArgs {
     void *k_cache, *v_cache;       // [n_kv][context][hd], f32 or bf16
     float *q_f32;                  // [t][n_head][hd] normalised, rotated queries, or null
     __nv_bfloat16 *q_bf16;         // same in bf16, or null when not needed
+    __nv_bfloat16 *gate_bf16;      // [t][n_head][hd] sigmoid of the gate in bf16, or null
     int t, pos, n_head, n_kv, hd, context, n_rot;
     float theta_scale, eps;
     bool kv_bf16;
@@ -69,14 +70,16 @@ int decode_mma_positions_per_tile();
 // [hd] in boxes of 128 rows x 64 dims) and whose keys and values it appended
 // to the bf16 cache (kv_map, as for the decode walk).
 struct PrefillArgs {
-    const float *qg;  // [t][n_head][2*hd]: the gate half is read here
     float *out;       // [t][n_head*hd]
     int *status;
     int t, pos, n_head, n_kv, context, k_row0, v_row0;
 };
 cudaError_t init_prefill_kernels();
+// gate_map: the prologue's bf16 sigmoid(gate) staging, laid out and boxed as
+// q_map
 cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
-                           const CUtensorMap &kv_map, cudaStream_t st);
+                           const CUtensorMap &kv_map, const CUtensorMap &gate_map,
+                           cudaStream_t st);
 constexpr int kPrefillQBoxRows = 128;
 
 cudaError_t init_full_attn_kernels();

@@ -2,9 +2,11 @@
 // tensor cores (tcgen05 + tensor memory), bf16 in, f32 accumulate, sm_100a.
 //
 // One CTA per (128-row query tile, query head).  Warp roles:
-//   warp 0      TMA producer: the query tile once (4 boxes of 128 rows x 64
-//               dims), then K and V tiles of 64 positions (4 + 4 boxes of
-//               64 x 64) into a 2-stage ring; 128-byte swizzle throughout
+//   warps 0,10  TMA producers: warp 0 the query tile once (4 boxes of 128
+//               rows x 64 dims) and then K tiles of 64 positions (4 boxes of
+//               64 x 64), warp 10 the V tiles, each into its own 2-slot ring
+//               (a K slot frees when its Q K^T is done, a V slot when its P V
+//               is); 128-byte swizzle throughout
 //   warp 1      tensor-memory allocator and the single MMA-issuing thread:
 //               S_j = Q K_j^T (M 128, N 64, K 256: 16 MMAs) into one of two
 //               S buffers, then O += P_{j-1} V_{j-1} (M 128, N 256, K 64: 4
@@ -15,8 +17,10 @@
 //               mask on the diagonal tiles, the row max exchanged through
 //               shared memory, online softmax in log2 units with a lazy
 //               rescale (O is corrected only when a row's max grows by more
-//               than 2^8), P written back as bf16 over the S buffer; at the
-//               end O / l times the sigmoid output gate, to global memory
+//               than 2^12), P written back as bf16 over the S buffer; at the
+//               end O / l times the sigmoid output gate (staged in bf16 by
+//               the prologue, loaded by TMA over the query tile once the last
+//               Q K^T is done), to global memory in whole 128-byte rows
 // Tensor memory (512 columns): O in columns 0-255, S buffers at 256 and 320;
 // P_j aliases the first 32 columns of its S buffer.  MMAs of one thread run
 // in issue order, so Q K^T of tile j+2 (same S buffer) cannot overtake the
@@ -35,7 +39,7 @@ namespace pf {
 constexpr int HD = 256;
 constexpr int BM = 128;          // query rows per CTA
 constexpr int BN = 64;           // key positions per tile
-constexpr int THREADS = 320;     // 10 warps
+constexpr int THREADS = 352;     // 11 warps
 constexpr int Q_BOX = BM * 128;  // 16 KiB: 128 rows x 64 dims
 constexpr int KV_BOX = BN * 128; // 8 KiB: 64 rows x 64 dims
 constexpr int Q_BYTES = 4 * Q_BOX;
@@ -45,7 +49,7 @@ constexpr int SMEM = Q_BYTES + 2 * STAGE + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t O_COL = 0, S_COL = 256;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr float RESCALE_LOG2 = 8.0f;
+constexpr float RESCALE_LOG2 = 12.0f;  // P up to 2^12: no range issue in bf16 or f32
 }  // namespace pf
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -65,11 +69,12 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 
 __global__ void __launch_bounds__(pf::THREADS, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap q_map,
-                   const __grid_constant__ CUtensorMap kv_map) {
+                   const __grid_constant__ CUtensorMap kv_map,
+                   const __grid_constant__ CUtensorMap gate_map) {
     using namespace pf;
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2],
-        p_full[2], o_ready, o_final;
+    __shared__ __align__(8) uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2],
+        s_full[2], p_full[2], o_ready, o_final, g_full;
     __shared__ uint32_t tmem_base_s;
     __shared__ int flag_s;
     __shared__ float red_m[2][2][BM], red_l[2][BM];  // the two halves of each row
@@ -94,12 +99,14 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         for (int s = 0; s < 2; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_empty[s], 1);
             mbar_init(&s_full[s], 1);
             mbar_init(&p_full[s], 8);
         }
         mbar_init(&o_ready, 1);
         mbar_init(&o_final, 1);
+        mbar_init(&g_full, 1);
         mbar_init(&mx_bar[0], 256);
         mbar_init(&mx_bar[1], 256);
         mbar_init(&l_bar, 256);
@@ -115,38 +122,52 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     tc::fence_after_sync();
     const uint32_t tmem = tmem_base_s;
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
+    if (warp == 0 || warp == 10) {
+        // ---------------- TMA producers ----------------
+        // warp 0: the query tile, then K tiles (a slot frees when its Q K^T is
+        // done); warp 10: V tiles (a slot frees when its P V is done).  Two
+        // warps, so K runs ahead of V by as much as the slots allow.
         if (lane == 0) {
-            prefetch_tensormap(&q_map);
-            prefetch_tensormap(&kv_map);
-            mbar_arrive_expect_tx(&q_full, Q_BYTES);
-            for (int b = 0; b < 4; ++b)
-                tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
-            const int krow = a.k_row0 + kh * a.context, vrow = a.v_row0 + kh * a.context;
+            const bool is_k = warp == 0;
+            if (is_k) {
+                prefetch_tensormap(&q_map);
+                prefetch_tensormap(&kv_map);
+                mbar_arrive_expect_tx(&q_full, Q_BYTES);
+                for (int b = 0; b < 4; ++b)
+                    tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
+            }
+            const int row0 = (is_k ? a.k_row0 : a.v_row0) + kh * a.context;
+            uint64_t *full = is_k ? k_full : v_full, *empty = is_k ? k_empty : v_empty;
             int issued = 0;
             for (int j = 0; j < n_kt; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, a.status)) {
+                if (j >= 2 && !mbar_wait(&empty[s], ((j >> 1) - 1) & 1, a.status)) {
                     flag_s = 1;
                     break;
                 }
-                unsigned char *st = smem + Q_BYTES + s * STAGE;
-                mbar_arrive_expect_tx(&k_full[s], KV_HALF);
+                unsigned char *st = smem + Q_BYTES + s * STAGE + (is_k ? 0 : KV_HALF);
+                mbar_arrive_expect_tx(&full[s], KV_HALF);
                 for (int b = 0; b < 4; ++b)
-                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, krow + j * BN, &k_full[s]);
-                mbar_arrive_expect_tx(&v_full[s], KV_HALF);
-                for (int b = 0; b < 4; ++b)
-                    tma_load_2d(st + KV_HALF + b * KV_BOX, &kv_map, b * 64, vrow + j * BN,
-                                &v_full[s]);
+                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + j * BN, &full[s]);
                 issued = j + 1;
             }
-            // everything started has landed before the CTA releases its memory
-            mbar_wait(&q_full, 0, a.status);
-            for (int j = max(0, issued - 2); j < issued; ++j) {
-                mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status);
-                mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.status);
+            if (is_k && issued == n_kt) {
+                // the last Q K^T done, the query tile is free: the output gate
+                // (sigmoid, bf16, staged by the prologue) takes its place
+                if (mbar_wait(&k_empty[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, a.status)) {
+                    prefetch_tensormap(&gate_map);
+                    mbar_arrive_expect_tx(&g_full, Q_BYTES);
+                    for (int b = 0; b < 4; ++b)
+                        tma_load_3d(smem + b * Q_BOX, &gate_map, b * 64, head, q0, &g_full);
+                    mbar_wait(&g_full, 0, a.status);
+                } else {
+                    flag_s = 1;
+                }
             }
+            // everything started has landed before the CTA releases its memory
+            if (is_k) mbar_wait(&q_full, 0, a.status);
+            for (int j = max(0, issued - 2); j < issued; ++j)
+                mbar_wait(&full[j & 1], (j >> 1) & 1, a.status);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -170,6 +191,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                         tc::mma_ss(d, da, db, id_qk, kk > 0);
                     }
                     tc::commit(&s_full[s]);
+                    tc::commit(&k_empty[s]);
                 }
                 if (j >= 1) {
                     const int jj = j - 1, s = jj & 1;
@@ -186,7 +208,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                         const uint64_t db = tc::smem_desc(vst + kk * 16 * 128, KV_BOX, 1024);
                         tc::mma_ts(tmem + O_COL, p + kk * 8, db, id_pv, jj > 0 || kk > 0);
                     }
-                    tc::commit(&kv_empty[s]);
+                    tc::commit(&v_empty[s]);
                     tc::commit(&o_ready);
                 }
             }
@@ -233,9 +255,29 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 mx0 = fmaxf(mx0, __uint_as_float(u[c]));
                 mx1 = fmaxf(mx1, __uint_as_float(u[c + 1]));
             }
-            // the row's max over both halves (scores scale by a positive constant)
+            // the row's max over both halves (scores scale by a positive
+            // constant): post this half's, then compute P optimistically with
+            // the running max while the partner's arrives; only a row whose
+            // max grows past the lazy threshold (rare) redoes the exponentials
             red_m[j & 1][h][r] = fmaxf(mx0, mx1);
             mbar_arrive(&mx_bar[j & 1]);
+            uint32_t pk[16];
+            float ps0 = 0.0f, ps1 = 0.0f;
+            auto exps = [&](float m) {
+                ps0 = 0.0f;
+                ps1 = 0.0f;
+                const float neg_m = -m;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * c]), scale, neg_m));
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * c + 1]), scale, neg_m));
+                    ps0 += p0;
+                    ps1 += p1;
+                    __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
+                    pk[c] = *reinterpret_cast<uint32_t *>(&hh);
+                }
+            };
+            exps(m_run);
             if (!__all_sync(0xffffffffu, mbar_wait(&mx_bar[j & 1], (j >> 1) & 1, a.status))) {
                 ok = false;
                 break;
@@ -268,18 +310,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 }
                 l_run *= corr;
                 m_run = m_new;
-            }
-            uint32_t pk[16];
-            float ps0 = 0.0f, ps1 = 0.0f;
-            const float neg_m = -m_run;
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * c]), scale, neg_m));
-                const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * c + 1]), scale, neg_m));
-                ps0 += p0;
-                ps1 += p1;
-                __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
-                pk[c] = *reinterpret_cast<uint32_t *>(&hh);
+                exps(m_run);
             }
             l_run += ps0 + ps1;
             tc::st16(sc + 16 * h, pk);
@@ -295,29 +326,40 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         mbar_arrive(&l_bar);
         if (!__all_sync(0xffffffffu, mbar_wait(&l_bar, 0, a.status))) ok = false;
         tc::fence_after_sync();
-        const int row = q0 + r;
         const float inv_l = 1.0f / (red_l[0][r] + red_l[1][r]);
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(&g_full, 0, a.status))) ok = false;
+        // O / l times the gate goes through shared memory (the K/V ring, idle
+        // now) so that the output stores are whole 128-byte rows per warp:
+        // per 32-column chunk, each thread parks its row's values, then each
+        // warp walks its 32 rows with lane = column
         const uint32_t oc = tmem + lane_off + O_COL + 128 * h;
+        float *stage = reinterpret_cast<float *>(smem + Q_BYTES) + h * (BM * 33);
+        const int n_rows = max(0, min(32, a.t - (q0 + quarter * 32)));  // valid rows of this warp
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
             tc::ld32(oc + c * 32, o);
             tc::wait_ld();
-            if (ok && row < a.t) {
-                const int d0 = 128 * h + c * 32;
-                const float *g = a.qg + ((size_t)row * a.n_head + head) * 2 * HD + HD + d0;
-                float *dst = a.out + ((size_t)row * a.n_head + head) * HD + d0;
+            // the row's 32 gate values: 64 bytes of a swizzled 128-byte box row
+            const int col0 = 128 * h + 32 * c;
+            const unsigned char *gbox = smem + (col0 >> 6) * Q_BOX;
+            uint4 gw[4];
 #pragma unroll
-                for (int e = 0; e < 32; e += 4) {
-                    const float4 gv = *reinterpret_cast<const float4 *>(g + e);
-                    float4 y;
-                    y.x = __uint_as_float(o[e]) * inv_l * sigmoidf_(gv.x);
-                    y.y = __uint_as_float(o[e + 1]) * inv_l * sigmoidf_(gv.y);
-                    y.z = __uint_as_float(o[e + 2]) * inv_l * sigmoidf_(gv.z);
-                    y.w = __uint_as_float(o[e + 3]) * inv_l * sigmoidf_(gv.w);
-                    *reinterpret_cast<float4 *>(dst + e) = y;
-                }
-            }
+            for (int k = 0; k < 4; ++k)
+                gw[k] = *reinterpret_cast<const uint4 *>(gbox + swz128(r, ((col0 & 63) >> 3) + k));
+            const __nv_bfloat16 *gb = reinterpret_cast<const __nv_bfloat16 *>(gw);
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+                stage[r * 33 + e] = __uint_as_float(o[e]) * inv_l * __bfloat162float(gb[e]);
+            __syncwarp();
+            const int col = col0 + lane;
+            const size_t row0 = (size_t)(q0 + quarter * 32) * a.n_head + head;
+#pragma unroll 8
+            for (int rr = 0; rr < 32; ++rr)
+                if (rr < n_rows && ok)
+                    __stcs(a.out + (row0 + (size_t)rr * a.n_head) * HD + col,
+                           stage[(quarter * 32 + rr) * 33 + lane]);
+            __syncwarp();
         }
     }
 
@@ -336,9 +378,10 @@ cudaError_t init_prefill_kernels() {
 }
 
 cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
-                           const CUtensorMap &kv_map, cudaStream_t st) {
+                           const CUtensorMap &kv_map, const CUtensorMap &gate_map,
+                           cudaStream_t st) {
     const int n_qt = (a.t + pf::BM - 1) / pf::BM;
-    prefill_kernel<<<n_qt * a.n_head, pf::THREADS, pf::SMEM, st>>>(a, q_map, kv_map);
+    prefill_kernel<<<n_qt * a.n_head, pf::THREADS, pf::SMEM, st>>>(a, q_map, kv_map, gate_map);
     return cudaGetLastError();
 }
 

@@ -36,6 +36,7 @@ struct rl_ctx {
     // scratch
     float *q_f32 = nullptr;
     __nv_bfloat16 *q_bf16 = nullptr;
+    __nv_bfloat16 *gate_bf16 = nullptr;  // prefill: sigmoid(gate) staging
     float *part_o = nullptr, *part_ml = nullptr;
     int64_t part_rows = 0;    // (row, cluster) pairs the partial buffers hold
     int *counters = nullptr;  // [max_batch][n_kv][8] decode arrival counters
@@ -44,6 +45,7 @@ struct rl_ctx {
     CUtensorMap kv_map{};
     // bf16 caches: TMA map of the staged bf16 queries [max_batch][n_head][hd]
     CUtensorMap q_map{};
+    CUtensorMap gate_map{};
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
     int *status = nullptr;    // device status word (rl::DEV_*)
@@ -172,7 +174,7 @@ void free_all(rl_ctx *x) {
     for (cudaEvent_t e : x->ev_pool) cudaEventDestroy(e);
     x->ev_pool.clear();
     void *ps[] = {x->kv, x->conv, x->ssm, x->q_norm, x->k_norm, x->conv1d, x->ssm_a,
-                  x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->part_o, x->part_ml,
+                  x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->gate_bf16, x->part_o, x->part_ml,
                   x->counters, x->rope_cs, x->rope_sn, x->stage, x->status};
     for (void *p : ps)
         if (p) cudaFree(p);
@@ -305,6 +307,7 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         x->part_rows = std::max<int64_t>(mb, 4 * (int64_t)x->num_sms);
         if ((code = alloc(x, &x->q_f32, mb * nh * hd)) ||
             (code = alloc(x, &x->q_bf16, mb * nh * hd)) ||
+            (code = alloc(x, &x->gate_bf16, c.kv_dtype == RL_KV_BF16 ? mb * nh * hd : 1)) ||
             (code = alloc(x, &x->part_o, (size_t)x->part_rows * nh * hd)) ||
             (code = alloc(x, &x->part_ml, (size_t)x->part_rows * nh * 8 * 2)) ||
             (code = alloc(x, &x->counters, (size_t)mb * c.n_head_kv * 8)))
@@ -327,6 +330,10 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
                                    (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
                                    64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
                 return bail(fail(x, RL_ECUDA, "encoding the query tensor map failed"));
+            if (rl::encode_bf16_3d(&x->gate_map, x->gate_bf16, c.head_dim, c.n_head, mb,
+                                   (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
+                                   64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
+                return bail(fail(x, RL_ECUDA, "encoding the gate tensor map failed"));
         }
     }
     // staging for the host entry points: the larger of the two paths' in+out
@@ -470,6 +477,7 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         a.rope_sn = ctx->rope_sn;
         a.q_f32 = prefill ? nullptr : ctx->q_f32;
         a.q_bf16 = prefill ? ctx->q_bf16 : nullptr;
+        a.gate_bf16 = prefill ? ctx->gate_bf16 : nullptr;
         a.t = t;
         a.pos = pos;
         a.n_head = c.n_head;
@@ -486,7 +494,6 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         }
         if (prefill) {
             rl::PrefillArgs pa{};
-            pa.qg = qg;
             pa.out = out;
             pa.status = ctx->status;
             pa.t = t;
@@ -498,7 +505,8 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
             pa.v_row0 = pa.k_row0 + c.n_head_kv * c.context;
             {
                 ProfScope ps(ctx, RL_PROF_PREFILL);
-                CK(ctx, rl::launch_prefill(pa, ctx->q_map, ctx->kv_map, ctx->stream));
+                CK(ctx, rl::launch_prefill(pa, ctx->q_map, ctx->kv_map, ctx->gate_map,
+                                           ctx->stream));
             }
             ctx->early_ok = false;
             ctx->prev_dn = 0;
