@@ -20,6 +20,24 @@ namespace rl {
 // RMSNorm's sum of squares is an f64 warp sum (forward.rs:1697-1711) and the
 // RoPE angles come from the per-context table, whose angles are advanced by
 // repeated f32 multiplication as forward.rs:1855-1861 does.
+// Eight consecutive cache elements in one or two 16-byte stores.
+__device__ __forceinline__ void store8(float *dst, const float *x) {
+    *reinterpret_cast<float4 *>(dst) = make_float4(x[0], x[1], x[2], x[3]);
+    *reinterpret_cast<float4 *>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
+}
+__device__ __forceinline__ uint32_t bf2_bits(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16 *dst, const float *x) {
+    uint4 u;
+    u.x = bf2_bits(x[0], x[1]);
+    u.y = bf2_bits(x[2], x[3]);
+    u.z = bf2_bits(x[4], x[5]);
+    u.w = bf2_bits(x[6], x[7]);
+    *reinterpret_cast<uint4 *>(dst) = u;
+}
+
 template <typename KV>
 __global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -35,11 +53,19 @@ __global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
     const int half = a.n_rot / 2;
     const float *cs_row = a.rope_cs ? a.rope_cs + (size_t)p * half : nullptr;
     const float *sn_row = a.rope_sn ? a.rope_sn + (size_t)p * half : nullptr;
-    float x[8], wv[8], c[8], sn[8];
-    *reinterpret_cast<float4 *>(x) = *reinterpret_cast<const float4 *>(src + lane * 8);
-    *reinterpret_cast<float4 *>(x + 4) = *reinterpret_cast<const float4 *>(src + lane * 8 + 4);
-    *reinterpret_cast<float4 *>(wv) = *reinterpret_cast<const float4 *>(w + lane * 8);
-    *reinterpret_cast<float4 *>(wv + 4) = *reinterpret_cast<const float4 *>(w + lane * 8 + 4);
+    float x[8], wv[8], c[8], sn[8], gt[8];
+    float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+    if (is_q && a.gate_bf16) {
+        g0 = *reinterpret_cast<const float4 *>(src + HD + lane * 8);
+        g1 = *reinterpret_cast<const float4 *>(src + HD + lane * 8 + 4);
+    }
+    const float4 x0 = *reinterpret_cast<const float4 *>(src + lane * 8);
+    const float4 x1 = *reinterpret_cast<const float4 *>(src + lane * 8 + 4);
+    const float4 w0 = *reinterpret_cast<const float4 *>(w + lane * 8);
+    const float4 w1 = *reinterpret_cast<const float4 *>(w + lane * 8 + 4);
+    x[0] = x0.x, x[1] = x0.y, x[2] = x0.z, x[3] = x0.w, x[4] = x1.x, x[5] = x1.y, x[6] = x1.z, x[7] = x1.w;
+    wv[0] = w0.x, wv[1] = w0.y, wv[2] = w0.z, wv[3] = w0.w, wv[4] = w1.x, wv[5] = w1.y, wv[6] = w1.z, wv[7] = w1.w;
+    gt[0] = g0.x, gt[1] = g0.y, gt[2] = g0.z, gt[3] = g0.w, gt[4] = g1.x, gt[5] = g1.y, gt[6] = g1.z, gt[7] = g1.w;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
         const int d = lane * 8 + e;
@@ -85,39 +111,24 @@ __global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
     }
     if (is_q) {
         const size_t o = ((size_t)i * a.n_head + hh) * HD + lane * 8;
-        if (a.q_f32) {
-            *reinterpret_cast<float4 *>(a.q_f32 + o) = make_float4(r[0], r[1], r[2], r[3]);
-            *reinterpret_cast<float4 *>(a.q_f32 + o + 4) = make_float4(r[4], r[5], r[6], r[7]);
-        }
-        if (a.q_bf16) {
-            __nv_bfloat162 b[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) b[e] = __floats2bfloat162_rn(r[2 * e], r[2 * e + 1]);
-            *reinterpret_cast<uint4 *>(a.q_bf16 + o) = *reinterpret_cast<uint4 *>(b);
-        }
+        if (a.q_f32) store8(a.q_f32 + o, r);
+        if (a.q_bf16) store8(a.q_bf16 + o, r);
         if (a.gate_bf16) {
             // the output gate, sigmoid(g) (forward.rs:1327-1340), staged in
             // bf16 for the prefill kernel's epilogue
-            float g[8];
-            *reinterpret_cast<float4 *>(g) = *reinterpret_cast<const float4 *>(src + HD + lane * 8);
-            *reinterpret_cast<float4 *>(g + 4) =
-                *reinterpret_cast<const float4 *>(src + HD + lane * 8 + 4);
-            __nv_bfloat162 b[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                b[e] = __floats2bfloat162_rn(sigmoidf_(g[2 * e]), sigmoidf_(g[2 * e + 1]));
-            *reinterpret_cast<uint4 *>(a.gate_bf16 + o) = *reinterpret_cast<uint4 *>(b);
+            for (int e = 0; e < 8; ++e) gt[e] = sigmoidf_(gt[e]);
+            store8(a.gate_bf16 + o, gt);
         }
     } else {
         const int kh = hh - a.n_head;
         const size_t to = ((size_t)kh * a.context + p) * HD + lane * 8;
-        KV *kc = static_cast<KV *>(a.k_cache), *vc = static_cast<KV *>(a.v_cache);
         const float *vsrc = a.v + ((size_t)i * a.n_kv + kh) * HD + lane * 8;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            kc[to + e] = from_f32<KV>(r[e]);
-            vc[to + e] = from_f32<KV>(vsrc[e]);
-        }
+        const float4 v0 = *reinterpret_cast<const float4 *>(vsrc);
+        const float4 v1 = *reinterpret_cast<const float4 *>(vsrc + 4);
+        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        store8(static_cast<KV *>(a.k_cache) + to, r);
+        store8(static_cast<KV *>(a.v_cache) + to, vv);
     }
 }
 
