@@ -129,6 +129,26 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
 int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qkv,
                         const float *z, const float *alpha, const float *beta, float *out);
 
+/*
+ * A sequence split across GPUs (long-context decode).  Each GPU's context
+ * holds positions lo .. lo + context - 1 of a sequence of seq_context
+ * positions (rl_set_shard; bf16 caches).  For one decode row at sequence
+ * position pos, rl_full_attn_partial walks this GPU's positions <= pos
+ * (appending the new key and value only on the GPU whose shard holds pos)
+ * and writes the shard's partial [n_head][head_dim + 2]: the unnormalised
+ * output, the running max (log2 units) and the sum of weights.  Once the
+ * callers have gathered every GPU's partial into parts [n_parts][n_head]
+ * [head_dim + 2] (an all-gather over NCCL), rl_merge_partials merges them
+ * with the log-sum-exp rule and applies the sigmoid output gate, giving the
+ * `heads` row rl_full_attn would have given (forward.rs:1259-1340).  All
+ * pointers are device pointers.  A sharded context refuses rl_full_attn.
+ */
+int rl_set_shard(rl_ctx *ctx, int lo, int seq_context);
+int rl_full_attn_partial(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
+                         const float *v, float *partial);
+int rl_merge_partials(rl_ctx *ctx, int n_parts, const float *parts, const float *qg,
+                      float *out);
+
 /* Commits `rows` >= 1 rows of the batch that just ran: pos += rows,
  * live = (live + rows) % slots (Runner::accept, forward.rs:675-688). */
 int rl_accept(rl_ctx *ctx, int rows);

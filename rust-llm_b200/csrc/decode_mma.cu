@@ -180,8 +180,10 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int pos_row = a.pos + row;
-    const int n_kv = pos_row + 1;
+    const int pos_row = a.pos + row;        // sequence position of this row
+    // this cache holds sequence positions shard_lo .. shard_lo + context - 1
+    const int loc_row = pos_row - a.shard_lo;  // the row's cache index (may lie outside)
+    const int n_kv = max(0, min(loc_row + 1, a.context));  // cached positions the row sees
     const int n_all = (n_kv + P - 1) / P;   // tiles of this row
     const int n_split = a.n_splits;          // CTAs sharing them
     const int head0 = row * a.n_head + kh * GROUP;
@@ -189,8 +191,8 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
     __nv_bfloat16 *const v_cache = static_cast<__nv_bfloat16 *>(a.v_cache_v);
     // every CTA of a KV head builds the appended row (any of them may draw
     // the tile holding it); split 0 writes it to the cache
-    const bool builds_new = FUSED;
-    const bool writes_new = FUSED && split == 0;
+    const bool builds_new = FUSED && loc_row >= 0 && loc_row < a.context;
+    const bool writes_new = builds_new && split == 0;
     const float *cs_row = a.rope_cs + (size_t)pos_row * (a.n_rot / 2);
     const float *sn_row = a.rope_sn + (size_t)pos_row * (a.n_rot / 2);
     const float *kv_in = (warp == 0 ? a.k_in : a.v_in) + (size_t)row * a.n_kv * HD + (size_t)kh * HD;
@@ -313,7 +315,7 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
                     for (int e = 0; e < 8; ++e) y[e] = hk.x[e];
                 }
                 __nv_bfloat16 *cache = (warp == 0 ? k_cache : v_cache) +
-                                       ((size_t)kh * a.context + pos_row) * HD + lane * 8;
+                                       ((size_t)kh * a.context + loc_row) * HD + lane * 8;
                 __nv_bfloat16 *keep = (warp == 0 ? newk_s : newv_s) + lane * 8;
                 uint4 packed;
                 packed.x = pack_bf16(y[0], y[1]);
@@ -371,10 +373,10 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
             const uint32_t kst = smem0 + s * STAGE_BYTES;
             const uint32_t vst = kst + HALF_BYTES;
             bool patched = false;
-            if (FUSED && pos_row >= base + wrow0 && pos_row < base + wrow0 + 16) {
+            if (builds_new && loc_row >= base + wrow0 && loc_row < base + wrow0 + 16) {
                 // the appended row is in this warp's block: the copy may have
                 // read it before it was written, so put the fresh one in place
-                const int r = pos_row - base;
+                const int r = loc_row - base;
                 const int b = lane >> 3, c = lane & 7;
                 unsigned char *st = smem + (size_t)s * STAGE_BYTES;
                 *reinterpret_cast<uint4 *>(st + b * BOX_BYTES + swz128(r, c)) =
@@ -604,8 +606,52 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
         float o = 0.0f;
 #pragma unroll
         for (int y = 0; y < kCombineLanes; ++y) o += red[y][tx];
-        a.out[(size_t)hh * dm::HD + d] = (o / L_s) * sigmoidf_(gate);
+        if (a.part_out) {
+            // one shard of a sequence split across GPUs: this GPU's partial
+            // (unnormalised output, max in log2 units, sum) for the merge
+            float *po_out = a.part_out + (size_t)hh * (dm::HD + 2);
+            po_out[d] = o;
+            if (blockIdx.y == 0 && tx == 0) {
+                float M = -INFINITY;
+                for (int s = 0; s < S; ++s) M = fmaxf(M, m_s[s]);
+                po_out[dm::HD] = M;
+                po_out[dm::HD + 1] = L_s;
+            }
+        } else {
+            a.out[(size_t)hh * dm::HD + d] = (o / L_s) * sigmoidf_(gate);
+        }
     }
+}
+
+// Merges the partials of a sequence split across GPUs, gathered as
+// parts [n_parts][rows * n_head][hd + 2] (unnormalised output, max in log2
+// units, sum), with the same log-sum-exp merge, then applies the sigmoid
+// output gate (forward.rs:1327-1340).  One CTA per (row, head), one thread
+// per dim.
+__global__ void __launch_bounds__(256) merge_parts_kernel(const float *parts, int n_parts,
+                                                          int rows_heads, const float *qg,
+                                                          float *out) {
+    const int hh = blockIdx.x, d = threadIdx.x;
+    const size_t stride = (size_t)rows_heads * (dm::HD + 2);
+    const float *p0 = parts + (size_t)hh * (dm::HD + 2);
+    float M = -INFINITY;
+    for (int g = 0; g < n_parts; ++g) M = fmaxf(M, p0[g * stride + dm::HD]);
+    float L = 0.0f, o = 0.0f;
+    for (int g = 0; g < n_parts; ++g) {
+        const float *pg = p0 + g * stride;
+        const float m = pg[dm::HD];
+        const float sc = m == -INFINITY ? 0.0f : exp2f(m - M);
+        L = fmaf(pg[dm::HD + 1], sc, L);
+        o = fmaf(pg[d], sc, o);
+    }
+    const float gate = qg[(size_t)hh * 2 * dm::HD + dm::HD + d];
+    out[(size_t)hh * dm::HD + d] = (o / L) * sigmoidf_(gate);
+}
+
+cudaError_t launch_merge_parts(const float *parts, int n_parts, int rows_heads, const float *qg,
+                               float *out, cudaStream_t st) {
+    merge_parts_kernel<<<rows_heads, dm::HD, 0, st>>>(parts, n_parts, rows_heads, qg, out);
+    return cudaGetLastError();
 }
 
 template <bool FUSED>

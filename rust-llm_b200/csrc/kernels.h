@@ -47,6 +47,12 @@ struct DecodeArgs {
     bool early_kv;
     // bf16 walk: tiles streamed before the consumers hold their inputs
     int early_tiles;
+    // the cache holds sequence positions shard_lo .. shard_lo + context - 1
+    // (0 unless the sequence is split across GPUs)
+    int shard_lo;
+    // non-null: the merge writes this shard's partial [t*n_head][hd + 2]
+    // (unnormalised output, max in log2 units, sum) instead of the output
+    float *part_out;
 };
 cudaError_t init_decode_kernels();
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);
@@ -61,6 +67,9 @@ int decode_max_active_clusters(bool kv_bf16, bool fused, int csize);
 cudaError_t init_decode_mma_kernels();
 cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st);
 cudaError_t launch_decode_combine(const DecodeArgs &a, cudaStream_t st);
+// parts [n_parts][rows_heads][hd + 2] -> out [rows_heads][hd], gated
+cudaError_t launch_merge_parts(const float *parts, int n_parts, int rows_heads, const float *qg,
+                               float *out, cudaStream_t st);
 constexpr int kDecodeBoxRows = 64, kDecodeBoxCols = 64;
 int decode_mma_max_active_ctas(bool fused);  // resident walk CTAs per SM
 int decode_mma_positions_per_tile();

@@ -64,6 +64,9 @@ struct rl_ctx {
     // its grid-dependency wait), 0 = anything else
     int prev_dn = 0, prev_layer = -1;
     float theta_scale = 1.0f;
+    // the cache holds sequence positions shard_lo .. shard_lo + context - 1
+    // of a sequence of seq_context positions (rl_set_shard)
+    int shard_lo = 0, seq_context = 0;
     std::string err;
     // per-kernel timing (rl_profile_*)
     bool prof_on = false;
@@ -245,6 +248,38 @@ int check_status(rl_ctx *x) {
     return RL_OK;
 }
 
+
+// The bf16 split-KV walk and its merge for rows whose furthest row sees
+// n_kv_max cached positions.  One wave of walk CTAs: as many splits per
+// (KV head, row) as keep every resident slot busy, each a whole number of
+// 64-position tiles.
+int bf16_walk(rl_ctx *ctx, rl::DecodeArgs &d, int64_t n_kv_max, int64_t groups, int t,
+              bool fused) {
+    const int P = rl::decode_mma_positions_per_tile();
+    const int64_t tiles = (n_kv_max + P - 1) / P;
+    const int64_t resident = (int64_t)std::max(1, ctx->mma_per_sm[fused ? 1 : 0]) * ctx->num_sms;
+    int64_t splits = std::max<int64_t>(1, resident / groups);
+    if (ctx->opt_splits > 0) splits = std::min<int64_t>(splits, ctx->opt_splits);
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, tiles));
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, ctx->part_rows / t));
+    splits = std::min<int64_t>(splits, 512);
+    d.chunk = (int)((tiles + splits - 1) / splits * P);
+    d.n_splits = (int)splits;
+    d.csize = 1;
+    d.early_kv = fused && ctx->early_ok;
+    d.early_tiles = (int)ctx->opt_early_tiles;
+    {
+        ProfScope ps(ctx, RL_PROF_DECODE);
+        CK(ctx, rl::launch_decode_mma(d, ctx->kv_map, ctx->stream));
+    }
+    {
+        ProfScope ps(ctx, RL_PROF_MERGE);
+        CK(ctx, rl::launch_decode_combine(d, ctx->stream));
+    }
+    ctx->early_ok = fused;
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
 }  // namespace
 
 void rl::set_thread_error(const char *msg) { tl_err = msg; }
@@ -269,6 +304,7 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     x->cfg.max_batch =
         std::max(1, std::min(std::max(x->cfg.max_batch, x->cfg.slots), x->cfg.context));
     x->device = device;
+    x->seq_context = x->cfg.context;
     const rl_config &c = x->cfg;
     auto bail = [&](int code) {
         tl_err = x->err;
@@ -456,6 +492,9 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     if (!qg || !k || !v || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
     if (((uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15)
         return fail(ctx, RL_EINVAL, "qg, k, v and out must be 16-byte aligned");
+    if (ctx->shard_lo != 0 || ctx->seq_context != c.context)
+        return fail(ctx, RL_EINVAL,
+                    "this context holds one shard of a split sequence: use rl_full_attn_partial");
     CK(ctx, cudaSetDevice(ctx->device));
     const bool bf16 = c.kv_dtype == RL_KV_BF16;
     const size_t half = (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
@@ -543,37 +582,10 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     d.fused = fused;
     d.k_row0 = layer * 2 * c.n_head_kv * c.context;
     d.v_row0 = d.k_row0 + c.n_head_kv * c.context;
+    d.shard_lo = 0;
+    d.part_out = nullptr;
 
-    if (bf16) {
-        // One wave of walk CTAs: as many splits per (KV head, row) as keep
-        // every resident slot busy, each a whole number of 64-position tiles.
-        const int P = rl::decode_mma_positions_per_tile();
-        const int64_t tiles = (n_kv_max + P - 1) / P;
-        const int64_t resident = (int64_t)std::max(1, ctx->mma_per_sm[fused ? 1 : 0]) * ctx->num_sms;
-        int64_t splits = std::max<int64_t>(1, resident / groups);
-        if (ctx->opt_splits > 0) splits = std::min<int64_t>(splits, ctx->opt_splits);
-        splits = std::min<int64_t>(splits, tiles);
-        splits = std::min<int64_t>(splits, std::max<int64_t>(1, ctx->part_rows / t));
-        splits = std::min<int64_t>(splits, 512);
-        int64_t chunk = (tiles + splits - 1) / splits * P;  // positions per split
-        splits = (n_kv_max + chunk - 1) / chunk;
-        d.chunk = (int)chunk;
-        d.n_splits = (int)splits;
-        d.csize = 1;
-        d.early_kv = fused && ctx->early_ok;
-        d.early_tiles = (int)ctx->opt_early_tiles;
-        {
-            ProfScope ps(ctx, RL_PROF_DECODE);
-            CK(ctx, rl::launch_decode_mma(d, ctx->kv_map, ctx->stream));
-        }
-        {
-            ProfScope ps(ctx, RL_PROF_MERGE);
-            CK(ctx, rl::launch_decode_combine(d, ctx->stream));
-        }
-        ctx->early_ok = fused;
-        ctx->prev_dn = 0;
-        return RL_OK;
-    }
+    if (bf16) return bf16_walk(ctx, d, n_kv_max, groups, t, fused);
 
     // f32 caches: split-KV walk on the CUDA cores.  The (split, KV head, row)
     // CTAs of one launch must all be resident at once (one wave); the splits
@@ -613,6 +625,105 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         CK(ctx, rl::launch_decode(d, ctx->stream));
     }
     ctx->early_ok = false;
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
+
+int rl_set_shard(rl_ctx *ctx, int lo, int seq_context) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (c.kv_dtype != RL_KV_BF16 || c.n_full < 1)
+        return fail(ctx, RL_EUNSUPPORTED, "a split sequence needs a bf16 KV cache");
+    if (lo < 0 || seq_context < c.context || (int64_t)lo + c.context > seq_context)
+        return fail(ctx, RL_EINVAL, "shard %d..%d does not lie inside a sequence of %d", lo,
+                    lo + c.context, seq_context);
+    CK(ctx, cudaSetDevice(ctx->device));
+    if (seq_context != ctx->seq_context) {
+        // the queries' RoPE angles are those of sequence positions
+        const size_t half = std::max(1, c.n_rot / 2);
+        float *cs = nullptr, *sn = nullptr;
+        int code;
+        if ((code = alloc(ctx, &cs, (size_t)seq_context * half)) ||
+            (code = alloc(ctx, &sn, (size_t)seq_context * half))) {
+            if (cs) cudaFree(cs);
+            return code;
+        }
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->rope_cs);
+        cudaFree(ctx->rope_sn);
+        ctx->rope_cs = cs;
+        ctx->rope_sn = sn;
+        CK(ctx, rl::launch_rope_table(cs, sn, seq_context, c.n_rot, ctx->theta_scale, ctx->stream));
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+    }
+    ctx->shard_lo = lo;
+    ctx->seq_context = seq_context;
+    ctx->early_ok = false;
+    return RL_OK;
+}
+
+int rl_full_attn_partial(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
+                         const float *v, float *partial) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_full)
+        return fail(ctx, RL_EINVAL, "full layer %d of %d", layer, c.n_full);
+    if (c.kv_dtype != RL_KV_BF16)
+        return fail(ctx, RL_EUNSUPPORTED, "a split sequence needs a bf16 KV cache");
+    if (pos < 0 || pos >= ctx->seq_context)
+        return fail(ctx, RL_ECONTEXT, "position %d is outside the sequence of %d", pos,
+                    ctx->seq_context);
+    if (!qg || !k || !v || !partial) return fail(ctx, RL_EINVAL, "NULL input or output");
+    if (((uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)partial) & 15)
+        return fail(ctx, RL_EINVAL, "qg, k, v and partial must be 16-byte aligned");
+    CK(ctx, cudaSetDevice(ctx->device));
+    void *k_cache = kv_layer(ctx, layer);
+    void *v_cache = (char *)k_cache + (size_t)c.n_head_kv * c.context * c.head_dim * kv_elem(c);
+    rl::DecodeArgs d{};
+    d.qg = qg;
+    d.k_in = k;
+    d.v_in = v;
+    d.q_f32 = ctx->q_f32;
+    d.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
+    d.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
+    d.rope_cs = ctx->rope_cs;
+    d.rope_sn = ctx->rope_sn;
+    d.k_cache_v = k_cache;
+    d.v_cache_v = v_cache;
+    d.part_o = ctx->part_o;
+    d.part_ml = ctx->part_ml;
+    d.counters = ctx->counters;
+    d.out = nullptr;
+    d.status = ctx->status;
+    d.pos = pos;
+    d.t = 1;
+    d.context = c.context;
+    d.n_head = c.n_head;
+    d.n_kv = c.n_head_kv;
+    d.n_rot = c.n_rot;
+    d.theta_scale = ctx->theta_scale;
+    d.eps = c.rms_eps;
+    d.kv_bf16 = true;
+    d.fused = true;
+    d.k_row0 = layer * 2 * c.n_head_kv * c.context;
+    d.v_row0 = d.k_row0 + c.n_head_kv * c.context;
+    d.shard_lo = ctx->shard_lo;
+    d.part_out = partial;
+    const int64_t local = std::max<int64_t>(
+        0, std::min<int64_t>((int64_t)pos + 1 - ctx->shard_lo, c.context));
+    return bf16_walk(ctx, d, local, c.n_head_kv, 1, true);
+}
+
+int rl_merge_partials(rl_ctx *ctx, int n_parts, const float *parts, const float *qg,
+                      float *out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (n_parts < 1 || !parts || !qg || !out)
+        return fail(ctx, RL_EINVAL, "n_parts >= 1 and non-NULL buffers");
+    CK(ctx, cudaSetDevice(ctx->device));
+    {
+        ProfScope ps(ctx, RL_PROF_MERGE);
+        CK(ctx, rl::launch_merge_parts(parts, n_parts, ctx->cfg.n_head, qg, out, ctx->stream));
+    }
     ctx->prev_dn = 0;
     return RL_OK;
 }

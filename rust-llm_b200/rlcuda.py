@@ -105,6 +105,9 @@ SIGNATURES = {
     "rl_profile_reset": ([_vp], _i),
     "rl_full_attn_noalloc": ([ctypes.POINTER(Config), _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp,
                               _vp, _vp], _i),
+    "rl_set_shard": ([_vp, _i, _i], _i),
+    "rl_full_attn_partial": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
+    "rl_merge_partials": ([_vp, _i, _vp, _vp, _vp], _i),
     "rl_version": ([], ctypes.c_char_p),
 }
 
@@ -246,6 +249,20 @@ class Context:
         """Device pointers (torch tensors or ints); enqueued, not waited for."""
         self._check(self._L.rl_full_attn(self._h, layer, pos, t, _ptr(qg), _ptr(k), _ptr(v),
                                          _ptr(out)))
+
+    # -- a sequence split across GPUs -----------------------------------
+    def set_shard(self, lo: int, seq_context: int):
+        self._check(self._L.rl_set_shard(self._h, lo, seq_context))
+
+    def full_attn_partial(self, layer, pos, qg, k, v, partial):
+        """Device tensors; partial [n_head][head_dim + 2] f32."""
+        self._check(self._L.rl_full_attn_partial(self._h, layer, pos, _ptr(qg), _ptr(k), _ptr(v),
+                                                 _ptr(partial)))
+
+    def merge_partials(self, parts, qg, out):
+        """parts [n_parts][n_head][head_dim + 2] f32 (device) -> out [n_head*head_dim]."""
+        self._check(self._L.rl_merge_partials(self._h, int(parts.shape[0]), _ptr(parts), _ptr(qg),
+                                              _ptr(out)))
 
     def linear_attn_host(self, layer, live, qkv, z, alpha, beta) -> np.ndarray:
         t = qkv.shape[0]
