@@ -50,6 +50,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def peaks_bf16():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return "measured", float(p["bf16_tflops"])
+    except Exception:
+        return "fallback", 1590.0
+
+
 def ncu_traffic():
     """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "decode_bf16_32k.txt")
@@ -253,6 +262,145 @@ def dn_step_bench(args, dev, stream, rlcuda, torch):
             "l2": "72 x 2 MiB of state per step, more than the 126 MB L2"}
 
 
+PF_T = 4096
+PF_LAYERS = 8
+PF_FLOP_PER_LAYER = 4 * 16 * 256 * PF_T * (PF_T + 1) // 2   # causal Q K^T + P V: 137,472,507,904
+
+
+def prefill_bench(args, dev, stream, rlcuda, torch):
+    """Config 2's full-attention layers: 8 layers of a 4096-token causal
+    prefill from an empty bf16 cache (norms + RoPE + append prologue, then the
+    tcgen05 prefill kernel); returns TFLOPS per layer with and without the
+    prologue, and the tensor-core kernel's share of the measured bf16 peak."""
+    cfg = rlcuda.qwen35_config(n_full=PF_LAYERS, n_linear=0, context=PF_T,
+                               kv_dtype=rlcuda.RL_KV_BF16, max_batch=PF_T)
+    ctx = rlcuda.Context(cfg, device=dev.index)
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    qg = torch.randn((PF_LAYERS, PF_T, 16 * 512), generator=gen, device=dev)
+    kk = torch.randn((PF_LAYERS, PF_T, 4 * 256), generator=gen, device=dev)
+    vv = torch.randn((PF_LAYERS, PF_T, 4 * 256), generator=gen, device=dev)
+    out = torch.empty((PF_LAYERS, PF_T, 16 * 256), device=dev)
+
+    def step():
+        for layer in range(PF_LAYERS):
+            ctx.full_attn(layer, 0, PF_T, qg[layer], kk[layer], vv[layer], out[layer])
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup // 4)):
+            step()
+    stream.synchronize()
+    ctx.sync()
+    steps = max(3, min(args.steps // 100, 20))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+    stream.synchronize()
+    ctx.sync()
+    layer_us = e0.elapsed_time(e1) * 1e3 / (steps * PF_LAYERS)
+    ctx.profile_reset()
+    ctx.profile(True)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    kms, kn = prof["prefill"]
+    pms, pn = prof["prologue"]
+    ctx.close()
+    kernel_us = kms * 1e3 / max(kn, 1)
+    _, peak = peaks_bf16()
+    return {"workload": "config 2 full-attention layers: 8 x 4096-token causal prefill, bf16 cache",
+            "flop_per_layer": PF_FLOP_PER_LAYER, "us_per_layer": layer_us,
+            "tflops_layer": PF_FLOP_PER_LAYER / (layer_us * 1e-6) / 1e12,
+            "kernel_us": kernel_us, "prologue_us": pms * 1e3 / max(pn, 1),
+            "tflops_kernel": PF_FLOP_PER_LAYER / (kernel_us * 1e-6) / 1e12,
+            "frac_kernel_of_measured_bf16": PF_FLOP_PER_LAYER / (kernel_us * 1e-6) / 1e12 / peak,
+            "peak_tflops": peak, "dtype": "bf16 x bf16 -> f32 (tcgen05 kind::f16)"}
+
+
+SPLIT_SEQ = 131072
+
+
+def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
+    """Config 4a: one sequence at 131072 positions, bf16 cache, 8 layers,
+    split along the sequence across the job's GPUs; per layer each GPU walks
+    its range, the partials (16,512 B per GPU) are all-gathered over NCCL and
+    merged with the output gate.  Returns µs per layer (max over ranks), the
+    gather alone, and each GPU's HBM rate over its share of the cache."""
+    import split_kv
+    lo, n = split_kv.shard_range(SPLIT_SEQ, world, rank)
+    cfg = rlcuda.qwen35_config(n_full=N_LAYERS, n_linear=0, context=n,
+                               kv_dtype=rlcuda.RL_KV_BF16, max_batch=1)
+    ctx = rlcuda.Context(cfg, device=dev.index)
+    ctx.set_stream(stream.cuda_stream)
+    shard = split_kv.GpuShard(ctx, lo, SPLIT_SEQ)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4 + rank)
+    for layer in range(N_LAYERS):
+        src = torch.randn((2, N_KV, n, HD), generator=gen, device=dev, dtype=torch.float32)
+        ctx.write_kv(layer, 0, src)
+        del src
+    torch.cuda.empty_cache()
+    gen.manual_seed(4)  # the step's inputs are the same on every rank
+    qg = torch.randn((N_LAYERS, N_HEAD * 2 * HD), generator=gen, device=dev)
+    kk = torch.randn((N_LAYERS, N_KV * HD), generator=gen, device=dev)
+    vv = torch.randn((N_LAYERS, N_KV * HD), generator=gen, device=dev)
+    out = torch.empty((N_LAYERS, N_HEAD * HD), device=dev)
+    dec = split_kv.SplitDecoder(shard, world, rank, N_HEAD, HD,
+                                make=lambda shape: torch.empty(shape, device=dev))
+    pos = SPLIT_SEQ - 1
+
+    def step():
+        for layer in range(N_LAYERS):
+            dec.step(layer, pos, qg[layer], kk[layer], vv[layer], out[layer])
+
+    def timed(fn, reps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+        stream.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    reps = max(10, min(args.steps // 10, 200))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step()
+    ms = timed(step, reps)
+
+    def gathers():
+        for _ in range(N_LAYERS):
+            if world > 1:
+                dist.all_gather_into_tensor(dec.gathered_flat, dec.partial)
+    g_ms = timed(gathers, reps)
+    ctx.sync()
+    ctx.close()
+    us = ms * 1e3 / (reps * N_LAYERS)
+    local_bytes = 2 * N_KV * n * HD * 2
+    return {"workload": "config 4a: 1 sequence x 131072 positions, 8 layers, bf16 cache split "
+                        f"across {world} GPU(s), NCCL all-gather of the partials",
+            "scaling": "strong", "us_per_layer": us,
+            "gather_us_per_layer": g_ms * 1e3 / (reps * N_LAYERS),
+            "kv_bytes_per_gpu_per_layer": local_bytes,
+            "hbm_gbs_per_gpu": local_bytes / (us * 1e-6) / 1e9,
+            "gather_bytes_per_gpu_per_layer": N_HEAD * (HD + 2) * 4}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -385,7 +533,10 @@ def run_ours(args):
     h2d = N_LAYERS * 4 * (N_HEAD * 2 * HD + 2 * N_KV * HD)
     d2h = N_LAYERS * 4 * N_HEAD * HD
 
+    split = (split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist)
+             if not args.no_split else None)
     dn = dn_step_bench(args, dev, stream, rlcuda, torch) if not args.no_dn else None
+    pf = prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -408,7 +559,9 @@ def run_ours(args):
                    "launch": "CUDA graph of the 8-layer step"},
         "hbm_gbs": hbm_gbs,
         "hbm_frac_of_8tbs": hbm_gbs / 8000.0,
-        "prefill_tflops": None,
+        "prefill_tflops": pf["tflops_layer"] if pf else None,
+        "prefill": pf,
+        "split_kv": split,
         "dn_step": dn,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -438,6 +591,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dn", action="store_true", help="skip the DeltaNet step section")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill section")
+    ap.add_argument("--no-split", action="store_true",
+                    help="skip the long-context split-sequence section")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="full-attention layers per step (8 in the model; fewer only to "
                          "keep a profiler capture small)")
