@@ -47,6 +47,7 @@
 // (crates/rust-llm/src/forward.rs:1783-1842) and its gate (:1327-1340).
 #include "common.cuh"
 #include "kernels.h"
+#include "mma.cuh"
 
 namespace rl {
 namespace dm {
@@ -69,32 +70,6 @@ static_assert((size_t)STAGES * STAGE_BYTES >=
                   (size_t)(CWARPS * GROUP * HD + CWARPS * GROUP * 2 + GROUP * HD) * 4,
               "the merge scratch reuses the stage ring");
 }  // namespace dm
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-// d += a (16x16, row) * b (16x8, col), bf16 in, f32 accumulate
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                          uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
-        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
-    return *reinterpret_cast<uint32_t *>(&v);
-}
-// The bf16 pair (hi, lo) of x: hi = bf16(x), lo = bf16(x - hi).
-__device__ __forceinline__ float bf16_hi(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // One lane's share (8 consecutive dims) of a 256-wide head before RMSNorm
 // and RoPE, with every global load issued before any is used.

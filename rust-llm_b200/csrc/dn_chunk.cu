@@ -1,0 +1,589 @@
+// Gated DeltaNet prefill in chunks of 64 tokens on the tensor cores, sm_100a.
+//
+// The reference runs the delta rule one token at a time (forward.rs:1906-1950):
+//   S <- g_t S;  d = beta_t (v_t - S^T k_t);  S += k_t d^T;  o_t = S^T q_t / sqrt(128)
+// With gamma_t the product of the decays since the chunk start and S_0 the
+// state before the chunk, that recurrence unrolls to (rows = tokens):
+//   (I + L) U = diag(beta) (V - diag(gamma) K S_0),  L[t][s] = beta_t gamma_t/gamma_s k_t.k_s (s < t)
+//   O   = diag(gamma) Q S_0 + (Q K^T o Mgamma) U,   Mgamma[t][s] = gamma_t/gamma_s (s <= t)
+//   S_C = gamma_C S_0 + K^T diag(gamma_C/gamma) U
+// so with T = (I + L)^-1, Ut = T diag(beta) V and W = T diag(beta gamma) K,
+// U = Ut - W S_0: every product is a small dense GEMM.  Four kernels:
+//   dn_prep_kernel        per token: causal conv + SiLU, q/k L2 norm, gates
+//                         (forward.rs:1530-1584, :2018-2059, :1720-1727)
+//   dn_chunk_local_kernel per (value head, chunk), all in parallel: K K^T and
+//                         Q K^T on mma.sync, T by forward substitution (f32),
+//                         Ut and W on mma.sync, P = Q K^T o Mgamma,
+//                         Q' = gamma Q, K' = gamma_C/gamma K
+//   dn_chunk_scan_kernel  per (value head, 32 state columns): the 64 chunks in
+//                         order, state in f32, U = Ut - W S, O = Q' S + P U,
+//                         S = gamma_C S + K'^T U
+// Every operand of every product is a bf16 pair x = hi + lo (a 16-bit
+// mantissa) and every product is the three mma.sync terms hi*hi + hi*lo +
+// lo*hi with f32 accumulation: the gated RMSNorm that follows normalises each
+// head, so a head whose readout nearly cancels needs its relative error
+// small, and single bf16 operands (8 bits) are not enough for that.
+//   dn_out_kernel         per token: gated RMSNorm times SiLU(z) (:1642-1652);
+//                         dn_hist_kernel leaves the last three raw inputs as the
+//                         conv history (the reference's history after the batch)
+// The state columns are independent of each other in the recurrence, so the
+// scan splits each head's 128 x 128 state over 4 CTAs.
+#include "common.cuh"
+#include "kernels.h"
+#include "mma.cuh"
+
+namespace rl {
+namespace dc {
+constexpr int S = 128;     // d_state
+constexpr int C = 64;      // chunk length
+constexpr int LDB = 136;   // padded bf16 row (272 B: ldmatrix rows in distinct bank groups)
+constexpr int LDP = 72;    // padded bf16 row of a 64-wide matrix (144 B)
+constexpr int LDF = 65;    // padded f32 row of a 64-wide matrix
+constexpr int JC = 32;     // state columns per scan CTA
+}  // namespace dc
+
+// ---------------------------------------------------------------------------
+// dn_prep_kernel: grid (t, 2*n_k + n_v), 128 threads, one channel each.
+__global__ void __launch_bounds__(128) dn_prep_kernel(const DnChunkArgs a) {
+    using namespace dc;
+    __shared__ double red[4];
+    const int i = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
+    const int key_dim = a.n_k * S, conv_dim = 2 * key_dim + a.n_v * S;
+    const int ch = g * S + c;
+    const float *w = a.conv1d + (size_t)ch * 4;
+    const float x = a.qkv[(size_t)i * conv_dim + ch];
+    float h[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        const int src = i - 3 + j;
+        h[j] = src >= 0 ? a.qkv[(size_t)src * conv_dim + ch] : a.conv_state[(size_t)ch * 3 + (src + 3)];
+    }
+    // forward.rs:2018-2031: x * w[3] first, then the history taps in order
+    float y = __fmul_rn(x, w[3]);
+#pragma unroll
+    for (int j = 0; j < 3; ++j) y = __fadd_rn(y, __fmul_rn(h[j], w[j]));
+    y = siluf_(y);
+    if (g < 2 * a.n_k) {
+        // L2 norm: rms_scale with eps/n, then 1/sqrt(n) (forward.rs:1720-1727)
+        double sq = warp_sum_d((double)__fmul_rn(y, y));
+        if ((c & 31) == 0) red[c >> 5] = sq;
+        __syncthreads();
+        const double sum = ((-0.0 + red[0]) + red[1]) + red[2] + red[3];
+        const float sc = rms_scale_from_sum(sum, S, a.eps / (float)S);
+        y = __fmul_rn(__fmul_rn(y, sc), 1.0f / sqrtf((float)S));
+        // q and k as bf16 pairs (hi + lo): their dot products feed P and L, and a
+        // nearly orthogonal pair's product needs more than bf16's 8 bits
+        const size_t o = g < a.n_k ? ((size_t)i * a.n_k + g) * S
+                                   : ((size_t)i * a.n_k + (g - a.n_k)) * S;
+        __nv_bfloat16 *hi = g < a.n_k ? a.qn : a.kn, *lo = g < a.n_k ? a.qn_lo : a.kn_lo;
+        hi[o + c] = __float2bfloat16_rn(y);
+        lo[o + c] = __float2bfloat16_rn(y - bf16_hi(y));
+    } else {
+        const int vh = g - 2 * a.n_k;
+        a.vn[((size_t)i * a.n_v + vh) * S + c] = __float2bfloat16_rn(y);
+        a.vn_lo[((size_t)i * a.n_v + vh) * S + c] = __float2bfloat16_rn(y - bf16_hi(y));
+        if (c == 0) {
+            // gates (forward.rs:1530-1546): log decay and beta
+            a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(
+                softplusf_(__fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh])), a.ssm_a[vh]);
+            a.bt[(size_t)i * a.n_v + vh] = sigmoidf_(a.beta[(size_t)i * a.n_v + vh]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Fragment loaders for m16n8k16 (A row-major [m][k], B given as rows [n][k]).
+__device__ __forceinline__ void ld_a(const __nv_bfloat16 *base, int ld, int m0, int k0, int lane,
+                                     uint32_t (&a)[4]) {
+    const int r = m0 + (lane & 7) + ((lane >> 3) & 1) * 8, c = k0 + (lane >> 4) * 8;
+    ldsm_x4(smem_u32(base + r * ld + c), a);
+}
+// B fragments of two n-tiles (n0, n0 + 8) from a matrix stored as rows n with k contiguous
+__device__ __forceinline__ void ld_b2(const __nv_bfloat16 *base, int ld, int n0, int k0, int lane,
+                                      uint32_t (&b)[4]) {
+    const int r = n0 + (lane & 7) + (lane >> 4) * 8, c = k0 + ((lane >> 3) & 1) * 8;
+    ldsm_x4(smem_u32(base + r * ld + c), b);
+}
+// B fragments of two n-tiles from a matrix stored as rows k with n contiguous
+__device__ __forceinline__ void ld_b2_t(const __nv_bfloat16 *base, int ld, int n0, int k0,
+                                        int lane, uint32_t (&b)[4]) {
+    const int r = k0 + (lane & 7) + ((lane >> 3) & 1) * 8, c = n0 + (lane >> 4) * 8;
+    ldsm_x4_t(smem_u32(base + r * ld + c), b);
+}
+// A fragment (m rows m0.., k cols k0..) of A = X^T, X stored as rows k with m contiguous
+__device__ __forceinline__ void ld_a_t(const __nv_bfloat16 *base, int ld, int m0, int k0,
+                                       int lane, uint32_t (&a)[4]) {
+    const int r = k0 + (lane & 7) + (lane >> 4) * 8, c = m0 + ((lane >> 3) & 1) * 8;
+    ldsm_x4_t(smem_u32(base + r * ld + c), a);
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// dn_chunk_local_kernel: grid (n_chunks, n_v), 128 threads (4 warps, 16 rows each).
+struct LocalSmem {
+    __nv_bfloat16 k[dc::C][dc::LDB], q[dc::C][dc::LDB], v[dc::C][dc::LDB];
+    __nv_bfloat16 kl[dc::C][dc::LDB], ql[dc::C][dc::LDB], vl[dc::C][dc::LDB];  // low halves
+    float kk[dc::C][dc::LDF], qk[dc::C][dc::LDF], t[dc::C][dc::LDF];
+    __nv_bfloat16 ta_hi[dc::C][dc::LDP], ta_lo[dc::C][dc::LDP];  // T diag(beta)
+    __nv_bfloat16 tb_hi[dc::C][dc::LDP], tb_lo[dc::C][dc::LDP];  // T diag(beta gamma)
+    float cum[dc::C], beta[dc::C];
+};
+
+__global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a) {
+    using namespace dc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    LocalSmem &sm = *reinterpret_cast<LocalSmem *>(smem_raw);
+    const int ck = blockIdx.x, vh = blockIdx.y, kh = vh % a.n_k;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t0 = ck * C, rows = min(C, a.t - t0);
+
+    // ---- operands of the chunk (rows past the batch are zero)
+    for (int e = tid; e < C * (S / 8); e += 128) {
+        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+        uint4 kz = make_uint4(0, 0, 0, 0), qz = kz, vz = kz, klz = kz, qlz = kz, vlz = kz;
+        if (r < rows) {
+            const size_t ko = ((size_t)(t0 + r) * a.n_k + kh) * S + c8;
+            kz = *reinterpret_cast<const uint4 *>(a.kn + ko);
+            qz = *reinterpret_cast<const uint4 *>(a.qn + ko);
+            klz = *reinterpret_cast<const uint4 *>(a.kn_lo + ko);
+            qlz = *reinterpret_cast<const uint4 *>(a.qn_lo + ko);
+            const size_t vo = ((size_t)(t0 + r) * a.n_v + vh) * S + c8;
+            vz = *reinterpret_cast<const uint4 *>(a.vn + vo);
+            vlz = *reinterpret_cast<const uint4 *>(a.vn_lo + vo);
+        }
+        *reinterpret_cast<uint4 *>(&sm.vl[r][c8]) = vlz;
+        *reinterpret_cast<uint4 *>(&sm.k[r][c8]) = kz;
+        *reinterpret_cast<uint4 *>(&sm.q[r][c8]) = qz;
+        *reinterpret_cast<uint4 *>(&sm.kl[r][c8]) = klz;
+        *reinterpret_cast<uint4 *>(&sm.ql[r][c8]) = qlz;
+        *reinterpret_cast<uint4 *>(&sm.v[r][c8]) = vz;
+    }
+    if (tid < C) {
+        sm.cum[tid] = tid < rows ? a.lg[(size_t)(t0 + tid) * a.n_v + vh] : 0.0f;
+        sm.beta[tid] = tid < rows ? a.bt[(size_t)(t0 + tid) * a.n_v + vh] : 0.0f;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // cumulative log decay: gamma_t = exp(cum[t])
+        float s = 0.0f;
+        for (int r = 0; r < C; ++r) sm.cum[r] = s = s + sm.cum[r];
+    }
+    // ---- K K^T and Q K^T (warp: 16 rows, all 64 columns), each as
+    // hi*hi + hi*lo + lo*hi of the bf16 pairs
+    {
+        float dk[8][4], dq[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dk[n][e] = dq[n][e] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < S / 16; ++ks) {
+            uint32_t ak[4], aq[4], akl[4], aql[4];
+            ld_a(&sm.k[0][0], LDB, warp * 16, ks * 16, lane, ak);
+            ld_a(&sm.q[0][0], LDB, warp * 16, ks * 16, lane, aq);
+            ld_a(&sm.kl[0][0], LDB, warp * 16, ks * 16, lane, akl);
+            ld_a(&sm.ql[0][0], LDB, warp * 16, ks * 16, lane, aql);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t b[4], bl[4];
+                ld_b2(&sm.k[0][0], LDB, np * 16, ks * 16, lane, b);
+                ld_b2(&sm.kl[0][0], LDB, np * 16, ks * 16, lane, bl);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    mma_16816(dk[2 * np + h], ak, b[2 * h], b[2 * h + 1]);
+                    mma_16816(dk[2 * np + h], ak, bl[2 * h], bl[2 * h + 1]);
+                    mma_16816(dk[2 * np + h], akl, b[2 * h], b[2 * h + 1]);
+                    mma_16816(dq[2 * np + h], aq, b[2 * h], b[2 * h + 1]);
+                    mma_16816(dq[2 * np + h], aq, bl[2 * h], bl[2 * h + 1]);
+                    mma_16816(dq[2 * np + h], aql, b[2 * h], b[2 * h + 1]);
+                }
+            }
+        }
+        const int r0 = warp * 16 + (lane >> 2), c0 = (lane & 3) * 2;
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            sm.kk[r0][n * 8 + c0] = dk[n][0];
+            sm.kk[r0][n * 8 + c0 + 1] = dk[n][1];
+            sm.kk[r0 + 8][n * 8 + c0] = dk[n][2];
+            sm.kk[r0 + 8][n * 8 + c0 + 1] = dk[n][3];
+            sm.qk[r0][n * 8 + c0] = dq[n][0];
+            sm.qk[r0][n * 8 + c0 + 1] = dq[n][1];
+            sm.qk[r0 + 8][n * 8 + c0] = dq[n][2];
+            sm.qk[r0 + 8][n * 8 + c0 + 1] = dq[n][3];
+        }
+    }
+    __syncthreads();
+    // ---- L (in place over kk) and T = (I + L)^-1, one column per thread
+    for (int e = tid; e < C * C; e += 128) {
+        const int r = e / C, s = e % C;
+        sm.kk[r][s] = s < r ? sm.beta[r] * __expf(sm.cum[r] - sm.cum[s]) * sm.kk[r][s] : 0.0f;
+    }
+    __syncthreads();
+    if (tid < C) {
+        const int s = tid;
+        for (int r = 0; r < C; ++r) {
+            float v = r == s ? 1.0f : 0.0f;
+            if (r > s) {
+                float acc = 0.0f;
+                for (int m = s; m < r; ++m) acc = fmaf(sm.kk[r][m], sm.t[m][s], acc);
+                v = -acc;
+            }
+            sm.t[r][s] = v;
+        }
+    }
+    __syncthreads();
+    // ---- T diag(beta) and T diag(beta gamma) as bf16 pairs
+    for (int e = tid; e < C * C; e += 128) {
+        const int r = e / C, s = e % C;
+        const float x = sm.t[r][s] * sm.beta[s];
+        const float y = x * __expf(sm.cum[s]);
+        const float xh = bf16_hi(x), yh = bf16_hi(y);
+        sm.ta_hi[r][s] = __float2bfloat16_rn(x);
+        sm.ta_lo[r][s] = __float2bfloat16_rn(x - xh);
+        sm.tb_hi[r][s] = __float2bfloat16_rn(y);
+        sm.tb_lo[r][s] = __float2bfloat16_rn(y - yh);
+    }
+    __syncthreads();
+    // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows, 128 cols)
+    const size_t blk = (size_t)vh * a.nc + ck;
+    float *ut_out = a.ut + blk * C * S;
+    __nv_bfloat16 *w_out = a.w + blk * C * S, *wl_out = a.w_lo + blk * C * S;
+    const int r0 = warp * 16 + (lane >> 2), c0 = (lane & 3) * 2;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {  // 64 output columns at a time
+        float du[8][4], dw[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) du[n][e] = dw[n][e] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks) {
+            uint32_t ah[4], al[4], bh[4], bl[4];
+            ld_a(&sm.ta_hi[0][0], LDP, warp * 16, ks * 16, lane, ah);
+            ld_a(&sm.ta_lo[0][0], LDP, warp * 16, ks * 16, lane, al);
+            ld_a(&sm.tb_hi[0][0], LDP, warp * 16, ks * 16, lane, bh);
+            ld_a(&sm.tb_lo[0][0], LDP, warp * 16, ks * 16, lane, bl);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                const int n0 = half * 64 + np * 16;
+                uint32_t vh_[4], vl_[4], kh_[4], kl_[4];
+                ld_b2_t(&sm.v[0][0], LDB, n0, ks * 16, lane, vh_);
+                ld_b2_t(&sm.vl[0][0], LDB, n0, ks * 16, lane, vl_);
+                ld_b2_t(&sm.k[0][0], LDB, n0, ks * 16, lane, kh_);
+                ld_b2_t(&sm.kl[0][0], LDB, n0, ks * 16, lane, kl_);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    mma_16816(du[2 * np + h], ah, vh_[2 * h], vh_[2 * h + 1]);
+                    mma_16816(du[2 * np + h], ah, vl_[2 * h], vl_[2 * h + 1]);
+                    mma_16816(du[2 * np + h], al, vh_[2 * h], vh_[2 * h + 1]);
+                    mma_16816(dw[2 * np + h], bh, kh_[2 * h], kh_[2 * h + 1]);
+                    mma_16816(dw[2 * np + h], bh, kl_[2 * h], kl_[2 * h + 1]);
+                    mma_16816(dw[2 * np + h], bl, kh_[2 * h], kh_[2 * h + 1]);
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            const int col = half * 64 + n * 8 + c0;
+            *reinterpret_cast<float2 *>(ut_out + r0 * S + col) = make_float2(du[n][0], du[n][1]);
+            *reinterpret_cast<float2 *>(ut_out + (r0 + 8) * S + col) = make_float2(du[n][2], du[n][3]);
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+                const float x0 = dw[n][2 * e2], x1 = dw[n][2 * e2 + 1];
+                const size_t o = (size_t)(r0 + 8 * e2) * S + col;
+                *reinterpret_cast<uint32_t *>(w_out + o) = pack_bf16(x0, x1);
+                *reinterpret_cast<uint32_t *>(wl_out + o) = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+            }
+        }
+    }
+    // ---- P = Q K^T o Mgamma (s <= t), Q' = gamma Q, K' = gamma_C / gamma K
+    __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
+    for (int e = tid; e < C * C; e += 128) {
+        const int r = e / C, s = e % C;
+        const float x = s <= r ? sm.qk[r][s] * __expf(sm.cum[r] - sm.cum[s]) : 0.0f;
+        p_out[e] = __float2bfloat16_rn(x);
+        pl_out[e] = __float2bfloat16_rn(x - bf16_hi(x));
+    }
+    const float cum_c = sm.cum[C - 1];
+    __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
+    __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
+    for (int e = tid; e < C * S; e += 128) {
+        const int r = e / S, c = e % S;
+        const float qf = __bfloat162float(sm.q[r][c]) + __bfloat162float(sm.ql[r][c]);
+        const float kf = __bfloat162float(sm.k[r][c]) + __bfloat162float(sm.kl[r][c]);
+        const float x = qf * __expf(sm.cum[r]), y = kf * __expf(cum_c - sm.cum[r]);
+        qp_out[e] = __float2bfloat16_rn(x);
+        qpl_out[e] = __float2bfloat16_rn(x - bf16_hi(x));
+        kp_out[e] = __float2bfloat16_rn(y);
+        kpl_out[e] = __float2bfloat16_rn(y - bf16_hi(y));
+    }
+    if (tid == 0) a.gc[blk] = __expf(cum_c);
+}
+
+// ---------------------------------------------------------------------------
+// dn_chunk_scan_kernel: grid (S / JC, n_v), 128 threads.  The chunks in
+// order; this CTA owns state columns j0 .. j0 + 31 of value head vh.  The
+// next chunk's W and Ut are fetched once the U phase has used this chunk's,
+// its Q', P and K' once the O and S phases have; the U phase of a chunk then
+// overlaps the arrival of its Q', P and K'.
+struct ScanSmem {
+    __nv_bfloat16 w[2][dc::C][dc::LDB], qp[2][dc::C][dc::LDB], kp[2][dc::C][dc::LDB];  // [hi, lo]
+    __nv_bfloat16 p[2][dc::C][dc::LDP];
+    float ut[dc::C][dc::JC];
+    float s[dc::S][dc::JC + 1];                                         // the state block, f32
+    __nv_bfloat16 st[2][2][dc::JC][dc::LDB];  // S^T [buffer][hi, lo]
+    __nv_bfloat16 ut_t[2][dc::JC][dc::LDP];   // U^T [hi, lo]
+};
+
+__device__ __forceinline__ void scan_load_wu(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
+                                             int j0, int tid) {
+    using namespace dc;
+    const __nv_bfloat16 *w = a.w + blk * C * S, *wl = a.w_lo + blk * C * S;
+    for (int e = tid; e < C * (S / 8); e += 128) {
+        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+        cp_async16(&sm.w[0][r][c8], w + r * S + c8);
+        cp_async16(&sm.w[1][r][c8], wl + r * S + c8);
+    }
+    const float *ut = a.ut + blk * C * S;
+    for (int e = tid; e < C * (JC / 4); e += 128) {
+        const int r = e / (JC / 4), c4 = (e % (JC / 4)) * 4;
+        cp_async16(&sm.ut[r][c4], ut + r * S + j0 + c4);
+    }
+}
+__device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
+                                              int tid) {
+    using namespace dc;
+    const __nv_bfloat16 *qp = a.qp + blk * C * S, *qpl = a.qp_lo + blk * C * S;
+    const __nv_bfloat16 *kp = a.kp + blk * C * S, *kpl = a.kp_lo + blk * C * S;
+    for (int e = tid; e < C * (S / 8); e += 128) {
+        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+        cp_async16(&sm.qp[0][r][c8], qp + r * S + c8);
+        cp_async16(&sm.qp[1][r][c8], qpl + r * S + c8);
+        cp_async16(&sm.kp[0][r][c8], kp + r * S + c8);
+        cp_async16(&sm.kp[1][r][c8], kpl + r * S + c8);
+    }
+    const __nv_bfloat16 *p = a.p + blk * C * C, *pl = a.p_lo + blk * C * C;
+    for (int e = tid; e < C * (C / 8); e += 128) {
+        const int r = e / (C / 8), c8 = (e % (C / 8)) * 8;
+        cp_async16(&sm.p[0][r][c8], p + r * C + c8);
+        cp_async16(&sm.p[1][r][c8], pl + r * C + c8);
+    }
+}
+
+// d += A B with A (16 rows from m0) given as a bf16 pair in row-major [m][k]
+// smem and B (two n-tile pairs = 32 columns) as a pair of [n][k] matrices;
+// three terms: hi*hi + hi*lo + lo*hi, over k from 0 to K.
+template <int K>
+__device__ __forceinline__ void mma3_rows(float (&d)[4][4], const __nv_bfloat16 *ah,
+                                          const __nv_bfloat16 *al, int lda, int m0,
+                                          const __nv_bfloat16 *bh, const __nv_bfloat16 *bl,
+                                          int ldb, int lane) {
+#pragma unroll
+    for (int ks = 0; ks < K / 16; ++ks) {
+        uint32_t xh[4], xl[4];
+        ld_a(ah, lda, m0, ks * 16, lane, xh);
+        ld_a(al, lda, m0, ks * 16, lane, xl);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+            uint32_t yh[4], yl[4];
+            ld_b2(bh, ldb, np * 16, ks * 16, lane, yh);
+            ld_b2(bl, ldb, np * 16, ks * 16, lane, yl);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
+                mma_16816(d[2 * np + h], xh, yl[2 * h], yl[2 * h + 1]);
+                mma_16816(d[2 * np + h], xl, yh[2 * h], yh[2 * h + 1]);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128, 1) dn_chunk_scan_kernel(const DnChunkArgs a) {
+    using namespace dc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ScanSmem &sm = *reinterpret_cast<ScanSmem *>(smem_raw);
+    const int j0 = blockIdx.x * JC, vh = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, c0 = (lane & 3) * 2;
+    const float scale = 1.0f / sqrtf((float)S);
+    float *state = a.ssm_state + (size_t)vh * a.slots * S * S + (size_t)a.live * S * S;
+    const size_t blk0 = (size_t)vh * a.nc;
+
+    scan_load_wu(sm, a, blk0, j0, tid);
+    cp_async_commit();
+    scan_load_qpk(sm, a, blk0, tid);
+    cp_async_commit();
+    for (int e = tid; e < S * JC; e += 128) {
+        const int i = e / JC, j = e % JC;
+        const float x = state[(size_t)i * S + j0 + j];
+        sm.s[i][j] = x;
+        sm.st[0][0][j][i] = __float2bfloat16_rn(x);
+        sm.st[0][1][j][i] = __float2bfloat16_rn(x - bf16_hi(x));
+    }
+    for (int ck = 0; ck < a.nc; ++ck) {
+        const int cur = ck & 1, nxt = cur ^ 1;
+        const bool more = ck + 1 < a.nc;
+        // W and Ut of this chunk have landed (its Q', P, K' may still be in flight)
+        cp_async_wait<1>();
+        __syncthreads();
+        // ---- U = Ut - W S (warp: rows 16w.., 32 columns)
+        {
+            float d[4][4] = {};
+            mma3_rows<S>(d, &sm.w[0][0][0], &sm.w[1][0][0], LDB, warp * 16, &sm.st[cur][0][0][0],
+                         &sm.st[cur][1][0][0], LDB, lane);
+            const int r0 = warp * 16 + g;
+#pragma unroll
+            for (int n = 0; n < 4; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int r = r0 + (e >> 1) * 8, c = n * 8 + c0 + (e & 1);
+                    const float u = sm.ut[r][c] - d[n][e];
+                    sm.ut_t[0][c][r] = __float2bfloat16_rn(u);
+                    sm.ut_t[1][c][r] = __float2bfloat16_rn(u - bf16_hi(u));
+                }
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        if (more) scan_load_wu(sm, a, blk0 + ck + 1, j0, tid);
+        cp_async_commit();
+        // ---- O = Q' S + P U (warp: rows 16w..)
+        {
+            float d[4][4] = {};
+            mma3_rows<S>(d, &sm.qp[0][0][0], &sm.qp[1][0][0], LDB, warp * 16, &sm.st[cur][0][0][0],
+                         &sm.st[cur][1][0][0], LDB, lane);
+            mma3_rows<C>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, warp * 16, &sm.ut_t[0][0][0],
+                         &sm.ut_t[1][0][0], LDP, lane);
+            const int r0 = warp * 16 + g;
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+                const int r = r0 + e2 * 8, tok = ck * C + r;
+                if (tok < a.t) {
+                    float *dst = a.opre + ((size_t)tok * a.n_v + vh) * S + j0;
+#pragma unroll
+                    for (int n = 0; n < 4; ++n)
+                        *reinterpret_cast<float2 *>(dst + n * 8 + c0) =
+                            make_float2(d[n][2 * e2] * scale, d[n][2 * e2 + 1] * scale);
+                }
+            }
+        }
+        // ---- S = gamma_C S + K'^T U (warp: state rows 32w.., 32 columns)
+        {
+            const float gc = a.gc[blk0 + ck];
+#pragma unroll
+            for (int mh = 0; mh < 2; ++mh) {
+                const int m0 = warp * 32 + mh * 16;
+                float d[4][4] = {};
+#pragma unroll
+                for (int ks = 0; ks < C / 16; ++ks) {
+                    uint32_t xh[4], xl[4];
+                    ld_a_t(&sm.kp[0][0][0], LDB, m0, ks * 16, lane, xh);
+                    ld_a_t(&sm.kp[1][0][0], LDB, m0, ks * 16, lane, xl);
+#pragma unroll
+                    for (int np = 0; np < 2; ++np) {
+                        uint32_t yh[4], yl[4];
+                        ld_b2(&sm.ut_t[0][0][0], LDP, np * 16, ks * 16, lane, yh);
+                        ld_b2(&sm.ut_t[1][0][0], LDP, np * 16, ks * 16, lane, yl);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
+                            mma_16816(d[2 * np + h], xh, yl[2 * h], yl[2 * h + 1]);
+                            mma_16816(d[2 * np + h], xl, yh[2 * h], yh[2 * h + 1]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int n = 0; n < 4; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int i = m0 + g + (e >> 1) * 8, j = n * 8 + c0 + (e & 1);
+                        const float x = fmaf(gc, sm.s[i][j], d[n][e]);
+                        sm.s[i][j] = x;
+                        sm.st[nxt][0][j][i] = __float2bfloat16_rn(x);
+                        sm.st[nxt][1][j][i] = __float2bfloat16_rn(x - bf16_hi(x));
+                    }
+            }
+        }
+        __syncthreads();  // Q', P, K' and U of this chunk are used up
+        if (more) scan_load_qpk(sm, a, blk0 + ck + 1, tid);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    for (int e = tid; e < S * JC; e += 128) {
+        const int i = e / JC, j = e % JC;
+        state[(size_t)i * S + j0 + j] = sm.s[i][j];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// dn_out_kernel: grid (t, n_v / 4), 4 warps, one (token, value head) each:
+// heads = rms_norm(o; norm, eps) * silu(z) (forward.rs:1642-1652).
+__global__ void __launch_bounds__(128) dn_out_kernel(const DnChunkArgs a) {
+    using namespace dc;
+    const int i = blockIdx.x, vh = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (vh >= a.n_v) return;
+    const size_t off = ((size_t)i * a.n_v + vh) * S + lane * 4;
+    const float4 o = *reinterpret_cast<const float4 *>(a.opre + off);
+    const float4 z = *reinterpret_cast<const float4 *>(a.z + off);
+    const float4 w = *reinterpret_cast<const float4 *>(a.norm + lane * 4);
+    double sq = (double)__fmul_rn(o.x, o.x) + (double)__fmul_rn(o.y, o.y) +
+                (double)__fmul_rn(o.z, o.z) + (double)__fmul_rn(o.w, o.w);
+    sq = warp_sum_d(sq);
+    const float sc = rms_scale_from_sum(sq, S, a.eps);
+    float4 y;
+    y.x = __fmul_rn(__fmul_rn(__fmul_rn(o.x, sc), w.x), siluf_(z.x));
+    y.y = __fmul_rn(__fmul_rn(__fmul_rn(o.y, sc), w.y), siluf_(z.y));
+    y.z = __fmul_rn(__fmul_rn(__fmul_rn(o.z, sc), w.z), siluf_(z.z));
+    y.w = __fmul_rn(__fmul_rn(__fmul_rn(o.w, sc), w.w), siluf_(z.w));
+    *reinterpret_cast<float4 *>(a.out + off) = y;
+}
+
+// The conv history after the batch: the last three raw inputs, newest last
+// (for a batch shorter than three, the oldest entries come from the history
+// before it).
+__global__ void dn_hist_kernel(const DnChunkArgs a) {
+    const int conv_dim = 2 * a.n_k * dc::S + a.n_v * dc::S;
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= conv_dim) return;
+    float *h = a.conv_state + (size_t)ch * 3;
+    float old[3] = {h[0], h[1], h[2]};
+    float nw[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        const int src = a.t - 3 + j;
+        nw[j] = src >= 0 ? a.qkv[(size_t)src * conv_dim + ch] : old[src + 3];
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) h[j] = nw[j];
+}
+
+cudaError_t init_dn_chunk_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(dn_chunk_local_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(LocalSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(ScanSmem));
+    return e;
+}
+
+cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st) {
+    using namespace dc;
+    dn_prep_kernel<<<dim3(a.t, 2 * a.n_k + a.n_v), S, 0, st>>>(a);
+    dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), 128, sizeof(LocalSmem), st>>>(a);
+    dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), 128, sizeof(ScanSmem), st>>>(a);
+    dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
+    const int conv_dim = 2 * a.n_k * S + a.n_v * S;
+    dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace rl

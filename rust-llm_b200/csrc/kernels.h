@@ -122,6 +122,29 @@ cudaError_t init_dn_kernels();
 cudaError_t launch_dn_step(const LinArgs &a, cudaStream_t st);
 int dn_max_group();
 
+// One chunked Gated DeltaNet prefill (dn_chunk.cu): t rows of one layer
+// updating ring slot `live` in place (slots == 1), in chunks of 64 tokens.
+struct DnChunkArgs {
+    const float *qkv, *z, *alpha, *beta;  // [t][conv_dim], [t][n_v*s], [t][n_v] x2
+    float *conv_state;                    // [conv_dim][kernel-1] of slot `live`
+    float *ssm_state;                     // [n_v][slots][s][s]
+    const float *conv1d, *ssm_a, *dt_bias, *norm;
+    float *out;                           // [t][n_v*s]
+    // scratch, sized for max_batch rows
+    __nv_bfloat16 *qn, *kn, *vn;          // [t][n_k][s], [t][n_k][s], [t][n_v][s]
+    __nv_bfloat16 *qn_lo, *kn_lo, *vn_lo;  // low halves: every operand is a bf16 pair
+    float *lg, *bt;                       // [t][n_v] log decay, beta
+    __nv_bfloat16 *w, *qp, *kp, *p;       // [n_v][nc][64][s] (p: [n_v][nc][64][64])
+    __nv_bfloat16 *w_lo, *qp_lo, *kp_lo, *p_lo;  // their low halves
+    float *ut, *gc;                       // [n_v][nc][64][s], [n_v][nc]
+    float *opre;                          // [t][n_v][s] readout before the gated norm
+    int *status;
+    int t, nc, n_k, n_v, live, slots;
+    float eps;
+};
+cudaError_t init_dn_chunk_kernels();
+cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st);
+
 // KV cache fill from f32 (host-visible test and bench helper): positions
 // [p0, p0+n) of every KV head, src [2][n_kv][n][hd] f32 on the device.
 cudaError_t launch_kv_fill(void *k_cache, void *v_cache, const float *src, int n_kv,

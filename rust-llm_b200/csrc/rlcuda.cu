@@ -46,11 +46,18 @@ struct rl_ctx {
     // bf16 caches: TMA map of the staged bf16 queries [max_batch][n_head][hd]
     CUtensorMap q_map{};
     CUtensorMap gate_map{};
+    // chunked DeltaNet prefill scratch (slots == 1 and max_batch >= 64)
+    __nv_bfloat16 *dn_qn = nullptr, *dn_kn = nullptr, *dn_vn = nullptr;
+    __nv_bfloat16 *dn_qn_lo = nullptr, *dn_kn_lo = nullptr, *dn_vn_lo = nullptr;
+    __nv_bfloat16 *dn_w_lo = nullptr, *dn_qp_lo = nullptr, *dn_kp_lo = nullptr, *dn_p_lo = nullptr;
+    float *dn_lg = nullptr, *dn_bt = nullptr;
+    __nv_bfloat16 *dn_w = nullptr, *dn_qp = nullptr, *dn_kp = nullptr, *dn_p = nullptr;
+    float *dn_ut = nullptr, *dn_gc = nullptr, *dn_opre = nullptr;
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
-    int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 0, opt_cluster = 0;
+    int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
     int64_t opt_early_tiles = 2;
     // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
@@ -178,7 +185,9 @@ void free_all(rl_ctx *x) {
     x->ev_pool.clear();
     void *ps[] = {x->kv, x->conv, x->ssm, x->q_norm, x->k_norm, x->conv1d, x->ssm_a,
                   x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->gate_bf16, x->part_o, x->part_ml,
-                  x->counters, x->rope_cs, x->rope_sn, x->stage, x->status};
+                  x->counters, x->rope_cs, x->rope_sn, x->stage, x->status,
+                  x->dn_qn, x->dn_kn, x->dn_vn, x->dn_qn_lo, x->dn_kn_lo, x->dn_vn_lo, x->dn_w_lo, x->dn_qp_lo, x->dn_kp_lo, x->dn_p_lo, x->dn_lg, x->dn_bt, x->dn_w, x->dn_qp, x->dn_kp,
+                  x->dn_p, x->dn_ut, x->dn_gc, x->dn_opre};
     for (void *p : ps)
         if (p) cudaFree(p);
     if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
@@ -319,7 +328,7 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     x->own_stream = true;
     if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
         rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess ||
-        rl::init_prefill_kernels() != cudaSuccess)
+        rl::init_prefill_kernels() != cudaSuccess || rl::init_dn_chunk_kernels() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
     for (int f = 0; f < 2; ++f) {
         for (int lc = 0; lc < 4; ++lc)
@@ -371,6 +380,25 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
                                    64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
                 return bail(fail(x, RL_ECUDA, "encoding the gate tensor map failed"));
         }
+    }
+    if (c.n_linear > 0 && c.slots == 1 && mb >= 64) {
+        const size_t nk = c.n_k_heads, nv = c.n_v_heads, nc = (mb + 63) / 64;
+        if ((code = alloc(x, &x->dn_qn, mb * nk * s)) || (code = alloc(x, &x->dn_kn, mb * nk * s)) ||
+            (code = alloc(x, &x->dn_qn_lo, mb * nk * s)) ||
+            (code = alloc(x, &x->dn_kn_lo, mb * nk * s)) ||
+            (code = alloc(x, &x->dn_vn_lo, mb * nv * s)) ||
+            (code = alloc(x, &x->dn_w_lo, nv * nc * 64 * s)) ||
+            (code = alloc(x, &x->dn_qp_lo, nv * nc * 64 * s)) ||
+            (code = alloc(x, &x->dn_kp_lo, nv * nc * 64 * s)) ||
+            (code = alloc(x, &x->dn_p_lo, nv * nc * 64 * 64)) ||
+            (code = alloc(x, &x->dn_vn, mb * nv * s)) || (code = alloc(x, &x->dn_lg, mb * nv)) ||
+            (code = alloc(x, &x->dn_bt, mb * nv)) || (code = alloc(x, &x->dn_w, nv * nc * 64 * s)) ||
+            (code = alloc(x, &x->dn_qp, nv * nc * 64 * s)) ||
+            (code = alloc(x, &x->dn_kp, nv * nc * 64 * s)) ||
+            (code = alloc(x, &x->dn_p, nv * nc * 64 * 64)) ||
+            (code = alloc(x, &x->dn_ut, nv * nc * 64 * s)) || (code = alloc(x, &x->dn_gc, nv * nc)) ||
+            (code = alloc(x, &x->dn_opre, mb * nv * s)))
+            return bail(code);
     }
     // staging for the host entry points: the larger of the two paths' in+out
     const size_t full_io = mb * (2 * hd * nh + 2 * hd * c.n_head_kv + hd * nh);
@@ -763,6 +791,56 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
         return fail(ctx, RL_EINVAL, "live slot %d of a ring of %d", live, c.slots);
     if (!qkv || !z || !alpha || !beta || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
     CK(ctx, cudaSetDevice(ctx->device));
+    if (c.slots == 1 && ctx->dn_w && ctx->opt_chunk_rows > 0 && t >= ctx->opt_chunk_rows) {
+        // chunked tensor-core prefill over the in-place state
+        rl::DnChunkArgs d{};
+        d.qkv = qkv;
+        d.z = z;
+        d.alpha = alpha;
+        d.beta = beta;
+        d.conv_state = ctx->conv + (size_t)layer * conv_layer_floats(c);
+        d.ssm_state = ctx->ssm + (size_t)layer * ssm_layer_floats(c);
+        d.conv1d = ctx->conv1d + (size_t)layer * conv_dim(c) * c.conv_kernel;
+        d.ssm_a = ctx->ssm_a + (size_t)layer * c.n_v_heads;
+        d.dt_bias = ctx->dt_bias + (size_t)layer * c.n_v_heads;
+        d.norm = ctx->ssm_norm + (size_t)layer * c.d_state;
+        d.out = out;
+        d.qn = ctx->dn_qn;
+        d.kn = ctx->dn_kn;
+        d.qn_lo = ctx->dn_qn_lo;
+        d.kn_lo = ctx->dn_kn_lo;
+        d.vn_lo = ctx->dn_vn_lo;
+        d.w_lo = ctx->dn_w_lo;
+        d.qp_lo = ctx->dn_qp_lo;
+        d.kp_lo = ctx->dn_kp_lo;
+        d.p_lo = ctx->dn_p_lo;
+        d.vn = ctx->dn_vn;
+        d.lg = ctx->dn_lg;
+        d.bt = ctx->dn_bt;
+        d.w = ctx->dn_w;
+        d.qp = ctx->dn_qp;
+        d.kp = ctx->dn_kp;
+        d.p = ctx->dn_p;
+        d.ut = ctx->dn_ut;
+        d.gc = ctx->dn_gc;
+        d.opre = ctx->dn_opre;
+        d.status = ctx->status;
+        d.t = t;
+        d.nc = (t + 63) / 64;
+        d.n_k = c.n_k_heads;
+        d.n_v = c.n_v_heads;
+        d.live = live;
+        d.slots = c.slots;
+        d.eps = c.rms_eps;
+        {
+            ProfScope ps(ctx, RL_PROF_DN_CHUNK);
+            CK(ctx, rl::launch_dn_chunk(d, ctx->stream));
+        }
+        // a step of this layer right after must not read the state early
+        ctx->prev_dn = 1;
+        ctx->prev_layer = layer;
+        return RL_OK;
+    }
     rl::LinArgs a{};
     a.qkv = qkv;
     a.z = z;
