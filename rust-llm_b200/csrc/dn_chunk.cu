@@ -40,49 +40,73 @@ constexpr int LDB = 136;   // padded bf16 row (272 B: ldmatrix rows in distinct 
 constexpr int LDP = 72;    // padded bf16 row of a 64-wide matrix (144 B)
 constexpr int LDF = 65;    // padded f32 row of a 64-wide matrix
 constexpr int JC = 32;     // state columns per scan CTA
+constexpr int SCAN_THREADS = 256;
 }  // namespace dc
 
 // ---------------------------------------------------------------------------
-// dn_prep_kernel: grid (t, 2*n_k + n_v), 128 threads, one channel each.
-__global__ void __launch_bounds__(128) dn_prep_kernel(const DnChunkArgs a) {
+// dn_prep_kernel: grid (t, groups / 8), 8 warps; one warp per (token, group
+// of 128 channels: a q head, a k head or a v head), 4 channels per lane.
+__device__ __forceinline__ void store_pair4(__nv_bfloat16 *hi, __nv_bfloat16 *lo, const float *y) {
+    uint2 h, l;
+    h.x = pack_bf16(y[0], y[1]);
+    h.y = pack_bf16(y[2], y[3]);
+    l.x = pack_bf16(y[0] - bf16_hi(y[0]), y[1] - bf16_hi(y[1]));
+    l.y = pack_bf16(y[2] - bf16_hi(y[2]), y[3] - bf16_hi(y[3]));
+    *reinterpret_cast<uint2 *>(hi) = h;
+    *reinterpret_cast<uint2 *>(lo) = l;
+}
+
+__global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
     using namespace dc;
-    __shared__ double red[4];
-    const int i = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int i = blockIdx.x, g = blockIdx.y * 8 + (threadIdx.x >> 5);
+    const int n_groups = 2 * a.n_k + a.n_v;
+    if (g >= n_groups) return;
     const int key_dim = a.n_k * S, conv_dim = 2 * key_dim + a.n_v * S;
-    const int ch = g * S + c;
-    const float *w = a.conv1d + (size_t)ch * 4;
-    const float x = a.qkv[(size_t)i * conv_dim + ch];
-    float h[3];
+    const int ch = g * S + lane * 4;
+    const float4 x4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t)i * conv_dim + ch);
+    const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+    float h[3][4];
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
         const int src = i - 3 + j;
-        h[j] = src >= 0 ? a.qkv[(size_t)src * conv_dim + ch] : a.conv_state[(size_t)ch * 3 + (src + 3)];
-    }
-    // forward.rs:2018-2031: x * w[3] first, then the history taps in order
-    float y = __fmul_rn(x, w[3]);
+        if (src >= 0) {
+            const float4 v = *reinterpret_cast<const float4 *>(a.qkv + (size_t)src * conv_dim + ch);
+            h[j][0] = v.x, h[j][1] = v.y, h[j][2] = v.z, h[j][3] = v.w;
+        } else {
 #pragma unroll
-    for (int j = 0; j < 3; ++j) y = __fadd_rn(y, __fmul_rn(h[j], w[j]));
-    y = siluf_(y);
+            for (int e = 0; e < 4; ++e) h[j][e] = a.conv_state[(size_t)(ch + e) * 3 + (src + 3)];
+        }
+    }
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float4 w = *reinterpret_cast<const float4 *>(a.conv1d + (size_t)(ch + e) * 4);
+        // forward.rs:2018-2031: x * w[3] first, then the history taps in order
+        float c = __fmul_rn(xs[e], w.w);
+        c = __fadd_rn(c, __fmul_rn(h[0][e], w.x));
+        c = __fadd_rn(c, __fmul_rn(h[1][e], w.y));
+        c = __fadd_rn(c, __fmul_rn(h[2][e], w.z));
+        y[e] = siluf_(c);
+    }
     if (g < 2 * a.n_k) {
         // L2 norm: rms_scale with eps/n, then 1/sqrt(n) (forward.rs:1720-1727)
-        double sq = warp_sum_d((double)__fmul_rn(y, y));
-        if ((c & 31) == 0) red[c >> 5] = sq;
-        __syncthreads();
-        const double sum = ((-0.0 + red[0]) + red[1]) + red[2] + red[3];
-        const float sc = rms_scale_from_sum(sum, S, a.eps / (float)S);
-        y = __fmul_rn(__fmul_rn(y, sc), 1.0f / sqrtf((float)S));
-        // q and k as bf16 pairs (hi + lo): their dot products feed P and L, and a
-        // nearly orthogonal pair's product needs more than bf16's 8 bits
-        const size_t o = g < a.n_k ? ((size_t)i * a.n_k + g) * S
-                                   : ((size_t)i * a.n_k + (g - a.n_k)) * S;
-        __nv_bfloat16 *hi = g < a.n_k ? a.qn : a.kn, *lo = g < a.n_k ? a.qn_lo : a.kn_lo;
-        hi[o + c] = __float2bfloat16_rn(y);
-        lo[o + c] = __float2bfloat16_rn(y - bf16_hi(y));
+        double sq = 0.0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sq += (double)__fmul_rn(y[e], y[e]);
+        sq = warp_sum_d(sq);
+        const float sc = rms_scale_from_sum(sq, S, a.eps / (float)S);
+        const float shrink = 1.0f / sqrtf((float)S);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), shrink);
+        const bool is_q = g < a.n_k;
+        const size_t o = ((size_t)i * a.n_k + (is_q ? g : g - a.n_k)) * S + lane * 4;
+        store_pair4((is_q ? a.qn : a.kn) + o, (is_q ? a.qn_lo : a.kn_lo) + o, y);
     } else {
         const int vh = g - 2 * a.n_k;
-        a.vn[((size_t)i * a.n_v + vh) * S + c] = __float2bfloat16_rn(y);
-        a.vn_lo[((size_t)i * a.n_v + vh) * S + c] = __float2bfloat16_rn(y - bf16_hi(y));
-        if (c == 0) {
+        const size_t o = ((size_t)i * a.n_v + vh) * S + lane * 4;
+        store_pair4(a.vn + o, a.vn_lo + o, y);
+        if (lane == 0) {
             // gates (forward.rs:1530-1546): log decay and beta
             a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(
                 softplusf_(__fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh])), a.ssm_a[vh]);
@@ -132,7 +156,7 @@ __device__ __forceinline__ void cp_async_wait() {
 struct LocalSmem {
     __nv_bfloat16 k[dc::C][dc::LDB], q[dc::C][dc::LDB], v[dc::C][dc::LDB];
     __nv_bfloat16 kl[dc::C][dc::LDB], ql[dc::C][dc::LDB], vl[dc::C][dc::LDB];  // low halves
-    float kk[dc::C][dc::LDF], qk[dc::C][dc::LDF], t[dc::C][dc::LDF];
+    float kk[dc::C][dc::LDF], qk[dc::C][dc::LDF], t[dc::C][dc::LDF], x[dc::C][dc::LDF];
     __nv_bfloat16 ta_hi[dc::C][dc::LDP], ta_lo[dc::C][dc::LDP];  // T diag(beta)
     __nv_bfloat16 tb_hi[dc::C][dc::LDP], tb_lo[dc::C][dc::LDP];  // T diag(beta gamma)
     float cum[dc::C], beta[dc::C];
@@ -227,20 +251,44 @@ __global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a
         const int r = e / C, s = e % C;
         sm.kk[r][s] = s < r ? sm.beta[r] * __expf(sm.cum[r] - sm.cum[s]) * sm.kk[r][s] : 0.0f;
     }
+    for (int e = tid; e < C * C; e += 128) sm.t[e / C][e % C] = 0.0f;
     __syncthreads();
+    // T = (I + L)^-1 in 16 x 16 blocks: the four diagonal blocks by forward
+    // substitution (one column per thread), then the blocks below the
+    // diagonal, one diagonal at a time: T_ij = -T_ii sum_{j<=k<i} L_ik T_kj
     if (tid < C) {
-        const int s = tid;
-        for (int r = 0; r < C; ++r) {
+        const int b0 = (tid >> 4) * 16, s = tid & 15;
+        for (int r = 0; r < 16; ++r) {
             float v = r == s ? 1.0f : 0.0f;
             if (r > s) {
                 float acc = 0.0f;
-                for (int m = s; m < r; ++m) acc = fmaf(sm.kk[r][m], sm.t[m][s], acc);
+                for (int m = s; m < r; ++m) acc = fmaf(sm.kk[b0 + r][b0 + m], sm.t[b0 + m][b0 + s], acc);
                 v = -acc;
             }
-            sm.t[r][s] = v;
+            sm.t[b0 + r][b0 + s] = v;
         }
     }
     __syncthreads();
+#pragma unroll 1
+    for (int dg = 1; dg < 4; ++dg) {
+        const int nb = 4 - dg;  // blocks on this diagonal: (j + dg, j), j < nb
+        for (int e = tid; e < nb * 256; e += 128) {
+            const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15, bi = bj + dg;
+            float acc = 0.0f;
+            for (int k = bj * 16; k < bi * 16; ++k) acc = fmaf(sm.kk[bi * 16 + r][k], sm.t[k][bj * 16 + c], acc);
+            sm.x[bi * 16 + r][bj * 16 + c] = acc;
+        }
+        __syncthreads();
+        for (int e = tid; e < nb * 256; e += 128) {
+            const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15, bi = bj + dg;
+            float acc = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 16; ++m)
+                acc = fmaf(sm.t[bi * 16 + r][bi * 16 + m], sm.x[bi * 16 + m][bj * 16 + c], acc);
+            sm.t[bi * 16 + r][bj * 16 + c] = -acc;
+        }
+        __syncthreads();
+    }
     // ---- T diag(beta) and T diag(beta gamma) as bf16 pairs
     for (int e = tid; e < C * C; e += 128) {
         const int r = e / C, s = e % C;
@@ -348,13 +396,13 @@ __device__ __forceinline__ void scan_load_wu(ScanSmem &sm, const DnChunkArgs &a,
                                              int j0, int tid) {
     using namespace dc;
     const __nv_bfloat16 *w = a.w + blk * C * S, *wl = a.w_lo + blk * C * S;
-    for (int e = tid; e < C * (S / 8); e += 128) {
+    for (int e = tid; e < C * (S / 8); e += SCAN_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
         cp_async16(&sm.w[0][r][c8], w + r * S + c8);
         cp_async16(&sm.w[1][r][c8], wl + r * S + c8);
     }
     const float *ut = a.ut + blk * C * S;
-    for (int e = tid; e < C * (JC / 4); e += 128) {
+    for (int e = tid; e < C * (JC / 4); e += SCAN_THREADS) {
         const int r = e / (JC / 4), c4 = (e % (JC / 4)) * 4;
         cp_async16(&sm.ut[r][c4], ut + r * S + j0 + c4);
     }
@@ -364,7 +412,7 @@ __device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a
     using namespace dc;
     const __nv_bfloat16 *qp = a.qp + blk * C * S, *qpl = a.qp_lo + blk * C * S;
     const __nv_bfloat16 *kp = a.kp + blk * C * S, *kpl = a.kp_lo + blk * C * S;
-    for (int e = tid; e < C * (S / 8); e += 128) {
+    for (int e = tid; e < C * (S / 8); e += SCAN_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
         cp_async16(&sm.qp[0][r][c8], qp + r * S + c8);
         cp_async16(&sm.qp[1][r][c8], qpl + r * S + c8);
@@ -372,7 +420,7 @@ __device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a
         cp_async16(&sm.kp[1][r][c8], kpl + r * S + c8);
     }
     const __nv_bfloat16 *p = a.p + blk * C * C, *pl = a.p_lo + blk * C * C;
-    for (int e = tid; e < C * (C / 8); e += 128) {
+    for (int e = tid; e < C * (C / 8); e += SCAN_THREADS) {
         const int r = e / (C / 8), c8 = (e % (C / 8)) * 8;
         cp_async16(&sm.p[0][r][c8], p + r * C + c8);
         cp_async16(&sm.p[1][r][c8], pl + r * C + c8);
@@ -380,23 +428,23 @@ __device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a
 }
 
 // d += A B with A (16 rows from m0) given as a bf16 pair in row-major [m][k]
-// smem and B (two n-tile pairs = 32 columns) as a pair of [n][k] matrices;
-// three terms: hi*hi + hi*lo + lo*hi, over k from 0 to K.
-template <int K>
-__device__ __forceinline__ void mma3_rows(float (&d)[4][4], const __nv_bfloat16 *ah,
+// smem and B (NP pairs of n-tiles from n0, 16 NP columns) as a pair of [n][k]
+// matrices; three terms: hi*hi + hi*lo + lo*hi, over k from 0 to K.
+template <int K, int NP>
+__device__ __forceinline__ void mma3_rows(float (&d)[2 * NP][4], const __nv_bfloat16 *ah,
                                           const __nv_bfloat16 *al, int lda, int m0,
                                           const __nv_bfloat16 *bh, const __nv_bfloat16 *bl,
-                                          int ldb, int lane) {
+                                          int ldb, int n0, int lane) {
 #pragma unroll
     for (int ks = 0; ks < K / 16; ++ks) {
         uint32_t xh[4], xl[4];
         ld_a(ah, lda, m0, ks * 16, lane, xh);
         ld_a(al, lda, m0, ks * 16, lane, xl);
 #pragma unroll
-        for (int np = 0; np < 2; ++np) {
+        for (int np = 0; np < NP; ++np) {
             uint32_t yh[4], yl[4];
-            ld_b2(bh, ldb, np * 16, ks * 16, lane, yh);
-            ld_b2(bl, ldb, np * 16, ks * 16, lane, yl);
+            ld_b2(bh, ldb, n0 + np * 16, ks * 16, lane, yh);
+            ld_b2(bl, ldb, n0 + np * 16, ks * 16, lane, yl);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
@@ -407,7 +455,7 @@ __device__ __forceinline__ void mma3_rows(float (&d)[4][4], const __nv_bfloat16 
     }
 }
 
-__global__ void __launch_bounds__(128, 1) dn_chunk_scan_kernel(const DnChunkArgs a) {
+__global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(const DnChunkArgs a) {
     using namespace dc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScanSmem &sm = *reinterpret_cast<ScanSmem *>(smem_raw);
@@ -422,7 +470,7 @@ __global__ void __launch_bounds__(128, 1) dn_chunk_scan_kernel(const DnChunkArgs
     cp_async_commit();
     scan_load_qpk(sm, a, blk0, tid);
     cp_async_commit();
-    for (int e = tid; e < S * JC; e += 128) {
+    for (int e = tid; e < S * JC; e += SCAN_THREADS) {
         const int i = e / JC, j = e % JC;
         const float x = state[(size_t)i * S + j0 + j];
         sm.s[i][j] = x;
@@ -435,17 +483,18 @@ __global__ void __launch_bounds__(128, 1) dn_chunk_scan_kernel(const DnChunkArgs
         // W and Ut of this chunk have landed (its Q', P, K' may still be in flight)
         cp_async_wait<1>();
         __syncthreads();
-        // ---- U = Ut - W S (warp: rows 16w.., 32 columns)
+        // ---- U = Ut - W S (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
+        const int wm = (warp & 3) * 16, wn = (warp >> 2) * 16;
         {
-            float d[4][4] = {};
-            mma3_rows<S>(d, &sm.w[0][0][0], &sm.w[1][0][0], LDB, warp * 16, &sm.st[cur][0][0][0],
-                         &sm.st[cur][1][0][0], LDB, lane);
-            const int r0 = warp * 16 + g;
+            float d[2][4] = {};
+            mma3_rows<S, 1>(d, &sm.w[0][0][0], &sm.w[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
+                            &sm.st[cur][1][0][0], LDB, wn, lane);
+            const int r0 = wm + g;
 #pragma unroll
-            for (int n = 0; n < 4; ++n)
+            for (int n = 0; n < 2; ++n)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int r = r0 + (e >> 1) * 8, c = n * 8 + c0 + (e & 1);
+                    const int r = r0 + (e >> 1) * 8, c = wn + n * 8 + c0 + (e & 1);
                     const float u = sm.ut[r][c] - d[n][e];
                     sm.ut_t[0][c][r] = __float2bfloat16_rn(u);
                     sm.ut_t[1][c][r] = __float2bfloat16_rn(u - bf16_hi(u));
@@ -455,32 +504,32 @@ __global__ void __launch_bounds__(128, 1) dn_chunk_scan_kernel(const DnChunkArgs
         __syncthreads();
         if (more) scan_load_wu(sm, a, blk0 + ck + 1, j0, tid);
         cp_async_commit();
-        // ---- O = Q' S + P U (warp: rows 16w..)
+        // ---- O = Q' S + P U (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
         {
-            float d[4][4] = {};
-            mma3_rows<S>(d, &sm.qp[0][0][0], &sm.qp[1][0][0], LDB, warp * 16, &sm.st[cur][0][0][0],
-                         &sm.st[cur][1][0][0], LDB, lane);
-            mma3_rows<C>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, warp * 16, &sm.ut_t[0][0][0],
-                         &sm.ut_t[1][0][0], LDP, lane);
-            const int r0 = warp * 16 + g;
+            float d[2][4] = {};
+            mma3_rows<S, 1>(d, &sm.qp[0][0][0], &sm.qp[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
+                            &sm.st[cur][1][0][0], LDB, wn, lane);
+            mma3_rows<C, 1>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, wm, &sm.ut_t[0][0][0],
+                            &sm.ut_t[1][0][0], LDP, wn, lane);
+            const int r0 = wm + g;
 #pragma unroll
             for (int e2 = 0; e2 < 2; ++e2) {
                 const int r = r0 + e2 * 8, tok = ck * C + r;
                 if (tok < a.t) {
-                    float *dst = a.opre + ((size_t)tok * a.n_v + vh) * S + j0;
+                    float *dst = a.opre + ((size_t)tok * a.n_v + vh) * S + j0 + wn;
 #pragma unroll
-                    for (int n = 0; n < 4; ++n)
+                    for (int n = 0; n < 2; ++n)
                         *reinterpret_cast<float2 *>(dst + n * 8 + c0) =
                             make_float2(d[n][2 * e2] * scale, d[n][2 * e2 + 1] * scale);
                 }
             }
         }
-        // ---- S = gamma_C S + K'^T U (warp: state rows 32w.., 32 columns)
+        // ---- S = gamma_C S + K'^T U (warp: state rows 16w.., 32 columns)
         {
             const float gc = a.gc[blk0 + ck];
 #pragma unroll
-            for (int mh = 0; mh < 2; ++mh) {
-                const int m0 = warp * 32 + mh * 16;
+            for (int mh = 0; mh < 1; ++mh) {
+                const int m0 = warp * 16;
                 float d[4][4] = {};
 #pragma unroll
                 for (int ks = 0; ks < C / 16; ++ks) {
@@ -517,7 +566,7 @@ __global__ void __launch_bounds__(128, 1) dn_chunk_scan_kernel(const DnChunkArgs
         cp_async_commit();
     }
     cp_async_wait<0>();
-    for (int e = tid; e < S * JC; e += 128) {
+    for (int e = tid; e < S * JC; e += SCAN_THREADS) {
         const int i = e / JC, j = e % JC;
         state[(size_t)i * S + j0 + j] = sm.s[i][j];
     }
@@ -577,9 +626,9 @@ cudaError_t init_dn_chunk_kernels() {
 
 cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st) {
     using namespace dc;
-    dn_prep_kernel<<<dim3(a.t, 2 * a.n_k + a.n_v), S, 0, st>>>(a);
+    dn_prep_kernel<<<dim3(a.t, (2 * a.n_k + a.n_v + 7) / 8), 256, 0, st>>>(a);
     dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), 128, sizeof(LocalSmem), st>>>(a);
-    dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), 128, sizeof(ScanSmem), st>>>(a);
+    dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
     const int conv_dim = 2 * a.n_k * S + a.n_v * S;
     dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, st>>>(a);
