@@ -324,6 +324,140 @@ def prefill_bench(args, dev, stream, rlcuda, torch):
             "peak_tflops": peak, "dtype": "bf16 x bf16 -> f32 (tcgen05 kind::f16)"}
 
 
+DN_PF_LAYERS = 24
+DN_PF_FLOP_PER_LAYER = 23.62e9  # per v head per 64-token chunk 5 C^2 d + 3 C d^2 MACs, x32 x64
+
+
+def dn_prefill_bench(args, dev, stream, rlcuda, torch):
+    """Config 2's DeltaNet layers: 24 layers of a 4096-token chunked prefill
+    (chunk 64) from seeded states, one input set shared by the layers (the
+    work per layer does not depend on the values); returns µs per layer and
+    the algorithmic tensor rate (the survey's per-layer FLOP count)."""
+    cfg = rlcuda.qwen35_config(n_full=0, n_linear=DN_PF_LAYERS, context=PF_T, slots=1,
+                               max_batch=PF_T)
+    ctx = rlcuda.Context(cfg, device=dev.index)
+    ctx.set_stream(stream.cuda_stream)
+    import numpy as np
+    r = np.random.default_rng(2)
+    for layer in range(DN_PF_LAYERS):
+        ctx.set_weights_linear(layer, r.normal(0, 0.5, (8192, 4)).astype(np.float32),
+                               -np.exp(r.uniform(0, np.log(16), 32)).astype(np.float32),
+                               r.normal(0, 0.1, 32).astype(np.float32), np.ones(128, np.float32))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    qkv = torch.randn((PF_T, 8192), generator=gen, device=dev)
+    z = torch.randn((PF_T, 4096), generator=gen, device=dev)
+    al = torch.randn((PF_T, 32), generator=gen, device=dev)
+    be = torch.randn((PF_T, 32), generator=gen, device=dev)
+    out = torch.empty((PF_T, 4096), device=dev)
+
+    def step():
+        for layer in range(DN_PF_LAYERS):
+            ctx.linear_attn(layer, 0, PF_T, qkv, z, al, be, out)
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    ctx.sync()
+    steps = 2
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+    stream.synchronize()
+    ctx.sync()
+    ctx.close()
+    us = e0.elapsed_time(e1) * 1e3 / (steps * DN_PF_LAYERS)
+    _, peak = peaks_bf16()
+    tf = DN_PF_FLOP_PER_LAYER / (us * 1e-6) / 1e12
+    return {"workload": "config 2 DeltaNet layers: 24 x 4096-token chunked prefill (chunk 64), "
+                        "f32 state between chunks",
+            "us_per_layer": us, "flop_per_layer": DN_PF_FLOP_PER_LAYER,
+            "tflops_algorithmic": tf, "frac_of_measured_bf16": tf / peak,
+            "note": "every product is three bf16 mma.sync terms (hi*hi + hi*lo + lo*hi), so "
+                    "the tensor pipes execute about 3x the algorithmic FLOP"}
+
+
+VERIFY_POS, VERIFY_K = 16384, 8
+VERIFY_ATTN_BYTES = 2 * N_KV * (VERIFY_POS + VERIFY_K) * HD * 2   # K + V, bf16: 67,141,632 B
+VERIFY_DN_BYTES = 32 * 128 * 128 * 4 * (1 + VERIFY_K)             # read slot 0, write 8 slots
+
+
+def verify_bench(args, dev, stream, rlcuda, torch):
+    """Config 3: a draft of k = 8 rows verified against a 16384-token context.
+    8 full-attention layers run the 8 causal rows over the bf16 cache; 24
+    DeltaNet layers run 8 sequential steps writing ring slots 1..8 of a
+    9-slot ring, so accept(j) for any j is a pointer move.  Each timed pass
+    restarts from slot 0 (the rollback)."""
+    import numpy as np
+    ctx_len = VERIFY_POS + VERIFY_K
+    fcfg = rlcuda.qwen35_config(n_full=N_LAYERS, n_linear=0, context=ctx_len,
+                                kv_dtype=rlcuda.RL_KV_BF16, max_batch=VERIFY_K)
+    dcfg = rlcuda.qwen35_config(n_full=0, n_linear=24, context=16, slots=VERIFY_K + 1,
+                                max_batch=VERIFY_K)
+    fctx = rlcuda.Context(fcfg, device=dev.index)
+    dctx = rlcuda.Context(dcfg, device=dev.index)
+    fctx.set_stream(stream.cuda_stream)
+    dctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    for layer in range(N_LAYERS):
+        src = torch.randn((2, N_KV, VERIFY_POS, HD), generator=gen, device=dev)
+        fctx.write_kv(layer, 0, src)
+        del src
+    r = np.random.default_rng(3)
+    for layer in range(24):
+        dctx.set_weights_linear(layer, r.normal(0, 0.5, (8192, 4)).astype(np.float32),
+                                -np.exp(r.uniform(0, np.log(16), 32)).astype(np.float32),
+                                r.normal(0, 0.1, 32).astype(np.float32), np.ones(128, np.float32))
+    qg = torch.randn((VERIFY_K, N_HEAD * 2 * HD), generator=gen, device=dev)
+    kk = torch.randn((VERIFY_K, N_KV * HD), generator=gen, device=dev)
+    vv = torch.randn((VERIFY_K, N_KV * HD), generator=gen, device=dev)
+    out = torch.empty((VERIFY_K, N_HEAD * HD), device=dev)
+    qkv = torch.randn((VERIFY_K, 8192), generator=gen, device=dev)
+    z = torch.randn((VERIFY_K, 4096), generator=gen, device=dev)
+    al = torch.randn((VERIFY_K, 32), generator=gen, device=dev)
+    be = torch.randn((VERIFY_K, 32), generator=gen, device=dev)
+    dout = torch.empty((VERIFY_K, 4096), device=dev)
+
+    def attn():
+        for layer in range(N_LAYERS):
+            fctx.full_attn(layer, VERIFY_POS, VERIFY_K, qg, kk, vv, out)
+
+    def dn():
+        for layer in range(24):
+            dctx.linear_attn(layer, 0, VERIFY_K, qkv, z, al, be, dout)
+
+    def timed(fn, reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn()
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+        stream.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    reps = max(10, min(args.steps // 20, 200))
+    a_us = timed(attn, reps) / N_LAYERS
+    d_us = timed(dn, reps) / 24
+    fctx.sync()
+    dctx.sync()
+    fctx.close()
+    dctx.close()
+    return {"workload": "config 3: k = 8 draft rows at position 16384; 8 full-attention "
+                        "layers (bf16 cache) + 24 DeltaNet layers over a 9-slot state ring",
+            "attn_us_per_layer": a_us, "attn_gbs": VERIFY_ATTN_BYTES / (a_us * 1e-6) / 1e9,
+            "dn_us_per_layer": d_us, "dn_gbs": VERIFY_DN_BYTES / (d_us * 1e-6) / 1e9,
+            "pass_us": a_us * N_LAYERS + d_us * 24}
+
+
 SPLIT_SEQ = 131072
 
 
@@ -537,6 +671,8 @@ def run_ours(args):
              if not args.no_split else None)
     dn = dn_step_bench(args, dev, stream, rlcuda, torch) if not args.no_dn else None
     pf = prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
+    dnpf = dn_prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
+    ver = verify_bench(args, dev, stream, rlcuda, torch) if not args.no_verify else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -561,6 +697,10 @@ def run_ours(args):
         "hbm_frac_of_8tbs": hbm_gbs / 8000.0,
         "prefill_tflops": pf["tflops_layer"] if pf else None,
         "prefill": pf,
+        "dn_prefill": dnpf,
+        "verify": ver,
+        "config2_attention_ms": ((pf["us_per_layer"] * PF_LAYERS + dnpf["us_per_layer"] *
+                                  DN_PF_LAYERS) / 1e3 if pf and dnpf else None),
         "split_kv": split,
         "dn_step": dn,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -592,6 +732,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dn", action="store_true", help="skip the DeltaNet step section")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill section")
+    ap.add_argument("--no-verify", action="store_true", help="skip the speculative-verify section")
     ap.add_argument("--no-split", action="store_true",
                     help="skip the long-context split-sequence section")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
