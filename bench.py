@@ -384,6 +384,8 @@ def dn_prefill_bench(args, dev, stream, rlcuda, torch):
 VERIFY_POS, VERIFY_K = 16384, 8
 VERIFY_ATTN_BYTES = 2 * N_KV * (VERIFY_POS + VERIFY_K) * HD * 2   # K + V, bf16: 67,141,632 B
 VERIFY_DN_BYTES = 32 * 128 * 128 * 4 * (1 + VERIFY_K)             # read slot 0, write 8 slots
+# Q K^T + P V over each row's causal prefix: 4 * 16 heads * 256 * sum_i (16384 + i + 1)
+VERIFY_ATTN_FLOP = 4 * N_HEAD * HD * sum(VERIFY_POS + i + 1 for i in range(VERIFY_K))
 
 
 def verify_bench(args, dev, stream, rlcuda, torch):
@@ -454,6 +456,9 @@ def verify_bench(args, dev, stream, rlcuda, torch):
     return {"workload": "config 3: k = 8 draft rows at position 16384; 8 full-attention "
                         "layers (bf16 cache) + 24 DeltaNet layers over a 9-slot state ring",
             "attn_us_per_layer": a_us, "attn_gbs": VERIFY_ATTN_BYTES / (a_us * 1e-6) / 1e9,
+            "attn_tflops": VERIFY_ATTN_FLOP / (a_us * 1e-6) / 1e12,
+            "attn_kernel": "prefill_kernel<verify> (tcgen05, 4 heads x 8 rows per tile, "
+                           "split over the key sequence) + decode_combine_kernel",
             "dn_us_per_layer": d_us, "dn_gbs": VERIFY_DN_BYTES / (d_us * 1e-6) / 1e9,
             "pass_us": a_us * N_LAYERS + d_us * 24}
 

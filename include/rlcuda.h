@@ -170,8 +170,11 @@ typedef enum {
                                  the chunked tensor-core kernel; 0 disables */
     RL_OPT_CLUSTER = 3,       /* force the cluster size (1, 2, 4, 8) of the f32 decode
                                  walk's splits (0: automatic) */
-    RL_OPT_EARLY_TILES = 4    /* bf16 decode: 64-position tiles a walk CTA streams before
+    RL_OPT_EARLY_TILES = 4,   /* bf16 decode: 64-position tiles a walk CTA streams before
                                  its inputs are loaded (1..3, default 2) */
+    RL_OPT_VERIFY_TC = 5      /* 1 (default): 2..32 rows over a bf16 cache take the
+                                 tensor-core verify kernel (bf16 P, the prefill
+                                 tolerance); 0: the exact split-KV walk */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);
@@ -203,7 +206,8 @@ typedef enum {
     RL_PROF_DN_STEP = 3,  /* DeltaNet token-sequential step */
     RL_PROF_PREFILL = 4,  /* tensor-core causal prefill attention */
     RL_PROF_DN_CHUNK = 5, /* DeltaNet chunked prefill */
-    RL_PROF_KERNELS = 6
+    RL_PROF_VERIFY = 6,   /* tensor-core multi-row verify attention */
+    RL_PROF_KERNELS = 7
 } rl_prof_kernel;
 int rl_profile_enable(rl_ctx *ctx, int on);
 int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches);

@@ -82,6 +82,11 @@ struct PrefillArgs {
     float *out;       // [t][n_head*hd]
     int *status;
     int t, pos, n_head, n_kv, context, k_row0, v_row0;
+    // verify form only: partials [t][n_head][n_splits][hd] and
+    // [t][n_head][n_splits][2] (max in log2 units, sum); split s walks key
+    // tiles s * split_tiles .. (s + 1) * split_tiles - 1
+    float *part_o, *part_ml;
+    int n_splits, split_tiles;
 };
 cudaError_t init_prefill_kernels();
 // gate_map: the prologue's bf16 sigmoid(gate) staging, laid out and boxed as
@@ -90,6 +95,13 @@ cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
                            const CUtensorMap &kv_map, const CUtensorMap &gate_map,
                            cudaStream_t st);
 constexpr int kPrefillQBoxRows = 128;
+// Multi-row verify (2..32 rows, 4 query heads per KV head) on the same
+// tensor-core tiles: one CTA per (key split, KV head), its 128 tile rows the
+// group's 4 heads x 32 rows.  vq_map: the bf16 query staging boxed 64 dims x
+// 1 head x kVerifyQBoxRows rows.  launch_decode_combine merges the partials.
+cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &vq_map,
+                             const CUtensorMap &kv_map, cudaStream_t st);
+constexpr int kVerifyQBoxRows = 32;
 
 cudaError_t init_full_attn_kernels();
 // cos/sin of every position's RoPE angles, [context][n_rot/2] each

@@ -67,6 +67,12 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// VERIFY: the multi-row verify form.  The CTA is (key split, KV head); tile
+// row r is draft row r % 32 of query head 4 * kv_head + r / 32, so the four
+// heads that share a KV head read its tiles once; the CTA walks only its
+// split's key tiles and writes an unnormalised partial (O, max, sum) per
+// (row, head) for the split merge, which applies the gate.
+template <bool VERIFY>
 __global__ void __launch_bounds__(pf::THREADS, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap q_map,
                    const __grid_constant__ CUtensorMap kv_map,
@@ -84,14 +90,26 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
 
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // heaviest query tiles first: they have the most key tiles
-    const int n_qt = (a.t + BM - 1) / BM;
-    const int qt = n_qt - 1 - (int)(blockIdx.x / a.n_head);
-    const int head = blockIdx.x % a.n_head;
-    const int kh = head / (a.n_head / a.n_kv);
-    const int q0 = qt * BM;
-    const int q_last = min(a.t, q0 + BM) - 1;              // last valid row of the tile
-    const int n_kt = (a.pos + q_last) / BN + 1;             // key tiles the tile needs
+    int head, kh, q0, j0, n_kt, split = 0;
+    if constexpr (VERIFY) {
+        kh = blockIdx.x % a.n_kv;
+        split = blockIdx.x / a.n_kv;
+        head = kh * 4;  // the group's first query head
+        q0 = 0;
+        const int n_tiles = (a.pos + a.t - 1) / BN + 1;
+        j0 = split * a.split_tiles;
+        n_kt = max(0, min(n_tiles, j0 + a.split_tiles) - j0);
+    } else {
+        // heaviest query tiles first: they have the most key tiles
+        const int n_qt = (a.t + BM - 1) / BM;
+        const int qt = n_qt - 1 - (int)(blockIdx.x / a.n_head);
+        head = blockIdx.x % a.n_head;
+        kh = head / (a.n_head / a.n_kv);
+        q0 = qt * BM;
+        const int q_last = min(a.t, q0 + BM) - 1;  // last valid row of the tile
+        j0 = 0;
+        n_kt = (a.pos + q_last) / BN + 1;           // key tiles the tile needs
+    }
     const uint32_t sbase = smem_u32(smem);
 
     if (tid == 0) {
@@ -133,8 +151,17 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 prefetch_tensormap(&q_map);
                 prefetch_tensormap(&kv_map);
                 mbar_arrive_expect_tx(&q_full, Q_BYTES);
-                for (int b = 0; b < 4; ++b)
-                    tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
+                if constexpr (VERIFY) {
+                    // 32-row boxes: head g of the group lands in tile rows
+                    // 32g..32g+31 (rows past t are computed and never stored)
+                    for (int g = 0; g < 4; ++g)
+                        for (int b = 0; b < 4; ++b)
+                            tma_load_3d(smem + b * Q_BOX + g * 32 * 128, &q_map, b * 64, head + g,
+                                        0, &q_full);
+                } else {
+                    for (int b = 0; b < 4; ++b)
+                        tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
+                }
             }
             const int row0 = (is_k ? a.k_row0 : a.v_row0) + kh * a.context;
             uint64_t *full = is_k ? k_full : v_full, *empty = is_k ? k_empty : v_empty;
@@ -148,10 +175,10 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 unsigned char *st = smem + Q_BYTES + s * STAGE + (is_k ? 0 : KV_HALF);
                 mbar_arrive_expect_tx(&full[s], KV_HALF);
                 for (int b = 0; b < 4; ++b)
-                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + j * BN, &full[s]);
+                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + (j0 + j) * BN, &full[s]);
                 issued = j + 1;
             }
-            if (is_k && issued == n_kt) {
+            if (!VERIFY && is_k && issued == n_kt) {
                 // the last Q K^T done, the query tile is free: the output gate
                 // (sigmoid, bf16, staged by the prologue) takes its place
                 if (mbar_wait(&k_empty[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, a.status)) {
@@ -226,7 +253,9 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         const int quarter = warp & 3;
         const int h = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;
-        const int qa = a.pos + q0 + r;  // absolute position of this row
+        // absolute position of this row (verify: draft row `lane` of head
+        // head + quarter)
+        const int qa = a.pos + (VERIFY ? lane : q0 + r);
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         const float scale = (1.0f / 16.0f) * LOG2E;
         const int first_masked = (a.pos + q0) / BN;  // earliest tile a row of the CTA masks
@@ -243,8 +272,8 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             uint32_t u[32];
             tc::ld32(sc + 32 * h, u);
             tc::wait_ld();
-            const int kv0 = j * BN + 32 * h;
-            if (j >= first_masked) {
+            const int kv0 = (j0 + j) * BN + 32 * h;
+            if (j0 + j >= first_masked) {
 #pragma unroll
                 for (int c = 0; c < 32; ++c)
                     if (kv0 + c > qa) u[c] = __float_as_uint(-INFINITY);
@@ -266,7 +295,9 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             auto exps = [&](float m) {
                 ps0 = 0.0f;
                 ps1 = 0.0f;
-                const float neg_m = -m;
+                // a row with every key so far masked (a verify split past
+                // the row) has m = -inf: its P is 0, not NaN
+                const float neg_m = m == -INFINITY ? 0.0f : -m;
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
                     const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * c]), scale, neg_m));
@@ -326,39 +357,65 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         mbar_arrive(&l_bar);
         if (!__all_sync(0xffffffffu, mbar_wait(&l_bar, 0, a.status))) ok = false;
         tc::fence_after_sync();
-        const float inv_l = 1.0f / (red_l[0][r] + red_l[1][r]);
-        if (ok && !__all_sync(0xffffffffu, mbar_wait(&g_full, 0, a.status))) ok = false;
-        // O / l times the gate goes through shared memory (the K/V ring, idle
-        // now) so that the output stores are whole 128-byte rows per warp:
-        // per 32-column chunk, each thread parks its row's values, then each
-        // warp walks its 32 rows with lane = column
+        const float l_row = red_l[0][r] + red_l[1][r];
+        const float inv_l = 1.0f / l_row;
+        if constexpr (VERIFY) {
+            // the split's (max, sum) of draft row `lane`, head head + quarter
+            if (h == 0 && lane < a.t && ok)
+                reinterpret_cast<float2 *>(a.part_ml)[((size_t)lane * a.n_head + head + quarter) *
+                                                          a.n_splits + split] =
+                    make_float2(m_run, l_row);
+        } else {
+            if (ok && !__all_sync(0xffffffffu, mbar_wait(&g_full, 0, a.status))) ok = false;
+        }
+        // O / l times the gate (verify: O as it stands) goes through shared
+        // memory (the K/V ring, idle now) so that the output stores are whole
+        // 128-byte rows per warp: per 32-column chunk, each thread parks its
+        // row's values, then each warp walks its 32 rows with lane = column
         const uint32_t oc = tmem + lane_off + O_COL + 128 * h;
         float *stage = reinterpret_cast<float *>(smem + Q_BYTES) + h * (BM * 33);
-        const int n_rows = max(0, min(32, a.t - (q0 + quarter * 32)));  // valid rows of this warp
+        // valid rows of this warp
+        const int n_rows = VERIFY ? min(32, a.t) : max(0, min(32, a.t - (q0 + quarter * 32)));
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
             tc::ld32(oc + c * 32, o);
             tc::wait_ld();
-            // the row's 32 gate values: 64 bytes of a swizzled 128-byte box row
             const int col0 = 128 * h + 32 * c;
-            const unsigned char *gbox = smem + (col0 >> 6) * Q_BOX;
-            uint4 gw[4];
+            if constexpr (VERIFY) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                gw[k] = *reinterpret_cast<const uint4 *>(gbox + swz128(r, ((col0 & 63) >> 3) + k));
-            const __nv_bfloat16 *gb = reinterpret_cast<const __nv_bfloat16 *>(gw);
+                for (int e = 0; e < 32; ++e) stage[r * 33 + e] = __uint_as_float(o[e]);
+            } else {
+                // the row's 32 gate values: 64 bytes of a swizzled 128-byte box row
+                const unsigned char *gbox = smem + (col0 >> 6) * Q_BOX;
+                uint4 gw[4];
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-                stage[r * 33 + e] = __uint_as_float(o[e]) * inv_l * __bfloat162float(gb[e]);
+                for (int k = 0; k < 4; ++k)
+                    gw[k] = *reinterpret_cast<const uint4 *>(gbox +
+                                                             swz128(r, ((col0 & 63) >> 3) + k));
+                const __nv_bfloat16 *gb = reinterpret_cast<const __nv_bfloat16 *>(gw);
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                    stage[r * 33 + e] = __uint_as_float(o[e]) * inv_l * __bfloat162float(gb[e]);
+            }
             __syncwarp();
             const int col = col0 + lane;
-            const size_t row0 = (size_t)(q0 + quarter * 32) * a.n_head + head;
+            if constexpr (VERIFY) {
+                const size_t hs = (size_t)(head + quarter) * a.n_splits + split;
+                const size_t row_stride = (size_t)a.n_head * a.n_splits * HD;
 #pragma unroll 8
-            for (int rr = 0; rr < 32; ++rr)
-                if (rr < n_rows && ok)
-                    __stcs(a.out + (row0 + (size_t)rr * a.n_head) * HD + col,
-                           stage[(quarter * 32 + rr) * 33 + lane]);
+                for (int rr = 0; rr < 32; ++rr)
+                    if (rr < n_rows && ok)
+                        __stcg(a.part_o + rr * row_stride + hs * HD + col,
+                               stage[(quarter * 32 + rr) * 33 + lane]);
+            } else {
+                const size_t row0 = (size_t)(q0 + quarter * 32) * a.n_head + head;
+#pragma unroll 8
+                for (int rr = 0; rr < 32; ++rr)
+                    if (rr < n_rows && ok)
+                        __stcs(a.out + (row0 + (size_t)rr * a.n_head) * HD + col,
+                               stage[(quarter * 32 + rr) * 33 + lane]);
+            }
             __syncwarp();
         }
     }
@@ -373,7 +430,10 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
 }
 
 cudaError_t init_prefill_kernels() {
-    return cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 pf::SMEM);
 }
 
@@ -381,7 +441,19 @@ cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
                            const CUtensorMap &kv_map, const CUtensorMap &gate_map,
                            cudaStream_t st) {
     const int n_qt = (a.t + pf::BM - 1) / pf::BM;
-    prefill_kernel<<<n_qt * a.n_head, pf::THREADS, pf::SMEM, st>>>(a, q_map, kv_map, gate_map);
+    prefill_kernel<false><<<n_qt * a.n_head, pf::THREADS, pf::SMEM, st>>>(a, q_map, kv_map,
+                                                                          gate_map);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &vq_map,
+                             const CUtensorMap &kv_map, cudaStream_t st) {
+    if (a.t < 1 || a.t > kVerifyQBoxRows || a.n_head != 4 * a.n_kv || a.n_splits < 1 ||
+        a.split_tiles < 1 || !a.part_o || !a.part_ml)
+        return cudaErrorInvalidValue;
+    // the gate map is not read in this form
+    prefill_kernel<true><<<a.n_splits * a.n_kv, pf::THREADS, pf::SMEM, st>>>(a, vq_map, kv_map,
+                                                                             vq_map);
     return cudaGetLastError();
 }
 

@@ -46,6 +46,8 @@ struct rl_ctx {
     // bf16 caches: TMA map of the staged bf16 queries [max_batch][n_head][hd]
     CUtensorMap q_map{};
     CUtensorMap gate_map{};
+    // the same staging boxed 32 rows high (tensor-core verify)
+    CUtensorMap vq_map{};
     // chunked DeltaNet prefill scratch (slots == 1 and max_batch >= 64)
     __nv_bfloat16 *dn_qn = nullptr, *dn_kn = nullptr, *dn_vn = nullptr;
     __nv_bfloat16 *dn_qn_lo = nullptr, *dn_kn_lo = nullptr, *dn_vn_lo = nullptr;
@@ -58,7 +60,7 @@ struct rl_ctx {
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
-    int64_t opt_early_tiles = 2;
+    int64_t opt_early_tiles = 2, opt_verify_tc = 1;
     // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
     // resident CTAs per SM of the bf16 walk: [fused]
@@ -289,6 +291,59 @@ int bf16_walk(rl_ctx *ctx, rl::DecodeArgs &d, int64_t n_kv_max, int64_t groups, 
     ctx->prev_dn = 0;
     return RL_OK;
 }
+// Tensor-core verify for t rows appended at pos (queries staged in bf16 by
+// the prologue): one CTA per (key split, KV head), as many splits as one
+// wave holds, each a whole number of 64-position tiles; the split merge
+// applies the gate.
+int verify_tc(rl_ctx *ctx, int layer, int pos, int t, const float *qg, float *out) {
+    const rl_config &c = ctx->cfg;
+    const int64_t tiles = ((int64_t)pos + t - 1) / 64 + 1;
+    int64_t splits = std::max<int64_t>(1, ctx->num_sms / c.n_head_kv);
+    if (ctx->opt_splits > 0) splits = std::min<int64_t>(splits, ctx->opt_splits);
+    splits = std::min<int64_t>(splits, tiles);
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, ctx->part_rows / t));
+    splits = std::min<int64_t>(splits, 512);
+    const int64_t per = (tiles + splits - 1) / splits;
+    splits = (tiles + per - 1) / per;  // every split holds at least one tile
+    rl::PrefillArgs pa{};
+    pa.status = ctx->status;
+    pa.t = t;
+    pa.pos = pos;
+    pa.n_head = c.n_head;
+    pa.n_kv = c.n_head_kv;
+    pa.context = c.context;
+    pa.k_row0 = layer * 2 * c.n_head_kv * c.context;
+    pa.v_row0 = pa.k_row0 + c.n_head_kv * c.context;
+    pa.part_o = ctx->part_o;
+    pa.part_ml = ctx->part_ml;
+    pa.n_splits = (int)splits;
+    pa.split_tiles = (int)per;
+    {
+        ProfScope ps(ctx, RL_PROF_VERIFY);
+        CK(ctx, rl::launch_verify_tc(pa, ctx->vq_map, ctx->kv_map, ctx->stream));
+    }
+    rl::DecodeArgs d{};
+    d.qg = qg;
+    d.part_o = ctx->part_o;
+    d.part_ml = ctx->part_ml;
+    d.out = out;
+    d.status = ctx->status;
+    d.pos = pos;
+    d.t = t;
+    d.context = c.context;
+    d.n_head = c.n_head;
+    d.n_kv = c.n_head_kv;
+    d.n_splits = (int)splits;
+    d.kv_bf16 = true;
+    d.part_out = nullptr;
+    {
+        ProfScope ps(ctx, RL_PROF_MERGE);
+        CK(ctx, rl::launch_decode_combine(d, ctx->stream));
+    }
+    ctx->early_ok = false;
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
 }  // namespace
 
 void rl::set_thread_error(const char *msg) { tl_err = msg; }
@@ -379,6 +434,10 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
                                    (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
                                    64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
                 return bail(fail(x, RL_ECUDA, "encoding the gate tensor map failed"));
+            if (rl::encode_bf16_3d(&x->vq_map, x->q_bf16, c.head_dim, c.n_head, mb,
+                                   (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
+                                   64, 1, rl::kVerifyQBoxRows) != cudaSuccess)
+                return bail(fail(x, RL_ECUDA, "encoding the verify query tensor map failed"));
         }
     }
     if (c.n_linear > 0 && c.slots == 1 && mb >= 64) {
@@ -530,6 +589,11 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     void *v_cache = (char *)k_cache + half;
     const bool fused = t == 1;
     const bool prefill = bf16 && ctx->opt_prefill_rows > 0 && t >= ctx->opt_prefill_rows;
+    // a speculative-verify batch: its rows and the group's four query heads
+    // share one tensor-core tile
+    const bool verify = bf16 && !prefill && !fused && ctx->opt_verify_tc &&
+                        t <= rl::kVerifyQBoxRows && c.n_head == 4 * c.n_head_kv;
+    const bool stage_bf16 = prefill || verify;
     if (!fused) {
         // rows of a batch attend to each other's keys: append them all first
         rl::FullArgs a{};
@@ -542,8 +606,8 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         a.v_cache = v_cache;
         a.rope_cs = ctx->rope_cs;
         a.rope_sn = ctx->rope_sn;
-        a.q_f32 = prefill ? nullptr : ctx->q_f32;
-        a.q_bf16 = prefill ? ctx->q_bf16 : nullptr;
+        a.q_f32 = stage_bf16 ? nullptr : ctx->q_f32;
+        a.q_bf16 = stage_bf16 ? ctx->q_bf16 : nullptr;
         a.gate_bf16 = prefill ? ctx->gate_bf16 : nullptr;
         a.t = t;
         a.pos = pos;
@@ -579,6 +643,7 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
             ctx->prev_dn = 0;
             return RL_OK;
         }
+        if (verify) return verify_tc(ctx, layer, pos, t, qg, out);
     }
     const int64_t n_kv_max = (int64_t)pos + t;
     const int64_t groups = (int64_t)c.n_head_kv * t;  // (KV head, row) pairs
@@ -926,6 +991,10 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
     case RL_OPT_SPLITS: ctx->opt_splits = value; return RL_OK;
     case RL_OPT_PREFILL_ROWS: ctx->opt_prefill_rows = value; return RL_OK;
     case RL_OPT_CHUNK_ROWS: ctx->opt_chunk_rows = value; return RL_OK;
+    case RL_OPT_VERIFY_TC:
+        if (value > 1) return fail(ctx, RL_EINVAL, "verify option must be 0 or 1");
+        ctx->opt_verify_tc = value;
+        return RL_OK;
     case RL_OPT_EARLY_TILES:
         if (value < 1 || value > 3) return fail(ctx, RL_EINVAL, "early tiles must be 1, 2 or 3");
         ctx->opt_early_tiles = value;
@@ -947,6 +1016,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_CHUNK_ROWS: return ctx->opt_chunk_rows;
     case RL_OPT_CLUSTER: return ctx->opt_cluster;
     case RL_OPT_EARLY_TILES: return ctx->opt_early_tiles;
+    case RL_OPT_VERIFY_TC: return ctx->opt_verify_tc;
     default: return -1;
     }
 }

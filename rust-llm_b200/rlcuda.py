@@ -24,8 +24,9 @@ LIB_PATH = os.environ.get("RLCUDA_LIB") or os.path.join(HERE, "librlcuda.so")
 RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED, RL_ENOMEM = (
     0, -1, -2, -3, -4, -5, -6, -7)
 RL_KV_F32, RL_KV_BF16 = 0, 1
-RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS, RL_OPT_CLUSTER, RL_OPT_EARLY_TILES = 0, 1, 2, 3, 4
-PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk")
+(RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS, RL_OPT_CLUSTER, RL_OPT_EARLY_TILES,
+ RL_OPT_VERIFY_TC) = 0, 1, 2, 3, 4, 5
+PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify")
 HOST, DEVICE = 0, 1
 
 _f32p = ctypes.POINTER(ctypes.c_float)
