@@ -172,7 +172,7 @@ typedef enum {
                                  walk's splits (0: automatic) */
     RL_OPT_EARLY_TILES = 4,   /* bf16 decode: 64-position tiles a walk CTA streams before
                                  its inputs are loaded (1..3, default 2) */
-    RL_OPT_VERIFY_TC = 5      /* 1 (default): 2..32 rows over a bf16 cache take the
+    RL_OPT_VERIFY_TC = 5      /* 1 (default): 2..8 rows over a bf16 cache take the
                                  tensor-core verify kernel (bf16 P, the prefill
                                  tolerance); 0: the exact split-KV walk */
 } rl_option;

@@ -171,6 +171,22 @@ __device__ __forceinline__ float rms_scale_from_sum(double sum, int n, float eps
     return 1.0f / sqrtf(__fadd_rn(mean, eps));
 }
 
+// Programmatic dependent launch: wait for the grid ahead on the stream to
+// complete (its writes visible); let the next grid on the stream launch.
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Named barrier `id` (1..15) over `n` threads (a multiple of 32).
+__device__ __forceinline__ void named_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float softplusf_(float x) {

@@ -131,13 +131,6 @@ __device__ __forceinline__ void lane_norm_rope(const LaneHead &h, float *dst, in
     __syncwarp();
 }
 
-__device__ __forceinline__ void grid_dep_wait() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void grid_dep_launch() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 template <bool FUSED>
 __global__ void __launch_bounds__(dm::THREADS, 1)
     decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ CUtensorMap kv_map) {

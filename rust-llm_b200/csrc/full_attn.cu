@@ -38,13 +38,20 @@ __device__ __forceinline__ void store8(__nv_bfloat16 *dst, const float *x) {
     *reinterpret_cast<uint4 *>(dst) = u;
 }
 
+// kv_only: the key heads alone (the verify kernel normalises its queries).
+// Each launch waits for the grid ahead (a programmatic dependent launch
+// makes that wait real) and then lets the next grid launch: when a kernel
+// starts, every kernel before the one just ahead has completed.
 template <typename KV>
 __global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_heads = a.n_head + a.n_kv;
+    const int n_heads = a.kv_only ? a.n_kv : a.n_head + a.n_kv;
     const int64_t item = (int64_t)blockIdx.x * 8 + warp;
     if (item >= (int64_t)a.t * n_heads) return;
-    const int i = (int)(item / n_heads), hh = (int)(item % n_heads), p = a.pos + i;
+    const int i = (int)(item / n_heads), p = a.pos + i;
+    const int hh = (int)(item % n_heads) + (a.kv_only ? a.n_head : 0);
     const bool is_q = hh < a.n_head;
     constexpr int HD = 256;
     const float *src = is_q ? a.qg + ((size_t)i * a.n_head + hh) * 2 * HD
@@ -137,7 +144,7 @@ __global__ void __launch_bounds__(256) full_prologue_kernel(const FullArgs a) {
 
 cudaError_t launch_full_prologue(const FullArgs &a, cudaStream_t st) {
     if (a.hd != 256 || (a.n_rot % 16) != 0) return cudaErrorInvalidValue;
-    const int64_t items = (int64_t)a.t * (a.n_head + a.n_kv);
+    const int64_t items = (int64_t)a.t * (a.kv_only ? a.n_kv : a.n_head + a.n_kv);
     const unsigned blocks = (unsigned)((items + 7) / 8);
     if (a.kv_bf16)
         full_prologue_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(a);

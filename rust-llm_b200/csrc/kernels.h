@@ -22,6 +22,9 @@ struct FullArgs {
     int t, pos, n_head, n_kv, hd, context, n_rot;
     float theta_scale, eps;
     bool kv_bf16;
+    // append the rows' keys and values only (the queries are normalised
+    // inside the tensor-core verify kernel)
+    bool kv_only;
 };
 
 // One launch of the split-KV decode kernel (decode_attn.cu).
@@ -87,6 +90,16 @@ struct PrefillArgs {
     // tiles s * split_tiles .. (s + 1) * split_tiles - 1
     float *part_o, *part_ml;
     int n_splits, split_tiles;
+    // verify form only: the raw rows (query | gate), the query norm weight,
+    // the RoPE table and eps; the kernel normalises and rotates the queries
+    // itself (n_rot 64)
+    const float *qg, *q_norm, *rope_cs, *rope_sn;
+    float eps;
+    // verify form only: the rows' raw keys and values [t][n_kv][hd], the key
+    // norm weight and this layer's bf16 caches [n_kv][context][hd]; the CTA
+    // whose key range holds a new position appends that row itself
+    const float *k_in, *v_in, *k_norm;
+    __nv_bfloat16 *k_cache, *v_cache;
 };
 cudaError_t init_prefill_kernels();
 // gate_map: the prologue's bf16 sigmoid(gate) staging, laid out and boxed as
@@ -95,13 +108,13 @@ cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
                            const CUtensorMap &kv_map, const CUtensorMap &gate_map,
                            cudaStream_t st);
 constexpr int kPrefillQBoxRows = 128;
-// Multi-row verify (2..32 rows, 4 query heads per KV head) on the same
-// tensor-core tiles: one CTA per (key split, KV head), its 128 tile rows the
-// group's 4 heads x 32 rows.  vq_map: the bf16 query staging boxed 64 dims x
-// 1 head x kVerifyQBoxRows rows.  launch_decode_combine merges the partials.
-cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &vq_map,
-                             const CUtensorMap &kv_map, cudaStream_t st);
-constexpr int kVerifyQBoxRows = 32;
+// Multi-row verify (1..8 rows, 4 query heads per KV head, n_rot 64) on the
+// same tensor-core tiles: one CTA per (key split, KV head), its 128 tile rows
+// the group's 4 heads x 32 rows (rows 8..31 of each head padding).  The
+// kernel appends the rows' keys and values and normalises the queries
+// itself; launch_decode_combine merges the partials.
+cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &kv_map, cudaStream_t st);
+constexpr int kVerifyRows = 8;
 
 cudaError_t init_full_attn_kernels();
 // cos/sin of every position's RoPE angles, [context][n_rot/2] each

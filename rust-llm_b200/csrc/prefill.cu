@@ -46,8 +46,13 @@ constexpr int Q_BYTES = 4 * Q_BOX;
 constexpr int KV_HALF = 4 * KV_BOX;  // K (or V) of one tile
 constexpr int STAGE = 2 * KV_HALF;
 constexpr int SMEM = Q_BYTES + 2 * STAGE + 1024;
+// verify form: the queries live in tensor memory, so the ring takes a third
+// K/V stage instead
+constexpr int QSTAGE = 3 * STAGE;               // verify: 4 x 8 query rows of 512 B
+constexpr int SMEM_VERIFY = QSTAGE + 32 * 512 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t O_COL = 0, S_COL = 256;
+constexpr uint32_t Q_COL = 384;  // verify: Q, bf16 pairs, 128 columns
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_LOG2 = 12.0f;  // P up to 2^12: no range issue in bf16 or f32
 }  // namespace pf
@@ -56,6 +61,27 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// A 16-byte global load issued where it stands: volatile asm keeps a batch of
+// them in program order ahead of the code that consumes them.
+__device__ __forceinline__ float4 ld_nc_f4(const float *p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+// Shared -> global bulk copy (16-byte aligned addresses, size a multiple of
+// 16) in the calling thread's bulk group.
+__device__ __forceinline__ void bulk_store(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_and_wait() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y,
@@ -79,8 +105,11 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                    const __grid_constant__ CUtensorMap gate_map) {
     using namespace pf;
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2],
-        s_full[2], p_full[2], o_ready, o_final, g_full;
+    // ring of NST K/V stages (verify: 3, the queries sit in tensor memory)
+    constexpr int NST = VERIFY ? 3 : 2;
+    constexpr int RING = VERIFY ? 0 : Q_BYTES;  // byte offset of the ring
+    __shared__ __align__(8) uint64_t q_full, k_full[NST], v_full[NST], k_empty[NST],
+        v_empty[NST], s_full[2], p_full[2], o_ready, o_final, g_full, kv_app, q_iss;
     __shared__ uint32_t tmem_base_s;
     __shared__ int flag_s;
     __shared__ float red_m[2][2][BM], red_l[2][BM];  // the two halves of each row
@@ -113,18 +142,23 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     const uint32_t sbase = smem_u32(smem);
 
     if (tid == 0) {
-        mbar_init(&q_full, 1);
-        for (int s = 0; s < 2; ++s) {
+        // verify: the eight softmax warps write the queries and arrive
+        mbar_init(&q_full, VERIFY ? 8 : 1);
+        for (int s = 0; s < NST; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
             mbar_init(&k_empty[s], 1);
             mbar_init(&v_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(&s_full[s], 1);
             mbar_init(&p_full[s], 8);
         }
         mbar_init(&o_ready, 1);
         mbar_init(&o_final, 1);
         mbar_init(&g_full, 1);
+        mbar_init(&kv_app, 8);
+        mbar_init(&q_iss, 8);
         mbar_init(&mx_bar[0], 256);
         mbar_init(&mx_bar[1], 256);
         mbar_init(&l_bar, 256);
@@ -139,6 +173,11 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_base_s;
+    // verify: launched as a programmatic dependent, so the set-up above
+    // overlaps the grid ahead; nothing is read before that grid completes
+    if constexpr (VERIFY) grid_dep_wait();
+    // verify: this CTA's key range holds positions of the appended rows
+    const bool appends = VERIFY && (j0 + n_kt) * BN > a.pos;
 
     if (warp == 0 || warp == 10) {
         // ---------------- TMA producers ----------------
@@ -147,32 +186,36 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         // warps, so K runs ahead of V by as much as the slots allow.
         if (lane == 0) {
             const bool is_k = warp == 0;
-            if (is_k) {
+            prefetch_tensormap(&kv_map);
+            if (is_k && !VERIFY) {
                 prefetch_tensormap(&q_map);
-                prefetch_tensormap(&kv_map);
                 mbar_arrive_expect_tx(&q_full, Q_BYTES);
-                if constexpr (VERIFY) {
-                    // 32-row boxes: head g of the group lands in tile rows
-                    // 32g..32g+31 (rows past t are computed and never stored)
-                    for (int g = 0; g < 4; ++g)
-                        for (int b = 0; b < 4; ++b)
-                            tma_load_3d(smem + b * Q_BOX + g * 32 * 128, &q_map, b * 64, head + g,
-                                        0, &q_full);
-                } else {
-                    for (int b = 0; b < 4; ++b)
-                        tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
-                }
+                for (int b = 0; b < 4; ++b)
+                    tma_load_3d(smem + b * Q_BOX, &q_map, b * 64, head, q0, &q_full);
             }
             const int row0 = (is_k ? a.k_row0 : a.v_row0) + kh * a.context;
             uint64_t *full = is_k ? k_full : v_full, *empty = is_k ? k_empty : v_empty;
             int issued = 0;
+            bool appended_visible = !appends;
+            // verify: the query loads go out ahead of the tile stream (they
+            // would queue behind every CTA's first burst of copies)
+            if (VERIFY && !mbar_wait(&q_iss, 0, a.status)) flag_s = 1;
             for (int j = 0; j < n_kt; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&empty[s], ((j >> 1) - 1) & 1, a.status)) {
+                const int s = j % NST;
+                if (j >= NST && !mbar_wait(&empty[s], (j / NST - 1) & 1, a.status)) {
                     flag_s = 1;
                     break;
                 }
-                unsigned char *st = smem + Q_BYTES + s * STAGE + (is_k ? 0 : KV_HALF);
+                if (!appended_visible && (j0 + j + 1) * BN > a.pos) {
+                    // this tile holds appended rows: the softmax warps have
+                    // written them to the cache
+                    if (!mbar_wait(&kv_app, 0, a.status)) {
+                        flag_s = 1;
+                        break;
+                    }
+                    appended_visible = true;
+                }
+                unsigned char *st = smem + RING + s * STAGE + (is_k ? 0 : KV_HALF);
                 mbar_arrive_expect_tx(&full[s], KV_HALF);
                 for (int b = 0; b < 4; ++b)
                     tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + (j0 + j) * BN, &full[s]);
@@ -192,9 +235,9 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 }
             }
             // everything started has landed before the CTA releases its memory
-            if (is_k) mbar_wait(&q_full, 0, a.status);
-            for (int j = max(0, issued - 2); j < issued; ++j)
-                mbar_wait(&full[j & 1], (j >> 1) & 1, a.status);
+            if (is_k && !VERIFY) mbar_wait(&q_full, 0, a.status);
+            for (int j = max(0, issued - NST); j < issued; ++j)
+                mbar_wait(&full[j % NST], (j / NST) & 1, a.status);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -205,31 +248,37 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             tc::fence_after_sync();
             for (int j = 0; ok && j <= n_kt; ++j) {
                 if (j < n_kt) {
-                    const int s = j & 1;
-                    if (!mbar_wait(&k_full[s], (j >> 1) & 1, a.status)) { ok = false; break; }
+                    const int s = j % NST, sb = j & 1;  // ring slot, S buffer
+                    if (!mbar_wait(&k_full[s], (j / NST) & 1, a.status)) { ok = false; break; }
                     tc::fence_after_sync();
-                    const uint32_t kst = sbase + Q_BYTES + s * STAGE;
-                    const uint32_t d = tmem + S_COL + s * BN;
+                    const uint32_t kst = sbase + RING + s * STAGE;
+                    const uint32_t d = tmem + S_COL + sb * BN;
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk) {
                         const uint32_t off = (kk & 3) * 32;  // 16 dims inside a 64-dim box
-                        const uint64_t da = tc::smem_desc(sbase + (kk >> 2) * Q_BOX + off, 16, 1024);
                         const uint64_t db = tc::smem_desc(kst + (kk >> 2) * KV_BOX + off, 16, 1024);
-                        tc::mma_ss(d, da, db, id_qk, kk > 0);
+                        if constexpr (VERIFY) {
+                            // A = Q from tensor memory: 16 dims are 8 columns
+                            tc::mma_ts(d, tmem + Q_COL + kk * 8, db, id_qk, kk > 0);
+                        } else {
+                            const uint64_t da =
+                                tc::smem_desc(sbase + (kk >> 2) * Q_BOX + off, 16, 1024);
+                            tc::mma_ss(d, da, db, id_qk, kk > 0);
+                        }
                     }
-                    tc::commit(&s_full[s]);
+                    tc::commit(&s_full[sb]);
                     tc::commit(&k_empty[s]);
                 }
                 if (j >= 1) {
-                    const int jj = j - 1, s = jj & 1;
-                    if (!mbar_wait(&p_full[s], (jj >> 1) & 1, a.status) ||
-                        !mbar_wait(&v_full[s], (jj >> 1) & 1, a.status)) {
+                    const int jj = j - 1, s = jj % NST, sb = jj & 1;
+                    if (!mbar_wait(&p_full[sb], (jj >> 1) & 1, a.status) ||
+                        !mbar_wait(&v_full[s], (jj / NST) & 1, a.status)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t vst = sbase + Q_BYTES + s * STAGE + KV_HALF;
-                    const uint32_t p = tmem + S_COL + s * BN;
+                    const uint32_t vst = sbase + RING + s * STAGE + KV_HALF;
+                    const uint32_t p = tmem + S_COL + sb * BN;
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk) {
                         const uint64_t db = tc::smem_desc(vst + kk * 16 * 128, KV_BOX, 1024);
@@ -261,6 +310,161 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         const int first_masked = (a.pos + q0) / BN;  // earliest tile a row of the CTA masks
         float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
+        if constexpr (VERIFY) {
+            // ---- the query rows, straight from the raw f32 input: per-head
+            // RMSNorm (f32 squares summed in f64, forward.rs:1697-1711) and
+            // RoPE on the first 64 dims with the context's angle table
+            // (:1851-1862), as bf16 pairs into tensor memory.  The 256
+            // softmax threads each take 32 dims of one (head, row) of the
+            // group's 4 heads x 8 rows, with all their loads in flight at
+            // once (the eight threads of a row meet by shuffles: the sum of
+            // squares, and dims d, d + 32 for the rotation), park the result
+            // in shared memory, and each row's owner moves its 64 columns to
+            // tensor memory; rows past t are zeros.
+            uint32_t *qstage = reinterpret_cast<uint32_t *>(smem + QSTAGE);
+            // lane l of a row's eight threads holds dims 4l + 32j + e (j < 8,
+            // e < 4): each load instruction reads whole 128-byte segments,
+            // and the rotation pairs (d, d + 32) sit in one thread
+            const int ts = tid - 64, l8 = ts & 7, rv = ts >> 3;  // lane in row, row slot
+            const int g = rv >> 3;                                  // head in the group
+            {
+                const int i = rv & 7;
+                const bool real = i < a.t;
+                const float *src =
+                    a.qg + ((size_t)(real ? i : 0) * a.n_head + head + g) * 2 * HD + 4 * l8;
+                const float *wq = a.q_norm + 4 * l8;
+                const int pr = real ? a.pos + i : a.pos;
+                float x[32], w[32];
+                // every load of the phase in one batch (rows past t read row
+                // 0 and are zeroed after)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 xv = ld_nc_f4(src + 32 * j), wv = ld_nc_f4(wq + 32 * j);
+                    x[4 * j] = xv.x, x[4 * j + 1] = xv.y, x[4 * j + 2] = xv.z, x[4 * j + 3] = xv.w;
+                    w[4 * j] = wv.x, w[4 * j + 1] = wv.y, w[4 * j + 2] = wv.z, w[4 * j + 3] = wv.w;
+                }
+                const float4 cv = ld_nc_f4(a.rope_cs + (size_t)pr * 32 + 4 * l8);
+                const float4 sv = ld_nc_f4(a.rope_sn + (size_t)pr * 32 + 4 * l8);
+                // issued, not yet arrived: the tile stream may start
+                __syncwarp();
+                if (lane == 0)
+                    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(
+                                     smem_u32(&q_iss))
+                                 : "memory");
+                if (!real) {
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) x[k] = 0.0f;
+                }
+                double sq = 0.0;
+#pragma unroll
+                for (int k = 0; k < 32; ++k) sq += (double)__fmul_rn(x[k], x[k]);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+                const float qs = rms_scale_from_sum(sq, HD, a.eps);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) x[k] = __fmul_rn(__fmul_rn(x[k], qs), w[k]);
+                // dims 4l + e (x[e]) rotate with 4l + 32 + e (x[4 + e])
+                const float c4[4] = {cv.x, cv.y, cv.z, cv.w}, s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float lo = x[e], hi = x[4 + e];
+                    x[e] = __fsub_rn(__fmul_rn(lo, c4[e]), __fmul_rn(hi, s4[e]));
+                    x[4 + e] = __fadd_rn(__fmul_rn(lo, s4[e]), __fmul_rn(hi, c4[e]));
+                }
+                // bf16 pairs: dims 4l + 32j + {0,1}, {2,3} are the row's
+                // columns 16j + 2l, 16j + 2l + 1
+                uint32_t *dst = qstage + rv * 128 + 2 * l8;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    __nv_bfloat162 b0 = __floats2bfloat162_rn(x[4 * j], x[4 * j + 1]);
+                    __nv_bfloat162 b1 = __floats2bfloat162_rn(x[4 * j + 2], x[4 * j + 3]);
+                    *reinterpret_cast<uint2 *>(dst + 16 * j) =
+                        make_uint2(*reinterpret_cast<uint32_t *>(&b0),
+                                   *reinterpret_cast<uint32_t *>(&b1));
+                }
+            }
+            named_sync(1, 256);
+            // the owner of tile row (head quarter, draft row lane) moves it
+            const uint32_t qcol = tmem + lane_off + Q_COL + 64 * h;
+            const uint32_t *row = qstage + (quarter * 8 + (lane & 7)) * 128 + 64 * h;
+#pragma unroll
+            for (int half32 = 0; half32 < 2; ++half32) {
+                uint32_t qreg[32];
+#pragma unroll
+                for (int k = 0; k < 32; k += 4) {
+                    const uint4 u = lane < a.t
+                                        ? *reinterpret_cast<const uint4 *>(row + 32 * half32 + k)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+                    qreg[k] = u.x, qreg[k + 1] = u.y, qreg[k + 2] = u.z, qreg[k + 3] = u.w;
+                }
+                tc::st32(qcol + 32 * half32, qreg);
+            }
+            tc::wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_full);
+            if (appends) {
+                // ---- the rows' keys and values (forward.rs:1262-1292): one
+                // warp per appended row in this CTA's key range, 8 dims a
+                // lane; the key gets the RMSNorm and RoPE of the queries,
+                // both go to the cache in bf16
+                const int i = warp - 2, p = a.pos + i;
+                if (i < a.t && p >= j0 * BN && p < (j0 + n_kt) * BN) {
+                    const float *kr = a.k_in + ((size_t)i * a.n_kv + kh) * HD + lane * 8;
+                    const float *vr = a.v_in + ((size_t)i * a.n_kv + kh) * HD + lane * 8;
+                    const float4 k0 = ld_nc_f4(kr), k1 = ld_nc_f4(kr + 4);
+                    const float4 v0 = ld_nc_f4(vr), v1 = ld_nc_f4(vr + 4);
+                    const float4 w0 = ld_nc_f4(a.k_norm + lane * 8), w1 = ld_nc_f4(a.k_norm + lane * 8 + 4);
+                    const int pr = (lane * 8) & 31;  // RoPE pair index of the first dim (lanes 0-7)
+                    const float *cs = a.rope_cs + (size_t)p * 32 + pr, *sn = a.rope_sn + (size_t)p * 32 + pr;
+                    const float4 c0 = ld_nc_f4(cs), c1 = ld_nc_f4(cs + 4);
+                    const float4 s0 = ld_nc_f4(sn), s1 = ld_nc_f4(sn + 4);
+                    const float kx[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+                    const float wx[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    const float cx[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    const float sx[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                    double sq = 0.0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) sq += (double)__fmul_rn(kx[e], kx[e]);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                    const float ks = rms_scale_from_sum(sq, HD, a.eps);
+                    float y[8], rk[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) y[e] = __fmul_rn(__fmul_rn(kx[e], ks), wx[e]);
+                    // dims d < 32 (lanes 0-3) rotate with d + 32 (lanes 4-7)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float up = __shfl_down_sync(0xffffffffu, y[e], 4);
+                        const float dn = __shfl_up_sync(0xffffffffu, y[e], 4);
+                        rk[e] = y[e];
+                        if (lane < 4)
+                            rk[e] = __fsub_rn(__fmul_rn(y[e], cx[e]), __fmul_rn(up, sx[e]));
+                        else if (lane < 8)
+                            rk[e] = __fadd_rn(__fmul_rn(dn, sx[e]), __fmul_rn(y[e], cx[e]));
+                    }
+                    const float vx[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                    uint4 ku, vu;
+                    uint32_t *kp = &ku.x, *vp = &vu.x;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        __nv_bfloat162 kb = __floats2bfloat162_rn(rk[2 * e], rk[2 * e + 1]);
+                        __nv_bfloat162 vb = __floats2bfloat162_rn(vx[2 * e], vx[2 * e + 1]);
+                        kp[e] = *reinterpret_cast<uint32_t *>(&kb);
+                        vp[e] = *reinterpret_cast<uint32_t *>(&vb);
+                    }
+                    const size_t row = ((size_t)kh * a.context + p) * HD + lane * 8;
+                    *reinterpret_cast<uint4 *>(a.k_cache + row) = ku;
+                    *reinterpret_cast<uint4 *>(a.v_cache + row) = vu;
+                    // the tensor-copy loads of this CTA read the rows next
+                    __threadfence();
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&kv_app);
+            }
+        }
         for (int j = 0; j < n_kt; ++j) {
             const int s = j & 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, a.status))) {
@@ -368,24 +572,51 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         } else {
             if (ok && !__all_sync(0xffffffffu, mbar_wait(&g_full, 0, a.status))) ok = false;
         }
-        // O / l times the gate (verify: O as it stands) goes through shared
-        // memory (the K/V ring, idle now) so that the output stores are whole
-        // 128-byte rows per warp: per 32-column chunk, each thread parks its
-        // row's values, then each warp walks its 32 rows with lane = column
         const uint32_t oc = tmem + lane_off + O_COL + 128 * h;
-        float *stage = reinterpret_cast<float *>(smem + Q_BYTES) + h * (BM * 33);
-        // valid rows of this warp
-        const int n_rows = VERIFY ? min(32, a.t) : max(0, min(32, a.t - (q0 + quarter * 32)));
+        if constexpr (VERIFY) {
+            // O as it stands (the merge normalises and gates): the real rows
+            // park in the idle ring as [head][row][260 floats] (rows padded
+            // off one bank), then one thread sends each 1 KiB row to its
+            // partial slot with a bulk copy
+            constexpr int OSTRIDE = 260;
+            float *ost = reinterpret_cast<float *>(smem + RING);
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tc::ld32(oc + c * 32, o);
-            tc::wait_ld();
-            const int col0 = 128 * h + 32 * c;
-            if constexpr (VERIFY) {
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tc::ld32(oc + c * 32, o);
+                tc::wait_ld();
+                if (lane < a.t) {
+                    float *dst = ost + (quarter * 8 + lane) * OSTRIDE + 128 * h + 32 * c;
 #pragma unroll
-                for (int e = 0; e < 32; ++e) stage[r * 33 + e] = __uint_as_float(o[e]);
-            } else {
+                    for (int e = 0; e < 32; e += 4)
+                        *reinterpret_cast<float4 *>(dst + e) =
+                            make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
+                                        __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            named_sync(1, 256);
+            if (tid == 64 && ok) {
+                for (int g = 0; g < 4; ++g)
+                    for (int i = 0; i < a.t; ++i)
+                        bulk_store(a.part_o +
+                                       (((size_t)i * a.n_head + head + g) * a.n_splits + split) * HD,
+                                   ost + (g * 8 + i) * OSTRIDE, HD * 4);
+                bulk_commit_and_wait();
+            }
+        } else {
+            // O / l times the gate goes through shared memory (the K/V ring,
+            // idle now) so that the output stores are whole 128-byte rows per
+            // warp: per 32-column chunk, each thread parks its row's values,
+            // then each warp walks its 32 rows with lane = column
+            float *stage = reinterpret_cast<float *>(smem + RING) + h * (BM * 33);
+            const int n_rows = max(0, min(32, a.t - (q0 + quarter * 32)));  // valid rows
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tc::ld32(oc + c * 32, o);
+                tc::wait_ld();
+                const int col0 = 128 * h + 32 * c;
                 // the row's 32 gate values: 64 bytes of a swizzled 128-byte box row
                 const unsigned char *gbox = smem + (col0 >> 6) * Q_BOX;
                 uint4 gw[4];
@@ -397,31 +628,23 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
 #pragma unroll
                 for (int e = 0; e < 32; ++e)
                     stage[r * 33 + e] = __uint_as_float(o[e]) * inv_l * __bfloat162float(gb[e]);
-            }
-            __syncwarp();
-            const int col = col0 + lane;
-            if constexpr (VERIFY) {
-                const size_t hs = (size_t)(head + quarter) * a.n_splits + split;
-                const size_t row_stride = (size_t)a.n_head * a.n_splits * HD;
-#pragma unroll 8
-                for (int rr = 0; rr < 32; ++rr)
-                    if (rr < n_rows && ok)
-                        __stcg(a.part_o + rr * row_stride + hs * HD + col,
-                               stage[(quarter * 32 + rr) * 33 + lane]);
-            } else {
+                __syncwarp();
+                const int col = col0 + lane;
                 const size_t row0 = (size_t)(q0 + quarter * 32) * a.n_head + head;
 #pragma unroll 8
                 for (int rr = 0; rr < 32; ++rr)
                     if (rr < n_rows && ok)
                         __stcs(a.out + (row0 + (size_t)rr * a.n_head) * HD + col,
                                stage[(quarter * 32 + rr) * 33 + lane]);
+                __syncwarp();
             }
-            __syncwarp();
         }
     }
 
     tc::fence_before_sync();
     __syncthreads();
+    // verify: the partials are written; the split merge may launch
+    if constexpr (VERIFY) grid_dep_launch();
     if (warp == 1) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, TMEM_COLS);
@@ -434,7 +657,7 @@ cudaError_t init_prefill_kernels() {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                pf::SMEM);
+                                pf::SMEM_VERIFY);
 }
 
 cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
@@ -446,15 +669,23 @@ cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
     return cudaGetLastError();
 }
 
-cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &vq_map,
-                             const CUtensorMap &kv_map, cudaStream_t st) {
-    if (a.t < 1 || a.t > kVerifyQBoxRows || a.n_head != 4 * a.n_kv || a.n_splits < 1 ||
-        a.split_tiles < 1 || !a.part_o || !a.part_ml)
+cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &kv_map, cudaStream_t st) {
+    if (a.t < 1 || a.t > kVerifyRows || a.n_head != 4 * a.n_kv || a.n_splits < 1 ||
+        a.split_tiles < 1 || !a.part_o || !a.part_ml || !a.qg || !a.q_norm || !a.rope_cs ||
+        !a.rope_sn || !a.k_in || !a.v_in || !a.k_norm || !a.k_cache || !a.v_cache)
         return cudaErrorInvalidValue;
-    // the gate map is not read in this form
-    prefill_kernel<true><<<a.n_splits * a.n_kv, pf::THREADS, pf::SMEM, st>>>(a, vq_map, kv_map,
-                                                                             vq_map);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_splits * a.n_kv);
+    cfg.blockDim = dim3(pf::THREADS);
+    cfg.dynamicSmemBytes = pf::SMEM_VERIFY;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // the query and gate maps are not read in this form
+    return cudaLaunchKernelEx(&cfg, prefill_kernel<true>, a, kv_map, kv_map, kv_map);
 }
 
 }  // namespace rl

@@ -46,8 +46,6 @@ struct rl_ctx {
     // bf16 caches: TMA map of the staged bf16 queries [max_batch][n_head][hd]
     CUtensorMap q_map{};
     CUtensorMap gate_map{};
-    // the same staging boxed 32 rows high (tensor-core verify)
-    CUtensorMap vq_map{};
     // chunked DeltaNet prefill scratch (slots == 1 and max_batch >= 64)
     __nv_bfloat16 *dn_qn = nullptr, *dn_kn = nullptr, *dn_vn = nullptr;
     __nv_bfloat16 *dn_qn_lo = nullptr, *dn_kn_lo = nullptr, *dn_vn_lo = nullptr;
@@ -291,11 +289,12 @@ int bf16_walk(rl_ctx *ctx, rl::DecodeArgs &d, int64_t n_kv_max, int64_t groups, 
     ctx->prev_dn = 0;
     return RL_OK;
 }
-// Tensor-core verify for t rows appended at pos (queries staged in bf16 by
-// the prologue): one CTA per (key split, KV head), as many splits as one
-// wave holds, each a whole number of 64-position tiles; the split merge
-// applies the gate.
-int verify_tc(rl_ctx *ctx, int layer, int pos, int t, const float *qg, float *out) {
+// Tensor-core verify for t rows appended at pos (the kernel appends their
+// keys and values and normalises and rotates the queries itself): one CTA
+// per (key split, KV head), as many splits as one wave holds, each a whole
+// number of 64-position tiles; the split merge applies the gate.
+int verify_tc(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const float *k,
+              const float *v, float *out) {
     const rl_config &c = ctx->cfg;
     const int64_t tiles = ((int64_t)pos + t - 1) / 64 + 1;
     int64_t splits = std::max<int64_t>(1, ctx->num_sms / c.n_head_kv);
@@ -318,9 +317,19 @@ int verify_tc(rl_ctx *ctx, int layer, int pos, int t, const float *qg, float *ou
     pa.part_ml = ctx->part_ml;
     pa.n_splits = (int)splits;
     pa.split_tiles = (int)per;
+    pa.qg = qg;
+    pa.q_norm = ctx->q_norm + (size_t)layer * c.head_dim;
+    pa.rope_cs = ctx->rope_cs;
+    pa.rope_sn = ctx->rope_sn;
+    pa.eps = c.rms_eps;
+    pa.k_in = k;
+    pa.v_in = v;
+    pa.k_norm = ctx->k_norm + (size_t)layer * c.head_dim;
+    pa.k_cache = static_cast<__nv_bfloat16 *>(kv_layer(ctx, layer));
+    pa.v_cache = pa.k_cache + (size_t)c.n_head_kv * c.context * c.head_dim;
     {
         ProfScope ps(ctx, RL_PROF_VERIFY);
-        CK(ctx, rl::launch_verify_tc(pa, ctx->vq_map, ctx->kv_map, ctx->stream));
+        CK(ctx, rl::launch_verify_tc(pa, ctx->kv_map, ctx->stream));
     }
     rl::DecodeArgs d{};
     d.qg = qg;
@@ -434,10 +443,6 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
                                    (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
                                    64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
                 return bail(fail(x, RL_ECUDA, "encoding the gate tensor map failed"));
-            if (rl::encode_bf16_3d(&x->vq_map, x->q_bf16, c.head_dim, c.n_head, mb,
-                                   (uint64_t)c.head_dim * 2, (uint64_t)c.head_dim * 2 * c.n_head,
-                                   64, 1, rl::kVerifyQBoxRows) != cudaSuccess)
-                return bail(fail(x, RL_ECUDA, "encoding the verify query tensor map failed"));
         }
     }
     if (c.n_linear > 0 && c.slots == 1 && mb >= 64) {
@@ -592,8 +597,9 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
     // a speculative-verify batch: its rows and the group's four query heads
     // share one tensor-core tile
     const bool verify = bf16 && !prefill && !fused && ctx->opt_verify_tc &&
-                        t <= rl::kVerifyQBoxRows && c.n_head == 4 * c.n_head_kv;
-    const bool stage_bf16 = prefill || verify;
+                        t <= rl::kVerifyRows && c.n_head == 4 * c.n_head_kv && c.n_rot == 64;
+    // the verify kernel appends the rows and normalises the queries itself
+    if (verify) return verify_tc(ctx, layer, pos, t, qg, k, v, out);
     if (!fused) {
         // rows of a batch attend to each other's keys: append them all first
         rl::FullArgs a{};
@@ -606,8 +612,8 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
         a.v_cache = v_cache;
         a.rope_cs = ctx->rope_cs;
         a.rope_sn = ctx->rope_sn;
-        a.q_f32 = stage_bf16 ? nullptr : ctx->q_f32;
-        a.q_bf16 = stage_bf16 ? ctx->q_bf16 : nullptr;
+        a.q_f32 = prefill ? nullptr : ctx->q_f32;
+        a.q_bf16 = prefill ? ctx->q_bf16 : nullptr;
         a.gate_bf16 = prefill ? ctx->gate_bf16 : nullptr;
         a.t = t;
         a.pos = pos;
@@ -643,7 +649,6 @@ int rl_full_attn(rl_ctx *ctx, int layer, int pos, int t, const float *qg, const 
             ctx->prev_dn = 0;
             return RL_OK;
         }
-        if (verify) return verify_tc(ctx, layer, pos, t, qg, out);
     }
     const int64_t n_kv_max = (int64_t)pos + t;
     const int64_t groups = (int64_t)c.n_head_kv * t;  // (KV head, row) pairs
