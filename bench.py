@@ -540,6 +540,86 @@ def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
             "gather_bytes_per_gpu_per_layer": N_HEAD * (HD + 2) * 4}
 
 
+BATCH_SEQS, BATCH_LO, BATCH_HI = 64, 4096, 32768
+
+
+def batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
+    """Config 4b: 64 independent sequences, contexts U[4096, 32768] (seed 5),
+    dealt to the job's GPUs longest first (no collective); one decode row per
+    sequence through 8 bf16 full-attention layers, one rl_ctx per sequence as
+    the reference's Runner holds one sequence, CUDA-graph captured.  Returns
+    µs per layer-step of the whole batch (max over ranks) and the aggregate
+    HBM rate of the cache bytes."""
+    import numpy as np
+    import split_kv
+    lens = [int(x) for x in np.random.default_rng(5).integers(BATCH_LO, BATCH_HI + 1,
+                                                              BATCH_SEQS)]
+    mine = split_kv.partition_sequences(lens, world)[rank]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5 + rank)
+    ctxs = []
+    for i in mine:
+        cfg = rlcuda.qwen35_config(n_full=N_LAYERS, n_linear=0, context=lens[i] + 1,
+                                   kv_dtype=rlcuda.RL_KV_BF16, max_batch=1)
+        c = rlcuda.Context(cfg, device=dev.index)
+        c.set_stream(stream.cuda_stream)
+        src = torch.randn((2, N_KV, lens[i], HD), generator=gen, device=dev)
+        for layer in range(N_LAYERS):
+            c.write_kv(layer, 0, src)
+        del src
+        ctxs.append(c)
+    torch.cuda.empty_cache()
+    qg = torch.randn((N_HEAD * 2 * HD,), generator=gen, device=dev)
+    kk = torch.randn((N_KV * HD,), generator=gen, device=dev)
+    vv = torch.randn((N_KV * HD,), generator=gen, device=dev)
+    outs = torch.empty((len(mine), N_HEAD * HD), device=dev)
+
+    def step():
+        for layer in range(N_LAYERS):
+            for j, i in enumerate(mine):
+                ctxs[j].full_attn(layer, lens[i], 1, qg, kk, vv, outs[j])
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    reps = max(3, min(args.steps // 50, 20))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    graph.reset()
+    for c in ctxs:
+        c.sync()
+        c.close()
+    torch.cuda.empty_cache()
+    us = ms * 1e3 / (reps * N_LAYERS)
+    total = sum(lens) * 2 * N_KV * HD * 2  # cache bytes of one layer over the batch
+    return {"workload": f"config 4b: {BATCH_SEQS} sequences, contexts U[{BATCH_LO}, {BATCH_HI}] "
+                        f"(seed 5), 8 bf16 full-attention layers, longest-first over {world} "
+                        "GPU(s), no collective",
+            "scaling": "strong", "sequences_per_gpu": len(mine),
+            "us_per_layer_step": us, "kv_bytes_per_layer": total,
+            "hbm_gbs_aggregate": total / (us * 1e-6) / 1e9,
+            "launches_per_step": 2 * N_LAYERS * len(mine)}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -678,6 +758,8 @@ def run_ours(args):
     pf = prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
     dnpf = dn_prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
     ver = verify_bench(args, dev, stream, rlcuda, torch) if not args.no_verify else None
+    batch = (batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist)
+             if not args.no_batch else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -707,6 +789,7 @@ def run_ours(args):
         "config2_attention_ms": ((pf["us_per_layer"] * PF_LAYERS + dnpf["us_per_layer"] *
                                   DN_PF_LAYERS) / 1e3 if pf and dnpf else None),
         "split_kv": split,
+        "batch_4b": batch,
         "dn_step": dn,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -738,6 +821,8 @@ def main():
     ap.add_argument("--no-dn", action="store_true", help="skip the DeltaNet step section")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill section")
     ap.add_argument("--no-verify", action="store_true", help="skip the speculative-verify section")
+    ap.add_argument("--no-batch", action="store_true",
+                    help="skip the config-4b batched multi-sequence section")
     ap.add_argument("--no-split", action="store_true",
                     help="skip the long-context split-sequence section")
     ap.add_argument("--layers", type=int, default=N_LAYERS,

@@ -96,3 +96,19 @@ class GpuShard:
 
     def merge(self, parts, qg, out):
         self.ctx.merge_partials(parts, qg, out)
+
+
+def partition_sequences(lengths, world: int) -> list[list[int]]:
+    """Independent sequences of a batch over `world` GPUs, no collective:
+    longest first, each to the GPU with the least total context so far (ties
+    to the lowest rank).  Returns each rank's sequence indices in the order
+    they were dealt.  Decode cost is proportional to context, so this
+    balances every GPU's cache traffic per step."""
+    order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
+    load = [0] * world
+    parts: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        parts[r].append(i)
+        load[r] += lengths[i]
+    return parts

@@ -115,3 +115,18 @@ def test_gloo_ranks_merge_to_the_single_pass_row(world, seq, pos):
     want = _merge(_partial(qg[:, :HD], K, V, pos + 1)[None], qg[:, HD:]).reshape(-1)
     for r in range(world):
         np.testing.assert_allclose(res[r], want, rtol=2e-5, atol=2e-6)
+
+
+def test_sequence_partition_balances_context():
+    """Config 4b's partition: 64 sequences with contexts U[4096, 32768],
+    longest first to the least-loaded GPU; every sequence exactly once and the
+    heaviest GPU within one longest sequence of the mean."""
+    import numpy as np
+    lens = [int(x) for x in np.random.default_rng(5).integers(4096, 32769, 64)]
+    for world in (1, 2, 4, 8):
+        parts = split_kv.partition_sequences(lens, world)
+        assert sorted(i for p in parts for i in p) == list(range(64))
+        loads = [sum(lens[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(lens)
+        assert max(loads) <= sum(lens) / world + max(lens)
+    assert split_kv.partition_sequences([5, 9, 1], 2) == [[1], [0, 2]]
