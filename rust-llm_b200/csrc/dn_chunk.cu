@@ -41,6 +41,7 @@ constexpr int LDP = 72;    // padded bf16 row of a 64-wide matrix (144 B)
 constexpr int LDF = 65;    // padded f32 row of a 64-wide matrix
 constexpr int JC = 32;     // state columns per scan CTA
 constexpr int SCAN_THREADS = 256;
+constexpr int LOCAL_THREADS = 256;  // chunk-local CTA: 8 warps
 }  // namespace dc
 
 // ---------------------------------------------------------------------------
@@ -146,13 +147,53 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// m16n8k16 fragments of f32 matrices in shared memory (row stride ld), each
+// split into a bf16 pair: A is the 16 x 16 block at (m0, k0), B the 16 x 8
+// block at (k0, n0).
+__device__ __forceinline__ void frag_a_f32(const float *base, int ld, int m0, int k0, int lane,
+                                           uint32_t (&hi)[4], uint32_t (&lo)[4]) {
+    const int g = lane >> 2, t2 = (lane & 3) * 2;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int r = m0 + g + (q & 1) * 8, c = k0 + t2 + (q >> 1) * 8;
+        const float x0 = base[r * ld + c], x1 = base[r * ld + c + 1];
+        hi[q] = pack_bf16(x0, x1);
+        lo[q] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+    }
+}
+__device__ __forceinline__ void frag_b_f32(const float *base, int ld, int k0, int n0, int lane,
+                                           uint32_t (&hi)[2], uint32_t (&lo)[2]) {
+    const int g = lane >> 2, t2 = (lane & 3) * 2;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int k = k0 + t2 + q * 8, n = n0 + g;
+        const float x0 = base[k * ld + n], x1 = base[(k + 1) * ld + n];
+        hi[q] = pack_bf16(x0, x1);
+        lo[q] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+    }
+}
+// d += a * b over bf16 pairs: hi*hi + hi*lo + lo*hi
+__device__ __forceinline__ void mma3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                     const uint32_t (&bh)[2], const uint32_t (&bl)[2]) {
+    mma_16816(d, ah, bh[0], bh[1]);
+    mma_16816(d, ah, bl[0], bl[1]);
+    mma_16816(d, al, bh[0], bh[1]);
+}
+
+// 16 bytes, or zeros when `valid` is false (the source is not read)
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ---------------------------------------------------------------------------
-// dn_chunk_local_kernel: grid (n_chunks, n_v), 128 threads (4 warps, 16 rows each).
+// dn_chunk_local_kernel: grid (n_chunks, n_v), 256 threads (8 warps: row block
+// warp % 4 of 16 rows, column half warp / 4 in the two product phases).
 struct LocalSmem {
     __nv_bfloat16 k[dc::C][dc::LDB], q[dc::C][dc::LDB], v[dc::C][dc::LDB];
     __nv_bfloat16 kl[dc::C][dc::LDB], ql[dc::C][dc::LDB], vl[dc::C][dc::LDB];  // low halves
@@ -162,7 +203,7 @@ struct LocalSmem {
     float cum[dc::C], beta[dc::C];
 };
 
-__global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a) {
+__global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const DnChunkArgs a) {
     using namespace dc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     LocalSmem &sm = *reinterpret_cast<LocalSmem *>(smem_raw);
@@ -170,57 +211,63 @@ __global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = ck * C, rows = min(C, a.t - t0);
 
-    // ---- operands of the chunk (rows past the batch are zero)
-    for (int e = tid; e < C * (S / 8); e += 128) {
+    // ---- operands of the chunk (rows past the batch are zero): every copy
+    // in flight at once
+#pragma unroll 2
+    for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
-        uint4 kz = make_uint4(0, 0, 0, 0), qz = kz, vz = kz, klz = kz, qlz = kz, vlz = kz;
-        if (r < rows) {
-            const size_t ko = ((size_t)(t0 + r) * a.n_k + kh) * S + c8;
-            kz = *reinterpret_cast<const uint4 *>(a.kn + ko);
-            qz = *reinterpret_cast<const uint4 *>(a.qn + ko);
-            klz = *reinterpret_cast<const uint4 *>(a.kn_lo + ko);
-            qlz = *reinterpret_cast<const uint4 *>(a.qn_lo + ko);
-            const size_t vo = ((size_t)(t0 + r) * a.n_v + vh) * S + c8;
-            vz = *reinterpret_cast<const uint4 *>(a.vn + vo);
-            vlz = *reinterpret_cast<const uint4 *>(a.vn_lo + vo);
+        const bool ok = r < rows;
+        const size_t ko = ((size_t)(t0 + (ok ? r : 0)) * a.n_k + kh) * S + c8;
+        const size_t vo = ((size_t)(t0 + (ok ? r : 0)) * a.n_v + vh) * S + c8;
+        cp_async16_zfill(&sm.k[r][c8], a.kn + ko, ok);
+        cp_async16_zfill(&sm.q[r][c8], a.qn + ko, ok);
+        cp_async16_zfill(&sm.kl[r][c8], a.kn_lo + ko, ok);
+        cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
+        cp_async16_zfill(&sm.v[r][c8], a.vn + vo, ok);
+        cp_async16_zfill(&sm.vl[r][c8], a.vn_lo + vo, ok);
+    }
+    cp_async_commit();
+    if (warp == 0) {
+        // cumulative log decay, gamma_t = exp(cum[t]): lane l holds tokens
+        // 2l and 2l + 1, an inclusive scan over the pairs' sums
+        const int ta = 2 * lane, tb = ta + 1;
+        const float la = ta < rows ? a.lg[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
+        const float lb = tb < rows ? a.lg[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
+        float inc = la + lb;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
         }
-        *reinterpret_cast<uint4 *>(&sm.vl[r][c8]) = vlz;
-        *reinterpret_cast<uint4 *>(&sm.k[r][c8]) = kz;
-        *reinterpret_cast<uint4 *>(&sm.q[r][c8]) = qz;
-        *reinterpret_cast<uint4 *>(&sm.kl[r][c8]) = klz;
-        *reinterpret_cast<uint4 *>(&sm.ql[r][c8]) = qlz;
-        *reinterpret_cast<uint4 *>(&sm.v[r][c8]) = vz;
+        sm.cum[tb] = inc;
+        sm.cum[ta] = inc - lb;
+        sm.beta[ta] = ta < rows ? a.bt[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
+        sm.beta[tb] = tb < rows ? a.bt[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
     }
-    if (tid < C) {
-        sm.cum[tid] = tid < rows ? a.lg[(size_t)(t0 + tid) * a.n_v + vh] : 0.0f;
-        sm.beta[tid] = tid < rows ? a.bt[(size_t)(t0 + tid) * a.n_v + vh] : 0.0f;
-    }
+    cp_async_wait<0>();
     __syncthreads();
-    if (tid == 0) {
-        // cumulative log decay: gamma_t = exp(cum[t])
-        float s = 0.0f;
-        for (int r = 0; r < C; ++r) sm.cum[r] = s = s + sm.cum[r];
-    }
     // ---- K K^T and Q K^T (warp: 16 rows, all 64 columns), each as
     // hi*hi + hi*lo + lo*hi of the bf16 pairs
     {
-        float dk[8][4], dq[8][4];
+        // warp: rows 16 * (warp % 4), columns 32 * (warp / 4) .. + 31
+        const int rw = (warp & 3) * 16, cn = (warp >> 2) * 32;
+        float dk[4][4], dq[4][4];
 #pragma unroll
-        for (int n = 0; n < 8; ++n)
+        for (int n = 0; n < 4; ++n)
 #pragma unroll
             for (int e = 0; e < 4; ++e) dk[n][e] = dq[n][e] = 0.0f;
 #pragma unroll
         for (int ks = 0; ks < S / 16; ++ks) {
             uint32_t ak[4], aq[4], akl[4], aql[4];
-            ld_a(&sm.k[0][0], LDB, warp * 16, ks * 16, lane, ak);
-            ld_a(&sm.q[0][0], LDB, warp * 16, ks * 16, lane, aq);
-            ld_a(&sm.kl[0][0], LDB, warp * 16, ks * 16, lane, akl);
-            ld_a(&sm.ql[0][0], LDB, warp * 16, ks * 16, lane, aql);
+            ld_a(&sm.k[0][0], LDB, rw, ks * 16, lane, ak);
+            ld_a(&sm.q[0][0], LDB, rw, ks * 16, lane, aq);
+            ld_a(&sm.kl[0][0], LDB, rw, ks * 16, lane, akl);
+            ld_a(&sm.ql[0][0], LDB, rw, ks * 16, lane, aql);
 #pragma unroll
-            for (int np = 0; np < 4; ++np) {
+            for (int np = 0; np < 2; ++np) {
                 uint32_t b[4], bl[4];
-                ld_b2(&sm.k[0][0], LDB, np * 16, ks * 16, lane, b);
-                ld_b2(&sm.kl[0][0], LDB, np * 16, ks * 16, lane, bl);
+                ld_b2(&sm.k[0][0], LDB, cn + np * 16, ks * 16, lane, b);
+                ld_b2(&sm.kl[0][0], LDB, cn + np * 16, ks * 16, lane, bl);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     mma_16816(dk[2 * np + h], ak, b[2 * h], b[2 * h + 1]);
@@ -232,9 +279,9 @@ __global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a
                 }
             }
         }
-        const int r0 = warp * 16 + (lane >> 2), c0 = (lane & 3) * 2;
+        const int r0 = rw + (lane >> 2), c0 = cn + (lane & 3) * 2;
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
+        for (int n = 0; n < 4; ++n) {
             sm.kk[r0][n * 8 + c0] = dk[n][0];
             sm.kk[r0][n * 8 + c0 + 1] = dk[n][1];
             sm.kk[r0 + 8][n * 8 + c0] = dk[n][2];
@@ -247,67 +294,103 @@ __global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a
     }
     __syncthreads();
     // ---- L (in place over kk) and T = (I + L)^-1, one column per thread
-    for (int e = tid; e < C * C; e += 128) {
-        const int r = e / C, s = e % C;
-        sm.kk[r][s] = s < r ? sm.beta[r] * __expf(sm.cum[r] - sm.cum[s]) * sm.kk[r][s] : 0.0f;
+    {
+        // this thread's column s is fixed (the CTA is a multiple of C)
+        const int s = tid & (C - 1);
+        const float cs = sm.cum[s];
+#pragma unroll 4
+        for (int r = tid / C; r < C; r += LOCAL_THREADS / C) {
+            sm.kk[r][s] = s < r ? sm.beta[r] * __expf(sm.cum[r] - cs) * sm.kk[r][s] : 0.0f;
+            sm.t[r][s] = 0.0f;
+        }
     }
-    for (int e = tid; e < C * C; e += 128) sm.t[e / C][e % C] = 0.0f;
     __syncthreads();
     // T = (I + L)^-1 in 16 x 16 blocks: the four diagonal blocks by forward
     // substitution (one column per thread), then the blocks below the
     // diagonal, one diagonal at a time: T_ij = -T_ii sum_{j<=k<i} L_ik T_kj
     if (tid < C) {
+        // column s of diagonal block b0, in registers (entries above the
+        // diagonal are zero, so the sums may run over every m < r)
         const int b0 = (tid >> 4) * 16, s = tid & 15;
+        float tc[16];
+#pragma unroll
         for (int r = 0; r < 16; ++r) {
-            float v = r == s ? 1.0f : 0.0f;
-            if (r > s) {
-                float acc = 0.0f;
-                for (int m = s; m < r; ++m) acc = fmaf(sm.kk[b0 + r][b0 + m], sm.t[b0 + m][b0 + s], acc);
-                v = -acc;
-            }
-            sm.t[b0 + r][b0 + s] = v;
-        }
-    }
-    __syncthreads();
-#pragma unroll 1
-    for (int dg = 1; dg < 4; ++dg) {
-        const int nb = 4 - dg;  // blocks on this diagonal: (j + dg, j), j < nb
-        for (int e = tid; e < nb * 256; e += 128) {
-            const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15, bi = bj + dg;
-            float acc = 0.0f;
-            for (int k = bj * 16; k < bi * 16; ++k) acc = fmaf(sm.kk[bi * 16 + r][k], sm.t[k][bj * 16 + c], acc);
-            sm.x[bi * 16 + r][bj * 16 + c] = acc;
-        }
-        __syncthreads();
-        for (int e = tid; e < nb * 256; e += 128) {
-            const int bj = e >> 8, r = (e >> 4) & 15, c = e & 15, bi = bj + dg;
             float acc = 0.0f;
 #pragma unroll
-            for (int m = 0; m < 16; ++m)
-                acc = fmaf(sm.t[bi * 16 + r][bi * 16 + m], sm.x[bi * 16 + m][bj * 16 + c], acc);
-            sm.t[bi * 16 + r][bj * 16 + c] = -acc;
+            for (int m = 0; m < r; ++m) acc = fmaf(sm.kk[b0 + r][b0 + m], tc[m], acc);
+            tc[r] = r == s ? 1.0f : (r > s ? -acc : 0.0f);
+        }
+#pragma unroll
+        for (int r = 0; r < 16; ++r) sm.t[b0 + r][b0 + s] = tc[r];
+    }
+    __syncthreads();
+    // the blocks below the diagonal, one diagonal dg at a time: warp j < 4 -
+    // dg takes block (i, j) = (j + dg, j), X = sum_{j <= k < i} L_ik T_kj and
+    // then T_ij = -T_ii X, both on the tensor cores as bf16 pairs
+#pragma unroll 1
+    for (int dg = 1; dg < 4; ++dg) {
+        if (warp < 4 - dg) {
+            const int bj = warp, bi = warp + dg;
+            const int g = lane >> 2, t2 = (lane & 3) * 2;
+            float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            for (int kb = bj; kb < bi; ++kb) {
+                uint32_t ah[4], al[4];
+                frag_a_f32(&sm.kk[0][0], LDF, 16 * bi, 16 * kb, lane, ah, al);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    uint32_t bh[2], bl[2];
+                    frag_b_f32(&sm.t[0][0], LDF, 16 * kb, 16 * bj + 8 * nt, lane, bh, bl);
+                    mma3(x[nt], ah, al, bh, bl);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sm.x[16 * bi + g][16 * bj + 8 * nt + t2] = x[nt][0];
+                sm.x[16 * bi + g][16 * bj + 8 * nt + t2 + 1] = x[nt][1];
+                sm.x[16 * bi + g + 8][16 * bj + 8 * nt + t2] = x[nt][2];
+                sm.x[16 * bi + g + 8][16 * bj + 8 * nt + t2 + 1] = x[nt][3];
+            }
+            __syncwarp();
+            uint32_t ah[4], al[4];
+            frag_a_f32(&sm.t[0][0], LDF, 16 * bi, 16 * bi, lane, ah, al);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                uint32_t bh[2], bl[2];
+                frag_b_f32(&sm.x[0][0], LDF, 16 * bi, 16 * bj + 8 * nt, lane, bh, bl);
+                float y[4] = {0.f, 0.f, 0.f, 0.f};
+                mma3(y, ah, al, bh, bl);
+                sm.t[16 * bi + g][16 * bj + 8 * nt + t2] = -y[0];
+                sm.t[16 * bi + g][16 * bj + 8 * nt + t2 + 1] = -y[1];
+                sm.t[16 * bi + g + 8][16 * bj + 8 * nt + t2] = -y[2];
+                sm.t[16 * bi + g + 8][16 * bj + 8 * nt + t2 + 1] = -y[3];
+            }
         }
         __syncthreads();
     }
     // ---- T diag(beta) and T diag(beta gamma) as bf16 pairs
-    for (int e = tid; e < C * C; e += 128) {
-        const int r = e / C, s = e % C;
-        const float x = sm.t[r][s] * sm.beta[s];
-        const float y = x * __expf(sm.cum[s]);
-        const float xh = bf16_hi(x), yh = bf16_hi(y);
-        sm.ta_hi[r][s] = __float2bfloat16_rn(x);
-        sm.ta_lo[r][s] = __float2bfloat16_rn(x - xh);
-        sm.tb_hi[r][s] = __float2bfloat16_rn(y);
-        sm.tb_lo[r][s] = __float2bfloat16_rn(y - yh);
+    {
+        // this thread's column s is fixed (the CTA is a multiple of C)
+        const int s = tid & (C - 1);
+        const float bs = sm.beta[s], gs = __expf(sm.cum[s]);
+#pragma unroll 4
+        for (int r = tid / C; r < C; r += LOCAL_THREADS / C) {
+            const float x = sm.t[r][s] * bs;
+            const float y = x * gs;
+            const float xh = bf16_hi(x), yh = bf16_hi(y);
+            sm.ta_hi[r][s] = __float2bfloat16_rn(x);
+            sm.ta_lo[r][s] = __float2bfloat16_rn(x - xh);
+            sm.tb_hi[r][s] = __float2bfloat16_rn(y);
+            sm.tb_lo[r][s] = __float2bfloat16_rn(y - yh);
+        }
     }
     __syncthreads();
-    // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows, 128 cols)
+    // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows, 64 cols)
     const size_t blk = (size_t)vh * a.nc + ck;
     float *ut_out = a.ut + blk * C * S;
     __nv_bfloat16 *w_out = a.w + blk * C * S, *wl_out = a.w_lo + blk * C * S;
-    const int r0 = warp * 16 + (lane >> 2), c0 = (lane & 3) * 2;
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {  // 64 output columns at a time
+    const int r0 = (warp & 3) * 16 + (lane >> 2), c0 = (lane & 3) * 2;
+    {
+        const int half = warp >> 2;  // this warp's 64 output columns
         float du[8][4], dw[8][4];
 #pragma unroll
         for (int n = 0; n < 8; ++n)
@@ -316,10 +399,10 @@ __global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a
 #pragma unroll
         for (int ks = 0; ks < C / 16; ++ks) {
             uint32_t ah[4], al[4], bh[4], bl[4];
-            ld_a(&sm.ta_hi[0][0], LDP, warp * 16, ks * 16, lane, ah);
-            ld_a(&sm.ta_lo[0][0], LDP, warp * 16, ks * 16, lane, al);
-            ld_a(&sm.tb_hi[0][0], LDP, warp * 16, ks * 16, lane, bh);
-            ld_a(&sm.tb_lo[0][0], LDP, warp * 16, ks * 16, lane, bl);
+            ld_a(&sm.ta_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, ah);
+            ld_a(&sm.ta_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, al);
+            ld_a(&sm.tb_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bh);
+            ld_a(&sm.tb_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bl);
 #pragma unroll
             for (int np = 0; np < 4; ++np) {
                 const int n0 = half * 64 + np * 16;
@@ -354,25 +437,56 @@ __global__ void __launch_bounds__(128) dn_chunk_local_kernel(const DnChunkArgs a
         }
     }
     // ---- P = Q K^T o Mgamma (s <= t), Q' = gamma Q, K' = gamma_C / gamma K
+    // (8 consecutive elements a thread: 16-byte stores)
     __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
-    for (int e = tid; e < C * C; e += 128) {
-        const int r = e / C, s = e % C;
-        const float x = s <= r ? sm.qk[r][s] * __expf(sm.cum[r] - sm.cum[s]) : 0.0f;
-        p_out[e] = __float2bfloat16_rn(x);
-        pl_out[e] = __float2bfloat16_rn(x - bf16_hi(x));
+#pragma unroll 2
+    for (int e8 = tid; e8 < C * C / 8; e8 += LOCAL_THREADS) {
+        const int r = e8 / (C / 8), s0 = (e8 % (C / 8)) * 8;
+        const float cr = sm.cum[r];
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int sa = s0 + 2 * k, sb = sa + 1;
+            const float x0 = sa <= r ? sm.qk[r][sa] * __expf(cr - sm.cum[sa]) : 0.0f;
+            const float x1 = sb <= r ? sm.qk[r][sb] * __expf(cr - sm.cum[sb]) : 0.0f;
+            hi[k] = pack_bf16(x0, x1);
+            lo[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+        }
+        *reinterpret_cast<uint4 *>(p_out + r * C + s0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(pl_out + r * C + s0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     const float cum_c = sm.cum[C - 1];
     __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
     __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
-    for (int e = tid; e < C * S; e += 128) {
-        const int r = e / S, c = e % S;
-        const float qf = __bfloat162float(sm.q[r][c]) + __bfloat162float(sm.ql[r][c]);
-        const float kf = __bfloat162float(sm.k[r][c]) + __bfloat162float(sm.kl[r][c]);
-        const float x = qf * __expf(sm.cum[r]), y = kf * __expf(cum_c - sm.cum[r]);
-        qp_out[e] = __float2bfloat16_rn(x);
-        qpl_out[e] = __float2bfloat16_rn(x - bf16_hi(x));
-        kp_out[e] = __float2bfloat16_rn(y);
-        kpl_out[e] = __float2bfloat16_rn(y - bf16_hi(y));
+#pragma unroll 2
+    for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
+        const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
+        const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
+        const uint4 qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
+        const uint4 ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
+        const uint4 kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
+        const uint4 kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
+        const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
+        const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
+        const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
+        const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
+        uint32_t xh[4], xl[4], yh[4], yl[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
+            const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
+            const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
+            const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
+            xh[k] = pack_bf16(x0, x1);
+            xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+            yh[k] = pack_bf16(y0, y1);
+            yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
+        }
+        const size_t o = (size_t)r * S + c0;
+        *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+        *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+        *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+        *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
     }
     if (tid == 0) a.gc[blk] = __expf(cum_c);
 }
@@ -627,7 +741,7 @@ cudaError_t init_dn_chunk_kernels() {
 cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st) {
     using namespace dc;
     dn_prep_kernel<<<dim3(a.t, (2 * a.n_k + a.n_v + 7) / 8), 256, 0, st>>>(a);
-    dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), 128, sizeof(LocalSmem), st>>>(a);
+    dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
     dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
     const int conv_dim = 2 * a.n_k * S + a.n_v * S;
