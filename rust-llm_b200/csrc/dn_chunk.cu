@@ -9,7 +9,7 @@
 //   S_C = gamma_C S_0 + K^T diag(gamma_C/gamma) U
 // so with T = (I + L)^-1, Ut = T diag(beta) V and W = T diag(beta gamma) K,
 // U = Ut - W S_0: every product is a small dense GEMM.  Four kernels:
-//   dn_prep_kernel        per token: causal conv + SiLU, q/k L2 norm, gates
+//   dn_prep_kernel        per 8 tokens: causal conv + SiLU, q/k L2 norm, gates
 //                         (forward.rs:1530-1584, :2018-2059, :1720-1727)
 //   dn_chunk_local_kernel per (value head, chunk), all in parallel: K K^T and
 //                         Q K^T on mma.sync, T by forward substitution (f32),
@@ -57,20 +57,26 @@ __device__ __forceinline__ void store_pair4(__nv_bfloat16 *hi, __nv_bfloat16 *lo
     *reinterpret_cast<uint2 *>(lo) = l;
 }
 
+// One warp per (8 consecutive tokens, group of 128 channels): the group's
+// conv weights are loaded once and the three-token history slides along in
+// registers.
+constexpr int PREP_TOKENS = 8;
 __global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
     using namespace dc;
     const int lane = threadIdx.x & 31;
-    const int i = blockIdx.x, g = blockIdx.y * 8 + (threadIdx.x >> 5);
+    const int i0 = blockIdx.x * PREP_TOKENS, g = blockIdx.y * 8 + (threadIdx.x >> 5);
     const int n_groups = 2 * a.n_k + a.n_v;
     if (g >= n_groups) return;
     const int key_dim = a.n_k * S, conv_dim = 2 * key_dim + a.n_v * S;
     const int ch = g * S + lane * 4;
-    const float4 x4 = *reinterpret_cast<const float4 *>(a.qkv + (size_t)i * conv_dim + ch);
-    const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+    float4 w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w[e] = *reinterpret_cast<const float4 *>(a.conv1d + (size_t)(ch + e) * 4);
+    // h[j] = input of token i - 3 + j (the saved history before the batch)
     float h[3][4];
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-        const int src = i - 3 + j;
+        const int src = i0 - 3 + j;
         if (src >= 0) {
             const float4 v = *reinterpret_cast<const float4 *>(a.qkv + (size_t)src * conv_dim + ch);
             h[j][0] = v.x, h[j][1] = v.y, h[j][2] = v.z, h[j][3] = v.w;
@@ -79,39 +85,54 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
             for (int e = 0; e < 4; ++e) h[j][e] = a.conv_state[(size_t)(ch + e) * 3 + (src + 3)];
         }
     }
-    float y[4];
+    float4 xin[PREP_TOKENS];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const float4 w = *reinterpret_cast<const float4 *>(a.conv1d + (size_t)(ch + e) * 4);
-        // forward.rs:2018-2031: x * w[3] first, then the history taps in order
-        float c = __fmul_rn(xs[e], w.w);
-        c = __fadd_rn(c, __fmul_rn(h[0][e], w.x));
-        c = __fadd_rn(c, __fmul_rn(h[1][e], w.y));
-        c = __fadd_rn(c, __fmul_rn(h[2][e], w.z));
-        y[e] = siluf_(c);
-    }
-    if (g < 2 * a.n_k) {
-        // L2 norm: rms_scale with eps/n, then 1/sqrt(n) (forward.rs:1720-1727)
-        double sq = 0.0;
+    for (int tt = 0; tt < PREP_TOKENS; ++tt)
+        xin[tt] = i0 + tt < a.t
+                      ? *reinterpret_cast<const float4 *>(a.qkv + (size_t)(i0 + tt) * conv_dim + ch)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sq += (double)__fmul_rn(y[e], y[e]);
-        sq = warp_sum_d(sq);
-        const float sc = rms_scale_from_sum(sq, S, a.eps / (float)S);
-        const float shrink = 1.0f / sqrtf((float)S);
+    for (int tt = 0; tt < PREP_TOKENS; ++tt) {
+        const int i = i0 + tt;
+        if (i >= a.t) break;  // warp-uniform
+        const float xs[4] = {xin[tt].x, xin[tt].y, xin[tt].z, xin[tt].w};
+        float y[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), shrink);
-        const bool is_q = g < a.n_k;
-        const size_t o = ((size_t)i * a.n_k + (is_q ? g : g - a.n_k)) * S + lane * 4;
-        store_pair4((is_q ? a.qn : a.kn) + o, (is_q ? a.qn_lo : a.kn_lo) + o, y);
-    } else {
-        const int vh = g - 2 * a.n_k;
-        const size_t o = ((size_t)i * a.n_v + vh) * S + lane * 4;
-        store_pair4(a.vn + o, a.vn_lo + o, y);
-        if (lane == 0) {
-            // gates (forward.rs:1530-1546): log decay and beta
-            a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(
-                softplusf_(__fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh])), a.ssm_a[vh]);
-            a.bt[(size_t)i * a.n_v + vh] = sigmoidf_(a.beta[(size_t)i * a.n_v + vh]);
+        for (int e = 0; e < 4; ++e) {
+            // forward.rs:2018-2031: x * w[3] first, then the history taps in order
+            float c = __fmul_rn(xs[e], w[e].w);
+            c = __fadd_rn(c, __fmul_rn(h[0][e], w[e].x));
+            c = __fadd_rn(c, __fmul_rn(h[1][e], w[e].y));
+            c = __fadd_rn(c, __fmul_rn(h[2][e], w[e].z));
+            y[e] = siluf_(c);
+            h[0][e] = h[1][e];
+            h[1][e] = h[2][e];
+            h[2][e] = xs[e];
+        }
+        if (g < 2 * a.n_k) {
+            // L2 norm: rms_scale with eps/n, then 1/sqrt(n) (forward.rs:1720-1727)
+            double sq = 0.0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sq += (double)__fmul_rn(y[e], y[e]);
+            sq = warp_sum_d(sq);
+            const float sc = rms_scale_from_sum(sq, S, a.eps / (float)S);
+            const float shrink = 1.0f / sqrtf((float)S);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), shrink);
+            const bool is_q = g < a.n_k;
+            const size_t o = ((size_t)i * a.n_k + (is_q ? g : g - a.n_k)) * S + lane * 4;
+            store_pair4((is_q ? a.qn : a.kn) + o, (is_q ? a.qn_lo : a.kn_lo) + o, y);
+        } else {
+            const int vh = g - 2 * a.n_k;
+            const size_t o = ((size_t)i * a.n_v + vh) * S + lane * 4;
+            store_pair4(a.vn + o, a.vn_lo + o, y);
+            if (lane == 0) {
+                // gates (forward.rs:1530-1546): log decay and beta
+                a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(
+                    softplusf_(__fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh])),
+                    a.ssm_a[vh]);
+                a.bt[(size_t)i * a.n_v + vh] = sigmoidf_(a.beta[(size_t)i * a.n_v + vh]);
+            }
         }
     }
 }
@@ -492,20 +513,25 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
 }
 
 // ---------------------------------------------------------------------------
-// dn_chunk_scan_kernel: grid (S / JC, n_v), 128 threads.  The chunks in
+// dn_chunk_scan_kernel: grid (S / JC, n_v), 256 threads.  The chunks in
 // order; this CTA owns state columns j0 .. j0 + 31 of value head vh.  The
 // next chunk's W and Ut are fetched once the U phase has used this chunk's,
-// its Q', P and K' once the O and S phases have; the U phase of a chunk then
-// overlaps the arrival of its Q', P and K'.
+// its Q', P and K' once the O and S phases have, so the U phase of a chunk
+// overlaps the arrival of its Q', P and K'.  S and U are kept as bf16
+// pairs in row-major [k][n] form (the B operands, read with transposing
+// ldmatrix), written with packed 4-byte stores.
+constexpr int LDU = dc::JC + 8;  // padded bf16 row of a 32-column matrix (80 B)
 struct ScanSmem {
     __nv_bfloat16 w[2][dc::C][dc::LDB], qp[2][dc::C][dc::LDB], kp[2][dc::C][dc::LDB];  // [hi, lo]
     __nv_bfloat16 p[2][dc::C][dc::LDP];
     float ut[dc::C][dc::JC];
-    float s[dc::S][dc::JC + 1];                                         // the state block, f32
-    __nv_bfloat16 st[2][2][dc::JC][dc::LDB];  // S^T [buffer][hi, lo]
-    __nv_bfloat16 ut_t[2][dc::JC][dc::LDP];   // U^T [hi, lo]
+    float s[dc::S][dc::JC + 1];                 // the state block, f32
+    __nv_bfloat16 st[2][2][dc::S][LDU];         // S [buffer][hi, lo] as [i][j]
+    __nv_bfloat16 up[2][dc::C][LDU];            // U [hi, lo] as [t][j]
 };
 
+// W (hi, lo) and this CTA's 32 columns of Ut for chunk block `blk`, 16-byte
+// asynchronous copies from every thread
 __device__ __forceinline__ void scan_load_wu(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
                                              int j0, int tid) {
     using namespace dc;
@@ -521,6 +547,7 @@ __device__ __forceinline__ void scan_load_wu(ScanSmem &sm, const DnChunkArgs &a,
         cp_async16(&sm.ut[r][c4], ut + r * S + j0 + c4);
     }
 }
+// Q', K' and P (hi, lo) for chunk block `blk`
 __device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
                                               int tid) {
     using namespace dc;
@@ -542,8 +569,9 @@ __device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a
 }
 
 // d += A B with A (16 rows from m0) given as a bf16 pair in row-major [m][k]
-// smem and B (NP pairs of n-tiles from n0, 16 NP columns) as a pair of [n][k]
-// matrices; three terms: hi*hi + hi*lo + lo*hi, over k from 0 to K.
+// smem and B (NP pairs of n-tiles from n0, 16 NP columns) as a pair of
+// row-major [k][n] matrices; three terms: hi*hi + hi*lo + lo*hi, over k from
+// 0 to K.
 template <int K, int NP>
 __device__ __forceinline__ void mma3_rows(float (&d)[2 * NP][4], const __nv_bfloat16 *ah,
                                           const __nv_bfloat16 *al, int lda, int m0,
@@ -557,8 +585,8 @@ __device__ __forceinline__ void mma3_rows(float (&d)[2 * NP][4], const __nv_bflo
 #pragma unroll
         for (int np = 0; np < NP; ++np) {
             uint32_t yh[4], yl[4];
-            ld_b2(bh, ldb, n0 + np * 16, ks * 16, lane, yh);
-            ld_b2(bl, ldb, n0 + np * 16, ks * 16, lane, yl);
+            ld_b2_t(bh, ldb, n0 + np * 16, ks * 16, lane, yh);
+            ld_b2_t(bl, ldb, n0 + np * 16, ks * 16, lane, yl);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
@@ -584,17 +612,20 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
     cp_async_commit();
     scan_load_qpk(sm, a, blk0, tid);
     cp_async_commit();
-    for (int e = tid; e < S * JC; e += SCAN_THREADS) {
-        const int i = e / JC, j = e % JC;
-        const float x = state[(size_t)i * S + j0 + j];
-        sm.s[i][j] = x;
-        sm.st[0][0][j][i] = __float2bfloat16_rn(x);
-        sm.st[0][1][j][i] = __float2bfloat16_rn(x - bf16_hi(x));
+    for (int e = tid; e < S * JC / 2; e += SCAN_THREADS) {
+        const int i = e / (JC / 2), j = (e % (JC / 2)) * 2;
+        const float2 x = *reinterpret_cast<const float2 *>(state + (size_t)i * S + j0 + j);
+        sm.s[i][j] = x.x;
+        sm.s[i][j + 1] = x.y;
+        *reinterpret_cast<uint32_t *>(&sm.st[0][0][i][j]) = pack_bf16(x.x, x.y);
+        *reinterpret_cast<uint32_t *>(&sm.st[0][1][i][j]) =
+            pack_bf16(x.x - bf16_hi(x.x), x.y - bf16_hi(x.y));
     }
     for (int ck = 0; ck < a.nc; ++ck) {
         const int cur = ck & 1, nxt = cur ^ 1;
         const bool more = ck + 1 < a.nc;
-        // W and Ut of this chunk have landed (its Q', P, K' may still be in flight)
+        // W and Ut of this chunk have landed (its Q', P, K' may still be in
+        // flight); the state of the step before is in place
         cp_async_wait<1>();
         __syncthreads();
         // ---- U = Ut - W S (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
@@ -602,29 +633,30 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
         {
             float d[2][4] = {};
             mma3_rows<S, 1>(d, &sm.w[0][0][0], &sm.w[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
-                            &sm.st[cur][1][0][0], LDB, wn, lane);
-            const int r0 = wm + g;
+                            &sm.st[cur][1][0][0], LDU, wn, lane);
 #pragma unroll
             for (int n = 0; n < 2; ++n)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int r = r0 + (e >> 1) * 8, c = wn + n * 8 + c0 + (e & 1);
-                    const float u = sm.ut[r][c] - d[n][e];
-                    sm.ut_t[0][c][r] = __float2bfloat16_rn(u);
-                    sm.ut_t[1][c][r] = __float2bfloat16_rn(u - bf16_hi(u));
+                for (int e2 = 0; e2 < 2; ++e2) {
+                    const int r = wm + g + e2 * 8, c = wn + n * 8 + c0;
+                    const float u0 = sm.ut[r][c] - d[n][2 * e2];
+                    const float u1 = sm.ut[r][c + 1] - d[n][2 * e2 + 1];
+                    *reinterpret_cast<uint32_t *>(&sm.up[0][r][c]) = pack_bf16(u0, u1);
+                    *reinterpret_cast<uint32_t *>(&sm.up[1][r][c]) =
+                        pack_bf16(u0 - bf16_hi(u0), u1 - bf16_hi(u1));
                 }
         }
         cp_async_wait<0>();
-        __syncthreads();
+        __syncthreads();  // U is complete, W and Ut used up; Q', P, K' have landed
         if (more) scan_load_wu(sm, a, blk0 + ck + 1, j0, tid);
         cp_async_commit();
         // ---- O = Q' S + P U (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
         {
             float d[2][4] = {};
             mma3_rows<S, 1>(d, &sm.qp[0][0][0], &sm.qp[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
-                            &sm.st[cur][1][0][0], LDB, wn, lane);
-            mma3_rows<C, 1>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, wm, &sm.ut_t[0][0][0],
-                            &sm.ut_t[1][0][0], LDP, wn, lane);
+                            &sm.st[cur][1][0][0], LDU, wn, lane);
+            mma3_rows<C, 1>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, wm, &sm.up[0][0][0],
+                            &sm.up[1][0][0], LDU, wn, lane);
             const int r0 = wm + g;
 #pragma unroll
             for (int e2 = 0; e2 < 2; ++e2) {
@@ -641,39 +673,39 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
         // ---- S = gamma_C S + K'^T U (warp: state rows 16w.., 32 columns)
         {
             const float gc = a.gc[blk0 + ck];
+            const int m0 = warp * 16;
+            float d[4][4] = {};
 #pragma unroll
-            for (int mh = 0; mh < 1; ++mh) {
-                const int m0 = warp * 16;
-                float d[4][4] = {};
+            for (int ks = 0; ks < C / 16; ++ks) {
+                uint32_t xh[4], xl[4];
+                ld_a_t(&sm.kp[0][0][0], LDB, m0, ks * 16, lane, xh);
+                ld_a_t(&sm.kp[1][0][0], LDB, m0, ks * 16, lane, xl);
 #pragma unroll
-                for (int ks = 0; ks < C / 16; ++ks) {
-                    uint32_t xh[4], xl[4];
-                    ld_a_t(&sm.kp[0][0][0], LDB, m0, ks * 16, lane, xh);
-                    ld_a_t(&sm.kp[1][0][0], LDB, m0, ks * 16, lane, xl);
+                for (int np = 0; np < 2; ++np) {
+                    uint32_t yh[4], yl[4];
+                    ld_b2_t(&sm.up[0][0][0], LDU, np * 16, ks * 16, lane, yh);
+                    ld_b2_t(&sm.up[1][0][0], LDU, np * 16, ks * 16, lane, yl);
 #pragma unroll
-                    for (int np = 0; np < 2; ++np) {
-                        uint32_t yh[4], yl[4];
-                        ld_b2(&sm.ut_t[0][0][0], LDP, np * 16, ks * 16, lane, yh);
-                        ld_b2(&sm.ut_t[1][0][0], LDP, np * 16, ks * 16, lane, yl);
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
-                            mma_16816(d[2 * np + h], xh, yl[2 * h], yl[2 * h + 1]);
-                            mma_16816(d[2 * np + h], xl, yh[2 * h], yh[2 * h + 1]);
-                        }
+                    for (int h = 0; h < 2; ++h) {
+                        mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
+                        mma_16816(d[2 * np + h], xh, yl[2 * h], yl[2 * h + 1]);
+                        mma_16816(d[2 * np + h], xl, yh[2 * h], yh[2 * h + 1]);
                     }
                 }
-#pragma unroll
-                for (int n = 0; n < 4; ++n)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i = m0 + g + (e >> 1) * 8, j = n * 8 + c0 + (e & 1);
-                        const float x = fmaf(gc, sm.s[i][j], d[n][e]);
-                        sm.s[i][j] = x;
-                        sm.st[nxt][0][j][i] = __float2bfloat16_rn(x);
-                        sm.st[nxt][1][j][i] = __float2bfloat16_rn(x - bf16_hi(x));
-                    }
             }
+#pragma unroll
+            for (int n = 0; n < 4; ++n)
+#pragma unroll
+                for (int e2 = 0; e2 < 2; ++e2) {
+                    const int i = m0 + g + e2 * 8, j = n * 8 + c0;
+                    const float x0 = fmaf(gc, sm.s[i][j], d[n][2 * e2]);
+                    const float x1 = fmaf(gc, sm.s[i][j + 1], d[n][2 * e2 + 1]);
+                    sm.s[i][j] = x0;
+                    sm.s[i][j + 1] = x1;
+                    *reinterpret_cast<uint32_t *>(&sm.st[nxt][0][i][j]) = pack_bf16(x0, x1);
+                    *reinterpret_cast<uint32_t *>(&sm.st[nxt][1][i][j]) =
+                        pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+                }
         }
         __syncthreads();  // Q', P, K' and U of this chunk are used up
         if (more) scan_load_qpk(sm, a, blk0 + ck + 1, tid);
@@ -740,7 +772,8 @@ cudaError_t init_dn_chunk_kernels() {
 
 cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st) {
     using namespace dc;
-    dn_prep_kernel<<<dim3(a.t, (2 * a.n_k + a.n_v + 7) / 8), 256, 0, st>>>(a);
+    dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
+                     st>>>(a);
     dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
     dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
