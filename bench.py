@@ -756,7 +756,7 @@ def run_ours(args):
              if not args.no_split else None)
     dn = dn_step_bench(args, dev, stream, rlcuda, torch) if not args.no_dn else None
     pf = prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
-    dnpf = dn_prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
+    dnpf = dn_prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_dn_prefill else None
     ver = verify_bench(args, dev, stream, rlcuda, torch) if not args.no_verify else None
     batch = (batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist)
              if not args.no_batch else None)
@@ -819,7 +819,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dn", action="store_true", help="skip the DeltaNet step section")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill section")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the full-attention prefill section")
+    ap.add_argument("--no-dn-prefill", action="store_true",
+                    help="skip the DeltaNet chunked-prefill section")
     ap.add_argument("--no-verify", action="store_true", help="skip the speculative-verify section")
     ap.add_argument("--no-batch", action="store_true",
                     help="skip the config-4b batched multi-sequence section")
