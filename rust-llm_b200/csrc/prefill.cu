@@ -8,12 +8,13 @@
 //               (a K slot frees when its Q K^T is done, a V slot when its P V
 //               is); 128-byte swizzle throughout
 //   warp 1      tensor-memory allocator and the single MMA-issuing thread:
-//               S_j = Q K_j^T (M 128, N 64, K 256: 16 MMAs) into one of two
-//               S buffers, then O += P_{j-1} V_{j-1} (M 128, N 256, K 64: 4
+//               S_j = Q K_j^T for a tile of 128 keys (two halves of M 128,
+//               N 64, K 256 from two ring stages: 32 MMAs) into one of two
+//               S buffers, then O += P_{j-1} V_{j-1} (M 128, N 256, K 128: 8
 //               MMAs) with P read from tensor memory, so the next tile's
 //               Q K^T runs while the softmax works on this one
 //   warps 2-9   softmax and epilogue, two threads per query row (each half
-//               of the tile's columns and of O): S from tensor memory, causal
+//               of the tile's 128 keys and of O): S from tensor memory, causal
 //               mask on the diagonal tiles, the row max exchanged through
 //               shared memory, online softmax in log2 units with a lazy
 //               rescale (O is corrected only when a row's max grows by more
@@ -21,8 +22,9 @@
 //               end O / l times the sigmoid output gate (staged in bf16 by
 //               the prologue, loaded by TMA over the query tile once the last
 //               Q K^T is done), to global memory in whole 128-byte rows
-// Tensor memory (512 columns): O in columns 0-255, S buffers at 256 and 320;
-// P_j aliases the first 32 columns of its S buffer.  MMAs of one thread run
+// Tensor memory (512 columns): O in columns 0-255, S buffers of 128 columns
+// at 256 and 384; P_j aliases the first 64 columns of its S buffer.  (The
+// verify form keeps 64-key tiles: S buffers at 256 and 320, Q at 384.)  MMAs of one thread run
 // in issue order, so Q K^T of tile j+2 (same S buffer) cannot overtake the
 // P V of tile j that reads P_j.
 //
@@ -105,8 +107,10 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                    const __grid_constant__ CUtensorMap gate_map) {
     using namespace pf;
     extern __shared__ unsigned char smem_raw[];
-    // ring of NST K/V stages (verify: 3, the queries sit in tensor memory)
+    // ring of NST K/V stages of BN keys (verify: 3, the queries sit in tensor
+    // memory); the softmax works on tiles of KT keys, RT ring stages each
     constexpr int NST = VERIFY ? 3 : 2;
+    constexpr int KT = VERIFY ? BN : 2 * BN, RT = KT / BN, HALF = KT / 2;
     constexpr int RING = VERIFY ? 0 : Q_BYTES;  // byte offset of the ring
     __shared__ __align__(8) uint64_t q_full, k_full[NST], v_full[NST], k_empty[NST],
         v_empty[NST], s_full[2], p_full[2], o_ready, o_final, g_full, kv_app, q_iss;
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         q0 = qt * BM;
         const int q_last = min(a.t, q0 + BM) - 1;  // last valid row of the tile
         j0 = 0;
-        n_kt = (a.pos + q_last) / BN + 1;           // key tiles the tile needs
+        n_kt = (a.pos + q_last) / KT + 1;           // key tiles the tile needs
     }
     const uint32_t sbase = smem_u32(smem);
 
@@ -177,7 +181,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     // overlaps the grid ahead; nothing is read before that grid completes
     if constexpr (VERIFY) grid_dep_wait();
     // verify: this CTA's key range holds positions of the appended rows
-    const bool appends = VERIFY && (j0 + n_kt) * BN > a.pos;
+    const bool appends = VERIFY && (j0 + n_kt) * KT > a.pos;
 
     if (warp == 0 || warp == 10) {
         // ---------------- TMA producers ----------------
@@ -200,13 +204,14 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             // verify: the query loads go out ahead of the tile stream (they
             // would queue behind every CTA's first burst of copies)
             if (VERIFY && !mbar_wait(&q_iss, 0, a.status)) flag_s = 1;
-            for (int j = 0; j < n_kt; ++j) {
-                const int s = j % NST;
-                if (j >= NST && !mbar_wait(&empty[s], (j / NST - 1) & 1, a.status)) {
+            const int n_rt = n_kt * RT;  // ring stages the CTA streams
+            for (int u = 0; u < n_rt; ++u) {
+                const int s = u % NST;
+                if (u >= NST && !mbar_wait(&empty[s], (u / NST - 1) & 1, a.status)) {
                     flag_s = 1;
                     break;
                 }
-                if (!appended_visible && (j0 + j + 1) * BN > a.pos) {
+                if (!appended_visible && (j0 * RT + u + 1) * BN > a.pos) {
                     // this tile holds appended rows: the softmax warps have
                     // written them to the cache
                     if (!mbar_wait(&kv_app, 0, a.status)) {
@@ -218,13 +223,15 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 unsigned char *st = smem + RING + s * STAGE + (is_k ? 0 : KV_HALF);
                 mbar_arrive_expect_tx(&full[s], KV_HALF);
                 for (int b = 0; b < 4; ++b)
-                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + (j0 + j) * BN, &full[s]);
-                issued = j + 1;
+                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + (j0 * RT + u) * BN,
+                                &full[s]);
+                issued = u + 1;
             }
-            if (!VERIFY && is_k && issued == n_kt) {
+            if (!VERIFY && is_k && issued == n_rt) {
                 // the last Q K^T done, the query tile is free: the output gate
                 // (sigmoid, bf16, staged by the prologue) takes its place
-                if (mbar_wait(&k_empty[(n_kt - 1) & 1], ((n_kt - 1) >> 1) & 1, a.status)) {
+                const int ul = n_rt - 1;
+                if (mbar_wait(&k_empty[ul % NST], (ul / NST) & 1, a.status)) {
                     prefetch_tensormap(&gate_map);
                     mbar_arrive_expect_tx(&g_full, Q_BYTES);
                     for (int b = 0; b < 4; ++b)
@@ -236,8 +243,8 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             }
             // everything started has landed before the CTA releases its memory
             if (is_k && !VERIFY) mbar_wait(&q_full, 0, a.status);
-            for (int j = max(0, issued - NST); j < issued; ++j)
-                mbar_wait(&full[j % NST], (j / NST) & 1, a.status);
+            for (int u = max(0, issued - NST); u < issued; ++u)
+                mbar_wait(&full[u % NST], (u / NST) & 1, a.status);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -248,43 +255,60 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
             tc::fence_after_sync();
             for (int j = 0; ok && j <= n_kt; ++j) {
                 if (j < n_kt) {
-                    const int s = j % NST, sb = j & 1;  // ring slot, S buffer
-                    if (!mbar_wait(&k_full[s], (j / NST) & 1, a.status)) { ok = false; break; }
+                    const int sb = j & 1;  // S buffer
+                    for (int r = 0; r < RT; ++r) {
+                        const int u = j * RT + r;
+                        if (!mbar_wait(&k_full[u % NST], (u / NST) & 1, a.status)) ok = false;
+                    }
+                    if (!ok) break;
                     tc::fence_after_sync();
-                    const uint32_t kst = sbase + RING + s * STAGE;
-                    const uint32_t d = tmem + S_COL + sb * BN;
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk) {
-                        const uint32_t off = (kk & 3) * 32;  // 16 dims inside a 64-dim box
-                        const uint64_t db = tc::smem_desc(kst + (kk >> 2) * KV_BOX + off, 16, 1024);
-                        if constexpr (VERIFY) {
-                            // A = Q from tensor memory: 16 dims are 8 columns
-                            tc::mma_ts(d, tmem + Q_COL + kk * 8, db, id_qk, kk > 0);
-                        } else {
-                            const uint64_t da =
-                                tc::smem_desc(sbase + (kk >> 2) * Q_BOX + off, 16, 1024);
-                            tc::mma_ss(d, da, db, id_qk, kk > 0);
+                    for (int r = 0; r < RT; ++r) {
+                        // keys r*BN.. of the tile from their ring stage, into
+                        // columns r*BN.. of the S buffer
+                        const int s = (j * RT + r) % NST;
+                        const uint32_t kst = sbase + RING + s * STAGE;
+                        const uint32_t d = tmem + S_COL + sb * KT + r * BN;
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; ++kk) {
+                            const uint32_t off = (kk & 3) * 32;  // 16 dims inside a 64-dim box
+                            const uint64_t db =
+                                tc::smem_desc(kst + (kk >> 2) * KV_BOX + off, 16, 1024);
+                            if constexpr (VERIFY) {
+                                // A = Q from tensor memory: 16 dims are 8 columns
+                                tc::mma_ts(d, tmem + Q_COL + kk * 8, db, id_qk, kk > 0);
+                            } else {
+                                const uint64_t da =
+                                    tc::smem_desc(sbase + (kk >> 2) * Q_BOX + off, 16, 1024);
+                                tc::mma_ss(d, da, db, id_qk, kk > 0);
+                            }
                         }
                     }
                     tc::commit(&s_full[sb]);
-                    tc::commit(&k_empty[s]);
+#pragma unroll
+                    for (int r = 0; r < RT; ++r) tc::commit(&k_empty[(j * RT + r) % NST]);
                 }
                 if (j >= 1) {
-                    const int jj = j - 1, s = jj % NST, sb = jj & 1;
-                    if (!mbar_wait(&p_full[sb], (jj >> 1) & 1, a.status) ||
-                        !mbar_wait(&v_full[s], (jj / NST) & 1, a.status)) {
-                        ok = false;
-                        break;
+                    const int jj = j - 1, sb = jj & 1;
+                    if (!mbar_wait(&p_full[sb], (jj >> 1) & 1, a.status)) { ok = false; break; }
+                    for (int r = 0; r < RT; ++r) {
+                        const int u = jj * RT + r;
+                        if (!mbar_wait(&v_full[u % NST], (u / NST) & 1, a.status)) ok = false;
                     }
+                    if (!ok) break;
                     tc::fence_after_sync();
-                    const uint32_t vst = sbase + RING + s * STAGE + KV_HALF;
-                    const uint32_t p = tmem + S_COL + sb * BN;
+                    const uint32_t p = tmem + S_COL + sb * KT;
 #pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk) {
-                        const uint64_t db = tc::smem_desc(vst + kk * 16 * 128, KV_BOX, 1024);
+                    for (int kk = 0; kk < KT / 16; ++kk) {
+                        // 16 keys: ring stage of the tile's part kk / (BN / 16)
+                        const int s = (jj * RT + kk / (BN / 16)) % NST;
+                        const uint32_t vst = sbase + RING + s * STAGE + KV_HALF;
+                        const uint64_t db =
+                            tc::smem_desc(vst + (kk % (BN / 16)) * 16 * 128, KV_BOX, 1024);
                         tc::mma_ts(tmem + O_COL, p + kk * 8, db, id_pv, jj > 0 || kk > 0);
                     }
-                    tc::commit(&v_empty[s]);
+#pragma unroll
+                    for (int r = 0; r < RT; ++r) tc::commit(&v_empty[(jj * RT + r) % NST]);
                     tc::commit(&o_ready);
                 }
             }
@@ -307,7 +331,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
         const int qa = a.pos + (VERIFY ? lane : q0 + r);
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         const float scale = (1.0f / 16.0f) * LOG2E;
-        const int first_masked = (a.pos + q0) / BN;  // earliest tile a row of the CTA masks
+        const int first_masked = (a.pos + q0) / KT;  // earliest tile a row of the CTA masks
         float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
         if constexpr (VERIFY) {
@@ -472,29 +496,35 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 break;
             }
             tc::fence_after_sync();
-            const uint32_t sc = tmem + lane_off + S_COL + s * BN;
-            uint32_t u[32];
-            tc::ld32(sc + 32 * h, u);
+            const uint32_t sc = tmem + lane_off + S_COL + s * KT;
+            // this thread's HALF keys of the tile, in chunks of 32
+            uint32_t u[RT][32];
+#pragma unroll
+            for (int q = 0; q < RT; ++q) tc::ld32(sc + HALF * h + 32 * q, u[q]);
             tc::wait_ld();
-            const int kv0 = (j0 + j) * BN + 32 * h;
+            const int kv0 = (j0 + j) * KT + HALF * h;
             if (j0 + j >= first_masked) {
 #pragma unroll
-                for (int c = 0; c < 32; ++c)
-                    if (kv0 + c > qa) u[c] = __float_as_uint(-INFINITY);
-            }
-            float mx0 = __uint_as_float(u[0]), mx1 = __uint_as_float(u[1]);
+                for (int q = 0; q < RT; ++q)
 #pragma unroll
-            for (int c = 2; c < 32; c += 2) {
-                mx0 = fmaxf(mx0, __uint_as_float(u[c]));
-                mx1 = fmaxf(mx1, __uint_as_float(u[c + 1]));
+                    for (int c = 0; c < 32; ++c)
+                        if (kv0 + 32 * q + c > qa) u[q][c] = __float_as_uint(-INFINITY);
             }
+            float mx0 = __uint_as_float(u[0][0]), mx1 = __uint_as_float(u[0][1]);
+#pragma unroll
+            for (int q = 0; q < RT; ++q)
+#pragma unroll
+                for (int c = (q == 0 ? 2 : 0); c < 32; c += 2) {
+                    mx0 = fmaxf(mx0, __uint_as_float(u[q][c]));
+                    mx1 = fmaxf(mx1, __uint_as_float(u[q][c + 1]));
+                }
             // the row's max over both halves (scores scale by a positive
             // constant): post this half's, then compute P optimistically with
             // the running max while the partner's arrives; only a row whose
             // max grows past the lazy threshold (rare) redoes the exponentials
             red_m[j & 1][h][r] = fmaxf(mx0, mx1);
             mbar_arrive(&mx_bar[j & 1]);
-            uint32_t pk[16];
+            uint32_t pk[RT][16];
             float ps0 = 0.0f, ps1 = 0.0f;
             auto exps = [&](float m) {
                 ps0 = 0.0f;
@@ -503,14 +533,18 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 // the row) has m = -inf: its P is 0, not NaN
                 const float neg_m = m == -INFINITY ? 0.0f : -m;
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * c]), scale, neg_m));
-                    const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * c + 1]), scale, neg_m));
-                    ps0 += p0;
-                    ps1 += p1;
-                    __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
-                    pk[c] = *reinterpret_cast<uint32_t *>(&hh);
-                }
+                for (int q = 0; q < RT; ++q)
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        const float p0 =
+                            ex2_approx(fmaf(__uint_as_float(u[q][2 * c]), scale, neg_m));
+                        const float p1 =
+                            ex2_approx(fmaf(__uint_as_float(u[q][2 * c + 1]), scale, neg_m));
+                        ps0 += p0;
+                        ps1 += p1;
+                        __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
+                        pk[q][c] = *reinterpret_cast<uint32_t *>(&hh);
+                    }
             };
             exps(m_run);
             if (!__all_sync(0xffffffffu, mbar_wait(&mx_bar[j & 1], (j >> 1) & 1, a.status))) {
@@ -548,7 +582,9 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                 exps(m_run);
             }
             l_run += ps0 + ps1;
-            tc::st16(sc + 16 * h, pk);
+            // P (bf16 pairs) over the first KT / 2 columns of the S buffer
+#pragma unroll
+            for (int q = 0; q < RT; ++q) tc::st16(sc + (HALF / 2) * h + 16 * q, pk[q]);
             tc::wait_st();
             tc::fence_before_sync();
             __syncwarp();
