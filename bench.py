@@ -469,16 +469,18 @@ SPLIT_SEQ = 131072
 def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
     """Config 4a: one sequence at 131072 positions, bf16 cache, 8 layers,
     split along the sequence across the job's GPUs; per layer each GPU walks
-    its range, the partials (16,512 B per GPU) are all-gathered over NCCL and
-    merged with the output gate.  Returns µs per layer (max over ranks), the
-    gather alone, and each GPU's HBM rate over its share of the cache."""
+    its range and its merge pushes the partial (16,512 B) into every GPU's
+    exchange buffer over NVLink (peer stores, then a flag); every GPU merges
+    with the output gate.  Returns µs per layer (max over ranks), the same
+    step with the partials all-gathered by NCCL instead, the all-gather
+    alone, and each GPU's HBM rate over its share of the cache."""
     import split_kv
     lo, n = split_kv.shard_range(SPLIT_SEQ, world, rank)
     cfg = rlcuda.qwen35_config(n_full=N_LAYERS, n_linear=0, context=n,
                                kv_dtype=rlcuda.RL_KV_BF16, max_batch=1)
     ctx = rlcuda.Context(cfg, device=dev.index)
     ctx.set_stream(stream.cuda_stream)
-    shard = split_kv.GpuShard(ctx, lo, SPLIT_SEQ)
+    shard = split_kv.GpuShard(ctx, lo, SPLIT_SEQ, exchange=world > 1, rank=rank, world=world)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4 + rank)
     for layer in range(N_LAYERS):
@@ -521,6 +523,14 @@ def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
         for _ in range(max(3, args.warmup)):
             step()
     ms = timed(step, reps)
+    nccl_ms = None
+    if world > 1:
+        shard.exchange = False  # the same step with an NCCL all-gather
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step()
+        nccl_ms = timed(step, reps)
+        shard.exchange = True
 
     def gathers():
         for _ in range(N_LAYERS):
@@ -532,8 +542,10 @@ def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
     us = ms * 1e3 / (reps * N_LAYERS)
     local_bytes = 2 * N_KV * n * HD * 2
     return {"workload": "config 4a: 1 sequence x 131072 positions, 8 layers, bf16 cache split "
-                        f"across {world} GPU(s), NCCL all-gather of the partials",
+                        f"across {world} GPU(s); partials exchanged through peer memory (NVLink "
+                        "stores + flags, merged on every GPU)",
             "scaling": "strong", "us_per_layer": us,
+            "nccl_us_per_layer": nccl_ms * 1e3 / (reps * N_LAYERS) if nccl_ms else None,
             "gather_us_per_layer": g_ms * 1e3 / (reps * N_LAYERS),
             "kv_bytes_per_gpu_per_layer": local_bytes,
             "hbm_gbs_per_gpu": local_bytes / (us * 1e-6) / 1e9,

@@ -144,6 +144,31 @@ int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qk
  * pointers are device pointers.  A sharded context refuses rl_full_attn.
  */
 int rl_set_shard(rl_ctx *ctx, int lo, int seq_context);
+/*
+ * The same decode row with the exchange over peer memory instead of NCCL:
+ * every GPU's merge pushes its partial into a slot of every GPU's exchange
+ * buffer (NVLink stores) and then raises its flag there; each GPU's merge
+ * kernel waits (bounded) for all flags of the step and merges from its own
+ * memory.  Set-up, once per context: rl_exchange_init(rank, world) allocates
+ * this GPU's buffer and writes its CUDA IPC handle (RL_IPC_HANDLE_BYTES);
+ * the callers exchange the handles (any host channel, in rank order) and
+ * call rl_exchange_connect with all of them.  rl_exchange_connect_ptrs
+ * takes device pointers instead (contexts of one process, e.g. shards
+ * emulated on one GPU: publish on every shard before merging on any).  Each
+ * step every GPU calls rl_split_publish then rl_split_merge (or
+ * rl_full_attn_split, both); all GPUs take the same steps.
+ */
+#define RL_IPC_HANDLE_BYTES 64
+#define RL_EXCHANGE_MAX_GPUS 8
+int rl_exchange_init(rl_ctx *ctx, int rank, int world, void *handle_out);
+int rl_exchange_connect(rl_ctx *ctx, const void *handles);
+int rl_exchange_connect_ptrs(rl_ctx *ctx, const uint64_t *bufs);
+uint64_t rl_exchange_buffer(const rl_ctx *ctx);
+int rl_split_publish(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
+                     const float *v);
+int rl_split_merge(rl_ctx *ctx, const float *qg, float *out);
+int rl_full_attn_split(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
+                       const float *v, float *out);
 int rl_full_attn_partial(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
                          const float *v, float *partial);
 int rl_merge_partials(rl_ctx *ctx, int n_parts, const float *parts, const float *qg,

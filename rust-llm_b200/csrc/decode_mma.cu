@@ -574,21 +574,112 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
         float o = 0.0f;
 #pragma unroll
         for (int y = 0; y < kCombineLanes; ++y) o += red[y][tx];
-        if (a.part_out) {
+        if (a.part_out || a.xpeers) {
             // one shard of a sequence split across GPUs: this GPU's partial
-            // (unnormalised output, max in log2 units, sum) for the merge
-            float *po_out = a.part_out + (size_t)hh * (dm::HD + 2);
-            po_out[d] = o;
-            if (blockIdx.y == 0 && tx == 0) {
-                float M = -INFINITY;
+            // (unnormalised output, max in log2 units, sum) for the merge,
+            // into the caller's buffer or into every GPU's exchange slot
+            float M = -INFINITY;
+            if (blockIdx.y == 0 && tx == 0)
                 for (int s = 0; s < S; ++s) M = fmaxf(M, m_s[s]);
-                po_out[dm::HD] = M;
-                po_out[dm::HD + 1] = L_s;
+            const int n_dst = a.part_out ? 1 : a.xworld;
+            for (int g = 0; g < n_dst; ++g) {
+                float *po_out = a.part_out
+                                    ? a.part_out + (size_t)hh * (dm::HD + 2)
+                                    : a.xpeers[g] +
+                                          (((size_t)a.xslot * a.xworld + a.xrank) * gridDim.x + hh) *
+                                              (dm::HD + 2);
+                po_out[d] = o;
+                if (blockIdx.y == 0 && tx == 0) {
+                    po_out[dm::HD] = M;
+                    po_out[dm::HD + 1] = L_s;
+                }
             }
         } else {
             a.out[(size_t)hh * dm::HD + d] = (o / L_s) * sigmoidf_(gate);
         }
     }
+    if (a.xpeers) {
+        // the last CTA to finish raises this GPU's flag in every exchange
+        // buffer, after every CTA's partial is visible system-wide
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int total = gridDim.x * gridDim.y;
+            if (atomicAdd(a.xcount, 1) == total - 1) {
+                *a.xcount = 0;
+                __threadfence_system();
+                for (int g = 0; g < a.xworld; ++g) {
+                    unsigned *flag = reinterpret_cast<unsigned *>(
+                                         reinterpret_cast<char *>(a.xpeers[g]) + a.xflag_off) +
+                                     a.xrank;
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(a.xepoch)
+                                 : "memory");
+                }
+            }
+        }
+    }
+}
+
+// The merge of a split sequence's partials from this GPU's exchange buffer
+// (every GPU pushed its partial and then its flag): one CTA per (row, head),
+// one thread per dim; thread 0 waits (bounded) for every flag to reach the
+// step's epoch.  Reference: the softmax over all positions (forward.rs:
+// 1831-1842) reassembled by the log-sum-exp rule, then the gate (:1327-1340).
+__global__ void __launch_bounds__(256) peer_merge_kernel(const float *xbuf, int world, int slot,
+                                                         unsigned epoch, int rows_heads,
+                                                         const float *qg, float *out,
+                                                         int *status) {
+    grid_dep_wait();  // this GPU's own partial and flag, and qg, are in place
+    const int hh = blockIdx.x, d = threadIdx.x;
+    const size_t stride = (size_t)rows_heads * (dm::HD + 2);
+    if (d == 0) {
+        const unsigned *flags = reinterpret_cast<const unsigned *>(
+            reinterpret_cast<const char *>(xbuf) + xbuf_flag_offset(world, rows_heads, dm::HD));
+        for (int g = 0; g < world; ++g) {
+            const long long start = clock64();
+            while (true) {
+                unsigned f;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + g)
+                             : "memory");
+                if ((int)(f - epoch) >= 0) break;
+                if (clock64() - start > WAIT_LIMIT_CYCLES) {
+                    atomicOr(status, DEV_TIMEOUT);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+    }
+    __syncthreads();
+    const float *p0 = xbuf + (size_t)slot * world * stride + (size_t)hh * (dm::HD + 2);
+    float M = -INFINITY;
+    for (int g = 0; g < world; ++g) M = fmaxf(M, __ldcv(p0 + g * stride + dm::HD));
+    float L = 0.0f, o = 0.0f;
+    for (int g = 0; g < world; ++g) {
+        const float *pg = p0 + g * stride;
+        const float m = __ldcv(pg + dm::HD);
+        const float sc = m == -INFINITY ? 0.0f : exp2f(m - M);
+        L = fmaf(__ldcv(pg + dm::HD + 1), sc, L);
+        o = fmaf(__ldcv(pg + d), sc, o);
+    }
+    const float gate = qg[(size_t)hh * 2 * dm::HD + dm::HD + d];
+    out[(size_t)hh * dm::HD + d] = (o / L) * sigmoidf_(gate);
+}
+
+cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned epoch,
+                              int rows_heads, const float *qg, float *out, int *status,
+                              cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows_heads);
+    cfg.blockDim = dim3(dm::HD);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, peer_merge_kernel, xbuf, world, slot, epoch, rows_heads, qg,
+                              out, status);
 }
 
 // Merges the partials of a sequence split across GPUs, gathered as

@@ -56,6 +56,14 @@ struct DecodeArgs {
     // non-null: the merge writes this shard's partial [t*n_head][hd + 2]
     // (unnormalised output, max in log2 units, sum) instead of the output
     float *part_out;
+    // non-null (a split sequence, peer exchange): the merge writes this GPU's
+    // partial into slot (xslot, xrank) of every GPU's exchange buffer and,
+    // once all its CTAs have, sets flag xrank of every GPU to xepoch
+    float *const *xpeers;  // [xworld] exchange buffers, as addressed from this GPU
+    int xrank, xworld, xslot;
+    unsigned xepoch;
+    size_t xflag_off;      // byte offset of the flags in an exchange buffer
+    int *xcount;           // arrival counter, zero between launches
 };
 cudaError_t init_decode_kernels();
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);
@@ -70,6 +78,22 @@ int decode_max_active_clusters(bool kv_bf16, bool fused, int csize);
 cudaError_t init_decode_mma_kernels();
 cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st);
 cudaError_t launch_decode_combine(const DecodeArgs &a, cudaStream_t st);
+// The exchange buffer of one GPU for a split sequence: partials
+// [2 slots][world][rows_heads][hd + 2] f32, then [world] u32 flags at a
+// 128-byte boundary.  Slot = epoch & 1.
+__host__ __device__ inline size_t xbuf_flag_offset(int world, int rows_heads, int hd) {
+    const size_t data = (size_t)2 * world * rows_heads * (hd + 2) * sizeof(float);
+    return (data + 127) / 128 * 128;
+}
+__host__ __device__ inline size_t xbuf_bytes(int world, int rows_heads, int hd) {
+    return xbuf_flag_offset(world, rows_heads, hd) + ((size_t)world * 4 + 127) / 128 * 128;
+}
+// Waits (bounded) until every GPU's flag in this GPU's exchange buffer has
+// reached `epoch`, then merges slot `slot`'s partials and applies the gate:
+// out [rows_heads][hd].  Launched as a programmatic dependent.
+cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned epoch,
+                              int rows_heads, const float *qg, float *out, int *status,
+                              cudaStream_t st);
 // parts [n_parts][rows_heads][hd + 2] -> out [rows_heads][hd], gated
 cudaError_t launch_merge_parts(const float *parts, int n_parts, int rows_heads, const float *qg,
                                float *out, cudaStream_t st);

@@ -74,6 +74,16 @@ struct rl_ctx {
     // the cache holds sequence positions shard_lo .. shard_lo + context - 1
     // of a sequence of seq_context positions (rl_set_shard)
     int shard_lo = 0, seq_context = 0;
+    // peer exchange of a split sequence (rl_exchange_*): this GPU's buffer,
+    // the table of every GPU's buffer as addressed from here, the buffers
+    // opened from other processes, the step's epoch and the arrival counter
+    float *xbuf = nullptr;
+    float **xpeers = nullptr;
+    std::vector<void *> xopened;
+    int xrank = 0, xworld = 0;
+    unsigned xepoch = 0;
+    int *xcount = nullptr;
+    bool xpublish = false;  // rl_full_attn_partial called by rl_split_publish
     std::string err;
     // per-kernel timing (rl_profile_*)
     bool prof_on = false;
@@ -506,6 +516,10 @@ void rl_ctx_destroy(rl_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (void *p : ctx->xopened) cudaIpcCloseMemHandle(p);
+    if (ctx->xbuf) cudaFree(ctx->xbuf);
+    if (ctx->xpeers) cudaFree(ctx->xpeers);
+    if (ctx->xcount) cudaFree(ctx->xcount);
     free_all(ctx);
     delete ctx;
 }
@@ -771,7 +785,8 @@ int rl_full_attn_partial(rl_ctx *ctx, int layer, int pos, const float *qg, const
     if (pos < 0 || pos >= ctx->seq_context)
         return fail(ctx, RL_ECONTEXT, "position %d is outside the sequence of %d", pos,
                     ctx->seq_context);
-    if (!qg || !k || !v || !partial) return fail(ctx, RL_EINVAL, "NULL input or output");
+    if (!qg || !k || !v || (!partial && !ctx->xpublish))
+        return fail(ctx, RL_EINVAL, "NULL input or output");
     if (((uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)partial) & 15)
         return fail(ctx, RL_EINVAL, "qg, k, v and partial must be 16-byte aligned");
     CK(ctx, cudaSetDevice(ctx->device));
@@ -807,9 +822,123 @@ int rl_full_attn_partial(rl_ctx *ctx, int layer, int pos, const float *qg, const
     d.v_row0 = d.k_row0 + c.n_head_kv * c.context;
     d.shard_lo = ctx->shard_lo;
     d.part_out = partial;
+    if (ctx->xpublish) {
+        const unsigned epoch = ++ctx->xepoch;
+        d.xpeers = ctx->xpeers;
+        d.xrank = ctx->xrank;
+        d.xworld = ctx->xworld;
+        d.xslot = (int)(epoch & 1);
+        d.xepoch = epoch;
+        d.xflag_off = rl::xbuf_flag_offset(ctx->xworld, c.n_head, c.head_dim);
+        d.xcount = ctx->xcount;
+    }
     const int64_t local = std::max<int64_t>(
         0, std::min<int64_t>((int64_t)pos + 1 - ctx->shard_lo, c.context));
     return bf16_walk(ctx, d, local, c.n_head_kv, 1, true);
+}
+
+int rl_exchange_init(rl_ctx *ctx, int rank, int world, void *handle_out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (world < 1 || rank < 0 || rank >= world || world > RL_EXCHANGE_MAX_GPUS)
+        return fail(ctx, RL_EINVAL, "rank %d of %d (at most %d GPUs)", rank, world,
+                    RL_EXCHANGE_MAX_GPUS);
+    if (ctx->xbuf) return fail(ctx, RL_EINVAL, "the exchange is already set up");
+    const rl_config &c = ctx->cfg;
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t bytes = rl::xbuf_bytes(world, c.n_head, c.head_dim);
+    // its own allocation, so that its IPC handle names exactly this buffer
+    CK(ctx, cudaMalloc(&ctx->xbuf, bytes));
+    CK(ctx, cudaMemset(ctx->xbuf, 0, bytes));
+    CK(ctx, cudaMalloc(&ctx->xcount, sizeof(int)));
+    CK(ctx, cudaMemset(ctx->xcount, 0, sizeof(int)));
+    CK(ctx, cudaMalloc(&ctx->xpeers, sizeof(float *) * world));
+    ctx->xrank = rank;
+    ctx->xworld = world;
+    ctx->xepoch = 0;
+    if (handle_out) {
+        cudaIpcMemHandle_t h;
+        CK(ctx, cudaIpcGetMemHandle(&h, ctx->xbuf));
+        static_assert(sizeof(h) == RL_IPC_HANDLE_BYTES, "IPC handle size");
+        memcpy(handle_out, &h, sizeof(h));
+    }
+    return RL_OK;
+}
+
+namespace {
+int upload_peers(rl_ctx *ctx, const std::vector<float *> &ptrs) {
+    CK(ctx, cudaMemcpy(ctx->xpeers, ptrs.data(), sizeof(float *) * ptrs.size(),
+                       cudaMemcpyHostToDevice));
+    return RL_OK;
+}
+}  // namespace
+
+int rl_exchange_connect(rl_ctx *ctx, const void *handles) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (!ctx->xbuf || !handles) return fail(ctx, RL_EINVAL, "rl_exchange_init first; handles");
+    CK(ctx, cudaSetDevice(ctx->device));
+    std::vector<float *> ptrs(ctx->xworld);
+    for (int g = 0; g < ctx->xworld; ++g) {
+        if (g == ctx->xrank) {
+            ptrs[g] = ctx->xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char *>(handles) + (size_t)g * RL_IPC_HANDLE_BYTES,
+               sizeof(h));
+        void *p = nullptr;
+        CK(ctx, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        ctx->xopened.push_back(p);
+        ptrs[g] = static_cast<float *>(p);
+    }
+    return upload_peers(ctx, ptrs);
+}
+
+int rl_exchange_connect_ptrs(rl_ctx *ctx, const uint64_t *bufs) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (!ctx->xbuf || !bufs) return fail(ctx, RL_EINVAL, "rl_exchange_init first; buffers");
+    CK(ctx, cudaSetDevice(ctx->device));
+    std::vector<float *> ptrs(ctx->xworld);
+    for (int g = 0; g < ctx->xworld; ++g)
+        ptrs[g] = g == ctx->xrank ? ctx->xbuf : reinterpret_cast<float *>(bufs[g]);
+    return upload_peers(ctx, ptrs);
+}
+
+uint64_t rl_exchange_buffer(const rl_ctx *ctx) {
+    return ctx ? reinterpret_cast<uint64_t>(ctx->xbuf) : 0;
+}
+
+int rl_split_publish(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
+                     const float *v) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (!ctx->xbuf) return fail(ctx, RL_EINVAL, "rl_exchange_init and _connect first");
+    // the walk and the merge of rl_full_attn_partial, the partial pushed to
+    // every GPU's exchange slot instead of a caller's buffer
+    ctx->xpublish = true;
+    const int code = rl_full_attn_partial(ctx, layer, pos, qg, k, v, nullptr);
+    ctx->xpublish = false;
+    return code;
+}
+
+int rl_split_merge(rl_ctx *ctx, const float *qg, float *out) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (!ctx->xbuf || ctx->xepoch == 0)
+        return fail(ctx, RL_EINVAL, "no partial published (rl_split_publish)");
+    if (!qg || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    CK(ctx, cudaSetDevice(ctx->device));
+    {
+        ProfScope ps(ctx, RL_PROF_MERGE);
+        CK(ctx, rl::launch_peer_merge(ctx->xbuf, ctx->xworld, (int)(ctx->xepoch & 1),
+                                      ctx->xepoch, ctx->cfg.n_head, qg, out, ctx->status,
+                                      ctx->stream));
+    }
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
+
+int rl_full_attn_split(rl_ctx *ctx, int layer, int pos, const float *qg, const float *k,
+                       const float *v, float *out) {
+    const int code = rl_split_publish(ctx, layer, pos, qg, k, v);
+    return code != RL_OK ? code : rl_split_merge(ctx, qg, out);
 }
 
 int rl_merge_partials(rl_ctx *ctx, int n_parts, const float *parts, const float *qg,

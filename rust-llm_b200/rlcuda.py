@@ -28,6 +28,8 @@ RL_KV_F32, RL_KV_BF16 = 0, 1
  RL_OPT_VERIFY_TC) = 0, 1, 2, 3, 4, 5
 PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify")
 HOST, DEVICE = 0, 1
+RL_IPC_HANDLE_BYTES = 64
+RL_EXCHANGE_MAX_GPUS = 8
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _vp = ctypes.c_void_p
@@ -109,6 +111,13 @@ SIGNATURES = {
     "rl_set_shard": ([_vp, _i, _i], _i),
     "rl_full_attn_partial": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "rl_merge_partials": ([_vp, _i, _vp, _vp, _vp], _i),
+    "rl_exchange_init": ([_vp, _i, _i, _vp], _i),
+    "rl_exchange_connect": ([_vp, _vp], _i),
+    "rl_exchange_connect_ptrs": ([_vp, ctypes.POINTER(ctypes.c_uint64)], _i),
+    "rl_exchange_buffer": ([_vp], ctypes.c_uint64),
+    "rl_split_publish": ([_vp, _i, _i, _vp, _vp, _vp], _i),
+    "rl_split_merge": ([_vp, _vp, _vp], _i),
+    "rl_full_attn_split": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "rl_version": ([], ctypes.c_char_p),
 }
 
@@ -264,6 +273,36 @@ class Context:
         """parts [n_parts][n_head][head_dim + 2] f32 (device) -> out [n_head*head_dim]."""
         self._check(self._L.rl_merge_partials(self._h, int(parts.shape[0]), _ptr(parts), _ptr(qg),
                                               _ptr(out)))
+
+    # -- split sequence over peer memory (rl_exchange_*) --------------------
+    def exchange_init(self, rank: int, world: int) -> bytes:
+        """Allocates this GPU's exchange buffer; returns its CUDA IPC handle."""
+        h = ctypes.create_string_buffer(RL_IPC_HANDLE_BYTES)
+        self._check(self._L.rl_exchange_init(self._h, rank, world, h))
+        return h.raw
+
+    def exchange_connect(self, handles):
+        """Every rank's handle, in rank order (this rank's own is ignored)."""
+        blob = b"".join(handles)
+        self._check(self._L.rl_exchange_connect(self._h, blob))
+
+    def exchange_connect_ptrs(self, bufs):
+        """Every rank's exchange buffer as a device pointer of this process."""
+        arr = (ctypes.c_uint64 * len(bufs))(*bufs)
+        self._check(self._L.rl_exchange_connect_ptrs(self._h, arr))
+
+    def exchange_buffer(self) -> int:
+        return int(self._L.rl_exchange_buffer(self._h))
+
+    def split_publish(self, layer, pos, qg, k, v):
+        self._check(self._L.rl_split_publish(self._h, layer, pos, _ptr(qg), _ptr(k), _ptr(v)))
+
+    def split_merge(self, qg, out):
+        self._check(self._L.rl_split_merge(self._h, _ptr(qg), _ptr(out)))
+
+    def full_attn_split(self, layer, pos, qg, k, v, out):
+        self._check(self._L.rl_full_attn_split(self._h, layer, pos, _ptr(qg), _ptr(k), _ptr(v),
+                                               _ptr(out)))
 
     def linear_attn_host(self, layer, live, qkv, z, alpha, beta) -> np.ndarray:
         t = qkv.shape[0]

@@ -75,6 +75,10 @@ class SplitDecoder:
 
     def step(self, layer: int, pos: int, qg, k, v, out):
         import torch.distributed as dist
+        if getattr(self.shard, "exchange", False):
+            # the partials cross NVLink as peer-memory stores (no NCCL)
+            self.shard.split(layer, pos, qg, k, v, out)
+            return out
         self.shard.partial(layer, pos, qg, k, v, self.partial)
         if self.world > 1:
             dist.all_gather_into_tensor(self.gathered_flat, self.partial, group=self.group)
@@ -85,17 +89,40 @@ class SplitDecoder:
 
 
 class GpuShard:
-    """The GPU side of a SplitDecoder: one rl_ctx holding this rank's range."""
+    """The GPU side of a SplitDecoder: one rl_ctx holding this rank's range.
+    With `exchange`, the partials cross between GPUs through peer memory
+    (rl_exchange_*, rl_full_attn_split) instead of an NCCL all-gather; the
+    ranks swap their buffers' CUDA IPC handles once over the process group."""
 
-    def __init__(self, ctx, lo: int, seq_context: int):
+    def __init__(self, ctx, lo: int, seq_context: int, exchange: bool = False,
+                 rank: int = 0, world: int = 1, group=None):
         self.ctx = ctx
+        self.exchange = exchange
         ctx.set_shard(lo, seq_context)
+        if exchange:
+            handle = ctx.exchange_init(rank, world)
+            handles = connect_handles(handle, world, group)
+            ctx.exchange_connect(handles)
 
     def partial(self, layer, pos, qg, k, v, out_partial):
         self.ctx.full_attn_partial(layer, pos, qg, k, v, out_partial)
 
     def merge(self, parts, qg, out):
         self.ctx.merge_partials(parts, qg, out)
+
+    def split(self, layer, pos, qg, k, v, out):
+        self.ctx.full_attn_split(layer, pos, qg, k, v, out)
+
+
+def connect_handles(handle: bytes, world: int, group=None) -> list:
+    """Every rank's exchange handle, in rank order (an all-gather of small
+    host objects over the process group; the handle itself for world 1)."""
+    if world == 1:
+        return [handle]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, handle, group=group)
+    return out
 
 
 def partition_sequences(lengths, world: int) -> list[list[int]]:

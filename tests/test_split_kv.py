@@ -130,3 +130,31 @@ def test_sequence_partition_balances_context():
         assert max(loads) - min(loads) <= max(lens)
         assert max(loads) <= sum(lens) / world + max(lens)
     assert split_kv.partition_sequences([5, 9, 1], 2) == [[1], [0, 2]]
+
+
+def _handles_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    got = split_kv.connect_handles(bytes([rank]) * 64, world)
+    q.put((rank, got))
+    dist.destroy_process_group()
+
+
+def test_exchange_handles_arrive_in_rank_order():
+    """The peer exchange's set-up swaps each rank's 64-byte IPC handle over
+    the process group; every rank must see all of them in rank order."""
+    world = 3
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_handles_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert res[r] == [bytes([g]) * 64 for g in range(world)]
+    assert split_kv.connect_handles(b"x" * 64, 1) == [b"x" * 64]

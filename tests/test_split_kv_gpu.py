@@ -63,3 +63,83 @@ def test_a_shard_context_refuses_the_single_gpu_entry_point():
                                np.zeros((1, 1024), np.float32))
         with pytest.raises(rlcuda.RlError):
             ctx.set_shard(400, 512)  # 400 + 128 runs past the sequence
+
+
+@pytest.mark.parametrize("world,seq", [(1, 700), (2, 4096), (4, 3000), (8, 8192)])
+def test_peer_exchange_merges_to_the_single_pass_row(world, seq):
+    """The exchange over peer memory (rl_split_publish / rl_split_merge),
+    shards emulated on one GPU with their buffers connected by pointer:
+    every shard publishes (pushing its partial and flag into every shard's
+    buffer), then every shard merges.  Two steps, so both slots and both
+    epochs are used; every shard's row must be the single-pass row."""
+    dev = torch.device("cuda", 0)
+    ctxs = []
+    for r in range(world):
+        lo, n = split_kv.shard_range(seq, world, r)
+        cfg = rlcuda.qwen35_config(n_full=1, n_linear=0, context=n, kv_dtype=rlcuda.RL_KV_BF16,
+                                   max_batch=1)
+        ctx = rlcuda.Context(cfg)
+        ctx.set_shard(lo, seq)
+        ctx.exchange_init(r, world)
+        ctxs.append(ctx)
+    bufs = [c.exchange_buffer() for c in ctxs]
+    for c in ctxs:
+        c.exchange_connect_ptrs(bufs)
+    for step, pos in enumerate((seq - 2, seq - 1)):
+        case = cases.full_case(90 + world + step, pos, 1, kv_bf16=True)
+        want, _ = cases.oracle_full(case, seq, kv_bf16=True)
+        qg = torch.from_numpy(case.qg.reshape(-1)).to(dev)
+        k = torch.from_numpy(case.k.reshape(-1)).to(dev)
+        v = torch.from_numpy(case.v.reshape(-1)).to(dev)
+        for r, c in enumerate(ctxs):
+            lo, n = split_kv.shard_range(seq, world, r)
+            m = min(n, max(0, pos - lo))
+            if m:
+                c.write_kv(0, 0, np.ascontiguousarray(case.cache[:, :, lo:lo + m]))
+            c.split_publish(0, pos, qg, k, v)
+        for c in ctxs:
+            c.sync()  # every flag is up before any merge waits on it
+        for c in ctxs:
+            out = torch.empty(16 * 256, device=dev)
+            c.split_merge(qg, out)
+            c.sync()
+            got = out.cpu().numpy()[None]
+            assert cases.rel_err_per_head(got, want, cases.HD) <= TOL, step
+    for c in ctxs:
+        c.close()
+
+
+def test_exchange_contract_errors():
+    cfg = rlcuda.qwen35_config(n_full=1, n_linear=0, context=128, kv_dtype=rlcuda.RL_KV_BF16,
+                               max_batch=1)
+    with rlcuda.Context(cfg) as ctx:
+        ctx.set_shard(0, 256)
+        x = torch.zeros(16 * 512, device="cuda")
+        with pytest.raises(rlcuda.RlError):
+            ctx.split_merge(x, torch.empty(4096, device="cuda"))  # nothing set up or published
+        with pytest.raises(rlcuda.RlError):
+            ctx.exchange_init(2, 2)  # rank outside the world
+        ctx.exchange_init(0, 1)
+        with pytest.raises(rlcuda.RlError):
+            ctx.exchange_init(0, 1)  # twice
+
+
+def test_peer_exchange_across_two_gpus():
+    """Two processes, one GPU each, the buffers shared by CUDA IPC handles
+    swapped over gloo: the ranks' rows equal the single-pass row."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join(
+        [here, os.path.join(here, "..", "rust-llm_b200"), os.path.join(here, "..", "oracle"),
+         os.environ.get("PYTHONPATH", "")]), NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(
+        ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+         "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
+         "29611", os.path.join(here, "split_exchange_worker.py")],
+        env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert r.stdout.count("exchange ok") == 2, r.stdout[-2000:]
