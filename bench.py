@@ -523,6 +523,10 @@ def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
         for _ in range(max(3, args.warmup)):
             step()
     ms = timed(step, reps)
+    def walks():
+        for layer in range(N_LAYERS):
+            shard.partial(layer, pos, qg[layer], kk[layer], vv[layer], dec.partial)
+    walk_ms = timed(walks, reps)
     nccl_ms = None
     if world > 1:
         shard.exchange = False  # the same step with an NCCL all-gather
@@ -546,6 +550,7 @@ def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
                         "stores + flags, merged on every GPU)",
             "scaling": "strong", "us_per_layer": us,
             "nccl_us_per_layer": nccl_ms * 1e3 / (reps * N_LAYERS) if nccl_ms else None,
+            "walk_us_per_layer": walk_ms * 1e3 / (reps * N_LAYERS),
             "gather_us_per_layer": g_ms * 1e3 / (reps * N_LAYERS),
             "kv_bytes_per_gpu_per_layer": local_bytes,
             "hbm_gbs_per_gpu": local_bytes / (us * 1e-6) / 1e9,

@@ -629,7 +629,8 @@ __global__ void __launch_bounds__(256) peer_merge_kernel(const float *xbuf, int 
                                                          unsigned epoch, int rows_heads,
                                                          const float *qg, float *out,
                                                          int *status) {
-    grid_dep_wait();  // this GPU's own partial and flag, and qg, are in place
+    grid_dep_wait();    // this GPU's own partial and flag, and qg, are in place
+    grid_dep_launch();  // the next layer's walk may start streaming meanwhile
     const int hh = blockIdx.x, d = threadIdx.x;
     const size_t stride = (size_t)rows_heads * (dm::HD + 2);
     if (d == 0) {
