@@ -564,9 +564,11 @@ def batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
     """Config 4b: 64 independent sequences, contexts U[4096, 32768] (seed 5),
     dealt to the job's GPUs longest first (no collective); one decode row per
     sequence through 8 bf16 full-attention layers, one rl_ctx per sequence as
-    the reference's Runner holds one sequence, CUDA-graph captured.  Returns
-    µs per layer-step of the whole batch (max over ranks) and the aggregate
-    HBM rate of the cache bytes."""
+    the reference's Runner holds one sequence, CUDA-graph captured.  Each
+    layer-step is one batched walk over all of the GPU's sequences
+    (rl_batch_full_attn); the same step through one rl_full_attn per
+    sequence is timed beside it.  Returns µs per layer-step of the whole
+    batch (max over ranks) and the aggregate HBM rate of the cache bytes."""
     import numpy as np
     import split_kv
     lens = [int(x) for x in np.random.default_rng(5).integers(BATCH_LO, BATCH_HI + 1,
@@ -586,47 +588,60 @@ def batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
         del src
         ctxs.append(c)
     torch.cuda.empty_cache()
-    qg = torch.randn((N_HEAD * 2 * HD,), generator=gen, device=dev)
-    kk = torch.randn((N_KV * HD,), generator=gen, device=dev)
-    vv = torch.randn((N_KV * HD,), generator=gen, device=dev)
-    outs = torch.empty((len(mine), N_HEAD * HD), device=dev)
+    nb = len(mine)
+    qg = torch.randn((nb, N_HEAD * 2 * HD), generator=gen, device=dev)
+    kk = torch.randn((nb, N_KV * HD), generator=gen, device=dev)
+    vv = torch.randn((nb, N_KV * HD), generator=gen, device=dev)
+    outs = torch.empty((nb, N_HEAD * HD), device=dev)
+    pos_t = torch.tensor([lens[i] for i in mine], dtype=torch.int32, device=dev)
+    batch = rlcuda.Batch(ctxs) if nb else None
 
-    def step():
+    def step_batched():
+        for layer in range(N_LAYERS):
+            batch.full_attn(layer, pos_t, qg, kk, vv, outs)
+
+    def step_each():
         for layer in range(N_LAYERS):
             for j, i in enumerate(mine):
-                ctxs[j].full_attn(layer, lens[i], 1, qg, kk, vv, outs[j])
+                ctxs[j].full_attn(layer, lens[i], 1, qg[j], kk[j], vv[j], outs[j])
 
-    with torch.cuda.stream(stream):
-        step()
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    reps = max(3, min(args.steps // 50, 20))
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            graph.replay()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        e1.record(stream)
-    stream.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
-    graph.reset()
+    def timed(step):
+        with torch.cuda.stream(stream):
+            step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        reps = max(3, min(args.steps // 50, 20))
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                graph.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (reps * N_LAYERS)], device=dev,
+                         dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        graph.reset()
+        return float(t.item())
+
+    us = timed(step_batched) if nb else 0.0
+    us_each = timed(step_each) if nb else 0.0
+    if batch:
+        batch.close()
     for c in ctxs:
         c.sync()
         c.close()
     torch.cuda.empty_cache()
-    us = ms * 1e3 / (reps * N_LAYERS)
     total = sum(lens) * 2 * N_KV * HD * 2  # cache bytes of one layer over the batch
     return {"workload": f"config 4b: {BATCH_SEQS} sequences, contexts U[{BATCH_LO}, {BATCH_HI}] "
                         f"(seed 5), 8 bf16 full-attention layers, longest-first over {world} "
@@ -634,7 +649,11 @@ def batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
             "scaling": "strong", "sequences_per_gpu": len(mine),
             "us_per_layer_step": us, "kv_bytes_per_layer": total,
             "hbm_gbs_aggregate": total / (us * 1e-6) / 1e9,
-            "launches_per_step": 2 * N_LAYERS * len(mine)}
+            "launch": "rl_batch_full_attn: one walk + one merge launch per layer for all of "
+                      "the GPU's sequences",
+            "launches_per_step": 2 * N_LAYERS,
+            "per_sequence_us_per_layer_step": us_each,
+            "per_sequence_hbm_gbs_aggregate": total / (us_each * 1e-6) / 1e9}
 
 
 def run_ours(args):

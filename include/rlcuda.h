@@ -186,6 +186,24 @@ int rl_live(const rl_ctx *ctx);
  * kernel flagged a bounded wait that gave up or a bad argument on the device. */
 int rl_sync(rl_ctx *ctx);
 
+/*
+ * Batched decode over many sequences on one GPU (no counterpart in the
+ * reference, whose Runner holds one sequence).  rl_batch_create takes n
+ * contexts (bf16 caches, same shapes, same device; each its own sequence);
+ * rl_batch_full_attn runs one decode row per sequence of a full layer in one
+ * walk launch: row i is sequence i at position pos[i] (a device array), with
+ * qg [n][n_head][2*hd], k, v [n][n_kv][hd] and out [n][n_head*hd] device
+ * arrays.  Each row appends its key and value to its own context, exactly
+ * as rl_full_attn(ctxs[i], layer, pos[i], 1, ...) would, and gives the same
+ * row.  The batch runs on ctxs[0]'s stream; a batch must not outlive its
+ * contexts.
+ */
+typedef struct rl_batch rl_batch;
+int rl_batch_create(rl_ctx *const *ctxs, int n, rl_batch **out);
+int rl_batch_full_attn(rl_batch *b, int layer, const int *pos, const float *qg, const float *k,
+                       const float *v, float *out);
+void rl_batch_destroy(rl_batch *b);
+
 /* Tuning and dispatch knobs (rl_set_option). */
 typedef enum {
     RL_OPT_SPLITS = 0,        /* force the KV splits of the decode walk (0: automatic) */

@@ -148,34 +148,40 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int pos_row = a.pos + row;        // sequence position of this row
+    // a batch row is its own sequence with its own cache and tensor map
+    const BatchRow *br = a.rows ? a.rows + row : nullptr;
+    const int pos_row = br ? a.batch_pos[row] : a.pos + row;  // sequence position of this row
+    const int ctx_row = br ? br->context : a.context;
+    const CUtensorMap *map = br ? br->map : &kv_map;
     // this cache holds sequence positions shard_lo .. shard_lo + context - 1
     const int loc_row = pos_row - a.shard_lo;  // the row's cache index (may lie outside)
-    const int n_kv = max(0, min(loc_row + 1, a.context));  // cached positions the row sees
+    const int n_kv = max(0, min(loc_row + 1, ctx_row));  // cached positions the row sees
     const int n_all = (n_kv + P - 1) / P;   // tiles of this row
     const int n_split = a.n_splits;          // CTAs sharing them
     const int head0 = row * a.n_head + kh * GROUP;
-    __nv_bfloat16 *const k_cache = static_cast<__nv_bfloat16 *>(a.k_cache_v);
-    __nv_bfloat16 *const v_cache = static_cast<__nv_bfloat16 *>(a.v_cache_v);
+    __nv_bfloat16 *const k_cache = static_cast<__nv_bfloat16 *>(br ? br->k_cache : a.k_cache_v);
+    __nv_bfloat16 *const v_cache = static_cast<__nv_bfloat16 *>(br ? br->v_cache : a.v_cache_v);
+    const float *const q_norm = br ? br->q_norm : a.q_norm;
+    const float *const k_norm = br ? br->k_norm : a.k_norm;
     // every CTA of a KV head builds the appended row (any of them may draw
     // the tile holding it); split 0 writes it to the cache
-    const bool builds_new = FUSED && loc_row >= 0 && loc_row < a.context;
+    const bool builds_new = FUSED && loc_row >= 0 && loc_row < ctx_row;
     const bool writes_new = builds_new && split == 0;
-    const float *cs_row = a.rope_cs + (size_t)pos_row * (a.n_rot / 2);
-    const float *sn_row = a.rope_sn + (size_t)pos_row * (a.n_rot / 2);
+    const float *cs_row = (br ? br->rope_cs : a.rope_cs) + (size_t)pos_row * (a.n_rot / 2);
+    const float *sn_row = (br ? br->rope_sn : a.rope_sn) + (size_t)pos_row * (a.n_rot / 2);
     const float *kv_in = (warp == 0 ? a.k_in : a.v_in) + (size_t)row * a.n_kv * HD + (size_t)kh * HD;
     if (FUSED && warp < CWARPS && lane < 8) {
         // warm L2 with this step's small inputs while the previous grid
         // finishes; the values themselves are read after the wait
         const float *q = a.qg + (size_t)(head0 + warp) * 2 * HD;
         asm volatile("prefetch.global.L2 [%0];" ::"l"(q + lane * 32));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.q_norm + lane * 32));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(q_norm + lane * 32));
         if (warp < 2) asm volatile("prefetch.global.L2 [%0];" ::"l"(kv_in + lane * 32));
         if (warp == 0 && lane == 0) {
             asm volatile("prefetch.global.L2 [%0];" ::"l"(cs_row));
             asm volatile("prefetch.global.L2 [%0];" ::"l"(sn_row));
         }
-        if (warp == 1) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.k_norm + lane * 32));
+        if (warp == 1) asm volatile("prefetch.global.L2 [%0];" ::"l"(k_norm + lane * 32));
     }
 
     if (tid == 0) {
@@ -207,12 +213,12 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
         // draw past the end; the last such draw resets the counter for the
         // next launch.
         if (lane == 0) {
-            prefetch_tensormap(&kv_map);
+            prefetch_tensormap(map);
             if (!a.early_kv) grid_dep_wait();
             int *counter = a.counters + ((size_t)row * a.n_kv + kh) * 8;
             const int n_dyn = max(0, n_all - kStaticRounds * n_split);
-            const int krow = a.k_row0 + kh * a.context;
-            const int vrow = a.v_row0 + kh * a.context;
+            const int krow = (br ? br->k_row0 : a.k_row0) + kh * ctx_row;
+            const int vrow = (br ? br->v_row0 : a.v_row0) + kh * ctx_row;
             const int early = max(1, min(a.early_tiles, STAGES));
             int issued = 0, round = 0, tile = split;
             bool stopped = false;
@@ -238,9 +244,9 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
                 unsigned char *st = smem + (size_t)s * STAGE_BYTES;
 #pragma unroll
                 for (int b = 0; b < NBOX; ++b) {
-                    tma_load_2d(st + b * BOX_BYTES, &kv_map, b * BOX_COLS, krow + tile * P,
+                    tma_load_2d(st + b * BOX_BYTES, map, b * BOX_COLS, krow + tile * P,
                                 &full_bar[s]);
-                    tma_load_2d(st + HALF_BYTES + b * BOX_BYTES, &kv_map, b * BOX_COLS,
+                    tma_load_2d(st + HALF_BYTES + b * BOX_BYTES, map, b * BOX_COLS,
                                 vrow + tile * P, &full_bar[s]);
                 }
                 ++issued;
@@ -267,10 +273,10 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
         grid_dep_wait();  // the step's inputs come from the kernel before
         if (FUSED) {
             LaneHead hq, hk;
-            load_lane_head(hq, a.qg + (size_t)(head0 + warp) * 2 * HD, a.q_norm, cs_row, sn_row,
+            load_lane_head(hq, a.qg + (size_t)(head0 + warp) * 2 * HD, q_norm, cs_row, sn_row,
                            a.n_rot, lane);
             if (builds_new && warp < 2)
-                load_lane_head(hk, kv_in, a.k_norm, cs_row, sn_row, a.n_rot, lane);
+                load_lane_head(hk, kv_in, k_norm, cs_row, sn_row, a.n_rot, lane);
             lane_norm_rope(hq, q_s[warp], a.n_rot, a.eps, lane);
             if (builds_new && warp < 2) {
                 float y[8];
@@ -283,7 +289,7 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
                     for (int e = 0; e < 8; ++e) y[e] = hk.x[e];
                 }
                 __nv_bfloat16 *cache = (warp == 0 ? k_cache : v_cache) +
-                                       ((size_t)kh * a.context + loc_row) * HD + lane * 8;
+                                       ((size_t)kh * ctx_row + loc_row) * HD + lane * 8;
                 __nv_bfloat16 *keep = (warp == 0 ? newk_s : newv_s) + lane * 8;
                 uint4 packed;
                 packed.x = pack_bf16(y[0], y[1]);

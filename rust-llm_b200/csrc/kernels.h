@@ -27,6 +27,16 @@ struct FullArgs {
     bool kv_only;
 };
 
+// One sequence of a batched bf16 decode (rl_batch_*): its context's cache of
+// one layer, seen through its own tensor map (kept in global memory).
+struct BatchRow {
+    const CUtensorMap *map;        // 64-byte aligned, in device memory
+    void *k_cache, *v_cache;       // this layer's [n_kv][context][hd] bf16
+    const float *q_norm, *k_norm;  // this layer's norm weights
+    const float *rope_cs, *rope_sn;
+    int context, k_row0, v_row0;   // tensor-map rows as in DecodeArgs
+};
+
 // One launch of the split-KV decode kernel (decode_attn.cu).
 struct DecodeArgs {
     const float *qg;              // [t][n_head][2*hd] raw query | gate
@@ -64,6 +74,10 @@ struct DecodeArgs {
     unsigned xepoch;
     size_t xflag_off;      // byte offset of the flags in an exchange buffer
     int *xcount;           // arrival counter, zero between launches
+    // non-null (bf16 walk, one row per sequence): row r is sequence r, at
+    // position batch_pos[r] of its own context, described by rows[r]
+    const BatchRow *rows;
+    const int *batch_pos;
 };
 cudaError_t init_decode_kernels();
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);

@@ -941,6 +941,155 @@ int rl_full_attn_split(rl_ctx *ctx, int layer, int pos, const float *qg, const f
     return code != RL_OK ? code : rl_split_merge(ctx, qg, out);
 }
 
+// ---- batched decode over the contexts of many sequences -------------------
+struct rl_batch {
+    std::vector<rl_ctx *> ctxs;
+    int n = 0, n_full = 0;
+    rl::BatchRow *rows = nullptr;     // [n_full][n]
+    CUtensorMap *maps = nullptr;      // [n], device copies of the contexts' maps
+    float *part_o = nullptr, *part_ml = nullptr;
+    int *counters = nullptr;          // [n][n_kv][8]
+    int splits = 1;
+};
+
+void rl_batch_destroy(rl_batch *b) {
+    if (!b) return;
+    if (!b->ctxs.empty()) {
+        cudaSetDevice(b->ctxs[0]->device);
+        cudaStreamSynchronize(b->ctxs[0]->stream);
+    }
+    cudaFree(b->rows);
+    cudaFree(b->maps);
+    cudaFree(b->part_o);
+    cudaFree(b->part_ml);
+    cudaFree(b->counters);
+    delete b;
+}
+
+int rl_batch_create(rl_ctx *const *ctxs, int n, rl_batch **out) {
+    if (!ctxs || n < 1 || !out) return fail(nullptr, RL_EINVAL, "contexts, n >= 1 and out");
+    *out = nullptr;
+    rl_ctx *c0 = ctxs[0];
+    if (!c0) return fail(nullptr, RL_EINVAL, "NULL context");
+    const rl_config &c = c0->cfg;
+    for (int i = 0; i < n; ++i) {
+        const rl_ctx *x = ctxs[i];
+        if (!x) return fail(nullptr, RL_EINVAL, "NULL context %d", i);
+        const rl_config &ci = x->cfg;
+        if (x->device != c0->device || ci.kv_dtype != RL_KV_BF16 || ci.n_full != c.n_full ||
+            ci.n_head != c.n_head || ci.n_head_kv != c.n_head_kv || ci.head_dim != c.head_dim ||
+            ci.n_rot != c.n_rot || ci.rms_eps != c.rms_eps || c.n_full < 1)
+            return fail(c0, RL_EINVAL,
+                        "context %d: a batch needs bf16 caches of the same shapes on one device",
+                        i);
+        if (x->shard_lo != 0 || x->seq_context != ci.context)
+            return fail(c0, RL_EINVAL, "context %d holds a shard of a split sequence", i);
+    }
+    if (cudaSetDevice(c0->device) != cudaSuccess)
+        return fail(c0, RL_ECUDA, "cudaSetDevice failed");
+    rl_batch *b = new rl_batch();
+    b->ctxs.assign(ctxs, ctxs + n);
+    b->n = n;
+    b->n_full = c.n_full;
+    // splits per (sequence, KV head): about eight waves of walk CTAs in all
+    const int64_t resident = (int64_t)std::max(1, c0->mma_per_sm[1]) * c0->num_sms;
+    b->splits = (int)std::max<int64_t>(
+        1, std::min<int64_t>(16, (8 * resident + (int64_t)c.n_head_kv * n - 1) /
+                                     ((int64_t)c.n_head_kv * n)));
+    const size_t rows_heads = (size_t)n * c.n_head;
+    bool ok = cudaMalloc(&b->rows, sizeof(rl::BatchRow) * c.n_full * n) == cudaSuccess &&
+              cudaMalloc(&b->maps, sizeof(CUtensorMap) * n) == cudaSuccess &&
+              cudaMalloc(&b->part_o, sizeof(float) * rows_heads * b->splits * c.head_dim) ==
+                  cudaSuccess &&
+              cudaMalloc(&b->part_ml, sizeof(float) * rows_heads * b->splits * 2) == cudaSuccess &&
+              cudaMalloc(&b->counters, sizeof(int) * n * c.n_head_kv * 8) == cudaSuccess &&
+              cudaMemset(b->counters, 0, sizeof(int) * n * c.n_head_kv * 8) == cudaSuccess;
+    if (ok) {
+        std::vector<CUtensorMap> maps(n);
+        std::vector<rl::BatchRow> rows((size_t)c.n_full * n);
+        for (int i = 0; i < n; ++i) {
+            rl_ctx *x = ctxs[i];
+            maps[i] = x->kv_map;
+            for (int l = 0; l < c.n_full; ++l) {
+                rl::BatchRow &r = rows[(size_t)l * n + i];
+                const rl_config &ci = x->cfg;
+                r.map = b->maps + i;
+                r.k_cache = kv_layer(x, l);
+                r.v_cache = (char *)r.k_cache +
+                            (size_t)ci.n_head_kv * ci.context * ci.head_dim * kv_elem(ci);
+                r.q_norm = x->q_norm + (size_t)l * ci.head_dim;
+                r.k_norm = x->k_norm + (size_t)l * ci.head_dim;
+                r.rope_cs = x->rope_cs;
+                r.rope_sn = x->rope_sn;
+                r.context = ci.context;
+                r.k_row0 = l * 2 * ci.n_head_kv * ci.context;
+                r.v_row0 = r.k_row0 + ci.n_head_kv * ci.context;
+            }
+        }
+        ok = cudaMemcpy(b->maps, maps.data(), sizeof(CUtensorMap) * n, cudaMemcpyHostToDevice) ==
+                 cudaSuccess &&
+             cudaMemcpy(b->rows, rows.data(), sizeof(rl::BatchRow) * rows.size(),
+                        cudaMemcpyHostToDevice) == cudaSuccess;
+    }
+    if (!ok) {
+        rl_batch_destroy(b);
+        return fail(c0, RL_ENOMEM, "allocating the batch's %d rows failed", n);
+    }
+    *out = b;
+    return RL_OK;
+}
+
+int rl_batch_full_attn(rl_batch *b, int layer, const int *pos, const float *qg, const float *k,
+                       const float *v, float *out) {
+    if (!b) return fail(nullptr, RL_EINVAL, "NULL batch");
+    rl_ctx *ctx = b->ctxs[0];
+    const rl_config &c = ctx->cfg;
+    if (layer < 0 || layer >= b->n_full)
+        return fail(ctx, RL_EINVAL, "full layer %d of %d", layer, b->n_full);
+    if (!pos || !qg || !k || !v || !out) return fail(ctx, RL_EINVAL, "NULL input or output");
+    if (((uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15)
+        return fail(ctx, RL_EINVAL, "qg, k, v and out must be 16-byte aligned");
+    CK(ctx, cudaSetDevice(ctx->device));
+    rl::DecodeArgs d{};
+    d.qg = qg;
+    d.k_in = k;
+    d.v_in = v;
+    d.part_o = b->part_o;
+    d.part_ml = b->part_ml;
+    d.counters = b->counters;
+    d.out = out;
+    d.status = ctx->status;
+    d.pos = 0;
+    d.t = b->n;
+    d.context = c.context;
+    d.n_head = c.n_head;
+    d.n_kv = c.n_head_kv;
+    d.n_rot = c.n_rot;
+    d.theta_scale = ctx->theta_scale;
+    d.eps = c.rms_eps;
+    d.kv_bf16 = true;
+    d.fused = true;
+    d.rows = b->rows + (size_t)layer * b->n;
+    d.batch_pos = pos;
+    d.n_splits = b->splits;
+    // each CTA's first tiles are its own; the rest come from the sequence's
+    // counter, so CTAs of short and long sequences alike end near together
+    d.chunk = 0;
+    d.csize = 1;
+    d.early_kv = false;
+    d.early_tiles = (int)ctx->opt_early_tiles;
+    {
+        ProfScope ps(ctx, RL_PROF_DECODE);
+        CK(ctx, rl::launch_decode_mma(d, ctx->kv_map, ctx->stream));
+    }
+    {
+        ProfScope ps(ctx, RL_PROF_MERGE);
+        CK(ctx, rl::launch_decode_combine(d, ctx->stream));
+    }
+    for (rl_ctx *x : b->ctxs) x->early_ok = false;
+    return RL_OK;
+}
+
 int rl_merge_partials(rl_ctx *ctx, int n_parts, const float *parts, const float *qg,
                       float *out) {
     if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");

@@ -118,6 +118,9 @@ SIGNATURES = {
     "rl_split_publish": ([_vp, _i, _i, _vp, _vp, _vp], _i),
     "rl_split_merge": ([_vp, _vp, _vp], _i),
     "rl_full_attn_split": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
+    "rl_batch_create": ([ctypes.POINTER(_vp), _i, ctypes.POINTER(_vp)], _i),
+    "rl_batch_full_attn": ([_vp, _i, _vp, _vp, _vp, _vp, _vp], _i),
+    "rl_batch_destroy": ([_vp], None),
     "rl_version": ([], ctypes.c_char_p),
 }
 
@@ -355,3 +358,36 @@ class Context:
         out = np.empty(self._state_shape(True), np.float32)
         self._check(self._L.rl_read_ssm(self._h, layer, out.ctypes.data, HOST))
         return out
+
+
+class Batch:
+    """Batched decode over many contexts (rl_batch_*): one walk launch per
+    layer for one decode row of every sequence.  Runs on the first context's
+    stream; close it before its contexts."""
+
+    def __init__(self, ctxs):
+        self.ctxs = list(ctxs)
+        self._L = self.ctxs[0]._L
+        arr = (_vp * len(self.ctxs))(*[c.handle for c in self.ctxs])
+        h = _vp()
+        code = self._L.rl_batch_create(arr, len(self.ctxs), ctypes.byref(h))
+        if code:
+            raise RlError(code, self._L.rl_last_error(self.ctxs[0].handle).decode())
+        self._h = h
+
+    def full_attn(self, layer, pos, qg, k, v, out):
+        """Device tensors: pos [n] int32, qg [n][n_head*2*hd], k, v [n][n_kv*hd],
+        out [n][n_head*hd]."""
+        self.ctxs[0]._check(self._L.rl_batch_full_attn(self._h, layer, _ptr(pos), _ptr(qg), _ptr(k),
+                                                       _ptr(v), _ptr(out)))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.rl_batch_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
