@@ -220,11 +220,15 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                     }
                     appended_visible = true;
                 }
-                unsigned char *st = smem + RING + s * STAGE + (is_k ? 0 : KV_HALF);
+                // K: box b of stage s at b * NST + s (the stages of a box are
+                // adjacent rows); V: stage s's four boxes together
                 mbar_arrive_expect_tx(&full[s], KV_HALF);
-                for (int b = 0; b < 4; ++b)
-                    tma_load_2d(st + b * KV_BOX, &kv_map, b * 64, row0 + (j0 * RT + u) * BN,
-                                &full[s]);
+                for (int b = 0; b < 4; ++b) {
+                    unsigned char *dst = is_k ? smem + RING + (b * NST + s) * KV_BOX
+                                              : smem + RING + NST * KV_HALF + s * KV_HALF +
+                                                    b * KV_BOX;
+                    tma_load_2d(dst, &kv_map, b * 64, row0 + (j0 * RT + u) * BN, &full[s]);
+                }
                 issued = u + 1;
             }
             if (!VERIFY && is_k && issued == n_rt) {
@@ -249,7 +253,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t id_qk = tc::idesc_bf16(BM, BN, false);
+            constexpr uint32_t id_qk = tc::idesc_bf16(BM, RT == NST ? KT : BN, false);
             constexpr uint32_t id_pv = tc::idesc_bf16(BM, HD, true);
             bool ok = mbar_wait(&q_full, 0, a.status);
             tc::fence_after_sync();
@@ -262,18 +266,21 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                     }
                     if (!ok) break;
                     tc::fence_after_sync();
+                    // a tile spanning every stage (RT == NST) is one operand of
+                    // KT rows: its stages are adjacent within each box
+                    constexpr int NQ = RT == NST ? 1 : RT;  // Q K^T issues per tile
 #pragma unroll
-                    for (int r = 0; r < RT; ++r) {
+                    for (int r = 0; r < NQ; ++r) {
                         // keys r*BN.. of the tile from their ring stage, into
                         // columns r*BN.. of the S buffer
-                        const int s = (j * RT + r) % NST;
-                        const uint32_t kst = sbase + RING + s * STAGE;
+                        const int s = RT == NST ? 0 : (j * RT + r) % NST;
+                        const uint32_t kst = sbase + RING + s * KV_BOX;
                         const uint32_t d = tmem + S_COL + sb * KT + r * BN;
 #pragma unroll
                         for (int kk = 0; kk < HD / 16; ++kk) {
                             const uint32_t off = (kk & 3) * 32;  // 16 dims inside a 64-dim box
-                            const uint64_t db =
-                                tc::smem_desc(kst + (kk >> 2) * KV_BOX + off, 16, 1024);
+                            const uint64_t db = tc::smem_desc(
+                                kst + (kk >> 2) * NST * KV_BOX + off, 16, 1024);
                             if constexpr (VERIFY) {
                                 // A = Q from tensor memory: 16 dims are 8 columns
                                 tc::mma_ts(d, tmem + Q_COL + kk * 8, db, id_qk, kk > 0);
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
                     for (int kk = 0; kk < KT / 16; ++kk) {
                         // 16 keys: ring stage of the tile's part kk / (BN / 16)
                         const int s = (jj * RT + kk / (BN / 16)) % NST;
-                        const uint32_t vst = sbase + RING + s * STAGE + KV_HALF;
+                        const uint32_t vst = sbase + RING + NST * KV_HALF + s * KV_HALF;
                         const uint64_t db =
                             tc::smem_desc(vst + (kk % (BN / 16)) * 16 * 128, KV_BOX, 1024);
                         tc::mma_ts(tmem + O_COL, p + kk * 8, db, id_pv, jj > 0 || kk > 0);
