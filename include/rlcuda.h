@@ -215,9 +215,14 @@ typedef enum {
                                  walk's splits (0: automatic) */
     RL_OPT_EARLY_TILES = 4,   /* bf16 decode: 64-position tiles a walk CTA streams before
                                  its inputs are loaded (1..3, default 2) */
-    RL_OPT_VERIFY_TC = 5      /* 1 (default): 2..8 rows over a bf16 cache take the
+    RL_OPT_VERIFY_TC = 5,     /* 1 (default): 2..8 rows over a bf16 cache take the
                                  tensor-core verify kernel (bf16 P, the prefill
                                  tolerance); 0: the exact split-KV walk */
+    RL_OPT_DN_ROWS = 6        /* 1 (default): DeltaNet calls outside the chunked prefill
+                                 take the rows kernel, each head's state columns split
+                                 over a cluster of four CTAs; 0: the one-CTA-per-head
+                                 step kernel.  Both run the rows in order and give a
+                                 batch the bits of its rows one call at a time. */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);

@@ -186,6 +186,28 @@ __device__ __forceinline__ void named_sync(int id, int n) {
 __device__ __forceinline__ void named_arrive(int id, int n) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
+// Split-phase cluster barrier: every thread of every CTA of the cluster
+// arrives (release), then waits (acquire) before the next arrive.
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store one double into the same shared variable of cluster CTA `rank`,
+// completing 8 bytes of transaction on that CTA's copy of mbarrier `bar`
+// (no fence: the receiver learns of it from its own barrier).
+__device__ __forceinline__ void st_async_cluster_f64(const void *local, const uint64_t *bar,
+                                                     int rank, double v) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+    const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+    uint32_t ra, rb;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(b), "r"(rank));
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f64 [%0], %1, [%2];" ::
+                     "r"(ra), "d"(v), "r"(rb)
+                 : "memory");
+}
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }

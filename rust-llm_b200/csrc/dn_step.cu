@@ -42,13 +42,6 @@ constexpr int RPT = S / RG;     // state rows per thread (32)
 constexpr int HIST = 3;         // conv_kernel - 1
 }  // namespace dn
 
-__device__ __forceinline__ void cluster_arrive_release() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() {
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // grid (n_v / n_k, n_k), cluster (n_v / n_k): blockIdx.x = g, vh = kh + g*n_k
 __global__ void __launch_bounds__(dn::THREADS, 1) dn_step_kernel(const LinArgs a) {
     using namespace dn;

@@ -184,6 +184,11 @@ struct LinArgs {
 cudaError_t init_dn_kernels();
 cudaError_t launch_dn_step(const LinArgs &a, cudaStream_t st);
 int dn_max_group();
+// The same rows, up to eight, through the closed-form rows kernel
+// (dn_rows.cu), whose shape limits dn_rows_fits states.
+bool dn_rows_fits(const LinArgs &a);
+cudaError_t init_dn_rows_kernel();
+cudaError_t launch_dn_rows(const LinArgs &a, cudaStream_t st);
 
 // One chunked Gated DeltaNet prefill (dn_chunk.cu): t rows of one layer
 // updating ring slot `live` in place (slots == 1), in chunks of 64 tokens.

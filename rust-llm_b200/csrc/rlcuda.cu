@@ -58,7 +58,7 @@ struct rl_ctx {
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
-    int64_t opt_early_tiles = 2, opt_verify_tc = 1;
+    int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1;
     // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
     // resident CTAs per SM of the bf16 walk: [fused]
@@ -402,7 +402,8 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     x->own_stream = true;
     if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
         rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess ||
-        rl::init_prefill_kernels() != cudaSuccess || rl::init_dn_chunk_kernels() != cudaSuccess)
+        rl::init_prefill_kernels() != cudaSuccess || rl::init_dn_chunk_kernels() != cudaSuccess ||
+        rl::init_dn_rows_kernel() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
     for (int f = 0; f < 2; ++f) {
         for (int lc = 0; lc < 4; ++lc)
@@ -1213,7 +1214,10 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
     a.early_state = !(ctx->prev_dn && ctx->prev_layer == layer);
     {
         ProfScope ps(ctx, RL_PROF_DN_STEP);
-        CK(ctx, rl::launch_dn_step(a, ctx->stream));
+        if (ctx->opt_dn_rows && rl::dn_rows_fits(a))
+            CK(ctx, rl::launch_dn_rows(a, ctx->stream));
+        else
+            CK(ctx, rl::launch_dn_step(a, ctx->stream));
     }
     ctx->prev_dn = 1;
     ctx->prev_layer = layer;
@@ -1278,6 +1282,10 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
         if (value > 1) return fail(ctx, RL_EINVAL, "verify option must be 0 or 1");
         ctx->opt_verify_tc = value;
         return RL_OK;
+    case RL_OPT_DN_ROWS:
+        if (value > 1) return fail(ctx, RL_EINVAL, "the rows-kernel option must be 0 or 1");
+        ctx->opt_dn_rows = value;
+        return RL_OK;
     case RL_OPT_EARLY_TILES:
         if (value < 1 || value > 3) return fail(ctx, RL_EINVAL, "early tiles must be 1, 2 or 3");
         ctx->opt_early_tiles = value;
@@ -1300,6 +1308,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_CLUSTER: return ctx->opt_cluster;
     case RL_OPT_EARLY_TILES: return ctx->opt_early_tiles;
     case RL_OPT_VERIFY_TC: return ctx->opt_verify_tc;
+    case RL_OPT_DN_ROWS: return ctx->opt_dn_rows;
     default: return -1;
     }
 }

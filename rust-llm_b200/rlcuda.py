@@ -25,7 +25,7 @@ RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED,
     0, -1, -2, -3, -4, -5, -6, -7)
 RL_KV_F32, RL_KV_BF16 = 0, 1
 (RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS, RL_OPT_CLUSTER, RL_OPT_EARLY_TILES,
- RL_OPT_VERIFY_TC) = 0, 1, 2, 3, 4, 5
+ RL_OPT_VERIFY_TC, RL_OPT_DN_ROWS) = 0, 1, 2, 3, 4, 5, 6
 PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify")
 HOST, DEVICE = 0, 1
 RL_IPC_HANDLE_BYTES = 64

@@ -18,12 +18,25 @@ import rlcuda
 
 TOL = 1e-4
 pytestmark = pytest.mark.gpu
+KERNEL = {"rows": 1}
+
+
+@pytest.fixture(autouse=True, params=[1, 0], ids=["rows_kernel", "step_kernel"])
+def dn_kernel(request):
+    """Every case runs on both step kernels: the rows kernel (each head's
+    columns over a cluster of four CTAs, the default) and the one-CTA-per-head
+    kernel (RL_OPT_DN_ROWS = 0)."""
+    KERNEL["rows"] = request.param
+    yield request.param
 
 
 def make_ctx(slots=1, max_batch=16, n_linear=1):
     cfg = rlcuda.qwen35_config(n_full=0, n_linear=n_linear, context=4096, slots=slots,
                                max_batch=max_batch)
-    return rlcuda.Context(cfg)
+    ctx = rlcuda.Context(cfg)
+    ctx.set_option(rlcuda.RL_OPT_DN_ROWS, KERNEL["rows"])
+    assert ctx.get_option(rlcuda.RL_OPT_DN_ROWS) == KERNEL["rows"]
+    return ctx
 
 
 def load(ctx, w, conv, ssm, layer=0):
@@ -90,6 +103,44 @@ def test_verify_rows_over_the_ring(slots, live, t):
         check_state(ctx, conv_w, ssm_w)
 
 
+@pytest.mark.parametrize("slots,live,t", [(1, 0, 1), (1, 0, 9), (1, 0, 40), (13, 5, 12),
+                                          (41, 7, 40), (5, 4, 11), (3, 2, 3)])
+def test_rows_across_blocks_and_ring_wraps(slots, live, t):
+    """Row counts on both sides of the rows kernel's blocks of eight (its
+    norm exchange runs once per block), batches longer than the ring (later
+    rows overwrite the slots of earlier ones, the live slot included), and
+    every snapshot checked against the oracle."""
+    r = orc.Rng(200 + slots + live + t)
+    rows = cases.lin_rows(r, t)
+    w = cases.lin_weights(r, unit_norm=False)
+    conv, ssm = cases.lin_state(r, slots, live)
+    conv_w, ssm_w = conv.copy(), ssm.copy()
+    want = cases.oracle_linear(w, rows, conv_w, ssm_w, slots, live)
+    with make_ctx(slots=slots, max_batch=64) as ctx:
+        load(ctx, w, conv, ssm)
+        got = run(ctx, rows, live)
+        assert cases.rel_err_per_head(got, want, cases.S) <= TOL
+        check_state(ctx, conv_w, ssm_w)
+
+
+def test_a_decay_that_underflows():
+    """Gate logits that drive g = exp(softplus(a + dt_bias) * A) to zero in
+    f32: the state and its snapshots become the rows' own outer products,
+    as in the sequential recurrence."""
+    r = orc.Rng(211)
+    rows = cases.lin_rows(r, 8)
+    rows.alpha[:] += 40.0
+    w = cases.lin_weights(r)
+    conv, ssm = cases.lin_state(r, 9)
+    conv_w, ssm_w = conv.copy(), ssm.copy()
+    want = cases.oracle_linear(w, rows, conv_w, ssm_w, 9, 0)
+    with make_ctx(slots=9) as ctx:
+        load(ctx, w, conv, ssm)
+        got = run(ctx, rows, 0)
+        assert cases.rel_err_per_head(got, want, cases.S) <= TOL
+        check_state(ctx, conv_w, ssm_w)
+
+
 def test_ring_slot_equals_in_place_bit_for_bit():
     """forward.rs:2207-2268 on the device: the same rows through a ring of 5
     and in place give the same outputs and the same final state, bit for bit."""
@@ -110,19 +161,21 @@ def test_ring_slot_equals_in_place_bit_for_bit():
         assert np.array_equal(a.read_conv(0)[0], b.read_conv(0)[4])
 
 
-def test_a_batch_equals_its_rows_one_at_a_time_bit_for_bit():
+@pytest.mark.parametrize("t", [8, 12])
+def test_a_batch_equals_its_rows_one_at_a_time_bit_for_bit(t):
     """verify rows == sequential passes (tests/speculate.rs:68-202): one call
-    of 8 rows and 8 calls of one row leave the same outputs and ring."""
-    r = orc.Rng(88)
-    rows = cases.lin_rows(r, 8)
+    of t rows and t calls of one row leave the same outputs and ring (12
+    rows cross the rows kernel's block of eight)."""
+    r = orc.Rng(88 + t)
+    rows = cases.lin_rows(r, t)
     w = cases.lin_weights(r)
-    conv, ssm = cases.lin_state(r, 9)
-    with make_ctx(9) as a, make_ctx(9) as b:
+    conv, ssm = cases.lin_state(r, t + 1)
+    with make_ctx(t + 1) as a, make_ctx(t + 1) as b:
         load(a, w, conv, ssm)
         load(b, w, conv, ssm)
         batch = run(a, rows, 0)
         single = []
-        for i in range(8):
+        for i in range(t):
             one = cases.LinRows(rows.qkv[i:i + 1], rows.z[i:i + 1], rows.alpha[i:i + 1],
                                 rows.beta[i:i + 1])
             single.append(run(b, one, i))
