@@ -17,7 +17,7 @@
 // Work split.  The 128 x 128 state of a value head is split by columns over 4
 // CTAs (32 columns each), one cluster of 4 * gv CTAs per key head (gv =
 // n_v / n_k value heads share a key head), grid (4 * gv, n_k).  A CTA has 8
-// warps; warp w owns columns 4w .. 4w+3
+// compute warps and a store warp; compute warp w owns columns 4w .. 4w+3
 // of the CTA's block; lane (rg, cg) = (l & 7, l >> 3) holds column 4w + cg
 // at the 16 rows rg + 8e, e = 0..15, in registers.  A column's reductions
 // over its 128 rows (S^T k, S^T q) are then 16 products in the lane and three
@@ -26,13 +26,18 @@
 // is taken out of the contraction (g (S^T k) rather than (g S)^T k), so only
 // one FMA per state element waits on the shuffles.
 //
-// State traffic goes through two 128 x 32 f32 tiles in shared memory, laid
-// out with the 128-byte swizzle so that the lanes' column-wise writes are
-// free of bank conflicts.  The live slot comes in by coalesced 16-byte loads
-// into a tile; each row's snapshot is written into tile n % 2 and, one row
-// later (when every warp has arrived on that tile's mbarrier, which it has
-// long done), read back and stored by coalesced 16-byte stores: 512
-// contiguous bytes per warp instruction, four full 128-byte rows.
+// State traffic goes through a ring of four 128 x 32 f32 tiles in shared
+// memory, laid out with the 128-byte swizzle so that the lanes' column-wise
+// writes are free of bank conflicts.  The live slot comes in by coalesced
+// 16-byte loads into a tile.  Each row's snapshot n is written into tile
+// n % 4; once every compute warp has arrived on that tile's full barrier,
+// the tile goes to its ring slot by a TMA tile store and comes back (empty
+// barrier) when the copy has read it, two copies later.  The compute warps
+// never issue a global store for the state.  Who sends the tiles depends on
+// the launch: where rows never write the slot they read (slots > t: the
+// verify pass) a ninth warp, the store warp, does it, and the CTAs run one to
+// an SM; elsewhere (decode, in-place batches) thread 0 does, one row late,
+// and two CTAs may share an SM.  The values are the same either way.
 //
 // The conv, the gates and the q/k L2 norms come first, for a block of up to
 // eight rows at once, and the gated RMSNorm last, warp r of the block taking
@@ -53,14 +58,19 @@ namespace dnr {
 constexpr int S = 128;                   // d_state the kernel is built for
 constexpr int NCB = 4;                   // column blocks (CTAs) per value head
 constexpr int CW = S / NCB;              // 32 state columns per CTA
-constexpr int NW = 8;                    // warps, 4 state columns each
-constexpr int THREADS = NW * 32;
+constexpr int NW = 8;                    // compute warps, 4 state columns each
+constexpr int CTHREADS = NW * 32;        // (and a store warp in one form)
 constexpr int MAXR = 8;                  // rows per block
 constexpr int HIST = 3;                  // conv_kernel - 1
 constexpr int RPL = S / 8;               // state rows per lane
 constexpr int KP = 20;                   // pitch (floats) of a lane's transposed k / q rows
+constexpr int NBUF = 4;                  // snapshot tiles
 constexpr int TILE = S * CW * 4;         // one tile: 128 rows x 128 bytes
-constexpr int SMEM = 2 * TILE + 1024;    // two snapshot tiles, with room to align
+constexpr int SMEM = NBUF * TILE + 1024; // the tile ring, with room to align
+// a launch whose rows never write the slot they read (slots > t) takes
+// clusters of one value head's 4 CTAs and asks for this much shared memory,
+// so that no SM holds two of its CTAs (ones sharing an SM run at half speed)
+constexpr int SMEM_SOLO = 120 * 1024;
 }  // namespace dnr
 
 // The warp-wide sums of eight per-lane values v[0..7] at once: a reduce-
@@ -108,8 +118,8 @@ __device__ __forceinline__ float4 ld4(const float *p) {
     return *reinterpret_cast<const float4 *>(p);
 }
 
-// One CTA block (128 rows x 32 columns) of a state slot between global and a
-// swizzled tile, by coalesced 16-byte accesses: thread tid moves rows
+// One CTA block (128 rows x 32 columns) of a state slot from global into a
+// swizzled tile, by coalesced 16-byte loads: thread tid moves rows
 // (tid >> 3) + 32 j, 16-byte chunk tid & 7 of each.
 __device__ __forceinline__ void tile_from_global(uint8_t *tile, const float *src, int tid) {
     using namespace dnr;
@@ -123,24 +133,20 @@ __device__ __forceinline__ void tile_from_global(uint8_t *tile, const float *src
         *reinterpret_cast<float4 *>(tile + row * 128 + ((c ^ (row & 7)) << 4)) = v[j];
     }
 }
-__device__ __forceinline__ void tile_to_global(const uint8_t *tile, float *dst, int tid) {
-    using namespace dnr;
-    const int c = tid & 7;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int row = (tid >> 3) + 32 * j;
-        const float4 v = *reinterpret_cast<const float4 *>(tile + row * 128 + ((c ^ (row & 7)) << 4));
-        *reinterpret_cast<float4 *>(dst + (size_t)row * S + c * 4) = v;
-    }
-}
-
-// grid (NCB * gv, n_k), cluster (NCB * gv): blockIdx.x = grp * NCB + cb is
-// also the CTA's rank in its cluster; value head vh = kh + grp * n_k, so that
-// vh % n_k == kh as in forward.rs:1602-1609.  MB: rows per block, 1 for a
-// single row (the decode step) or MAXR; a row's arithmetic is the same in
-// both (the sums of squares take the same tree), so they agree bit for bit.
-template <int MB>
-__global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs a) {
+// grid (NCB * gv, n_k), blockIdx.x = grp * NCB + cb; value head vh = kh +
+// grp * n_k, so that vh % n_k == kh as in forward.rs:1602-1609.  Clusters
+// are (NCB * gv) CTAs (a key head, whose CTAs share the q/k history) or, when
+// no row writes the slot the rows read, NCB CTAs (a value head).
+// MB: rows per block, 1 for a single row (the decode step) or MAXR; a row's
+// arithmetic is the same in both (the sums of squares take the same tree),
+// so they agree bit for bit.  SW: a store warp sends the snapshot tiles (else
+// thread 0 does).
+// `map` covers every layer's state as rows of 128 f32 (box 128 rows x 32
+// columns, 128-byte swizzle); head vh, slot s of this layer starts at row
+// a.ssm_row0 + (vh * slots + s) * 128.
+template <int MB, bool SW>
+__global__ void __maxnreg__(112)
+    dn_rows_kernel(const LinArgs a, const __grid_constant__ CUtensorMap map) {
     using namespace dnr;
     extern __shared__ uint8_t dsm[];
     uint8_t *tiles = reinterpret_cast<uint8_t *>(
@@ -150,12 +156,13 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
     __shared__ float g_s[MB], beta_s[MB];
     __shared__ double nred[MB][NW];       // q/k sums of squares by warp
     __shared__ double osum[2][NCB][MB];   // output sums of squares by block parity, column block
-    __shared__ __align__(8) uint64_t tbar[2], xbar[2];
+    __shared__ __align__(8) uint64_t full[NBUF], empty[NBUF], xbar[2];
 
     const int n_k = a.n_k, n_v = a.n_v, slots = a.slots, t = a.t, live = a.live;
     const int cb = blockIdx.x % NCB, grp = blockIdx.x / NCB, kh = blockIdx.y;
     const int vh = kh + grp * n_k;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool store_warp = SW && warp == NW;
     const int rg = lane & 7, cg = lane >> 3;
     const int col = warp * 4 + cg;  // this lane's state column within the CTA's block
     const int key_dim = n_k * S, d_inner = n_v * S, conv_dim = 2 * key_dim + d_inner;
@@ -167,11 +174,32 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
     const float scale = 1.0f / sqrtf((float)S);
     const float shrink = 1.0f / sqrtf((float)S);
     const float l2_eps = a.eps / (float)S;
-    float *head = a.ssm_state + (size_t)vh * slots * S * S + cb * CW;  // slot 0, this block
+    const float *head = a.ssm_state + (size_t)vh * slots * S * S + cb * CW;  // slot 0, this block
+    const int row0 = a.ssm_row0 + vh * slots * S;  // map row of this head's slot 0
+    // snapshot m to its slot once every compute warp has written it; the
+    // tile of snapshot m - 2 goes back once its copy has read it
+    auto send = [&](int m) {
+        const int b = m % NBUF;
+        if (!mbar_wait(&full[b], (m / NBUF) & 1, a.status)) return false;
+        const int slot = slots > 1 ? (live + m + 1) % slots : live;
+        tma_store_2d(&map, cb * CW, row0 + slot * S, tiles + b * TILE);
+        bulk_commit();
+        if (m >= 2) {
+            bulk_wait_read<2>();
+            mbar_arrive(&empty[(m - 2) % NBUF]);
+        }
+        return true;
+    };
+    uint32_t crank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+    const int rank0 = (int)crank - cb;  // cluster rank of this head's column block 0
 
     if (tid == 0) {
-        mbar_init(&tbar[0], NW);
-        mbar_init(&tbar[1], NW);
+#pragma unroll
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(&full[b], NW);
+            mbar_init(&empty[b], 1);
+        }
         mbar_init(&xbar[0], 1);
         mbar_init(&xbar[1], 1);
         fence_barrier_init();  // before the cluster barrier lets a peer store into xbar
@@ -196,11 +224,13 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
     float h[HIST], hv[HIST];
     const float *hist_live = a.conv_state + (size_t)live * conv_dim * HIST;
     auto load_state = [&]() {
-        tile_from_global(tiles + TILE, head + (size_t)live * S * S, tid);
+        if (!store_warp) {
+            tile_from_global(tiles + (NBUF - 1) * TILE, head + (size_t)live * S * S, tid);
 #pragma unroll
-        for (int e = 0; e < HIST; ++e) {
-            h[e] = hist_live[(size_t)ch * HIST + e];
-            hv[e] = hist_live[(size_t)vch * HIST + e];
+            for (int e = 0; e < HIST; ++e) {
+                h[e] = hist_live[(size_t)ch * HIST + e];
+                hv[e] = hist_live[(size_t)vch * HIST + e];
+            }
         }
         cluster_arrive_release();  // this CTA has read the history it shares
     };
@@ -210,11 +240,20 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
     if (!a.early_state) load_state();
     // every CTA of the cluster has read the q/k history: it may be written
     cluster_wait_acquire();
-    __syncthreads();  // the live state is in tile 1
+
+    if (store_warp) {
+        if (lane == 0) {
+            for (int m = 0; m < nst; ++m)
+                if (!send(m)) break;
+            bulk_wait_all();  // the copies are done before the tiles go away
+        }
+        return;
+    }
+    named_sync(1, CTHREADS);  // the live state is in the last tile
     float st[RPL];
 #pragma unroll
     for (int e = 0; e < RPL; ++e)
-        st[e] = *reinterpret_cast<const float *>(tiles + TILE + tile_off(rg + 8 * e, col));
+        st[e] = *reinterpret_cast<const float *>(tiles + (NBUF - 1) * TILE + tile_off(rg + 8 * e, col));
 
     int n = 0;  // snapshots written so far
     for (int blk = 0, par = 0; blk < t; blk += MB, par ^= 1) {
@@ -290,7 +329,7 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
                 if (lane == 0) nred[0][warp] = s1;
             }
             if (row_w) v_s[warp][lane] = cv;
-            __syncthreads();
+            named_sync(1, CTHREADS);
             const int w0 = warp < 4 ? 0 : 4, rr = MB == MAXR ? (lane >> 2) & 7 : 0;
             my = 1.0f;
             if (rr < nb) {
@@ -309,11 +348,11 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
                 if (r < nb) dst[r * 8 * KP] = __fmul_rn(__fmul_rn(c[r], sc), shrink);
             }
         }
-        __syncthreads();
+        named_sync(1, CTHREADS);
         // ---- the rows, one after the other (forward.rs:1964-2010), each warp
         // on its own four columns: contract with k, decay, delta, add its
-        // outer product, contract with q; snapshot n goes into tile n % 2 and
-        // is stored while the next row runs
+        // outer product, contract with q; snapshot n goes into tile n % 4 and
+        // is sent while the next row runs
 #pragma unroll 1
         for (int r = 0; r < nb; ++r) {
             float kk[RPL], qq[RPL];
@@ -346,29 +385,25 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
             const float o = col_sum(o0 + o1);
             if (rg == 0) o_s[r][col] = o;
             if (slots > 1 || blk + r == t - 1) {
-                if (n >= 1) {  // the snapshot before, complete in its tile
-                    const int p = (n - 1) & 1;
-                    mbar_wait(&tbar[p], ((n - 1) >> 1) & 1, a.status);
-                    const int slot = slots > 1 ? (live + n) % slots : live;
-                    tile_to_global(tiles + p * TILE, head + (size_t)slot * S * S, tid);
-                }
-                uint8_t *tile = tiles + (n & 1) * TILE;
+                const int b = n % NBUF;
+                // the tile's previous snapshot (n - 4) has been read by its copy
+                if (n >= NBUF) mbar_wait(&empty[b], (n / NBUF - 1) & 1, a.status);
+                uint8_t *tile = tiles + b * TILE;
 #pragma unroll
                 for (int e = 0; e < RPL; ++e)
                     *reinterpret_cast<float *>(tile + tile_off(rg + 8 * e, col)) = st[e];
+                fence_proxy_async_smem();  // the tile copy reads these writes
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tbar[n & 1]);
+                if (lane == 0) mbar_arrive(&full[b]);
+                if (!SW && tid == 0 && n >= 1) send(n - 1);
                 ++n;
             }
         }
         if (tid == 0) mbar_arrive_expect_tx(&xbar[par], (uint32_t)(nb * NCB * sizeof(double)));
-        __syncthreads();
-        if (blk + MB >= t) {
-            // ---- the last snapshot, complete in its tile after the barrier
-            // above: its stores go out while the norm exchange runs
-            const int slot = slots > 1 ? (live + nst) % slots : live;
-            tile_to_global(tiles + ((nst - 1) & 1) * TILE, head + (size_t)slot * S * S, tid);
-        }
+        named_sync(1, CTHREADS);
+        // the last snapshot, complete in its tile after the barrier above,
+        // goes out while the norm exchange runs
+        if (!SW && blk + MB >= t && tid == 0) send(nst - 1);
         // ---- gated RMSNorm (forward.rs:1642-1652): warp r takes row r at the
         // CTA's 32 columns; its sum of squares goes to the head's four CTAs
         // by asynchronous stores that complete on each one's barrier
@@ -376,7 +411,7 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
             const float o = __fmul_rn(o_s[warp][lane], scale);
             const double ss = warp_sum_d((double)__fmul_rn(o, o));
             if (lane < NCB)
-                st_async_cluster_f64(&osum[par][cb][warp], &xbar[par], grp * NCB + lane, ss);
+                st_async_cluster_f64(&osum[par][cb][warp], &xbar[par], rank0 + lane, ss);
             mbar_wait(&xbar[par], (blk / MB >> 1) & 1, a.status);
             double sum = -0.0;
 #pragma unroll
@@ -386,14 +421,20 @@ __global__ void __launch_bounds__(dnr::THREADS, 2) dn_rows_kernel(const LinArgs 
                 __fmul_rn(__fmul_rn(__fmul_rn(o, sc), wn), siluf_(zz));
         }
     }
+    if (!SW && tid == 0) bulk_wait_all();  // the copies are done before the tiles go away
 }
 
 cudaError_t init_dn_rows_kernel() {
-    cudaError_t e = cudaFuncSetAttribute(dn_rows_kernel<1>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, dnr::SMEM);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(dn_rows_kernel<dnr::MAXR>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, dnr::SMEM);
+    const void *k[4] = {(const void *)dn_rows_kernel<1, false>,
+                        (const void *)dn_rows_kernel<dnr::MAXR, false>,
+                        (const void *)dn_rows_kernel<1, true>,
+                        (const void *)dn_rows_kernel<dnr::MAXR, true>};
+    for (const void *f : k) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, dnr::SMEM_SOLO);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 // The rows kernel's shape limits: d_state 128, conv kernel 4, and a key
@@ -403,24 +444,29 @@ bool dn_rows_fits(const LinArgs &a) {
            a.n_v % a.n_k == 0 && dnr::NCB * (a.n_v / a.n_k) <= 8;
 }
 
-cudaError_t launch_dn_rows(const LinArgs &a, cudaStream_t st) {
+cudaError_t launch_dn_rows(const LinArgs &a, const CUtensorMap &map, cudaStream_t st) {
     const int gv = a.n_v / a.n_k;
+    // rows that never write the live slot leave the shared q/k history alone
+    const bool solo = a.slots > a.t;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(dnr::NCB * gv, a.n_k);
-    cfg.blockDim = dim3(dnr::THREADS);
-    cfg.dynamicSmemBytes = dnr::SMEM;
+    cfg.blockDim = dim3(dnr::CTHREADS + (solo ? 32 : 0));
+    cfg.dynamicSmemBytes = solo ? dnr::SMEM_SOLO : dnr::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = dnr::NCB * gv;
+    attr[0].val.clusterDim.x = solo ? dnr::NCB : dnr::NCB * gv;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return a.t == 1 ? cudaLaunchKernelEx(&cfg, dn_rows_kernel<1>, a)
-                    : cudaLaunchKernelEx(&cfg, dn_rows_kernel<dnr::MAXR>, a);
+    if (solo)
+        return a.t == 1 ? cudaLaunchKernelEx(&cfg, dn_rows_kernel<1, true>, a, map)
+                        : cudaLaunchKernelEx(&cfg, dn_rows_kernel<dnr::MAXR, true>, a, map);
+    return a.t == 1 ? cudaLaunchKernelEx(&cfg, dn_rows_kernel<1, false>, a, map)
+                    : cudaLaunchKernelEx(&cfg, dn_rows_kernel<dnr::MAXR, false>, a, map);
 }
 
 }  // namespace rl

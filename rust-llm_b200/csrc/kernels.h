@@ -179,6 +179,8 @@ struct LinArgs {
     // the state and conv history may be read before the grid-dependency
     // wait: the kernel just ahead on the stream is not a step of this layer
     bool early_state;
+    // the rows kernel's state map row of this layer's head 0, slot 0
+    int ssm_row0;
 };
 
 cudaError_t init_dn_kernels();
@@ -186,9 +188,11 @@ cudaError_t launch_dn_step(const LinArgs &a, cudaStream_t st);
 int dn_max_group();
 // The same rows, up to eight, through the closed-form rows kernel
 // (dn_rows.cu), whose shape limits dn_rows_fits states.
+// `map`: every layer's state as rows of d_state f32, boxes of 128 rows x 32
+// columns with the 128-byte swizzle (encode_f32_2d).
 bool dn_rows_fits(const LinArgs &a);
 cudaError_t init_dn_rows_kernel();
-cudaError_t launch_dn_rows(const LinArgs &a, cudaStream_t st);
+cudaError_t launch_dn_rows(const LinArgs &a, const CUtensorMap &map, cudaStream_t st);
 
 // One chunked Gated DeltaNet prefill (dn_chunk.cu): t rows of one layer
 // updating ring slot `live` in place (slots == 1), in chunks of 64 tokens.

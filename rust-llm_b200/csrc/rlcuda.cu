@@ -46,6 +46,8 @@ struct rl_ctx {
     // bf16 caches: TMA map of the staged bf16 queries [max_batch][n_head][hd]
     CUtensorMap q_map{};
     CUtensorMap gate_map{};
+    CUtensorMap ssm_map{};  // every layer's DeltaNet state, rows of d_state f32
+    bool ssm_map_ok = false;
     // chunked DeltaNet prefill scratch (slots == 1 and max_batch >= 64)
     __nv_bfloat16 *dn_qn = nullptr, *dn_kn = nullptr, *dn_vn = nullptr;
     __nv_bfloat16 *dn_qn_lo = nullptr, *dn_kn_lo = nullptr, *dn_vn_lo = nullptr;
@@ -455,6 +457,13 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
                                    64, 1, rl::kPrefillQBoxRows) != cudaSuccess)
                 return bail(fail(x, RL_ECUDA, "encoding the gate tensor map failed"));
         }
+    }
+    if (c.n_linear > 0 && c.d_state == 128) {
+        // the rows kernel's tiles: 128 rows x 32 columns of one head's slot
+        const uint64_t rows = (uint64_t)c.n_linear * c.n_v_heads * c.slots * s;
+        x->ssm_map_ok = rows < (1ull << 31) &&
+                        rl::encode_f32_2d(&x->ssm_map, x->ssm, rows, s, s * 4, 128, 32) ==
+                            cudaSuccess;
     }
     if (c.n_linear > 0 && c.slots == 1 && mb >= 64) {
         const size_t nk = c.n_k_heads, nv = c.n_v_heads, nc = (mb + 63) / 64;
@@ -1212,10 +1221,11 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
     a.kernel = c.conv_kernel;
     a.eps = c.rms_eps;
     a.early_state = !(ctx->prev_dn && ctx->prev_layer == layer);
+    a.ssm_row0 = layer * c.n_v_heads * c.slots * c.d_state;
     {
         ProfScope ps(ctx, RL_PROF_DN_STEP);
-        if (ctx->opt_dn_rows && rl::dn_rows_fits(a))
-            CK(ctx, rl::launch_dn_rows(a, ctx->stream));
+        if (ctx->opt_dn_rows && ctx->ssm_map_ok && rl::dn_rows_fits(a))
+            CK(ctx, rl::launch_dn_rows(a, ctx->ssm_map, ctx->stream));
         else
             CK(ctx, rl::launch_dn_step(a, ctx->stream));
     }

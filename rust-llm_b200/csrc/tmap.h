@@ -23,4 +23,10 @@ cudaError_t encode_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uint
                            uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                            uint32_t b0, uint32_t b1, uint32_t b2);
 
+// A 2-D f32 tensor of `rows` rows of `cols` elements (row pitch
+// `row_bytes`, a multiple of 16), moved in boxes of box_rows x box_cols with
+// the 128-byte swizzle (box_cols * 4 <= 128), loaded and stored.
+cudaError_t encode_f32_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                          uint64_t row_bytes, uint32_t box_rows, uint32_t box_cols);
+
 }  // namespace rl
