@@ -45,6 +45,11 @@ constexpr int LOCAL_THREADS = 256;  // chunk-local CTA: 8 warps
 }  // namespace dc
 
 // ---------------------------------------------------------------------------
+// SiLU from the hardware exp2 and an approximate divide: within a few f32
+// ulps of x / (1 + e^-x), far inside the bf16-pair products that follow
+// (the accurate library forms made the prep and output kernels issue-bound).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // dn_prep_kernel: grid (t, groups / 8), 8 warps; one warp per (token, group
 // of 128 channels: a q head, a k head or a v head), 4 channels per lane.
 __device__ __forceinline__ void store_pair4(__nv_bfloat16 *hi, __nv_bfloat16 *lo, const float *y) {
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
             c = __fadd_rn(c, __fmul_rn(h[0][e], w[e].x));
             c = __fadd_rn(c, __fmul_rn(h[1][e], w[e].y));
             c = __fadd_rn(c, __fmul_rn(h[2][e], w[e].z));
-            y[e] = siluf_(c);
+            y[e] = silu_fast(c);
             h[0][e] = h[1][e];
             h[1][e] = h[2][e];
             h[2][e] = xs[e];
@@ -734,10 +739,10 @@ __global__ void __launch_bounds__(128) dn_out_kernel(const DnChunkArgs a) {
     sq = warp_sum_d(sq);
     const float sc = rms_scale_from_sum(sq, S, a.eps);
     float4 y;
-    y.x = __fmul_rn(__fmul_rn(__fmul_rn(o.x, sc), w.x), siluf_(z.x));
-    y.y = __fmul_rn(__fmul_rn(__fmul_rn(o.y, sc), w.y), siluf_(z.y));
-    y.z = __fmul_rn(__fmul_rn(__fmul_rn(o.z, sc), w.z), siluf_(z.z));
-    y.w = __fmul_rn(__fmul_rn(__fmul_rn(o.w, sc), w.w), siluf_(z.w));
+    y.x = __fmul_rn(__fmul_rn(__fmul_rn(o.x, sc), w.x), silu_fast(z.x));
+    y.y = __fmul_rn(__fmul_rn(__fmul_rn(o.y, sc), w.y), silu_fast(z.y));
+    y.z = __fmul_rn(__fmul_rn(__fmul_rn(o.z, sc), w.z), silu_fast(z.z));
+    y.w = __fmul_rn(__fmul_rn(__fmul_rn(o.w, sc), w.w), silu_fast(z.w));
     *reinterpret_cast<float4 *>(a.out + off) = y;
 }
 
