@@ -114,6 +114,10 @@ __device__ __forceinline__ uint32_t tile_off(int row, int col) {
     return (uint32_t)(row * 128 + ((((col >> 2) ^ row) & 7) << 4) + ((col & 3) << 2));
 }
 
+// SiLU from the hardware exp2 and an approximate divide: within a few f32
+// ulps of x / (1 + e^-x), well inside the step's 1e-4 bar
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 __device__ __forceinline__ float4 ld4(const float *p) {
     return *reinterpret_cast<const float4 *>(p);
 }
@@ -290,7 +294,7 @@ __global__ void __maxnreg__(112)
                 float y = __fmul_rn(x[r], w[3]);
 #pragma unroll
                 for (int e = 0; e < HIST; ++e) y = __fadd_rn(y, __fmul_rn(h[e], w[e]));
-                c[r] = siluf_(y);
+                c[r] = silu_fast(y);
                 h[0] = h[1], h[1] = h[2], h[2] = x[r];
                 if (writes_qk && last_in_slot(blk + r)) {
                     float *hs = a.conv_state + (size_t)((live + blk + r + 1) % slots) * conv_dim * HIST +
@@ -305,7 +309,7 @@ __global__ void __maxnreg__(112)
             float y = __fmul_rn(xt[3], wv[3]);
 #pragma unroll
             for (int e = 0; e < HIST; ++e) y = __fadd_rn(y, __fmul_rn(xt[e], wv[e]));
-            cv = siluf_(y);
+            cv = silu_fast(y);
             if (last_in_slot(gr)) {
                 float *hs = a.conv_state + (size_t)((live + gr + 1) % slots) * conv_dim * HIST +
                             (size_t)vch * HIST;
@@ -418,7 +422,7 @@ __global__ void __maxnreg__(112)
             for (int q = 0; q < NCB; ++q) sum += osum[par][q][warp];
             const float sc = rms_scale_from_sum(sum, S, a.eps);
             a.out[(size_t)(blk + warp) * d_inner + (size_t)vh * S + cb * CW + lane] =
-                __fmul_rn(__fmul_rn(__fmul_rn(o, sc), wn), siluf_(zz));
+                __fmul_rn(__fmul_rn(__fmul_rn(o, sc), wn), silu_fast(zz));
         }
     }
     if (!SW && tid == 0) bulk_wait_all();  // the copies are done before the tiles go away
