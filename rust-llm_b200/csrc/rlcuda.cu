@@ -57,6 +57,14 @@ struct rl_ctx {
     float *dn_ut = nullptr, *dn_gc = nullptr, *dn_opre = nullptr;
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
+    // pinned host staging for the *_host entry points (calls of up to
+    // hpin_rows rows): the status word, then the packed inputs and the
+    // output.  Copies from and to the callers' own (usually pageable)
+    // buffers are host memcpys; the device copies are asynchronous.
+    void *hpin_base = nullptr;
+    int *hstatus = nullptr;
+    float *hpin = nullptr;
+    int hpin_rows = 0;
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
@@ -202,6 +210,7 @@ void free_all(rl_ctx *x) {
                   x->dn_p, x->dn_ut, x->dn_gc, x->dn_opre};
     for (void *p : ps)
         if (p) cudaFree(p);
+    if (x->hpin_base) cudaFreeHost(x->hpin_base);
     if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
 }
 
@@ -258,8 +267,16 @@ cudaError_t h2d(rl_ctx *x, void *dst, const void *src, size_t bytes) {
 
 int check_status(rl_ctx *x) {
     int st = 0;
-    CK(x, cudaMemcpyAsync(&st, x->status, sizeof(int), cudaMemcpyDeviceToHost, x->stream));
-    CK(x, cudaStreamSynchronize(x->stream));
+    if (x->hstatus) {
+        // through the pinned word: an asynchronous copy, then the one wait
+        CK(x, cudaMemcpyAsync(x->hstatus, x->status, sizeof(int), cudaMemcpyDeviceToHost,
+                              x->stream));
+        CK(x, cudaStreamSynchronize(x->stream));
+        st = *x->hstatus;
+    } else {
+        CK(x, cudaMemcpyAsync(&st, x->status, sizeof(int), cudaMemcpyDeviceToHost, x->stream));
+        CK(x, cudaStreamSynchronize(x->stream));
+    }
     if (st) {
         CK(x, cudaMemsetAsync(x->status, 0, sizeof(int), x->stream));
         if (st & rl::DEV_TIMEOUT)
@@ -489,6 +506,20 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     const size_t lin_io = mb * (cd + 2 * s * c.n_v_heads + 2 * c.n_v_heads);
     x->stage_floats = std::max(c.n_full ? full_io : 0, c.n_linear ? lin_io : 0);
     if ((code = alloc(x, &x->stage, x->stage_floats))) return bail(code);
+    {
+        // pinned staging for calls of up to 64 rows (without it, the host
+        // entry points copy from and to the callers' buffers directly)
+        const int rows = (int)std::min<size_t>(mb, 64);
+        const size_t bytes = 64 + (x->stage_floats / mb) * rows * sizeof(float);
+        if (cudaMallocHost(&x->hpin_base, bytes) == cudaSuccess) {
+            x->hstatus = static_cast<int *>(x->hpin_base);
+            x->hpin = reinterpret_cast<float *>(static_cast<char *>(x->hpin_base) + 64);
+            x->hpin_rows = rows;
+        } else {
+            x->hpin_base = nullptr;
+            cudaGetLastError();
+        }
+    }
     // theta_scale = theta^(-2/n_rot), computed on the host exactly as
     // forward.rs:1853 does, so the device advances the same f32 angle
     x->theta_scale = c.n_rot > 0 ? std::pow(c.rope_theta, -2.0f / (float)c.n_rot) : 1.0f;
@@ -1127,6 +1158,25 @@ int rl_full_attn_host(rl_ctx *ctx, int layer, int pos, int t, const float *qg, c
     const size_t nk = (size_t)t * c.head_dim * c.n_head_kv;
     const size_t no = (size_t)t * c.head_dim * c.n_head;
     float *dq = ctx->stage, *dk = dq + nqg, *dv = dk + nk, *dout = dv + nk;
+    if (ctx->hpin && t <= ctx->hpin_rows) {
+        // the inputs packed in the pinned staging in the device staging's
+        // order (the previous call's copies have completed: every call ends
+        // in a wait), one copy in, one out
+        float *hp = ctx->hpin, *hout = hp + nqg + 2 * nk;
+        std::memcpy(hp, qg, nqg * 4);
+        std::memcpy(hp + nqg, k, nk * 4);
+        std::memcpy(hp + nqg + nk, v, nk * 4);
+        CK(ctx, cudaMemcpyAsync(dq, hp, (nqg + 2 * nk) * 4, cudaMemcpyHostToDevice, ctx->stream));
+        int code = rl_full_attn(ctx, layer, pos, t, dq, dk, dv, dout);
+        if (code) {
+            cudaStreamSynchronize(ctx->stream);  // the staging's copy is done before reuse
+            return code;
+        }
+        CK(ctx, cudaMemcpyAsync(hout, dout, no * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        code = check_status(ctx);
+        std::memcpy(out, hout, no * 4);
+        return code;
+    }
     CK(ctx, cudaMemcpyAsync(dq, qg, nqg * 4, cudaMemcpyHostToDevice, ctx->stream));
     CK(ctx, cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
     CK(ctx, cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, ctx->stream));
@@ -1246,6 +1296,25 @@ int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qk
     const size_t nx = (size_t)t * conv_dim(c), nz = (size_t)t * c.n_v_heads * c.d_state;
     const size_t ng = (size_t)t * c.n_v_heads;
     float *dx = ctx->stage, *dz = dx + nx, *da = dz + nz, *db = da + ng, *dout = db + ng;
+    if (ctx->hpin && t <= ctx->hpin_rows) {
+        // as rl_full_attn_host: packed pinned inputs, one copy in, one out
+        float *hp = ctx->hpin, *hout = hp + nx + nz + 2 * ng;
+        std::memcpy(hp, qkv, nx * 4);
+        std::memcpy(hp + nx, z, nz * 4);
+        std::memcpy(hp + nx + nz, alpha, ng * 4);
+        std::memcpy(hp + nx + nz + ng, beta, ng * 4);
+        CK(ctx, cudaMemcpyAsync(dx, hp, (nx + nz + 2 * ng) * 4, cudaMemcpyHostToDevice,
+                                ctx->stream));
+        int code = rl_linear_attn(ctx, layer, live, t, dx, dz, da, db, dout);
+        if (code) {
+            cudaStreamSynchronize(ctx->stream);  // the staging's copy is done before reuse
+            return code;
+        }
+        CK(ctx, cudaMemcpyAsync(hout, dout, nz * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        code = check_status(ctx);
+        std::memcpy(out, hout, nz * 4);
+        return code;
+    }
     CK(ctx, cudaMemcpyAsync(dx, qkv, nx * 4, cudaMemcpyHostToDevice, ctx->stream));
     CK(ctx, cudaMemcpyAsync(dz, z, nz * 4, cudaMemcpyHostToDevice, ctx->stream));
     CK(ctx, cudaMemcpyAsync(da, alpha, ng * 4, cudaMemcpyHostToDevice, ctx->stream));
