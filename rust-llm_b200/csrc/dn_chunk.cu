@@ -40,7 +40,8 @@ constexpr int LDB = 136;   // padded bf16 row (272 B: ldmatrix rows in distinct 
 constexpr int LDP = 72;    // padded bf16 row of a 64-wide matrix (144 B)
 constexpr int LDF = 65;    // padded f32 row of a 64-wide matrix
 constexpr int JC = 32;     // state columns per scan CTA
-constexpr int SCAN_THREADS = 256;
+constexpr int SCAN_THREADS = 512;  // chunk scan: 8 chain warps + 8 output warps
+constexpr int GROUP_THREADS = 256;
 constexpr int LOCAL_THREADS = 256;  // chunk-local CTA: 8 warps
 }  // namespace dc
 
@@ -532,7 +533,7 @@ struct ScanSmem {
     float ut[dc::C][dc::JC];
     float s[dc::S][dc::JC + 1];                 // the state block, f32
     __nv_bfloat16 st[2][2][dc::S][LDU];         // S [buffer][hi, lo] as [i][j]
-    __nv_bfloat16 up[2][dc::C][LDU];            // U [hi, lo] as [t][j]
+    __nv_bfloat16 up[2][2][dc::C][LDU];         // U [buffer][hi, lo] as [t][j]
 };
 
 // W (hi, lo) and this CTA's 32 columns of Ut for chunk block `blk`, 16-byte
@@ -541,32 +542,40 @@ __device__ __forceinline__ void scan_load_wu(ScanSmem &sm, const DnChunkArgs &a,
                                              int j0, int tid) {
     using namespace dc;
     const __nv_bfloat16 *w = a.w + blk * C * S, *wl = a.w_lo + blk * C * S;
-    for (int e = tid; e < C * (S / 8); e += SCAN_THREADS) {
+    for (int e = tid; e < C * (S / 8); e += GROUP_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
         cp_async16(&sm.w[0][r][c8], w + r * S + c8);
         cp_async16(&sm.w[1][r][c8], wl + r * S + c8);
     }
     const float *ut = a.ut + blk * C * S;
-    for (int e = tid; e < C * (JC / 4); e += SCAN_THREADS) {
+    for (int e = tid; e < C * (JC / 4); e += GROUP_THREADS) {
         const int r = e / (JC / 4), c4 = (e % (JC / 4)) * 4;
         cp_async16(&sm.ut[r][c4], ut + r * S + j0 + c4);
     }
 }
-// Q', K' and P (hi, lo) for chunk block `blk`
-__device__ __forceinline__ void scan_load_qpk(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
-                                              int tid) {
+// K' (hi, lo) for chunk block `blk`
+__device__ __forceinline__ void scan_load_k(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
+                                            int tid) {
     using namespace dc;
-    const __nv_bfloat16 *qp = a.qp + blk * C * S, *qpl = a.qp_lo + blk * C * S;
     const __nv_bfloat16 *kp = a.kp + blk * C * S, *kpl = a.kp_lo + blk * C * S;
-    for (int e = tid; e < C * (S / 8); e += SCAN_THREADS) {
+    for (int e = tid; e < C * (S / 8); e += GROUP_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
-        cp_async16(&sm.qp[0][r][c8], qp + r * S + c8);
-        cp_async16(&sm.qp[1][r][c8], qpl + r * S + c8);
         cp_async16(&sm.kp[0][r][c8], kp + r * S + c8);
         cp_async16(&sm.kp[1][r][c8], kpl + r * S + c8);
     }
+}
+// Q' and P (hi, lo) for chunk block `blk`
+__device__ __forceinline__ void scan_load_qp(ScanSmem &sm, const DnChunkArgs &a, size_t blk,
+                                             int tid) {
+    using namespace dc;
+    const __nv_bfloat16 *qp = a.qp + blk * C * S, *qpl = a.qp_lo + blk * C * S;
+    for (int e = tid; e < C * (S / 8); e += GROUP_THREADS) {
+        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+        cp_async16(&sm.qp[0][r][c8], qp + r * S + c8);
+        cp_async16(&sm.qp[1][r][c8], qpl + r * S + c8);
+    }
     const __nv_bfloat16 *p = a.p + blk * C * C, *pl = a.p_lo + blk * C * C;
-    for (int e = tid; e < C * (C / 8); e += SCAN_THREADS) {
+    for (int e = tid; e < C * (C / 8); e += GROUP_THREADS) {
         const int r = e / (C / 8), c8 = (e % (C / 8)) * 8;
         cp_async16(&sm.p[0][r][c8], p + r * C + c8);
         cp_async16(&sm.p[1][r][c8], pl + r * C + c8);
@@ -607,34 +616,43 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScanSmem &sm = *reinterpret_cast<ScanSmem *>(smem_raw);
     const int j0 = blockIdx.x * JC, vh = blockIdx.y;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
+    // warps 0-7 run the chain U_c = Ut - W S_{c-1}, S_c = gamma S_{c-1} + K'^T U_c;
+    // warps 8-15 the output O_c = Q' S_{c-1} + P U_c, which nothing later needs,
+    // while the chain goes on with S_c and U_{c+1} (U is double-buffered; S_{c+1}
+    // waits until O_c has read S_{c-1}, whose buffer it takes).  Named
+    // barriers: 1 the chain warps, 2 the output warps, 3 U_c ready (the chain
+    // arrives, the output warps wait), 4 O_c done (the other way).
+    const bool chain = tid < GROUP_THREADS;
+    const int ltid = chain ? tid : tid - GROUP_THREADS, lwarp = ltid >> 5;
     const int g = lane >> 2, c0 = (lane & 3) * 2;
     const float scale = 1.0f / sqrtf((float)S);
     float *state = a.ssm_state + (size_t)vh * a.slots * S * S + (size_t)a.live * S * S;
     const size_t blk0 = (size_t)vh * a.nc;
+    const int wm = (lwarp & 3) * 16, wn = (lwarp >> 2) * 16;  // U and O: 16 x 16 per warp
 
-    scan_load_wu(sm, a, blk0, j0, tid);
-    cp_async_commit();
-    scan_load_qpk(sm, a, blk0, tid);
-    cp_async_commit();
-    for (int e = tid; e < S * JC / 2; e += SCAN_THREADS) {
-        const int i = e / (JC / 2), j = (e % (JC / 2)) * 2;
-        const float2 x = *reinterpret_cast<const float2 *>(state + (size_t)i * S + j0 + j);
-        sm.s[i][j] = x.x;
-        sm.s[i][j + 1] = x.y;
-        *reinterpret_cast<uint32_t *>(&sm.st[0][0][i][j]) = pack_bf16(x.x, x.y);
-        *reinterpret_cast<uint32_t *>(&sm.st[0][1][i][j]) =
-            pack_bf16(x.x - bf16_hi(x.x), x.y - bf16_hi(x.y));
-    }
-    for (int ck = 0; ck < a.nc; ++ck) {
-        const int cur = ck & 1, nxt = cur ^ 1;
-        const bool more = ck + 1 < a.nc;
-        // W and Ut of this chunk have landed (its Q', P, K' may still be in
-        // flight); the state of the step before is in place
-        cp_async_wait<1>();
-        __syncthreads();
-        // ---- U = Ut - W S (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
-        const int wm = (warp & 3) * 16, wn = (warp >> 2) * 16;
+    if (chain) {
+        scan_load_wu(sm, a, blk0, j0, ltid);
+        cp_async_commit();
+        scan_load_k(sm, a, blk0, ltid);
+        cp_async_commit();
+        for (int e = ltid; e < S * JC / 2; e += GROUP_THREADS) {
+            const int i = e / (JC / 2), j = (e % (JC / 2)) * 2;
+            const float2 x = *reinterpret_cast<const float2 *>(state + (size_t)i * S + j0 + j);
+            sm.s[i][j] = x.x;
+            sm.s[i][j + 1] = x.y;
+            *reinterpret_cast<uint32_t *>(&sm.st[0][0][i][j]) = pack_bf16(x.x, x.y);
+            *reinterpret_cast<uint32_t *>(&sm.st[0][1][i][j]) =
+                pack_bf16(x.x - bf16_hi(x.x), x.y - bf16_hi(x.y));
+        }
+        for (int ck = 0; ck < a.nc; ++ck) {
+            const int cur = ck & 1, nxt = cur ^ 1, ub = ck & 1;
+            const bool more = ck + 1 < a.nc;
+            // W and Ut of this chunk have landed (its K' may be in flight);
+            // the state of the step before is in place
+            cp_async_wait<1>();
+            named_sync(1, GROUP_THREADS);
+            // ---- U = Ut - W S (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
         {
             float d[2][4] = {};
             mma3_rows<S, 1>(d, &sm.w[0][0][0], &sm.w[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
@@ -646,39 +664,27 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
                     const int r = wm + g + e2 * 8, c = wn + n * 8 + c0;
                     const float u0 = sm.ut[r][c] - d[n][2 * e2];
                     const float u1 = sm.ut[r][c + 1] - d[n][2 * e2 + 1];
-                    *reinterpret_cast<uint32_t *>(&sm.up[0][r][c]) = pack_bf16(u0, u1);
-                    *reinterpret_cast<uint32_t *>(&sm.up[1][r][c]) =
+                    *reinterpret_cast<uint32_t *>(&sm.up[ub][0][r][c]) = pack_bf16(u0, u1);
+                    *reinterpret_cast<uint32_t *>(&sm.up[ub][1][r][c]) =
                         pack_bf16(u0 - bf16_hi(u0), u1 - bf16_hi(u1));
                 }
         }
-        cp_async_wait<0>();
-        __syncthreads();  // U is complete, W and Ut used up; Q', P, K' have landed
-        if (more) scan_load_wu(sm, a, blk0 + ck + 1, j0, tid);
-        cp_async_commit();
-        // ---- O = Q' S + P U (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
-        {
-            float d[2][4] = {};
-            mma3_rows<S, 1>(d, &sm.qp[0][0][0], &sm.qp[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
-                            &sm.st[cur][1][0][0], LDU, wn, lane);
-            mma3_rows<C, 1>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, wm, &sm.up[0][0][0],
-                            &sm.up[1][0][0], LDU, wn, lane);
-            const int r0 = wm + g;
-#pragma unroll
-            for (int e2 = 0; e2 < 2; ++e2) {
-                const int r = r0 + e2 * 8, tok = ck * C + r;
-                if (tok < a.t) {
-                    float *dst = a.opre + ((size_t)tok * a.n_v + vh) * S + j0 + wn;
-#pragma unroll
-                    for (int n = 0; n < 2; ++n)
-                        *reinterpret_cast<float2 *>(dst + n * 8 + c0) =
-                            make_float2(d[n][2 * e2] * scale, d[n][2 * e2 + 1] * scale);
-                }
-            }
-        }
+            named_sync(1, GROUP_THREADS);  // U is complete, W and Ut used up
+            // S_c takes the buffer of S_{c-2}, and U_{c+1} that of U_{c-1}: the
+            // output of the chunk before must have read both.  Waiting for it
+            // here, before U_c is announced, also keeps the two barriers in
+            // strict alternation: the output warps cannot arrive for O_c
+            // before this wait has taken their arrival for O_{c-1}.
+            if (ck > 0) named_sync(4, SCAN_THREADS);
+            named_arrive(3, SCAN_THREADS);  // U_c and S_{c-1} for the output warps
+            if (more) scan_load_wu(sm, a, blk0 + ck + 1, j0, ltid);
+            cp_async_commit();
+            cp_async_wait<1>();  // this chunk's K'
+            named_sync(1, GROUP_THREADS);
         // ---- S = gamma_C S + K'^T U (warp: state rows 16w.., 32 columns)
         {
             const float gc = a.gc[blk0 + ck];
-            const int m0 = warp * 16;
+            const int m0 = lwarp * 16;
             float d[4][4] = {};
 #pragma unroll
             for (int ks = 0; ks < C / 16; ++ks) {
@@ -688,8 +694,8 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
 #pragma unroll
                 for (int np = 0; np < 2; ++np) {
                     uint32_t yh[4], yl[4];
-                    ld_b2_t(&sm.up[0][0][0], LDU, np * 16, ks * 16, lane, yh);
-                    ld_b2_t(&sm.up[1][0][0], LDU, np * 16, ks * 16, lane, yl);
+                    ld_b2_t(&sm.up[ub][0][0][0], LDU, np * 16, ks * 16, lane, yh);
+                    ld_b2_t(&sm.up[ub][1][0][0], LDU, np * 16, ks * 16, lane, yl);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         mma_16816(d[2 * np + h], xh, yh[2 * h], yh[2 * h + 1]);
@@ -712,14 +718,50 @@ __global__ void __launch_bounds__(dc::SCAN_THREADS, 1) dn_chunk_scan_kernel(cons
                         pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
                 }
         }
-        __syncthreads();  // Q', P, K' and U of this chunk are used up
-        if (more) scan_load_qpk(sm, a, blk0 + ck + 1, tid);
+            named_sync(1, GROUP_THREADS);  // K' used up
+            if (more) scan_load_k(sm, a, blk0 + ck + 1, ltid);
+            cp_async_commit();
+        }
+        named_sync(4, SCAN_THREADS);  // the last chunk's output is done
+        cp_async_wait<0>();
+        for (int e = ltid; e < S * JC; e += GROUP_THREADS) {
+            const int i = e / JC, j = e % JC;
+            state[(size_t)i * S + j0 + j] = sm.s[i][j];
+        }
+    } else {
+        scan_load_qp(sm, a, blk0, ltid);
         cp_async_commit();
-    }
-    cp_async_wait<0>();
-    for (int e = tid; e < S * JC; e += SCAN_THREADS) {
-        const int i = e / JC, j = e % JC;
-        state[(size_t)i * S + j0 + j] = sm.s[i][j];
+        for (int ck = 0; ck < a.nc; ++ck) {
+            const int cur = ck & 1, ub = ck & 1;
+            const bool more = ck + 1 < a.nc;
+            named_sync(3, SCAN_THREADS);  // U_c and S_{c-1} are in place
+            cp_async_wait<0>();           // this chunk's Q' and P
+            named_sync(2, GROUP_THREADS);
+        // ---- O = Q' S + P U (warp: rows 16 (w % 4).., columns 16 (w / 4)..)
+        {
+            float d[2][4] = {};
+            mma3_rows<S, 1>(d, &sm.qp[0][0][0], &sm.qp[1][0][0], LDB, wm, &sm.st[cur][0][0][0],
+                            &sm.st[cur][1][0][0], LDU, wn, lane);
+            mma3_rows<C, 1>(d, &sm.p[0][0][0], &sm.p[1][0][0], LDP, wm, &sm.up[ub][0][0][0],
+                            &sm.up[ub][1][0][0], LDU, wn, lane);
+            const int r0 = wm + g;
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+                const int r = r0 + e2 * 8, tok = ck * C + r;
+                if (tok < a.t) {
+                    float *dst = a.opre + ((size_t)tok * a.n_v + vh) * S + j0 + wn;
+#pragma unroll
+                    for (int n = 0; n < 2; ++n)
+                        *reinterpret_cast<float2 *>(dst + n * 8 + c0) =
+                            make_float2(d[n][2 * e2] * scale, d[n][2 * e2 + 1] * scale);
+                }
+            }
+        }
+            named_sync(2, GROUP_THREADS);  // Q' and P used up
+            named_arrive(4, SCAN_THREADS);  // O_c done
+            if (more) scan_load_qp(sm, a, blk0 + ck + 1, ltid);
+            cp_async_commit();
+        }
     }
 }
 
