@@ -16,8 +16,8 @@
 //                         Ut and W on mma.sync, P = Q K^T o Mgamma,
 //                         Q' = gamma Q, K' = gamma_C/gamma K
 //   dn_chunk_scan_kernel  per (value head, 32 state columns): the 64 chunks in
-//                         order, state in f32, U = Ut - W S, O = Q' S + P U,
-//                         S = gamma_C S + K'^T U
+//                         order, state in f32, U = Ut - W S and S = gamma_C S
+//                         + K'^T U on eight warps, O = Q' S + P U on eight more
 // Every operand of every product is a bf16 pair x = hi + lo (a 16-bit
 // mantissa) and every product is the three mma.sync terms hi*hi + hi*lo +
 // lo*hi with f32 accumulation: the gated RMSNorm that follows normalises each
@@ -519,13 +519,13 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
 }
 
 // ---------------------------------------------------------------------------
-// dn_chunk_scan_kernel: grid (S / JC, n_v), 256 threads.  The chunks in
-// order; this CTA owns state columns j0 .. j0 + 31 of value head vh.  The
-// next chunk's W and Ut are fetched once the U phase has used this chunk's,
-// its Q', P and K' once the O and S phases have, so the U phase of a chunk
-// overlaps the arrival of its Q', P and K'.  S and U are kept as bf16
-// pairs in row-major [k][n] form (the B operands, read with transposing
-// ldmatrix), written with packed 4-byte stores.
+// dn_chunk_scan_kernel: grid (S / JC, n_v), 512 threads.  The chunks in
+// order; this CTA owns state columns j0 .. j0 + 31 of value head vh.  Warps
+// 0-7 run the U/S chain and fetch the next chunk's W and Ut (once U is done)
+// and K' (once S is); warps 8-15 compute the output and fetch the next Q' and
+// P.  S and U are kept as bf16 pairs in row-major [k][n] form (the B
+// operands, read with transposing ldmatrix), written with packed 4-byte
+// stores.
 constexpr int LDU = dc::JC + 8;  // padded bf16 row of a 32-column matrix (80 B)
 struct ScanSmem {
     __nv_bfloat16 w[2][dc::C][dc::LDB], qp[2][dc::C][dc::LDB], kp[2][dc::C][dc::LDB];  // [hi, lo]
