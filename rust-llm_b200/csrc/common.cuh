@@ -200,6 +200,13 @@ __device__ __forceinline__ float rms_scale_from_sum(double sum, int n, float eps
     return 1.0f / sqrtf(__fadd_rn(mean, eps));
 }
 
+// The same scale with the hardware reciprocal square root (within 2 ulp of
+// 1 / sqrt), for norms on a kernel's critical path; n a power of two.
+__device__ __forceinline__ float rms_scale_fast(double sum, int n, float eps) {
+    const float mean = static_cast<float>(sum * (1.0 / (double)n));
+    return rsqrtf(__fadd_rn(mean, eps));
+}
+
 // Programmatic dependent launch: wait for the grid ahead on the stream to
 // complete (its writes visible); let the next grid on the stream launch.
 __device__ __forceinline__ void grid_dep_wait() {

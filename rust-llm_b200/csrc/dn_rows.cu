@@ -118,13 +118,6 @@ __device__ __forceinline__ uint32_t tile_off(int row, int col) {
 // ulps of x / (1 + e^-x), well inside the step's 1e-4 bar
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// rms_scale_from_sum with the hardware reciprocal square root (within 2 ulp
-// of 1 / sqrt): both norms of a row sit on the kernel's critical path
-__device__ __forceinline__ float rms_scale_fast(double sum, float eps) {
-    const float mean = static_cast<float>(sum * (1.0 / (double)dnr::S));
-    return rsqrtf(__fadd_rn(mean, eps));
-}
-
 __device__ __forceinline__ float4 ld4(const float *p) {
     return *reinterpret_cast<const float4 *>(p);
 }
@@ -352,7 +345,7 @@ __global__ void __maxnreg__(112)
                 double sum = -0.0;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) sum += nred[rr][w0 + q];
-                my = rms_scale_fast(sum, l2_eps);
+                my = rms_scale_fast(sum, S, l2_eps);  // both norms sit on the critical path
             }
         }
         {
@@ -432,7 +425,7 @@ __global__ void __maxnreg__(112)
             double sum = -0.0;
 #pragma unroll
             for (int q = 0; q < NCB; ++q) sum += osum[par][q][warp];
-            const float sc = rms_scale_fast(sum, a.eps);
+            const float sc = rms_scale_fast(sum, S, a.eps);
             a.out[(size_t)(blk + warp) * d_inner + (size_t)vh * S + cb * CW + lane] =
                 __fmul_rn(__fmul_rn(__fmul_rn(o, sc), wn), silu_fast(zz));
         }
