@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) sq += (double)__fmul_rn(y[e], y[e]);
             sq = warp_sum_d(sq);
-            const float sc = rms_scale_from_sum(sq, S, a.eps / (float)S);
+            const float sc = rms_scale_fast(sq, S, a.eps / (float)S);
             const float shrink = 1.0f / sqrtf((float)S);
 #pragma unroll
             for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), shrink);
@@ -134,10 +134,12 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
             store_pair4(a.vn + o, a.vn_lo + o, y);
             if (lane == 0) {
                 // gates (forward.rs:1530-1546): log decay and beta
-                a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(
-                    softplusf_(__fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh])),
-                    a.ssm_a[vh]);
-                a.bt[(size_t)i * a.n_v + vh] = sigmoidf_(a.beta[(size_t)i * a.n_v + vh]);
+                // (hardware exp2 / log2: one lane runs these while the warp waits)
+                const float x = __fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh]);
+                const float sp = x > 20.0f ? x : __logf(1.0f + __expf(x));
+                a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(sp, a.ssm_a[vh]);
+                a.bt[(size_t)i * a.n_v + vh] =
+                    __fdividef(1.0f, 1.0f + __expf(-a.beta[(size_t)i * a.n_v + vh]));
             }
         }
     }
@@ -779,7 +781,7 @@ __global__ void __launch_bounds__(128) dn_out_kernel(const DnChunkArgs a) {
     double sq = (double)__fmul_rn(o.x, o.x) + (double)__fmul_rn(o.y, o.y) +
                 (double)__fmul_rn(o.z, o.z) + (double)__fmul_rn(o.w, o.w);
     sq = warp_sum_d(sq);
-    const float sc = rms_scale_from_sum(sq, S, a.eps);
+    const float sc = rms_scale_fast(sq, S, a.eps);
     float4 y;
     y.x = __fmul_rn(__fmul_rn(__fmul_rn(o.x, sc), w.x), silu_fast(z.x));
     y.y = __fmul_rn(__fmul_rn(__fmul_rn(o.y, sc), w.y), silu_fast(z.y));
