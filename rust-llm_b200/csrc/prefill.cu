@@ -177,9 +177,10 @@ __global__ void __launch_bounds__(pf::THREADS, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_base_s;
-    // verify: launched as a programmatic dependent, so the set-up above
-    // overlaps the grid ahead; nothing is read before that grid completes
-    if constexpr (VERIFY) grid_dep_wait();
+    // both forms are launched as programmatic dependents, so the set-up
+    // above overlaps the grid ahead (prefill: the prologue, whose blocks let
+    // it launch at their start); nothing is read before that grid completes
+    grid_dep_wait();
     // verify: this CTA's key range holds positions of the appended rows
     const bool appends = VERIFY && (j0 + n_kt) * KT > a.pos;
 
@@ -707,9 +708,17 @@ cudaError_t launch_prefill(const PrefillArgs &a, const CUtensorMap &q_map,
                            const CUtensorMap &kv_map, const CUtensorMap &gate_map,
                            cudaStream_t st) {
     const int n_qt = (a.t + pf::BM - 1) / pf::BM;
-    prefill_kernel<false><<<n_qt * a.n_head, pf::THREADS, pf::SMEM, st>>>(a, q_map, kv_map,
-                                                                          gate_map);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_qt * a.n_head);
+    cfg.blockDim = dim3(pf::THREADS);
+    cfg.dynamicSmemBytes = pf::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_kernel<false>, a, q_map, kv_map, gate_map);
 }
 
 cudaError_t launch_verify_tc(const PrefillArgs &a, const CUtensorMap &kv_map, cudaStream_t st) {
