@@ -218,11 +218,19 @@ typedef enum {
     RL_OPT_VERIFY_TC = 5,     /* 1 (default): 2..8 rows over a bf16 cache take the
                                  tensor-core verify kernel (bf16 P, the prefill
                                  tolerance); 0: the exact split-KV walk */
-    RL_OPT_DN_ROWS = 6        /* 1 (default): DeltaNet calls outside the chunked prefill
+    RL_OPT_DN_ROWS = 6,       /* 1 (default): DeltaNet calls outside the chunked prefill
                                  take the rows kernel, each head's state columns split
                                  over a cluster of four CTAs; 0: the one-CTA-per-head
                                  step kernel.  Both run the rows in order and give a
                                  batch the bits of its rows one call at a time. */
+    RL_OPT_WAIT_LIMIT_US = 7, /* how long rl_split_merge's kernel waits for the other
+                                 GPUs' flags before it gives up, in microseconds
+                                 (0, the default: one second).  A wait that gives up
+                                 makes the next rl_sync return RL_ETIMEOUT; the
+                                 context stays usable. */
+    RL_OPT_WALK_SPANS = 8     /* 1: every bf16 decode walk records its span on the
+                                 global timer (RL_PROF_WALK_SPAN); 0 (default): off.
+                                 Costs two atomics per CTA. */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);
@@ -255,7 +263,12 @@ typedef enum {
     RL_PROF_PREFILL = 4,  /* tensor-core causal prefill attention */
     RL_PROF_DN_CHUNK = 5, /* DeltaNet chunked prefill */
     RL_PROF_VERIFY = 6,   /* tensor-core multi-row verify attention */
-    RL_PROF_KERNELS = 7
+    RL_PROF_WALK_SPAN = 7, /* bf16 decode walk, timed on the GPU's global timer from
+                              its first CTA's start to its last CTA's end, inside
+                              whatever stream or graph it runs in (no events, so
+                              programmatic launch overlap is kept); needs
+                              RL_OPT_WALK_SPANS = 1 */
+    RL_PROF_KERNELS = 8
 } rl_prof_kernel;
 int rl_profile_enable(rl_ctx *ctx, int on);
 int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches);
@@ -284,13 +297,23 @@ int rl_profile_reset(rl_ctx *ctx);
  * work overlaps on the GPU (other streams, other host threads) race: run them
  * one after another.  The first call on a device, with that device current,
  * resolves the array's device address and the kernels' launch limits; make
- * that first call before any stream capture.  A device-side wait that gives
- * up leaves `out` unwritten; there is no status channel beyond the return
- * code, which covers argument and launch errors. */
+ * that first call before any stream capture.  The return code covers
+ * argument and launch errors; every pointer must be 16-byte aligned and
+ * n_rot a multiple of 16, or the call returns RL_EINVAL before it enqueues
+ * anything.  A device-side wait that gives up (about a second) leaves `out`
+ * unwritten and sets a sticky status word in the array's last 256 bytes,
+ * which rl_noalloc_status reads. */
 #define RL_NOALLOC_SCRATCH_BYTES (4u << 20)
 int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_cache, void *v_cache,
                          const float *q_norm, const float *k_norm, int pos, int t,
                          const float *qg, const float *k, const float *v, float *out);
+/* The device-side status of the rl_full_attn_noalloc calls enqueued on the
+ * current device since the last read: waits for `stream`, then returns
+ * RL_OK, RL_ETIMEOUT (a kernel's bounded wait gave up, so some `out` is not
+ * valid) or RL_EINVAL (a kernel flagged a bad argument), and clears the
+ * word.  Allocates nothing.  No counterpart in the reference: it is the
+ * no-alloc path's stand-in for the status an rl_ctx keeps (rl_sync). */
+int rl_noalloc_status(void *stream);
 
 /* Library version string; never NULL. */
 const char *rl_version(void);

@@ -17,6 +17,16 @@ constexpr int DEV_BAD_ARG = 2;
 // A bounded wait gives up after this many SM clocks (about a second at the
 // B200's 1.0-2.0 GHz), sets DEV_TIMEOUT and lets the kernel return.
 constexpr long long WAIT_LIMIT_CYCLES = 2000000000ll;
+// The default limit, in nanoseconds, of a wait on another GPU's flag (the
+// context option RL_OPT_WAIT_LIMIT_US overrides it).
+constexpr unsigned long long PEER_WAIT_LIMIT_NS = 1000000000ull;
+
+// The global nanosecond timer (the same on every SM of the GPU).
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (a.span && tid == 0) atomicMin(a.span, globaltimer_ns());
     // a batch row is its own sequence with its own cache and tensor map
     const BatchRow *br = a.rows ? a.rows + row : nullptr;
     const int pos_row = br ? a.batch_pos[row] : a.pos + row;  // sequence position of this row
@@ -505,6 +506,18 @@ __global__ void __launch_bounds__(dm::THREADS, 1)
     if (tid == 0 && flag_s) atomicOr(a.status, DEV_TIMEOUT);
     // triggered last: a merge resident for the whole walk slowed it down
     __syncthreads();
+    if (a.span && tid == 0) {
+        // the launch's span: from its first CTA's start to its last CTA's end
+        const unsigned long long now = globaltimer_ns();
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        if (atomicAdd(a.span + 1, 1ull) == total - 1) {
+            const unsigned long long t0 = atomicAdd(a.span, 0ull);
+            atomicAdd(a.span + 2, now - t0);
+            atomicAdd(a.span + 3, 1ull);
+            atomicExch(a.span, ~0ull);
+            atomicExch(a.span + 1, 0ull);
+        }
+    }
     grid_dep_launch();
 }
 
@@ -634,7 +647,8 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
 __global__ void __launch_bounds__(256) peer_merge_kernel(const float *xbuf, int world, int slot,
                                                          unsigned epoch, int rows_heads,
                                                          const float *qg, float *out,
-                                                         int *status) {
+                                                         int *status,
+                                                         unsigned long long limit_ns) {
     grid_dep_wait();    // this GPU's own partial and flag, and qg, are in place
     grid_dep_launch();  // the next layer's walk may start streaming meanwhile
     const int hh = blockIdx.x, d = threadIdx.x;
@@ -642,15 +656,17 @@ __global__ void __launch_bounds__(256) peer_merge_kernel(const float *xbuf, int 
     if (d == 0) {
         const unsigned *flags = reinterpret_cast<const unsigned *>(
             reinterpret_cast<const char *>(xbuf) + xbuf_flag_offset(world, rows_heads, dm::HD));
+        // one limit for the whole wait, on the global nanosecond timer
+        const unsigned long long start = globaltimer_ns();
         for (int g = 0; g < world; ++g) {
-            const long long start = clock64();
             while (true) {
                 unsigned f;
                 asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + g)
                              : "memory");
                 if ((int)(f - epoch) >= 0) break;
-                if (clock64() - start > WAIT_LIMIT_CYCLES) {
+                if (globaltimer_ns() - start > limit_ns) {
                     atomicOr(status, DEV_TIMEOUT);
+                    g = world;  // give up on every remaining flag
                     break;
                 }
                 __nanosleep(32);
@@ -675,7 +691,7 @@ __global__ void __launch_bounds__(256) peer_merge_kernel(const float *xbuf, int 
 
 cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned epoch,
                               int rows_heads, const float *qg, float *out, int *status,
-                              cudaStream_t st) {
+                              unsigned long long limit_ns, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(rows_heads);
     cfg.blockDim = dim3(dm::HD);
@@ -686,7 +702,7 @@ cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned e
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, peer_merge_kernel, xbuf, world, slot, epoch, rows_heads, qg,
-                              out, status);
+                              out, status, limit_ns);
 }
 
 // Merges the partials of a sequence split across GPUs, gathered as

@@ -22,7 +22,8 @@
 // mantissa) and every product is the three mma.sync terms hi*hi + hi*lo +
 // lo*hi with f32 accumulation: the gated RMSNorm that follows normalises each
 // head, so a head whose readout nearly cancels needs its relative error
-// small, and single bf16 operands (8 bits) are not enough for that.
+// small, and single bf16 operands (8 bits) are not enough for that.  Q K^T
+// goes further: q and k are bf16 triples (24 bits) and it takes six terms.
 //   dn_out_kernel         per token: gated RMSNorm times SiLU(z) (:1642-1652);
 //                         dn_hist_kernel leaves the last three raw inputs as the
 //                         conv history (the reference's history after the batch)
@@ -61,6 +62,21 @@ __device__ __forceinline__ void store_pair4(__nv_bfloat16 *hi, __nv_bfloat16 *lo
     l.y = pack_bf16(y[2] - bf16_hi(y[2]), y[3] - bf16_hi(y[3]));
     *reinterpret_cast<uint2 *>(hi) = h;
     *reinterpret_cast<uint2 *>(lo) = l;
+}
+// The bf16 triple (hi, lo, l2) of four values: x = hi + lo + l2 to 24 bits.
+__device__ __forceinline__ void store_triple4(__nv_bfloat16 *hi, __nv_bfloat16 *lo,
+                                              __nv_bfloat16 *l2, const float *y) {
+    store_pair4(hi, lo, y);
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float h = bf16_hi(y[e]);
+        r[e] = (y[e] - h) - bf16_hi(y[e] - h);
+    }
+    uint2 w;
+    w.x = pack_bf16(r[0], r[1]);
+    w.y = pack_bf16(r[2], r[3]);
+    *reinterpret_cast<uint2 *>(l2) = w;
 }
 
 // One warp per (8 consecutive tokens, group of 128 channels): the group's
@@ -127,7 +143,8 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
             for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), shrink);
             const bool is_q = g < a.n_k;
             const size_t o = ((size_t)i * a.n_k + (is_q ? g : g - a.n_k)) * S + lane * 4;
-            store_pair4((is_q ? a.qn : a.kn) + o, (is_q ? a.qn_lo : a.kn_lo) + o, y);
+            store_triple4((is_q ? a.qn : a.kn) + o, (is_q ? a.qn_lo : a.kn_lo) + o,
+                          (is_q ? a.qn_l2 : a.kn_l2) + o, y);
         } else {
             const int vh = g - 2 * a.n_k;
             const size_t o = ((size_t)i * a.n_v + vh) * S + lane * 4;
@@ -227,8 +244,16 @@ struct LocalSmem {
     __nv_bfloat16 k[dc::C][dc::LDB], q[dc::C][dc::LDB], v[dc::C][dc::LDB];
     __nv_bfloat16 kl[dc::C][dc::LDB], ql[dc::C][dc::LDB], vl[dc::C][dc::LDB];  // low halves
     float kk[dc::C][dc::LDF], qk[dc::C][dc::LDF], t[dc::C][dc::LDF], x[dc::C][dc::LDF];
-    __nv_bfloat16 ta_hi[dc::C][dc::LDP], ta_lo[dc::C][dc::LDP];  // T diag(beta)
-    __nv_bfloat16 tb_hi[dc::C][dc::LDP], tb_lo[dc::C][dc::LDP];  // T diag(beta gamma)
+    union {
+        struct {
+            __nv_bfloat16 ta_hi[dc::C][dc::LDP], ta_lo[dc::C][dc::LDP];  // T diag(beta)
+            __nv_bfloat16 tb_hi[dc::C][dc::LDP], tb_lo[dc::C][dc::LDP];  // T diag(beta gamma)
+        };
+        // the third terms of q and k, read by Q K^T only (before T exists)
+        struct {
+            __nv_bfloat16 q2[dc::C][dc::LDB], k2[dc::C][dc::LDB];
+        };
+    };
     float cum[dc::C], beta[dc::C];
 };
 
@@ -254,6 +279,8 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
         cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
         cp_async16_zfill(&sm.v[r][c8], a.vn + vo, ok);
         cp_async16_zfill(&sm.vl[r][c8], a.vn_lo + vo, ok);
+        cp_async16_zfill(&sm.k2[r][c8], a.kn_l2 + ko, ok);
+        cp_async16_zfill(&sm.q2[r][c8], a.qn_l2 + ko, ok);
     }
     cp_async_commit();
     if (warp == 0) {
@@ -275,8 +302,12 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     }
     cp_async_wait<0>();
     __syncthreads();
-    // ---- K K^T and Q K^T (warp: 16 rows, all 64 columns), each as
-    // hi*hi + hi*lo + lo*hi of the bf16 pairs
+    // ---- K K^T as hi*hi + hi*lo + lo*hi of the bf16 pairs, and Q K^T of
+    // the bf16 triples (hi*hi + hi*lo + lo*hi + lo*lo + hi*l2 + l2*hi): the
+    // readout P U of a token whose state has all but decayed away cancels
+    // down to the q.k products of its own chunk, and the per-head gated norm
+    // that follows magnifies their error; pairs (16 bits) measured 1.3e-2 of
+    // such a head's output at 4096 tokens, triples stay at the f32 level
     {
         // warp: rows 16 * (warp % 4), columns 32 * (warp / 4) .. + 31
         const int rw = (warp & 3) * 16, cn = (warp >> 2) * 32;
@@ -287,16 +318,18 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
             for (int e = 0; e < 4; ++e) dk[n][e] = dq[n][e] = 0.0f;
 #pragma unroll
         for (int ks = 0; ks < S / 16; ++ks) {
-            uint32_t ak[4], aq[4], akl[4], aql[4];
+            uint32_t ak[4], aq[4], akl[4], aql[4], aq2[4];
             ld_a(&sm.k[0][0], LDB, rw, ks * 16, lane, ak);
             ld_a(&sm.q[0][0], LDB, rw, ks * 16, lane, aq);
             ld_a(&sm.kl[0][0], LDB, rw, ks * 16, lane, akl);
             ld_a(&sm.ql[0][0], LDB, rw, ks * 16, lane, aql);
+            ld_a(&sm.q2[0][0], LDB, rw, ks * 16, lane, aq2);
 #pragma unroll
             for (int np = 0; np < 2; ++np) {
-                uint32_t b[4], bl[4];
+                uint32_t b[4], bl[4], b2[4];
                 ld_b2(&sm.k[0][0], LDB, cn + np * 16, ks * 16, lane, b);
                 ld_b2(&sm.kl[0][0], LDB, cn + np * 16, ks * 16, lane, bl);
+                ld_b2(&sm.k2[0][0], LDB, cn + np * 16, ks * 16, lane, b2);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     mma_16816(dk[2 * np + h], ak, b[2 * h], b[2 * h + 1]);
@@ -305,6 +338,9 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
                     mma_16816(dq[2 * np + h], aq, b[2 * h], b[2 * h + 1]);
                     mma_16816(dq[2 * np + h], aq, bl[2 * h], bl[2 * h + 1]);
                     mma_16816(dq[2 * np + h], aql, b[2 * h], b[2 * h + 1]);
+                    mma_16816(dq[2 * np + h], aql, bl[2 * h], bl[2 * h + 1]);
+                    mma_16816(dq[2 * np + h], aq, b2[2 * h], b2[2 * h + 1]);
+                    mma_16816(dq[2 * np + h], aq2, b[2 * h], b[2 * h + 1]);
                 }
             }
         }

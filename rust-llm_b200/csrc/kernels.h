@@ -78,6 +78,9 @@ struct DecodeArgs {
     // position batch_pos[r] of its own context, described by rows[r]
     const BatchRow *rows;
     const int *batch_pos;
+    // non-null: the bf16 walk records its span on the global timer into
+    // this launch's slot, {first CTA start, CTAs done, sum of spans, launches}
+    unsigned long long *span;
 };
 cudaError_t init_decode_kernels();
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st);
@@ -107,7 +110,7 @@ __host__ __device__ inline size_t xbuf_bytes(int world, int rows_heads, int hd) 
 // out [rows_heads][hd].  Launched as a programmatic dependent.
 cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned epoch,
                               int rows_heads, const float *qg, float *out, int *status,
-                              cudaStream_t st);
+                              unsigned long long limit_ns, cudaStream_t st);
 // parts [n_parts][rows_heads][hd + 2] -> out [rows_heads][hd], gated
 cudaError_t launch_merge_parts(const float *parts, int n_parts, int rows_heads, const float *qg,
                                float *out, cudaStream_t st);
@@ -205,6 +208,7 @@ struct DnChunkArgs {
     // scratch, sized for max_batch rows
     __nv_bfloat16 *qn, *kn, *vn;          // [t][n_k][s], [t][n_k][s], [t][n_v][s]
     __nv_bfloat16 *qn_lo, *kn_lo, *vn_lo;  // low halves: every operand is a bf16 pair
+    __nv_bfloat16 *qn_l2, *kn_l2;         // third terms of q and k (Q K^T needs 24 bits)
     float *lg, *bt;                       // [t][n_v] log decay, beta
     __nv_bfloat16 *w, *qp, *kp, *p;       // [n_v][nc][64][s] (p: [n_v][nc][64][64])
     __nv_bfloat16 *w_lo, *qp_lo, *kp_lo, *p_lo;  // their low halves

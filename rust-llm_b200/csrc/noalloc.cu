@@ -78,6 +78,12 @@ int setup(int device, DeviceState **out) {
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
+// The array's last 256 bytes hold the status word the kernels OR a
+// rl::DEV_* bit into when a bounded wait gives up.  It is sticky: calls
+// never clear it; rl_noalloc_status reads and clears it.  The rest of the
+// array is the per-call layout.
+constexpr size_t kStatusOffset = RL_NOALLOC_SCRATCH_BYTES - 256;
+
 }  // namespace
 
 extern "C" int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_cache,
@@ -93,10 +99,19 @@ extern "C" int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_
         return fail(RL_EINVAL, "kv_dtype is neither RL_KV_F32 nor RL_KV_BF16");
     if (c.n_rot < 0 || c.n_rot > c.head_dim || (c.n_rot & 1))
         return fail(RL_EINVAL, "n_rot must be even and at most head_dim");
+    if (c.n_rot % 16)
+        return fail(RL_EINVAL,
+                    "the kernels rotate whole 8-dim lanes: n_rot must be a multiple of 16");
     if (t < 1 || pos < 0 || (int64_t)pos + t > c.context)
         return fail(RL_ECONTEXT, "the rows do not fit the context");
     if (((uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15)
         return fail(RL_EINVAL, "qg, k, v and out must be 16-byte aligned");
+    // the prologue reads the norm weights as 16-byte vectors and the walks
+    // read the caches with 16-byte loads and bulk copies
+    if (((uintptr_t)q_norm | (uintptr_t)k_norm) & 15)
+        return fail(RL_EINVAL, "q_norm and k_norm must be 16-byte aligned");
+    if (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
+        return fail(RL_EINVAL, "k_cache and v_cache must be 16-byte aligned");
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return fail(RL_ECUDA, "cudaGetDevice failed");
     DeviceState *d = nullptr;
@@ -130,9 +145,8 @@ extern "C" int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_
     const size_t q_bytes = align256((size_t)t * nh * hd * sizeof(float));
     const size_t po_bytes = align256((size_t)t * nh * n_cl * hd * sizeof(float));
     const size_t pml_bytes = align256((size_t)t * nh * n_cl * 8 * 2 * sizeof(float));
-    // counters, then one status word a kernel sets if a bounded wait gives up
-    const size_t cnt_bytes = align256(((size_t)t * nkv * 8 + 1) * sizeof(int));
-    if (q_bytes + po_bytes + pml_bytes + cnt_bytes > RL_NOALLOC_SCRATCH_BYTES)
+    const size_t cnt_bytes = align256((size_t)t * nkv * 8 * sizeof(int));
+    if (q_bytes + po_bytes + pml_bytes + cnt_bytes > kStatusOffset)
         return fail(RL_EINVAL,
                     "this call needs more scratch than RL_NOALLOC_SCRATCH_BYTES holds; use fewer "
                     "rows or rl_full_attn");
@@ -142,8 +156,8 @@ extern "C" int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_
     float *part_ml = reinterpret_cast<float *>(base + q_bytes + po_bytes);
     int *counters = reinterpret_cast<int *>(base + q_bytes + po_bytes + pml_bytes);
 
-    // the arrival counters and the status word must start at zero; a
-    // previous call that gave up part-way could have left them otherwise
+    // the arrival counters must start at zero; a previous call that gave up
+    // part-way could have left them otherwise
     if (cudaMemsetAsync(counters, 0, cnt_bytes, st) != cudaSuccess)
         return fail(RL_ECUDA, "clearing the counters failed");
 
@@ -184,7 +198,7 @@ extern "C" int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_
     dd.part_ml = part_ml;
     dd.counters = counters;
     dd.out = out;
-    dd.status = counters + (size_t)t * nkv * 8;
+    dd.status = reinterpret_cast<int *>(base + kStatusOffset);
     dd.pos = pos;
     dd.t = t;
     dd.context = c.context;
@@ -199,5 +213,27 @@ extern "C" int rl_full_attn_noalloc(const rl_config *cfg, void *stream, void *k_
     dd.kv_bf16 = bf16;
     dd.fused = false;
     if (rl::launch_decode(dd, st) != cudaSuccess) return fail(RL_ECUDA, "decode launch failed");
+    return RL_OK;
+}
+
+extern "C" int rl_noalloc_status(void *stream) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(RL_ECUDA, "cudaGetDevice failed");
+    DeviceState *d = nullptr;
+    int code = setup(device, &d);
+    if (code) return code;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int *word = reinterpret_cast<int *>(d->scratch + kStatusOffset);
+    int bits = 0;
+    // read, then clear, in stream order behind the calls it reports on
+    if (cudaMemcpyAsync(&bits, word, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaMemsetAsync(word, 0, sizeof(int), st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(RL_ECUDA, "reading the no-alloc status word failed");
+    if (bits & rl::DEV_TIMEOUT)
+        return fail(RL_ETIMEOUT, "a kernel of an earlier rl_full_attn_noalloc call gave up a "
+                                 "bounded wait; its output is not valid");
+    if (bits) return fail(RL_EINVAL, "a kernel of an earlier rl_full_attn_noalloc call flagged "
+                                     "a bad argument");
     return RL_OK;
 }

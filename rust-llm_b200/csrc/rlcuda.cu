@@ -51,6 +51,7 @@ struct rl_ctx {
     // chunked DeltaNet prefill scratch (slots == 1 and max_batch >= 64)
     __nv_bfloat16 *dn_qn = nullptr, *dn_kn = nullptr, *dn_vn = nullptr;
     __nv_bfloat16 *dn_qn_lo = nullptr, *dn_kn_lo = nullptr, *dn_vn_lo = nullptr;
+    __nv_bfloat16 *dn_qn_l2 = nullptr, *dn_kn_l2 = nullptr;
     __nv_bfloat16 *dn_w_lo = nullptr, *dn_qp_lo = nullptr, *dn_kp_lo = nullptr, *dn_p_lo = nullptr;
     float *dn_lg = nullptr, *dn_bt = nullptr;
     __nv_bfloat16 *dn_w = nullptr, *dn_qp = nullptr, *dn_kp = nullptr, *dn_p = nullptr;
@@ -69,6 +70,9 @@ struct rl_ctx {
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
     int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1;
+    int64_t opt_wait_limit_us = 0;  // 0: rl::PEER_WAIT_LIMIT_NS
+    // RL_OPT_WALK_SPANS: [n_full][4] {first start, CTAs done, span sum, launches}
+    unsigned long long *spans = nullptr;
     // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
     // resident CTAs per SM of the bf16 walk: [fused]
@@ -206,10 +210,11 @@ void free_all(rl_ctx *x) {
     void *ps[] = {x->kv, x->conv, x->ssm, x->q_norm, x->k_norm, x->conv1d, x->ssm_a,
                   x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->gate_bf16, x->part_o, x->part_ml,
                   x->counters, x->rope_cs, x->rope_sn, x->stage, x->status,
-                  x->dn_qn, x->dn_kn, x->dn_vn, x->dn_qn_lo, x->dn_kn_lo, x->dn_vn_lo, x->dn_w_lo, x->dn_qp_lo, x->dn_kp_lo, x->dn_p_lo, x->dn_lg, x->dn_bt, x->dn_w, x->dn_qp, x->dn_kp,
+                  x->dn_qn, x->dn_kn, x->dn_vn, x->dn_qn_lo, x->dn_kn_lo, x->dn_vn_lo, x->dn_qn_l2, x->dn_kn_l2, x->dn_w_lo, x->dn_qp_lo, x->dn_kp_lo, x->dn_p_lo, x->dn_lg, x->dn_bt, x->dn_w, x->dn_qp, x->dn_kp,
                   x->dn_p, x->dn_ut, x->dn_gc, x->dn_opre};
     for (void *p : ps)
         if (p) cudaFree(p);
+    if (x->spans) cudaFree(x->spans);
     if (x->hpin_base) cudaFreeHost(x->hpin_base);
     if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
 }
@@ -265,6 +270,16 @@ cudaError_t h2d(rl_ctx *x, void *dst, const void *src, size_t bytes) {
     return e;
 }
 
+// Every layer's span slot back to {no start yet, 0 done, 0, 0}, once the
+// stream has drained.
+int reset_spans(rl_ctx *x) {
+    std::vector<unsigned long long> h((size_t)x->cfg.n_full * 4, 0ull);
+    for (int l = 0; l < x->cfg.n_full; ++l) h[4 * l] = ~0ull;
+    CK(x, cudaStreamSynchronize(x->stream));
+    CK(x, cudaMemcpy(x->spans, h.data(), h.size() * sizeof(h[0]), cudaMemcpyHostToDevice));
+    return RL_OK;
+}
+
 int check_status(rl_ctx *x) {
     int st = 0;
     if (x->hstatus) {
@@ -306,6 +321,10 @@ int bf16_walk(rl_ctx *ctx, rl::DecodeArgs &d, int64_t n_kv_max, int64_t groups, 
     d.csize = 1;
     d.early_kv = fused && ctx->early_ok;
     d.early_tiles = (int)ctx->opt_early_tiles;
+    if (ctx->spans && !d.rows) {
+        const int64_t layer = d.k_row0 / (2 * (int64_t)ctx->cfg.n_head_kv * ctx->cfg.context);
+        d.span = ctx->spans + 4 * layer;
+    }
     {
         ProfScope ps(ctx, RL_PROF_DECODE);
         CK(ctx, rl::launch_decode_mma(d, ctx->kv_map, ctx->stream));
@@ -487,6 +506,8 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         if ((code = alloc(x, &x->dn_qn, mb * nk * s)) || (code = alloc(x, &x->dn_kn, mb * nk * s)) ||
             (code = alloc(x, &x->dn_qn_lo, mb * nk * s)) ||
             (code = alloc(x, &x->dn_kn_lo, mb * nk * s)) ||
+            (code = alloc(x, &x->dn_qn_l2, mb * nk * s)) ||
+            (code = alloc(x, &x->dn_kn_l2, mb * nk * s)) ||
             (code = alloc(x, &x->dn_vn_lo, mb * nv * s)) ||
             (code = alloc(x, &x->dn_w_lo, nv * nc * 64 * s)) ||
             (code = alloc(x, &x->dn_qp_lo, nv * nc * 64 * s)) ||
@@ -968,9 +989,12 @@ int rl_split_merge(rl_ctx *ctx, const float *qg, float *out) {
     CK(ctx, cudaSetDevice(ctx->device));
     {
         ProfScope ps(ctx, RL_PROF_MERGE);
+        const unsigned long long limit_ns =
+            ctx->opt_wait_limit_us > 0 ? (unsigned long long)ctx->opt_wait_limit_us * 1000ull
+                                       : rl::PEER_WAIT_LIMIT_NS;
         CK(ctx, rl::launch_peer_merge(ctx->xbuf, ctx->xworld, (int)(ctx->xepoch & 1),
                                       ctx->xepoch, ctx->cfg.n_head, qg, out, ctx->status,
-                                      ctx->stream));
+                                      limit_ns, ctx->stream));
     }
     ctx->prev_dn = 0;
     return RL_OK;
@@ -1217,6 +1241,8 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
         d.kn = ctx->dn_kn;
         d.qn_lo = ctx->dn_qn_lo;
         d.kn_lo = ctx->dn_kn_lo;
+        d.qn_l2 = ctx->dn_qn_l2;
+        d.kn_l2 = ctx->dn_kn_l2;
         d.vn_lo = ctx->dn_vn_lo;
         d.w_lo = ctx->dn_w_lo;
         d.qp_lo = ctx->dn_qp_lo;
@@ -1374,6 +1400,26 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
             return fail(ctx, RL_EINVAL, "cluster size must be 0 (automatic), 1, 2, 4 or 8");
         ctx->opt_cluster = value;
         return RL_OK;
+    case RL_OPT_WAIT_LIMIT_US:
+        if (value > 60000000)
+            return fail(ctx, RL_EINVAL, "a wait limit above 60 s is not a limit");
+        ctx->opt_wait_limit_us = value;
+        return RL_OK;
+    case RL_OPT_WALK_SPANS:
+        if (value > 1) return fail(ctx, RL_EINVAL, "the span option must be 0 or 1");
+        CK(ctx, cudaSetDevice(ctx->device));
+        if (value && !ctx->spans) {
+            if (ctx->cfg.n_full < 1) return RL_OK;
+            CK(ctx, cudaMalloc((void **)&ctx->spans,
+                               (size_t)ctx->cfg.n_full * 4 * sizeof(unsigned long long)));
+            return reset_spans(ctx);
+        }
+        if (!value && ctx->spans) {
+            CK(ctx, cudaStreamSynchronize(ctx->stream));
+            CK(ctx, cudaFree(ctx->spans));
+            ctx->spans = nullptr;
+        }
+        return RL_OK;
     default: return fail(ctx, RL_EINVAL, "unknown option %d", option);
     }
 }
@@ -1388,6 +1434,8 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_EARLY_TILES: return ctx->opt_early_tiles;
     case RL_OPT_VERIFY_TC: return ctx->opt_verify_tc;
     case RL_OPT_DN_ROWS: return ctx->opt_dn_rows;
+    case RL_OPT_WAIT_LIMIT_US: return ctx->opt_wait_limit_us;
+    case RL_OPT_WALK_SPANS: return ctx->spans ? 1 : 0;
     default: return -1;
     }
 }
@@ -1403,6 +1451,23 @@ int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches
     if (kernel < 0 || kernel >= RL_PROF_KERNELS)
         return fail(ctx, RL_EINVAL, "unknown kernel %d", kernel);
     CK(ctx, cudaSetDevice(ctx->device));
+    if (kernel == RL_PROF_WALK_SPAN) {
+        double ns = 0.0;
+        int64_t n = 0;
+        if (ctx->spans) {
+            std::vector<unsigned long long> h((size_t)ctx->cfg.n_full * 4);
+            CK(ctx, cudaStreamSynchronize(ctx->stream));
+            CK(ctx, cudaMemcpy(h.data(), ctx->spans, h.size() * sizeof(h[0]),
+                               cudaMemcpyDeviceToHost));
+            for (int l = 0; l < ctx->cfg.n_full; ++l) {
+                ns += (double)h[4 * l + 2];
+                n += (int64_t)h[4 * l + 3];
+            }
+        }
+        if (total_ms) *total_ms = ns * 1e-6;
+        if (launches) *launches = n;
+        return RL_OK;
+    }
     if (drain_profile(ctx)) return fail(ctx, RL_ECUDA, "profile events could not be read");
     if (total_ms) *total_ms = ctx->prof_ms[kernel];
     if (launches) *launches = ctx->prof_launches[kernel];
@@ -1414,7 +1479,7 @@ int rl_profile_reset(rl_ctx *ctx) {
     CK(ctx, cudaSetDevice(ctx->device));
     drain_profile(ctx);
     for (int k = 0; k < RL_PROF_KERNELS; ++k) ctx->prof_ms[k] = 0.0, ctx->prof_launches[k] = 0;
-    return RL_OK;
+    return ctx->spans ? reset_spans(ctx) : RL_OK;
 }
 
 // ---- state access ----------------------------------------------------------

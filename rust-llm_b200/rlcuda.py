@@ -25,8 +25,9 @@ RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED,
     0, -1, -2, -3, -4, -5, -6, -7)
 RL_KV_F32, RL_KV_BF16 = 0, 1
 (RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS, RL_OPT_CLUSTER, RL_OPT_EARLY_TILES,
- RL_OPT_VERIFY_TC, RL_OPT_DN_ROWS) = 0, 1, 2, 3, 4, 5, 6
-PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify")
+ RL_OPT_VERIFY_TC, RL_OPT_DN_ROWS, RL_OPT_WAIT_LIMIT_US, RL_OPT_WALK_SPANS) = range(9)
+PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify",
+                "walk_span")
 HOST, DEVICE = 0, 1
 RL_IPC_HANDLE_BYTES = 64
 RL_EXCHANGE_MAX_GPUS = 8
@@ -108,6 +109,7 @@ SIGNATURES = {
     "rl_profile_reset": ([_vp], _i),
     "rl_full_attn_noalloc": ([ctypes.POINTER(Config), _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp,
                               _vp, _vp], _i),
+    "rl_noalloc_status": ([_vp], _i),
     "rl_set_shard": ([_vp, _i, _i], _i),
     "rl_full_attn_partial": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "rl_merge_partials": ([_vp, _i, _vp, _vp, _vp], _i),

@@ -11,6 +11,7 @@ state N(0,0.1), z N(0,1).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -18,6 +19,8 @@ import numpy as np
 import oracle as orc
 
 N_HEAD, N_KV, HD = 16, 4, 256
+# the oracle shares heads over every host core, as Pool::chunks does
+THREADS = max(1, min(64, os.cpu_count() or 1))
 S, N_K, N_V, KERNEL = 128, 16, 32, 4
 CONV_DIM = 2 * N_K * S + N_V * S
 
@@ -69,7 +72,7 @@ def full_case(seed: int, pos: int, t: int, kv_bf16: bool = False, unit_norms: bo
     return FullCase(pos, qg, k, v, cache, qn, kn)
 
 
-def oracle_full(case: FullCase, context: int, kv_bf16=False, threads=8):
+def oracle_full(case: FullCase, context: int, kv_bf16=False, threads=THREADS):
     """Runs the oracle on a fresh [2][4][context][256] cache holding the case's
     positions; returns (out [t][4096], cache after the append)."""
     cfg = orc.qwen35_config(context, kv_bf16)
@@ -126,7 +129,7 @@ def lin_state(r: orc.Rng, slots: int, live: int = 0):
     return conv, ssm
 
 
-def oracle_linear(w: LinWeights, rows: LinRows, conv, ssm, slots, live, threads=8):
+def oracle_linear(w: LinWeights, rows: LinRows, conv, ssm, slots, live, threads=THREADS):
     cfg = orc.qwen35_config(16)
     return orc.linear_attn(cfg, slots, live, rows.qkv, rows.z, rows.alpha, rows.beta, conv, ssm,
                            w.conv1d, w.ssm_a, w.dt_bias, w.norm, threads)

@@ -60,41 +60,89 @@ class ToyStack:
                     dt_bias=(0.1 * r.standard_normal(N_V)).astype(np.float32),
                     norm=(1.0 + 0.1 * r.standard_normal(S)).astype(np.float32)))
 
+    def logits(self, backend, rows, pos: int, live: int = 0) -> np.ndarray:
+        """One pass of the stack over a batch of rows at positions pos.. (ring
+        slot `live` for the DeltaNet layers); the logits of every row.  Every
+        host-side product is taken one row at a time, so a row's numbers do
+        not depend on the batch around it: a verify batch's row then differs
+        from the same token's single pass only through the attention ops."""
+        x = self.embed[np.asarray(rows)]                           # [t][d]
+        for il, lw in enumerate(self.layers):
+            h = np.stack([_rms(r) for r in x])
+            if is_full(il):
+                o = backend.full(il // 4, pos, _proj(lw["wqg"], h), _proj(lw["wk"], h),
+                                 _proj(lw["wv"], h))
+            else:
+                o = backend.linear(il - (il + 1) // 4, live, _proj(lw["wqkv"], h),
+                                   _proj(lw["wz"], h), _proj(lw["wa"], h), _proj(lw["wb"], h))
+            x = (x + _proj(lw["wo"], o)).astype(np.float32)
+        return np.stack([self.head @ _rms(r) for r in x]).astype(np.float32)
+
     def run(self, backend, prompt, n_new: int):
         """Feeds the prompt as one batch of rows, then decodes greedily one
         row at a time; returns the n_new generated tokens."""
-        rows = np.asarray(prompt)
-        pos = 0
-        out = []
-        for _ in range(n_new):
-            x = self.embed[rows]                                   # [t][d]
-            for il, lw in enumerate(self.layers):
-                h = x / np.sqrt((x * x).mean(axis=1, keepdims=True) + 1e-6)
-                if is_full(il):
-                    o = backend.full(il // 4, pos, h @ lw["wqg"].T, h @ lw["wk"].T,
-                                     h @ lw["wv"].T)
-                else:
-                    o = backend.linear(il - (il + 1) // 4, h @ lw["wqkv"].T, h @ lw["wz"].T,
-                                       h @ lw["wa"].T, h @ lw["wb"].T)
-                x = (x + o @ lw["wo"].T).astype(np.float32)
-            pos += len(rows)
-            hf = x[-1] / np.sqrt((x[-1] * x[-1]).mean() + 1e-6)
-            nxt = int(np.argmax(self.head @ hf))
+        r = Runner(self, backend)
+        nxt = int(np.argmax(r.forward_batch(prompt)))
+        out = [nxt]
+        for _ in range(n_new - 1):
+            nxt = int(np.argmax(r.forward_batch([nxt])))
             out.append(nxt)
-            rows = np.asarray([nxt])
         return out
 
 
-class OracleBackend:
-    """The oracle's restatement, with f32 caches and states it owns."""
+def _rms(x):
+    return (x / np.sqrt((x * x).mean() + 1e-6)).astype(np.float32)
 
-    def __init__(self, stack: ToyStack, context: int):
+
+def _proj(w, h):
+    return np.stack([w @ r for r in h]).astype(np.float32)
+
+
+class Runner:
+    """The reference Runner's position and ring bookkeeping over a backend
+    (forward.rs:641-688): forward_batch runs rows and commits them all;
+    verify runs rows and commits none; accept(rows >= 1) moves pos and the
+    live ring slot, with no copy, so a rollback is a smaller accept."""
+
+    def __init__(self, stack: ToyStack, backend):
+        self.stack, self.backend = stack, backend
+        self.slots = getattr(backend, "slots", 1)
+        self.pos = self.live = 0
+        self.batch = 0
+
+    def verify(self, rows) -> np.ndarray:
+        assert len(rows) <= self.slots or self.slots == 1
+        out = self.stack.logits(self.backend, rows, self.pos, self.live)
+        self.batch = len(rows)
+        return out
+
+    def accept(self, rows: int):
+        assert 1 <= rows <= self.batch
+        self.pos += rows
+        self.live = (self.live + rows) % self.slots
+        if hasattr(self.backend, "accept"):
+            self.backend.accept(rows)
+        self.batch = 0
+
+    def forward_batch(self, rows) -> np.ndarray:
+        """The logits of the token after the last row."""
+        out = self.stack.logits(self.backend, rows, self.pos, self.live)
+        self.batch = len(rows)
+        self.accept(len(rows))
+        return out[-1]
+
+
+class OracleBackend:
+    """The oracle's restatement, with f32 caches and ring states it owns."""
+
+    def __init__(self, stack: ToyStack, context: int, slots: int = 1):
         self.cfg = orc.qwen35_config(context)
         self.stack = stack
+        self.slots = slots
         self.kv = [np.zeros((2, N_KV, context, HD), np.float32) for _ in range(N_LAYERS // 4)]
         n_lin = N_LAYERS - N_LAYERS // 4
-        self.conv = [np.zeros((1, CONV_DIM, 3), np.float32) for _ in range(n_lin)]
-        self.ssm = [np.zeros((N_V, 1, S, S), np.float32) for _ in range(n_lin)]
+        self.conv = [np.zeros((slots, CONV_DIM, 3), np.float32) for _ in range(n_lin)]
+        self.ssm = [np.zeros((N_V, slots, S, S), np.float32) for _ in range(n_lin)]
         self.full_w = [lw for il, lw in enumerate(stack.layers) if is_full(il)]
         self.lin_w = [lw for il, lw in enumerate(stack.layers) if not is_full(il)]
 
@@ -103,9 +151,9 @@ class OracleBackend:
         return orc.full_attn(self.cfg, pos, qg, k, v, self.kv[layer], w["q_norm"], w["k_norm"],
                              threads=8)
 
-    def linear(self, layer, qkv, z, alpha, beta):
+    def linear(self, layer, live, qkv, z, alpha, beta):
         w = self.lin_w[layer]
-        return orc.linear_attn(self.cfg, 1, 0, qkv, z, alpha, beta, self.conv[layer],
+        return orc.linear_attn(self.cfg, self.slots, live, qkv, z, alpha, beta, self.conv[layer],
                                self.ssm[layer], w["conv1d"], w["ssm_a"], w["dt_bias"], w["norm"],
                                threads=8)
 
@@ -113,11 +161,13 @@ class OracleBackend:
 class DeviceBackend:
     """The sm_100a library through rl_full_attn_host / rl_linear_attn_host."""
 
-    def __init__(self, stack: ToyStack, context: int, max_batch: int, kv_dtype=None):
+    def __init__(self, stack: ToyStack, context: int, max_batch: int, kv_dtype=None,
+                 slots: int = 1):
         import rlcuda
         kv_dtype = rlcuda.RL_KV_F32 if kv_dtype is None else kv_dtype
+        self.slots = slots
         cfg = rlcuda.qwen35_config(n_full=N_LAYERS // 4, n_linear=N_LAYERS - N_LAYERS // 4,
-                                   context=context, slots=1, kv_dtype=kv_dtype,
+                                   context=context, slots=slots, kv_dtype=kv_dtype,
                                    max_batch=max_batch)
         self.ctx = rlcuda.Context(cfg)
         fi = li = 0
@@ -133,8 +183,12 @@ class DeviceBackend:
     def full(self, layer, pos, qg, k, v):
         return self.ctx.full_attn_host(layer, pos, qg, k, v)
 
-    def linear(self, layer, qkv, z, alpha, beta):
-        return self.ctx.linear_attn_host(layer, 0, qkv, z, alpha, beta)
+    def linear(self, layer, live, qkv, z, alpha, beta):
+        return self.ctx.linear_attn_host(layer, live, qkv, z, alpha, beta)
+
+    def accept(self, rows):
+        # the context's own pos / live follow the runner's (rl_accept)
+        self.ctx.accept(rows)
 
     def close(self):
         self.ctx.close()

@@ -61,3 +61,29 @@ def test_unsupported_shapes_are_refused_before_any_device_work():
     with pytest.raises(rlcuda.RlError) as e:
         rlcuda.Context(cfg)
     assert e.value.code == rlcuda.RL_EINVAL
+
+
+def test_noalloc_refuses_misaligned_or_bad_arguments_before_any_launch():
+    """rl_full_attn_noalloc checks its arguments before it touches the
+    device, so these run without a GPU: the pointers are never dereferenced."""
+    import ctypes
+    L = rlcuda.lib()
+    cfg = rlcuda.qwen35_config(n_full=1, n_linear=0, context=1024, kv_dtype=rlcuda.RL_KV_BF16,
+                               max_batch=1)
+    good = 0x10000
+
+    def call(cfg=cfg, **over):
+        p = dict(k_cache=good, v_cache=good, q_norm=good, k_norm=good, qg=good, k=good, v=good,
+                 out=good)
+        p.update(over)
+        return L.rl_full_attn_noalloc(ctypes.byref(cfg), None, p["k_cache"], p["v_cache"],
+                                      p["q_norm"], p["k_norm"], 10, 1, p["qg"], p["k"], p["v"],
+                                      p["out"])
+
+    for name in ("k_cache", "v_cache", "q_norm", "k_norm", "qg", "k", "v", "out"):
+        assert call(**{name: good + 8}) == rlcuda.RL_EINVAL, name
+        assert name.encode() in L.rl_last_error(None), name
+    bad = rlcuda.qwen35_config(n_full=1, n_linear=0, context=1024, kv_dtype=rlcuda.RL_KV_BF16)
+    bad.n_rot = 8
+    assert call(cfg=bad) == rlcuda.RL_EINVAL
+    assert b"multiple of 16" in L.rl_last_error(None)

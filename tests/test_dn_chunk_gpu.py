@@ -40,8 +40,11 @@ def run_chunked(t, seed, unit_norm=True):
     return got, want, conv_got, conv_w, ssm_got, ssm_w, chunk_launches
 
 
-@pytest.mark.parametrize("t", [64, 100, 257, 1024])
+@pytest.mark.parametrize("t", [64, 100, 257, 1024, 4096])
 def test_chunked_prefill_matches_the_token_sequential_oracle(t):
+    """t = 4096 is the benchmarked config-2 DeltaNet layer: the state is
+    carried through 64 chunks, where the bf16-pair products' error would
+    grow if it were going to."""
     got, want, conv_got, conv_w, ssm_got, ssm_w, n = run_chunked(t, 900 + t)
     assert n == 1, "the call did not take the chunked kernels"
     assert np.isfinite(got).all()

@@ -65,12 +65,21 @@ def test_rows_match_the_oracle(pos, t):
     assert cases.rel_err_per_head(got, want, cases.HD) <= TOL
 
 
-@pytest.mark.parametrize("pos", [4095, 5000])
+@pytest.mark.parametrize("pos", [4095, 5000, 32767])
 def test_decode_bf16_cache(pos):
+    """pos 32767 over a 32768-entry cache is the benchmarked decode (the
+    metric's workload): the fused single-launch walk with its atomic tile
+    dealing over 37+ tiles per split."""
     case = cases.full_case(20, pos, 1, kv_bf16=True)
-    want, _ = cases.oracle_full(case, pos + 1, kv_bf16=True)
+    want, kv_want = cases.oracle_full(case, pos + 1, kv_bf16=True)
     with make_ctx(pos + 1, rlcuda.RL_KV_BF16) as ctx:
-        assert cases.rel_err_per_head(run_case(ctx, case), want, cases.HD) <= TOL
+        ctx.profile_reset()
+        got = run_case(ctx, case)
+        prof = ctx.profile_read()
+        assert prof["decode"][1] == 1 and prof["prologue"][1] == 0, prof
+        assert cases.rel_err_per_head(got, want, cases.HD) <= TOL
+        row = ctx.read_kv(0, pos, 1)
+        assert cases.rel_err_per_head(row, kv_want[:, :, pos:pos + 1], cases.HD) <= 1e-6
 
 
 def test_speculative_verify_rows_bf16():

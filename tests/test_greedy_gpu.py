@@ -29,3 +29,31 @@ def test_greedy_tokens_identical(seed):
     assert got == want, (got, want)
     # a sanity check on the harness itself: the stack does not emit one token
     assert len(set(want)) > 3, want
+
+
+def test_speculative_verify_and_accept_give_the_sequential_tokens():
+    """The speculative side of the greedy check (tests/speculate.rs:49-60 and
+    on, forward.rs:641-688): on the device, a verify batch of DRAFT + 1 rows
+    over a ring of DRAFT + 1 DeltaNet slots, then accept(k) up to the first
+    wrong draft (a rollback of the rest, by pointer), then single rows.  The
+    batch's rows predict the oracle's sequential tokens, their logits agree
+    with the single passes' to 1e-4, and the tokens after the rollback are
+    those of an oracle runner that only ever saw the k rows."""
+    import numpy as np
+    import test_greedy_harness as th
+    stack = gh.ToyStack(5)
+    ctx = 64
+    rows, want, tails = th.sequential_reference(stack,
+                                                lambda s: gh.OracleBackend(stack, ctx, s))
+    for what, batch in th.spec_batches(rows):
+        dev = gh.DeviceBackend(stack, ctx, max_batch=len(th.SPEC_PROMPT), slots=th.DRAFT + 1)
+        try:
+            logits, accepted, got = th.speculative_run(stack, dev, batch, rows)
+            assert dev.ctx.pos == len(th.SPEC_PROMPT) + accepted + 1 + 4
+        finally:
+            dev.close()
+        for r in range(accepted + 1):
+            assert int(np.argmax(logits[r])) == int(np.argmax(want[r])), (what, r)
+            err = np.abs(logits[r] - want[r]).max() / np.abs(want[r]).max()
+            assert err <= 1e-4, (what, r, err)
+        assert got == tails[accepted], (what, got, tails[accepted])

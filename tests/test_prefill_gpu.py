@@ -36,10 +36,11 @@ def run_prefill(case, context, max_batch):
 
 
 @pytest.mark.parametrize("pos,t", [(0, 64), (0, 128), (0, 200), (37, 131), (500, 256),
-                                   (0, 1024), (1000, 640)])
+                                   (0, 1024), (1000, 640), (0, 4096)])
 def test_prefill_matches_the_oracle(pos, t):
     """Query tiles of 128 rows and key tiles of 64: ragged last tiles on both
-    sides, a prefix already in the cache (pos > 0) and the causal diagonal."""
+    sides, a prefix already in the cache (pos > 0) and the causal diagonal.
+    (0, 4096) is the benchmarked config-2 prefill of a full-attention layer."""
     case = cases.full_case(300 + pos + t, pos, t, kv_bf16=True)
     context = pos + t + 5
     want, kv_want = cases.oracle_full(case, context, kv_bf16=True)

@@ -35,13 +35,17 @@ def _bind():
     return fn
 
 
+@pytest.mark.parametrize("t", [1, 4])
 @pytest.mark.parametrize("kv_dtype", [rlcuda.RL_KV_BF16, rlcuda.RL_KV_F32])
-def test_noalloc_matches_the_context_entry_point_on_two_steps(kv_dtype):
+def test_noalloc_matches_the_context_entry_point_on_two_steps(kv_dtype, t):
+    """t = 1 is a decode step; t = 4 is a batch whose rows see each other's
+    appended keys (the context runs it on the exact split-KV walk, with the
+    tensor-core verify kernel switched off)."""
     import torch
     fn = _bind()
     context, pos0 = 3000, 2900
     cfg = rlcuda.qwen35_config(n_full=1, n_linear=0, context=context, kv_dtype=kv_dtype,
-                               max_batch=1)
+                               max_batch=t)
     r = orc.Rng(2024)
     cache = r.normal((2, 4, pos0, 256))
     q_norm = r.normal(256, 1.0, 0.2)
@@ -58,29 +62,32 @@ def test_noalloc_matches_the_context_entry_point_on_two_steps(kv_dtype):
     kn = torch.from_numpy(k_norm).to(dev)
     stream = torch.cuda.current_stream(dev)
     with rlcuda.Context(cfg) as ctx:
+        ctx.set_option(rlcuda.RL_OPT_VERIFY_TC, 0)
         ctx.write_kv(0, 0, cache)
         ctx.set_weights_full(0, q_norm, k_norm)
         for step in range(2):  # two calls in a row share the static scratch
-            pos = pos0 + step
-            qg = r.normal((1, 16 * 512))
-            k = r.normal((1, 4 * 256))
-            v = r.normal((1, 4 * 256))
+            pos = pos0 + step * t
+            qg = r.normal((t, 16 * 512))
+            k = r.normal((t, 4 * 256))
+            v = r.normal((t, 4 * 256))
             want = ctx.full_attn_host(0, pos, qg, k, v)
             d_qg, d_k, d_v = (torch.from_numpy(x).to(dev) for x in (qg, k, v))
-            out = torch.full((1, 16 * 256), float("nan"), device=dev)
+            out = torch.full((t, 16 * 256), float("nan"), device=dev)
             code = fn(ctypes.byref(cfg), stream.cuda_stream, k_cache.data_ptr(),
-                      v_cache.data_ptr(), qn.data_ptr(), kn.data_ptr(), pos, 1,
+                      v_cache.data_ptr(), qn.data_ptr(), kn.data_ptr(), pos, t,
                       d_qg.data_ptr(), d_k.data_ptr(), d_v.data_ptr(), out.data_ptr())
             assert code == 0, rlcuda.lib().rl_last_error(None).decode()
             torch.cuda.synchronize()
             got = out.cpu().numpy()
             err = cases.rel_err_per_head(got, want, 256)
             assert err <= TOL, (step, err)
-            # the appended row landed in the caller's cache, as in the context's
-            row = ctx.read_kv(0, pos, 1)
-            mine = np.stack([k_cache[:, pos:pos + 1].float().cpu().numpy(),
-                             v_cache[:, pos:pos + 1].float().cpu().numpy()])
-            assert np.array_equal(row, mine), step
+            # the appended rows landed in the caller's cache, as in the context's
+            rows = ctx.read_kv(0, pos, t)
+            mine = np.stack([k_cache[:, pos:pos + t].float().cpu().numpy(),
+                             v_cache[:, pos:pos + t].float().cpu().numpy()])
+            assert np.array_equal(rows, mine), step
+        # no kernel of these calls gave up a bounded wait
+        assert rlcuda.lib().rl_noalloc_status(stream.cuda_stream) == 0
 
 
 def test_noalloc_refuses_a_call_whose_scratch_does_not_fit():
