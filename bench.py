@@ -12,9 +12,14 @@ layer has its own 128 MiB cache, so a step streams 1 GiB, eight times the
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun, one process per GPU; each GPU decodes its own
-sequence (sequence-partitioned decode, no collective), so per-GPU work is
-fixed as N grows ("scaling": "weak") and `value` aggregates over all GPUs.
+N > 1 runs under torchrun, one process per GPU.  The step is then one
+sequence of N x 32768 positions split along the sequence, 32768 per GPU (the
+same cache bytes per GPU as N = 1, so "scaling": "weak"): per layer every GPU
+walks its range, pushes its partial (max, sum, output; 16,512 B) into every
+GPU's exchange buffer over NVLink peer memory and merges the N partials.
+`value` is the latency of one layer of that sequence, the max over ranks.
+Config 4a proper (131072 positions split over the N GPUs, strong scaling) and
+4b (64 sequences dealt over the GPUs, no collective) are sections of the line.
 
 `--impl reference` times the reference's CPU implementation of the path (the
 C++ restatement in oracle/, all host threads, f32 cache) on the same workload
@@ -72,61 +77,98 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons during the timed region."""
+    """SM clocks, power and clock-event reasons of one GPU, read through NVML
+    (read-only queries) every `period_s` on a background thread, from before
+    the warm-up until after the timed region, plus one read right before and
+    one right after the timed region (`mark`)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
-
-    def __enter__(self):
+    def __init__(self, torch_device, period_s: float = 0.01):
+        self.period = period_s
+        self.samples = []  # (t, sm_mhz, reasons bitmask, power W)
+        self.marks = {}
+        self.handle = None
+        self.max_mhz = None
+        self._stop = threading.Event()
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(torch_device)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+            except Exception:
+                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id,
+                                             props.pci_device_id)
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.nvml = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle,
+                                                                  pynvml.NVML_CLOCK_SM))
         except Exception:
-            self.proc = None
-        return self
+            self.handle = None
 
     def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        n = self.nvml
+        sm = float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+        try:
+            reasons = int(n.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+        except Exception:
+            reasons = int(n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle))
+        try:
+            pw = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+        except Exception:
+            pw = None
+        return (time.perf_counter(), sm, reasons, pw)
 
-    def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
+    def _loop(self):
+        while not self._stop.is_set():
             try:
-                self.proc.wait(timeout=5)
+                self.samples.append(self._read())
             except Exception:
-                self.proc.kill()
+                pass
+            self._stop.wait(self.period)
+
+    def start(self):
+        if self.handle is not None:
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
+        return self
+
+    def mark(self, name):
+        if self.handle is not None:
+            try:
+                r = self._read()
+                self.samples.append(r)
+                self.marks[name] = r
+            except Exception:
+                pass
+
+    def stop(self):
+        self._stop.set()
+        if self.handle is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.handle is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": "nvml unavailable"}
+        t0 = self.marks.get("timed_start", self.samples[0])[0]
+        t1 = self.marks.get("timed_end", self.samples[-1])[0]
+        timed = [x for x in self.samples if t0 <= x[0] <= t1]
+        window = timed if len(timed) >= 3 else self.samples
+        sm = sorted(x[1] for x in window)
+        reasons = sorted({name for x in window for name, bit in self.REASONS if x[2] & bit})
+        pw = [x[3] for x in window if x[3] is not None]
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(window), "samples_timed_region": len(timed),
+                "samples_total": len(self.samples),
+                "window": "timed region" if window is timed else "warm-up through timed region",
+                "sm_mhz_min": sm[0], "power_w_max": max(pw) if pw else None,
+                "sm_mhz_at_timed_start": self.marks.get("timed_start", (0, None))[1],
+                "sm_mhz_at_timed_end": self.marks.get("timed_end", (0, None))[1],
+                "period_ms": self.period * 1e3, "source": "NVML, read-only queries"}
 
 
 def dist_setup():
@@ -252,6 +294,26 @@ def dn_step_bench(args, dev, stream, rlcuda, torch):
     ctx.profile(False)
     ms, n = prof["dn_step"]
     graph.reset()
+    # end to end through the host entry point (rl_linear_attn_host): every
+    # layer's inputs from pinned host memory and its output back, host clock
+    h_qkv = torch.empty((DN_LAYERS, 1, 8192), pin_memory=True)
+    h_z = torch.empty((DN_LAYERS, 1, 4096), pin_memory=True)
+    h_al = torch.empty((DN_LAYERS, 1, 32), pin_memory=True)
+    h_be = torch.empty((DN_LAYERS, 1, 32), pin_memory=True)
+    h_qkv.copy_(qkv.cpu().view(DN_LAYERS, 1, -1))
+    h_z.copy_(z.cpu().view(DN_LAYERS, 1, -1))
+    h_al.copy_(al.cpu().view(DN_LAYERS, 1, -1))
+    h_be.copy_(be.cpu().view(DN_LAYERS, 1, -1))
+    nq, nz, na, nb = h_qkv.numpy(), h_z.numpy(), h_al.numpy(), h_be.numpy()
+    for layer in range(DN_LAYERS):  # warm
+        ctx.linear_attn_host(layer, 0, nq[layer], nz[layer], na[layer], nb[layer])
+    e2e_steps = max(3, min(args.steps // 50, 50))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for layer in range(DN_LAYERS):
+            last = ctx.linear_attn_host(layer, 0, nq[layer], nz[layer], na[layer], nb[layer])
+    e2e_us = (time.perf_counter() - t0) * 1e6 / (e2e_steps * DN_LAYERS)
+    assert np.isfinite(last).all()
     ctx.close()
     peak, _ = peaks()
     gbs = DN_BYTES_PER_LAYER / (us * 1e-6) / 1e9
@@ -259,7 +321,11 @@ def dn_step_bench(args, dev, stream, rlcuda, torch):
             "us_per_layer": us, "bytes_per_layer": DN_BYTES_PER_LAYER, "gbs": gbs,
             "frac_of_measured_hbm": gbs / peak, "frac_of_8tbs": gbs / 8000.0,
             "avg_launch_us_alone": ms * 1e3 / max(n, 1),
-            "l2": "72 x 2 MiB of state per step, more than the 126 MB L2"}
+            "l2": "72 x 2 MiB of state per step, more than the 126 MB L2",
+            "e2e": {"value": e2e_us, "unit": "us/layer",
+                    "h2d_bytes_per_layer": 4 * (8192 + 4096 + 64),
+                    "d2h_bytes_per_layer": 4 * 4096,
+                    "how": "rl_linear_attn_host per layer, pinned host buffers, host clock"}}
 
 
 PF_T = 4096
@@ -292,7 +358,7 @@ def prefill_bench(args, dev, stream, rlcuda, torch):
             step()
     stream.synchronize()
     ctx.sync()
-    steps = max(3, min(args.steps // 100, 20))
+    steps = max(10, min(args.steps // 100, 20))
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -461,6 +527,81 @@ def verify_bench(args, dev, stream, rlcuda, torch):
                            "split over the key sequence) + decode_combine_kernel",
             "dn_us_per_layer": d_us, "dn_gbs": VERIFY_DN_BYTES / (d_us * 1e-6) / 1e9,
             "pass_us": a_us * N_LAYERS + d_us * 24}
+
+
+PROJ_FULL = ((8192, 2560), (1024, 2560), (1024, 2560), (2560, 4096))   # (rows, k): qg, k, v, o
+PROJ_DN = ((8192, 2560), (4096, 2560), (32, 2560), (32, 2560), (2560, 4096))  # qkv, z, a, b, out
+
+
+def proj_bench(args, dev, stream, rlcuda, torch):
+    """The projections either side of the attention spans for one decode token
+    through the 32-layer stack (8 full-attention layers: qg, k, v, o; 24
+    DeltaNet layers: qkv, z, alpha, beta, out), Q4_K weights (GGUF blocks,
+    distinct per layer: 734 MB, more than L2), int8 activations quantized per
+    product group as Exec::matmul_group does.  CUDA-graph captured; returns µs
+    per layer and the HBM rate of the weight bytes."""
+    cfg = rlcuda.qwen35_config(n_full=1, n_linear=0, context=64, max_batch=1)
+    ctx = rlcuda.Context(cfg, device=dev.index)
+    ctx.set_stream(stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    row_bytes = lambda k: (k + 255) // 256 * 144
+
+    def weight(rows, k):
+        w = torch.randint(0, 256, (rows * (k // 256), 144), generator=gen, device=dev,
+                          dtype=torch.uint8)
+        w[:, 0:4] = torch.tensor([0x00, 0x20, 0x00, 0x1c], dtype=torch.uint8, device=dev)  # d, dmin
+        return w
+    layers = [("full", [weight(r, k) for r, k in PROJ_FULL]) for _ in range(N_LAYERS)] + \
+             [("dn", [weight(r, k) for r, k in PROJ_DN]) for _ in range(24)]
+    wbytes = sum(w.numel() for _, ws in layers for w in ws)
+    x_in = torch.randn((1, 2560), generator=gen, device=dev)
+    x_heads = torch.randn((1, 4096), generator=gen, device=dev)
+    outs = {rows: torch.empty((1, rows), device=dev) for rows in (8192, 4096, 2560, 1024, 32)}
+
+    def step():
+        # per layer Exec::matmul_group's two groups: the in-projections of the
+        # normed input, one launch, and the out-projection of the heads
+        for kind, ws in layers:
+            shapes = PROJ_FULL if kind == "full" else PROJ_DN
+            ctx.act_quantize(x_in, 1, 2560)
+            ctx.matvec_group([(12, w, rows, outs[rows]) for (rows, _), w in
+                              zip(shapes[:-1], ws[:-1])])
+            ctx.act_quantize(x_heads, 1, 4096)
+            ctx.matvec(12, ws[-1], shapes[-1][0], outs[shapes[-1][0]])
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    ctx.sync()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    reps = max(10, min(args.steps // 10, 100))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ctx.sync()
+    step_us = e0.elapsed_time(e1) * 1e3 / reps
+    graph.reset()
+    ctx.close()
+    peak, _ = peaks()
+    gbs = wbytes / (step_us * 1e-6) / 1e9
+    n_layers = len(layers)
+    return {"workload": "decode projections of the 32-layer stack (8 full: qg, k, v, o; 24 "
+                        "DeltaNet: qkv, z, alpha, beta, out), Q4_K weights, t = 1",
+            "us_per_token": step_us, "us_per_layer": step_us / n_layers,
+            "weight_bytes_per_token": wbytes, "gbs": gbs, "frac_of_measured_hbm": gbs / peak,
+            "launches_per_token": n_layers * 4,
+            "arith": "int8 activations per 256-value block, integer block dots (dp4a), f32 "
+                     "block scales in the reference's order (bit-identical to its scalar tier)"}
 
 
 SPLIT_SEQ = 131072
@@ -656,12 +797,21 @@ def batch_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
             "per_sequence_hbm_gbs_aggregate": total / (us_each * 1e-6) / 1e9}
 
 
+def max_over_ranks(x, world, dev, torch, dist):
+    if world == 1:
+        return float(x)
+    t = torch.tensor([float(x)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_ours(args):
     import numpy as np
     import torch
     import torch.distributed as dist
 
     import rlcuda
+    import split_kv
 
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
@@ -670,9 +820,22 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
+    clocks = ClockSampler(dev).start()  # through warm-up and the timed region
+
+    # N = 1: one sequence at 32k.  N > 1: one sequence of N x 32k positions,
+    # each GPU holding a contiguous 32k of it (the same cache bytes per GPU
+    # as N = 1, so "weak" scaling), its partial merged over NVLink peer memory
+    # every layer; `value` is still the latency of one layer of the sequence.
+    seq = CTX * world
+    lo, n = split_kv.shard_range(seq, world, rank)
+    assert n == CTX
     cfg = rlcuda.qwen35_config(n_full=N_LAYERS, n_linear=0, context=CTX,
                                kv_dtype=rlcuda.RL_KV_BF16, max_batch=1)
     ctx = rlcuda.Context(cfg, device=local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream.cuda_stream)
+    if world > 1:
+        split_kv.GpuShard(ctx, lo, seq, exchange=True, rank=rank, world=world)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     for layer in range(N_LAYERS):
@@ -680,117 +843,141 @@ def run_ours(args):
         ctx.write_kv(layer, 0, src)
         del src
     torch.cuda.empty_cache()
+    gen.manual_seed(1234)  # the row's inputs: the same on every GPU of the sequence
     qg = torch.randn((N_LAYERS, 1, N_HEAD * 2 * HD), generator=gen, device=dev)
     kk = torch.randn((N_LAYERS, 1, N_KV * HD), generator=gen, device=dev)
     vv = torch.randn((N_LAYERS, 1, N_KV * HD), generator=gen, device=dev)
     out = torch.empty((N_LAYERS, 1, N_HEAD * HD), device=dev)
-    pos = CTX - 1
-
-    stream = torch.cuda.Stream(device=dev)
-    ctx.set_stream(stream.cuda_stream)
+    pos = seq - 1
 
     def step():
         for layer in range(N_LAYERS):
-            ctx.full_attn(layer, pos, 1, qg[layer], kk[layer], vv[layer], out[layer])
-
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        step()
-    stream.synchronize()
-    ctx.sync()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    # replays run on the current stream: keep it the library's stream, which
-    # the timing events below are recorded on
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            graph.replay()
-    stream.synchronize()
+            if world == 1:
+                ctx.full_attn(layer, pos, 1, qg[layer], kk[layer], vv[layer], out[layer])
+            else:
+                ctx.full_attn_split(layer, pos, qg[layer], kk[layer], vv[layer], out[layer])
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
+    def capture():
+        barrier()
+        with torch.cuda.stream(stream):
+            step()
+        stream.synchronize()
+        ctx.sync()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        return g
+
+    def replay(g, n):
+        # replays run on the current stream: keep it the library's stream,
+        # which the timing events are recorded on
+        with torch.cuda.stream(stream):
+            for _ in range(n):
+                g.replay()
+
+    graph = capture()
+    replay(graph, args.warmup)
+    stream.synchronize()
+
     # ---- timed region: K graph replays of the 8-layer decode step
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks, torch.cuda.stream(stream):
+    clocks.mark("timed_start")
+    with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(args.steps):
             graph.replay()
         e1.record(stream)
-        stream.synchronize()
+    stream.synchronize()
+    clocks.mark("timed_end")
     barrier()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev, torch, dist)
     ctx.sync()
-    launches = args.steps * N_LAYERS * 2  # walk + merge per layer and token
-    layer_decodes = args.steps * N_LAYERS * world
-    us_per_layer = ms * 1e3 / layer_decodes
-    hbm_gbs = layer_decodes * KV_BYTES_PER_LAYER / (ms / 1e3) / 1e9
+    graph.reset()
+    kernels_per_layer = 2 if world == 1 else 3  # walk + merge (+ peer merge)
+    launches = args.steps * N_LAYERS * kernels_per_layer
+    us_per_layer = ms * 1e3 / (args.steps * N_LAYERS)
+    hbm_gbs = world * KV_BYTES_PER_LAYER / (us_per_layer * 1e-6) / 1e9
 
-    # ---- the dominant kernel alone: CUDA events around each decode launch on
-    # the library's stream, same workload, no graph
-    # A sleep kernel first backs up the stream, so each event pair brackets
-    # the kernel alone and not the host's launch latency.
-    prof_steps = min(args.steps, 300)
+    # ---- the walk kernel inside the same graph-timed, programmatically
+    # overlapped step: each launch stamps its first CTA's start and its last
+    # CTA's end on the GPU's global timer (no events, so the overlap stays)
+    ctx.set_option(rlcuda.RL_OPT_WALK_SPANS, 1)
+    graph = capture()
+    replay(graph, args.warmup)
+    stream.synchronize()
     ctx.profile_reset()
-    ctx.profile(True)
+    span_steps = max(args.steps, 20)
+    barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        for b in range(0, prof_steps, 10):
-            torch.cuda._sleep(20_000_000)
-            for _ in range(min(10, prof_steps - b)):
-                step()
-    prof = ctx.profile_read()
-    ctx.profile(False)
-    dec_ms, dec_n = prof["decode"]
-    avg_us = dec_ms * 1e3 / max(dec_n, 1)
+        e2.record(stream)
+        replay(graph, span_steps)
+        e3.record(stream)
+    stream.synchronize()
+    span_ms, span_n = ctx.profile_read()["walk_span"]
+    span_step_us = max_over_ranks(e2.elapsed_time(e3) * 1e3 / (span_steps * N_LAYERS), world,
+                                  dev, torch, dist)
+    avg_us = max_over_ranks(span_ms * 1e3 / max(span_n, 1), world, dev, torch, dist)
+    graph.reset()
+    ctx.set_option(rlcuda.RL_OPT_WALK_SPANS, 0)
     achieved = KV_BYTES_PER_LAYER / (avg_us * 1e-6) / 1e9
     peak, peak_kind = peaks()
-    shares = {k: round(v[0] / max(sum(x[0] for x in prof.values()), 1e-9), 4)
-              for k, v in prof.items() if v[1]}
+    assert avg_us <= span_step_us * 1.001, (avg_us, span_step_us)
 
-    # ---- end to end through the host entry point: pinned host inputs copied
-    # in and the result copied out inside the timed region, every layer
+    # ---- end to end through the public API with host buffers, on a host
+    # clock: per layer the row's inputs go in from pinned host memory and its
+    # output comes back (a caller needs it before the layer's projection)
     h_qg = torch.empty((N_LAYERS, 1, N_HEAD * 2 * HD), pin_memory=True)
     h_k = torch.empty((N_LAYERS, 1, N_KV * HD), pin_memory=True)
     h_v = torch.empty((N_LAYERS, 1, N_KV * HD), pin_memory=True)
+    h_out = torch.empty((N_LAYERS, 1, N_HEAD * HD), pin_memory=True)
     h_qg.copy_(qg.cpu())
     h_k.copy_(kk.cpu())
     h_v.copy_(vv.cpu())
     n_qg, n_k, n_v = h_qg.numpy(), h_k.numpy(), h_v.numpy()
+
+    def e2e_layer(layer):
+        if world == 1:
+            return ctx.full_attn_host(layer, pos, n_qg[layer], n_k[layer], n_v[layer])
+        with torch.cuda.stream(stream):
+            qg[layer].copy_(h_qg[layer], non_blocking=True)
+            kk[layer].copy_(h_k[layer], non_blocking=True)
+            vv[layer].copy_(h_v[layer], non_blocking=True)
+            ctx.full_attn_split(layer, pos, qg[layer], kk[layer], vv[layer], out[layer])
+            h_out[layer].copy_(out[layer], non_blocking=True)
+        stream.synchronize()
+        return h_out[layer].numpy()
+
     e2e_steps = max(3, min(args.steps // 10, 500))
     for layer in range(N_LAYERS):  # warm
-        ctx.full_attn_host(layer, pos, n_qg[layer], n_k[layer], n_v[layer])
+        e2e_layer(layer)
     barrier()
-    e2 = torch.cuda.Event(enable_timing=True)
-    e3 = torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
+    t0 = time.perf_counter()
     last = None
     for _ in range(e2e_steps):
         for layer in range(N_LAYERS):
-            last = ctx.full_attn_host(layer, pos, n_qg[layer], n_k[layer], n_v[layer])
-    e3.record(stream)
-    stream.synchronize()
-    e2e_ms = e2.elapsed_time(e3)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+            last = e2e_layer(layer)
+    t1 = time.perf_counter()
+    e2e_us = max_over_ranks((t1 - t0) * 1e6 / (e2e_steps * N_LAYERS), world, dev, torch, dist)
     assert last is not None and np.isfinite(last).all()
-    e2e_us = e2e_ms * 1e3 / (e2e_steps * N_LAYERS * world)
+    ctx.sync()
     h2d = N_LAYERS * 4 * (N_HEAD * 2 * HD + 2 * N_KV * HD)
     d2h = N_LAYERS * 4 * N_HEAD * HD
+    ctx.close()
+    clocks.stop()
 
     split = (split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist)
              if not args.no_split else None)
     dn = dn_step_bench(args, dev, stream, rlcuda, torch) if not args.no_dn else None
+    proj = proj_bench(args, dev, stream, rlcuda, torch) if not args.no_proj else None
     pf = prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_prefill else None
     dnpf = dn_prefill_bench(args, dev, stream, rlcuda, torch) if not args.no_dn_prefill else None
     ver = verify_bench(args, dev, stream, rlcuda, torch) if not args.no_verify else None
@@ -806,43 +993,56 @@ def run_ours(args):
                          f"C++ restatement of forward.rs, {threads} threads"}
 
     traffic = ncu_traffic()
+    if world == 1:
+        parallelism = "one GPU, one sequence"
+        workload = "decode32k"
+    else:
+        parallelism = (f"sequence split x{world}: one sequence of {seq} positions, {CTX} per "
+                       "GPU; per layer each GPU walks its range and pushes its partial "
+                       "(16,512 B) to every GPU over NVLink peer memory, every GPU merges")
+        workload = f"decode32k per GPU, one {seq}-position sequence"
     line = {
         "metric": METRIC, "value": us_per_layer, "unit": "us/layer", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic N(0,1) KV/q/k/v/gate, torch.Generator seed 1234+rank",
-        "config": {"workload": "decode32k", "context": CTX, "layers": N_LAYERS,
-                   "heads": [N_HEAD, N_KV, HD], "kv_dtype": "bf16", "rows": 1,
-                   "parallelism": f"sequence-partitioned x{world}, no collective",
-                   "l2": "inputs larger than L2: 8 layers x 128 MiB KV per step",
-                   "launch": "CUDA graph of the 8-layer step"},
+        "data": "synthetic N(0,1) KV (torch.Generator seed 1234+rank) and q/k/v/gate (seed 1234)",
+        "config": {"workload": workload, "context_per_gpu": CTX, "sequence": seq,
+                   "layers": N_LAYERS, "heads": [N_HEAD, N_KV, HD], "kv_dtype": "bf16",
+                   "rows": 1, "parallelism": parallelism,
+                   "l2": "inputs larger than L2: 8 layers x 128 MiB KV per GPU per step",
+                   "launch": "CUDA graph of the 8-layer step, programmatic launch overlap"},
         "hbm_gbs": hbm_gbs,
-        "hbm_frac_of_8tbs": hbm_gbs / 8000.0,
+        "hbm_frac_of_8tbs": hbm_gbs / 8000.0 / world,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "decode_mma_kernel<fused> (split-KV walk)",
+                     "peak_source": peak_kind, "avg_launch_us": avg_us,
+                     "avg_launch_from": "global-timer span of every walk launch (first CTA "
+                                        "start to last CTA end) inside the graph-timed step",
+                     "span_step_us_per_layer": span_step_us,
+                     "walk_share_of_layer": avg_us / span_step_us},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "how": "host clock around every layer's pinned copy in, the call and the copy "
+                       "of its output back"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
         "prefill_tflops": pf["tflops_layer"] if pf else None,
         "prefill": pf,
         "dn_prefill": dnpf,
         "verify": ver,
         "config2_attention_ms": ((pf["us_per_layer"] * PF_LAYERS + dnpf["us_per_layer"] *
                                   DN_PF_LAYERS) / 1e3 if pf and dnpf else None),
-        "split_kv": split,
-        "batch_4b": batch,
         "dn_step": dn,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "decode_mma_kernel<fused> (split-KV walk)",
-                     "peak_source": peak_kind,
-                     "avg_launch_us": avg_us, "launch_share": shares},
-        "cpu_baseline": cpu,
-        "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches,
-        "clocks": clocks.summary(),
+        "projections": proj,
+        "batch_4b": batch,
+        "split_kv": split,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    graph.reset()
-    ctx.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 
@@ -864,6 +1064,8 @@ def main():
                     help="skip the config-4b batched multi-sequence section")
     ap.add_argument("--no-split", action="store_true",
                     help="skip the long-context split-sequence section")
+    ap.add_argument("--no-proj", action="store_true",
+                    help="skip the projections (k-quant matvec) section")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="full-attention layers per step (8 in the model; fewer only to "
                          "keep a profiler capture small)")

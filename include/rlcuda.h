@@ -228,9 +228,12 @@ typedef enum {
                                  (0, the default: one second).  A wait that gives up
                                  makes the next rl_sync return RL_ETIMEOUT; the
                                  context stays usable. */
-    RL_OPT_WALK_SPANS = 8     /* 1: every bf16 decode walk records its span on the
+    RL_OPT_WALK_SPANS = 8,    /* 1: every bf16 decode walk records its span on the
                                  global timer (RL_PROF_WALK_SPAN); 0 (default): off.
                                  Costs two atomics per CTA. */
+    RL_OPT_DN_SCAN_TC = 9     /* 1 (default): the chunked DeltaNet prefill walks its
+                                 chunks with the tcgen05 scan (one CTA per value head,
+                                 the state in tensor memory); 0: the mma.sync scan */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);
@@ -273,6 +276,26 @@ typedef enum {
 int rl_profile_enable(rl_ctx *ctx, int on);
 int rl_profile_read(rl_ctx *ctx, int kernel, double *total_ms, int64_t *launches);
 int rl_profile_reset(rl_ctx *ctx);
+
+/* ---- projections -------------------------------------------------------
+ * The matmuls either side of the attention spans (forward.rs:1250, :1342,
+ * :1517, :1656 through Exec::matmul_group, :1157-1180), on the device, in the
+ * reference's arithmetic: rl_act_quantize is Activations::quantize_batch
+ * (crates/llm-core/src/quant.rs:337-372): t rows of k f32 activations
+ * (device, [t][k]) to int8 per 256-value super-block; rl_matvec is one weight
+ * of the group (Pool::matvec_group, pool.rs:289-342, with the scalar dots of
+ * crates/llm-core/src/kernels/mod.rs:245-320): out [t][rows] (device) = W . x
+ * for W (device) of GGML type 12 Q4_K, 14 Q6_K or 8 Q8_0, rows of k values in
+ * the GGUF block layout, against the activations the last rl_act_quantize
+ * left.  Each output is the scalar tier's bit for bit.  rl_act_quantize
+ * allocates once, when a batch needs more scratch than any before it (call it
+ * at the largest size before capturing a graph). */
+int rl_act_quantize(rl_ctx *ctx, const float *x, int t, int k);
+int rl_matvec(rl_ctx *ctx, int ggml_type, const void *w, int rows, float *out);
+/* The whole group of Exec::matmul_group in one launch: n (1..8) weights that
+ * share the activations, e.g. a layer's qg, k and v (forward.rs:1250). */
+int rl_matvec_group(rl_ctx *ctx, int n, const int *types, const void *const *ws, const int *rows,
+                    float *const *outs);
 
 /* ---- full attention without allocation ---------------------------------
  * No counterpart in the reference: its runner owns all of its memory, so it

@@ -8,6 +8,7 @@
 // glibc libm, and no FMA contraction (built with -ffp-contract=off).
 #include "oracle.h"
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <condition_variable>
@@ -521,6 +522,200 @@ void orc_linear_attn(const orc_config *c, size_t slots, size_t live, size_t t,
             const float *zz = z + i * d_inner + h * s;
             for (size_t j = 0; j < s; ++j) head[j] *= orc_silu(zz[j]);
         }
+}
+
+// ---- projections: int8 activations against k-quant weight rows ----------
+// crates/llm-core/src/quant.rs (read_f16 :120-122, q4k_scale_min :215-226,
+// Activations::quantize_batch :337-372) and the scalar tier of
+// crates/llm-core/src/kernels/mod.rs (matvec_row :218-243, q4k_dot_scalar
+// :245-271, q6k_dot_scalar :273-301, q80_dot_scalar :303-320).
+
+// The reference kernel tests' xorshift64* stream (crates/llm-core/tests/
+// kernels.rs:48-61), n raw outputs; *state is the generator's state.
+void orc_xorshift_stream(uint64_t *state, uint64_t *out, size_t n) {
+    uint64_t x = *state;
+    for (size_t i = 0; i < n; ++i) {
+        x ^= x >> 12;
+        x ^= x << 25;
+        x ^= x >> 27;
+        out[i] = x * 0x2545F4914F6CDD1Dull;
+    }
+    *state = x;
+}
+
+// half::f16::to_f32: IEEE binary16 to binary32, exact (subnormals included).
+float orc_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            // subnormal: m * 2^-24, exact in f32
+            float f = (float)m * 0x1p-24f;
+            std::memcpy(&bits, &f, 4);
+            bits |= sign;
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112) << 23) | (m << 13);
+    }
+    float out;
+    std::memcpy(&out, &bits, 4);
+    return out;
+}
+
+static float rd16(const uint8_t *b, size_t off) {
+    return orc_f16_to_f32((uint16_t)(b[off] | (b[off + 1] << 8)));
+}
+
+static void scale_min_k4(size_t j, const uint8_t *s, uint8_t *sc, uint8_t *m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (uint8_t)((s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4));
+        *m = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+    }
+}
+
+void orc_q8k_quantize(const float *x, size_t k, size_t t, float *d, int8_t *qs, int16_t *bsums) {
+    const size_t nb = (k + 255) / 256;
+    for (size_t r = 0; r < t; ++r) {
+        for (size_t b = 0; b < nb; ++b) {
+            const float *chunk = x + r * k + b * 256;
+            const size_t n = std::min<size_t>(256, k - b * 256);
+            float amax = 0.0f;  // fold(0.0, |m, v| m.max(v.abs()))
+            for (size_t i = 0; i < n; ++i) amax = std::fmax(amax, std::fabs(chunk[i]));
+            const size_t blk = r * nb + b;
+            d[blk] = amax / 127.0f;
+            const float id = amax > 0.0f ? 127.0f / amax : 0.0f;
+            int8_t *q = qs + blk * 256;
+            for (size_t i = 0; i < 256; ++i) q[i] = 0;
+            for (size_t i = 0; i < n; ++i) {
+                float v = std::round(chunk[i] * id);  // round half away from zero
+                v = std::fmin(std::fmax(v, -127.0f), 127.0f);
+                q[i] = (int8_t)v;
+            }
+            for (size_t g = 0; g < 16; ++g) {
+                int s16 = 0;
+                for (size_t i = 0; i < 16; ++i) s16 += q[g * 16 + i];
+                bsums[blk * 16 + g] = (int16_t)s16;
+            }
+        }
+    }
+}
+
+float orc_dot_q4k(const uint8_t *w, const float *ad, const int8_t *aq, const int16_t *absums,
+                  size_t nb) {
+    float sum = 0.0f;
+    for (size_t ib = 0; ib < nb; ++ib) {
+        const uint8_t *b = w + ib * 144;
+        const float d = rd16(b, 0), dmin = rd16(b, 2);
+        const uint8_t *scales = b + 4, *qs = b + 16;
+        const int8_t *qa_blk = aq + ib * 256;
+        const int16_t *bs = absums + ib * 16;
+        int32_t isum = 0, imin = 0;
+        for (size_t j = 0; j < 8; ++j) {
+            uint8_t sc, m;
+            scale_min_k4(j, scales, &sc, &m);
+            const uint8_t *qw = qs + (j / 2) * 32;
+            const int8_t *qa = qa_blk + j * 32;
+            const int shift = j % 2 == 0 ? 0 : 4;
+            int32_t dot = 0;
+            for (size_t l = 0; l < 32; ++l) dot += (int32_t)((qw[l] >> shift) & 0xF) * qa[l];
+            isum += (int32_t)sc * dot;
+            imin += (int32_t)m * ((int32_t)bs[j * 2] + (int32_t)bs[j * 2 + 1]);
+        }
+        sum += ad[ib] * (d * (float)isum - dmin * (float)imin);
+    }
+    return sum;
+}
+
+float orc_dot_q6k(const uint8_t *w, const float *ad, const int8_t *aq, size_t nb) {
+    float sum = 0.0f;
+    for (size_t ib = 0; ib < nb; ++ib) {
+        const uint8_t *b = w + ib * 210;
+        const uint8_t *ql = b, *qh = b + 128, *sc = b + 192;
+        const float d = rd16(b, 208);
+        const int8_t *qa = aq + ib * 256;
+        int32_t isum = 0;
+        for (size_t h = 0; h < 2; ++h) {
+            const uint8_t *ql_h = ql + h * 64, *qh_h = qh + h * 32;
+            for (size_t g = 0; g < 4; ++g) {
+                for (size_t l = 0; l < 32; ++l) {
+                    uint8_t low;
+                    switch (g) {
+                    case 0: low = ql_h[l] & 0xF; break;
+                    case 1: low = ql_h[32 + l] & 0xF; break;
+                    case 2: low = ql_h[l] >> 4; break;
+                    default: low = ql_h[32 + l] >> 4; break;
+                    }
+                    const int32_t q = (int32_t)(low | (((qh_h[l] >> (2 * g)) & 3) << 4)) - 32;
+                    const int32_t s = (int8_t)sc[h * 8 + 2 * g + l / 16];
+                    isum += s * q * qa[h * 128 + g * 32 + l];
+                }
+            }
+        }
+        sum += ad[ib] * d * (float)isum;
+    }
+    return sum;
+}
+
+float orc_dot_q80(const uint8_t *w, const float *ad, const int8_t *aq, size_t k) {
+    float sum = 0.0f;
+    for (size_t ib = 0; ib < (k + 31) / 32; ++ib) {
+        const uint8_t *b = w + ib * 34;
+        const float dw = rd16(b, 0);
+        const size_t blk = ib / 8;
+        const int8_t *qa = aq + blk * 256 + (ib % 8) * 32;
+        int32_t dot = 0;
+        for (size_t l = 0; l < 32; ++l) dot += (int32_t)(int8_t)b[2 + l] * qa[l];
+        sum += dw * ad[blk] * (float)dot;
+    }
+    return sum;
+}
+
+// Bytes of one weight row of k values (GgmlType::bytes_for, quant.rs).
+size_t orc_row_bytes(int type, size_t k) {
+    switch (type) {
+    case 12: return (k + 255) / 256 * 144;  // Q4_K
+    case 14: return (k + 255) / 256 * 210;  // Q6_K
+    case 8: return (k + 31) / 32 * 34;      // Q8_0
+    default: return 0;
+    }
+}
+
+// Exec::matmul_group's per-weight product (forward.rs:1157-1180 through
+// Pool::matvec_group, pool.rs:289-342): the rows quantized once, then
+// out[tt][r] = row r . row tt of the activations, token-major.
+int orc_matvec(int type, const uint8_t *w, size_t rows, size_t k, const float *x, size_t t,
+               float *out, int threads) {
+    const size_t stride = orc_row_bytes(type, k);
+    if (!stride) return -1;
+    const size_t nb = (k + 255) / 256;
+    std::vector<float> d(t * nb);
+    std::vector<int8_t> qs(t * nb * 256);
+    std::vector<int16_t> bs(t * nb * 16);
+    orc_q8k_quantize(x, k, t, d.data(), qs.data(), bs.data());
+    const size_t chunk = 256;
+    pool_for(threads).run((rows + chunk - 1) / chunk, [&](size_t c) {
+        for (size_t r = c * chunk; r < std::min(rows, (c + 1) * chunk); ++r) {
+            const uint8_t *row = w + r * stride;
+            for (size_t tt = 0; tt < t; ++tt) {
+                const float *ad = d.data() + tt * nb;
+                const int8_t *aq = qs.data() + tt * nb * 256;
+                float v;
+                if (type == 12) v = orc_dot_q4k(row, ad, aq, bs.data() + tt * nb * 16, nb);
+                else if (type == 14) v = orc_dot_q6k(row, ad, aq, nb);
+                else v = orc_dot_q80(row, ad, aq, k);
+                out[tt * rows + r] = v;
+            }
+        }
+    });
+    return 0;
 }
 
 }  // extern "C"

@@ -131,6 +131,24 @@ void orc_linear_attn(const orc_config *c, size_t slots, size_t live, size_t t,
                      const float *conv1d, const float *ssm_a, const float *dt_bias,
                      const float *norm, float *out, int threads);
 
+/* ---- projections (crates/llm-core/src/quant.rs, kernels/mod.rs) -------- */
+/* GGML type ids: 8 Q8_0, 12 Q4_K, 14 Q6_K (quant.rs:36-70). */
+float orc_f16_to_f32(uint16_t h);
+/* n raw outputs of the reference kernel tests' xorshift64* generator. */
+void orc_xorshift_stream(uint64_t *state, uint64_t *out, size_t n);
+/* Activations::quantize_batch: t rows of k f32 -> per 256-value super-block
+ * d [t][nb], qs [t][nb][256] (tail zero), bsums [t][nb][16]. */
+void orc_q8k_quantize(const float *x, size_t k, size_t t, float *d, int8_t *qs, int16_t *bsums);
+/* The scalar tier's dot of one weight row with one quantized activation row. */
+float orc_dot_q4k(const uint8_t *w, const float *ad, const int8_t *aq, const int16_t *absums,
+                  size_t nb);
+float orc_dot_q6k(const uint8_t *w, const float *ad, const int8_t *aq, size_t nb);
+float orc_dot_q80(const uint8_t *w, const float *ad, const int8_t *aq, size_t k);
+size_t orc_row_bytes(int type, size_t k);
+/* out [t][rows] = W [rows][k] (type) . x [t][k], activations quantized first. */
+int orc_matvec(int type, const uint8_t *w, size_t rows, size_t k, const float *x, size_t t,
+               float *out, int threads);
+
 #ifdef __cplusplus
 }
 #endif

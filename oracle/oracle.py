@@ -92,6 +92,23 @@ def lib() -> ctypes.CDLL:
         L.orc_linear_attn.argtypes = [ctypes.POINTER(Config), _sz, _sz, _sz, _f32p, _f32p,
                                       _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                       _f32p, _f32p, ctypes.c_int]
+        _i8p = ctypes.POINTER(ctypes.c_int8)
+        _i16p = ctypes.POINTER(ctypes.c_int16)
+        _u8p = ctypes.POINTER(ctypes.c_uint8)
+        L.orc_xorshift_stream.argtypes = [_u64p, _u64p, _sz]
+        L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.orc_f16_to_f32.restype = ctypes.c_float
+        L.orc_q8k_quantize.argtypes = [_f32p, _sz, _sz, _f32p, _i8p, _i16p]
+        L.orc_dot_q4k.argtypes = [_u8p, _f32p, _i8p, _i16p, _sz]
+        L.orc_dot_q4k.restype = ctypes.c_float
+        L.orc_dot_q6k.argtypes = [_u8p, _f32p, _i8p, _sz]
+        L.orc_dot_q6k.restype = ctypes.c_float
+        L.orc_dot_q80.argtypes = [_u8p, _f32p, _i8p, _sz]
+        L.orc_dot_q80.restype = ctypes.c_float
+        L.orc_row_bytes.argtypes = [ctypes.c_int, _sz]
+        L.orc_row_bytes.restype = _sz
+        L.orc_matvec.argtypes = [ctypes.c_int, _u8p, _sz, _sz, _f32p, _sz, _f32p, ctypes.c_int]
+        L.orc_matvec.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -250,4 +267,48 @@ def linear_attn(cfg: Config, slots, live, qkv, z, alpha, beta, conv_state, ssm_s
     lib().orc_linear_attn(ctypes.byref(cfg), slots, live, t, *(P(a) for a in args),
                           P(conv_state), P(ssm_state), P(conv1d), P(ssm_a), P(dt_bias),
                           P(norm), P(out), threads)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Projections: int8 activations against k-quant weight rows
+# (crates/llm-core/src/quant.rs, kernels/mod.rs)
+
+Q8_0, Q4_K, Q6_K = 8, 12, 14
+
+
+def row_bytes(ggml_type: int, k: int) -> int:
+    return int(lib().orc_row_bytes(ggml_type, k))
+
+
+def q8k_quantize(x: np.ndarray, k: int):
+    """Activations::quantize_batch (quant.rs:337-372): x [t][k] -> (d [t][nb],
+    qs [t][nb][256] int8, bsums [t][nb][16] int16)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, k)
+    t, nb = x.shape[0], (k + 255) // 256
+    d = np.empty((t, nb), np.float32)
+    qs = np.empty((t, nb, 256), np.int8)
+    bs = np.empty((t, nb, 16), np.int16)
+    lib().orc_q8k_quantize(P(x), k, t, P(d), qs.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)),
+                           bs.ctypes.data_as(ctypes.POINTER(ctypes.c_int16)))
+    return d, qs, bs
+
+
+def matvec(ggml_type: int, w: np.ndarray, rows: int, k: int, x: np.ndarray, threads=1):
+    """The scalar tier's out [t][rows] = W . x with x quantized first
+    (Exec::matmul_group, forward.rs:1157-1180; kernels/mod.rs:218-320)."""
+    w = np.ascontiguousarray(w, np.uint8)
+    assert w.size >= rows * row_bytes(ggml_type, k)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, k)
+    out = np.empty((x.shape[0], rows), np.float32)
+    code = lib().orc_matvec(ggml_type, w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), rows, k,
+                            P(x), x.shape[0], P(out), threads)
+    assert code == 0, ggml_type
+    return out
+
+
+def xorshift_stream(state: np.ndarray, n: int) -> np.ndarray:
+    """n raw xorshift64* outputs; `state` (a 1-element uint64 array) advances."""
+    out = np.empty(n, np.uint64)
+    lib().orc_xorshift_stream(state.ctypes.data_as(_u64p), out.ctypes.data_as(_u64p), n)
     return out

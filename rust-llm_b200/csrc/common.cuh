@@ -21,6 +21,13 @@ constexpr long long WAIT_LIMIT_CYCLES = 2000000000ll;
 // context option RL_OPT_WAIT_LIMIT_US overrides it).
 constexpr unsigned long long PEER_WAIT_LIMIT_NS = 1000000000ull;
 
+// A value with its step's epoch in one 64-bit store (single-copy atomic at
+// system scope), to another GPU's memory or this one's.
+__device__ __forceinline__ void xstore(unsigned long long *dst, float v, unsigned epoch) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+}
+
 // The global nanosecond timer (the same on every SM of the GPU).
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
@@ -136,6 +143,12 @@ __device__ __forceinline__ void bulk_wait_all() {
 // async-proxy (TMA) reads of them.
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Brings `bytes` (a multiple of 16, 16-byte aligned) of global memory into
+// L2 without waiting for it.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
@@ -261,4 +274,25 @@ __device__ __forceinline__ float softplusf_(float x) {
     return x > 20.0f ? x : log1pf(expf(x));
 }
 
+}  // namespace rl
+
+namespace rl {
+// Reads a value stored by xstore once it carries `epoch`, waiting until
+// `start + limit_ns` at most (then `late` is set and the value is whatever
+// is there).
+__device__ __forceinline__ float xload(const unsigned long long *src, unsigned epoch,
+                                       unsigned long long start, unsigned long long limit_ns,
+                                       bool &late) {
+    unsigned long long w;
+    while (true) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
+        if ((unsigned)(w >> 32) == epoch || late) break;
+        if (globaltimer_ns() - start > limit_ns) {
+            late = true;
+            break;
+        }
+        __nanosleep(20);
+    }
+    return __uint_as_float((unsigned)w);
+}
 }  // namespace rl

@@ -47,6 +47,7 @@
 // (crates/rust-llm/src/forward.rs:1783-1842) and its gate (:1327-1340).
 #include "common.cuh"
 #include "kernels.h"
+#include "rlcuda.h"
 #include "mma.cuh"
 
 namespace rl {
@@ -538,6 +539,10 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
     const int d = blockIdx.y * kCombineDims + tx;
     const int S = a.n_splits;
     const float gate = a.qg[(size_t)hh * 2 * dm::HD + dm::HD + d];
+    // a split sequence's publish: this CTA's own step count (only this CTA
+    // touches its word, and only after every thread has read it)
+    const int xcta = hh * gridDim.y + blockIdx.y;
+    const unsigned xE = a.xpeers ? a.xepochs[xcta] + 1 : 0u;
     const float2 *ml = reinterpret_cast<const float2 *>(a.part_ml) + (size_t)hh * S;
     const float *po = a.part_o + (size_t)hh * S * dm::HD + d;
     // the first batch of partials goes out with the (max, sum) loads
@@ -600,17 +605,26 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
             float M = -INFINITY;
             if (blockIdx.y == 0 && tx == 0)
                 for (int s = 0; s < S; ++s) M = fmaxf(M, m_s[s]);
-            const int n_dst = a.part_out ? 1 : a.xworld;
-            for (int g = 0; g < n_dst; ++g) {
-                float *po_out = a.part_out
-                                    ? a.part_out + (size_t)hh * (dm::HD + 2)
-                                    : a.xpeers[g] +
-                                          (((size_t)a.xslot * a.xworld + a.xrank) * gridDim.x + hh) *
-                                              (dm::HD + 2);
+            if (a.part_out) {
+                float *po_out = a.part_out + (size_t)hh * (dm::HD + 2);
                 po_out[d] = o;
                 if (blockIdx.y == 0 && tx == 0) {
                     po_out[dm::HD] = M;
                     po_out[dm::HD + 1] = L_s;
+                }
+            } else {
+                // every value goes to every GPU's slot with the step's epoch in
+                // the same 64-bit store, so the reader checks each value itself
+                // and no fence or flag is needed
+                for (int g = 0; g < a.xworld; ++g) {
+                    unsigned long long *dst =
+                        reinterpret_cast<unsigned long long *>(a.xpeers[g]) +
+                        (((size_t)(xE & 1) * a.xworld + a.xrank) * gridDim.x + hh) * (dm::HD + 2);
+                    xstore(dst + d, o, xE);
+                    if (blockIdx.y == 0 && tx == 0) {
+                        xstore(dst + dm::HD, M, xE);
+                        xstore(dst + dm::HD + 1, L_s, xE);
+                    }
                 }
             }
         } else {
@@ -618,79 +632,65 @@ __global__ void __launch_bounds__(kCombineDims *kCombineLanes)
         }
     }
     if (a.xpeers) {
-        // the last CTA to finish raises this GPU's flag in every exchange
-        // buffer, after every CTA's partial is visible system-wide
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const int total = gridDim.x * gridDim.y;
-            if (atomicAdd(a.xcount, 1) == total - 1) {
-                *a.xcount = 0;
-                __threadfence_system();
-                for (int g = 0; g < a.xworld; ++g) {
-                    unsigned *flag = reinterpret_cast<unsigned *>(
-                                         reinterpret_cast<char *>(a.xpeers[g]) + a.xflag_off) +
-                                     a.xrank;
-                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(a.xepoch)
-                                 : "memory");
-                }
-            }
-        }
+        __syncthreads();  // every thread has read this CTA's step count
+        if (threadIdx.x == 0) a.xepochs[xcta] = xE;
     }
 }
 
-// The merge of a split sequence's partials from this GPU's exchange buffer
-// (every GPU pushed its partial and then its flag): one CTA per (row, head),
-// one thread per dim; thread 0 waits (bounded) for every flag to reach the
-// step's epoch.  Reference: the softmax over all positions (forward.rs:
-// 1831-1842) reassembled by the log-sum-exp rule, then the gate (:1327-1340).
-__global__ void __launch_bounds__(256) peer_merge_kernel(const float *xbuf, int world, int slot,
-                                                         unsigned epoch, int rows_heads,
-                                                         const float *qg, float *out,
-                                                         int *status,
+// The merge of a split sequence's partials from this GPU's exchange buffer,
+// where every GPU stored each value with the step's epoch beside it: one CTA
+// per (row, head), one thread per dim.  It launches as soon as the publishing
+// merge ahead of it has started and needs no flag: thread d waits (bounded)
+// until every GPU's value d of this head carries the step's epoch (the CTA's
+// own count of steps), threads 0.. and 32.. the same for the GPUs' (max,
+// sum).  Reference: the softmax over all positions (forward.rs:1831-1842)
+// reassembled by the log-sum-exp rule, then the gate (:1327-1340).
+__global__ void __launch_bounds__(256) peer_merge_kernel(const unsigned long long *xbuf,
+                                                         int world, int rows_heads,
+                                                         const float *qg, float *out, int *status,
+                                                         unsigned *epochs,
                                                          unsigned long long limit_ns) {
-    grid_dep_wait();    // this GPU's own partial and flag, and qg, are in place
     grid_dep_launch();  // the next layer's walk may start streaming meanwhile
+    __shared__ float m_s[RL_EXCHANGE_MAX_GPUS], l_s[RL_EXCHANGE_MAX_GPUS];
+    __shared__ int late_s;
     const int hh = blockIdx.x, d = threadIdx.x;
+    const unsigned E = epochs[hh] + 1;  // written last by this CTA's previous step
     const size_t stride = (size_t)rows_heads * (dm::HD + 2);
-    if (d == 0) {
-        const unsigned *flags = reinterpret_cast<const unsigned *>(
-            reinterpret_cast<const char *>(xbuf) + xbuf_flag_offset(world, rows_heads, dm::HD));
-        // one limit for the whole wait, on the global nanosecond timer
-        const unsigned long long start = globaltimer_ns();
-        for (int g = 0; g < world; ++g) {
-            while (true) {
-                unsigned f;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + g)
-                             : "memory");
-                if ((int)(f - epoch) >= 0) break;
-                if (globaltimer_ns() - start > limit_ns) {
-                    atomicOr(status, DEV_TIMEOUT);
-                    g = world;  // give up on every remaining flag
-                    break;
-                }
-                __nanosleep(32);
-            }
-        }
+    const unsigned long long *p0 = xbuf + (size_t)(E & 1) * world * stride + (size_t)hh * (dm::HD + 2);
+    const unsigned long long start = globaltimer_ns();
+    bool late = false;
+    if (d == 0) late_s = 0;
+    if ((d & 31) < world && d < 64) {
+        const int g = d & 31;
+        const float v = xload(p0 + g * stride + dm::HD + (d >> 5), E, start, limit_ns, late);
+        (d < 32 ? m_s : l_s)[g] = v;
     }
+    float vals[RL_EXCHANGE_MAX_GPUS];
+#pragma unroll
+    for (int g = 0; g < RL_EXCHANGE_MAX_GPUS; ++g)
+        if (g < world) vals[g] = xload(p0 + g * stride + d, E, start, limit_ns, late);
+    if (late) late_s = 1;
     __syncthreads();
-    const float *p0 = xbuf + (size_t)slot * world * stride + (size_t)hh * (dm::HD + 2);
+    if (d == 0 && late_s) atomicOr(status, DEV_TIMEOUT);
     float M = -INFINITY;
-    for (int g = 0; g < world; ++g) M = fmaxf(M, __ldcv(p0 + g * stride + dm::HD));
+    for (int g = 0; g < world; ++g) M = fmaxf(M, m_s[g]);
     float L = 0.0f, o = 0.0f;
-    for (int g = 0; g < world; ++g) {
-        const float *pg = p0 + g * stride;
-        const float m = __ldcv(pg + dm::HD);
-        const float sc = m == -INFINITY ? 0.0f : exp2f(m - M);
-        L = fmaf(__ldcv(pg + dm::HD + 1), sc, L);
-        o = fmaf(__ldcv(pg + d), sc, o);
+#pragma unroll
+    for (int g = 0; g < RL_EXCHANGE_MAX_GPUS; ++g) {
+        if (g < world) {
+            const float sc = m_s[g] == -INFINITY ? 0.0f : exp2f(m_s[g] - M);
+            L = fmaf(l_s[g], sc, L);
+            o = fmaf(vals[g], sc, o);
+        }
     }
     const float gate = qg[(size_t)hh * 2 * dm::HD + dm::HD + d];
     out[(size_t)hh * dm::HD + d] = (o / L) * sigmoidf_(gate);
+    __syncthreads();
+    if (d == 0) epochs[hh] = E;
 }
 
-cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned epoch,
-                              int rows_heads, const float *qg, float *out, int *status,
+cudaError_t launch_peer_merge(const unsigned long long *xbuf, int world, int rows_heads,
+                              const float *qg, float *out, int *status, unsigned *epochs,
                               unsigned long long limit_ns, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(rows_heads);
@@ -701,8 +701,8 @@ cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned e
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, peer_merge_kernel, xbuf, world, slot, epoch, rows_heads, qg,
-                              out, status, limit_ns);
+    return cudaLaunchKernelEx(&cfg, peer_merge_kernel, xbuf, world, rows_heads, qg, out, status,
+                              epochs, limit_ns);
 }
 
 // Merges the partials of a sequence split across GPUs, gathered as

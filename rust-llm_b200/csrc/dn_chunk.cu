@@ -852,15 +852,21 @@ cudaError_t init_dn_chunk_kernels() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(ScanSmem));
+    if (e == cudaSuccess) e = init_dn_scan_tc_kernel();
     return e;
 }
 
-cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st) {
+cudaError_t launch_dn_chunk(const DnChunkArgs &a, const DnScanMaps *scan_maps, cudaStream_t st) {
     using namespace dc;
     dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
                      st>>>(a);
     dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
-    dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
+    if (scan_maps) {
+        const cudaError_t e = launch_dn_scan_tc(a, *scan_maps, st);
+        if (e != cudaSuccess) return e;
+    } else {
+        dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
+    }
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
     const int conv_dim = 2 * a.n_k * S + a.n_v * S;
     dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, st>>>(a);

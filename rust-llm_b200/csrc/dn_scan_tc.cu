@@ -1,0 +1,420 @@
+// The chunk scan of the chunked Gated DeltaNet prefill on the fifth-generation
+// tensor cores (tcgen05, tensor memory, TMA), sm_100a.
+//
+// The chunk-local kernel (dn_chunk.cu) leaves, per (value head, chunk of 64
+// tokens): W = T diag(beta gamma) K, Ut = T diag(beta) V, Q' = gamma Q,
+// K' = gamma_C/gamma K, P = Q K^T o Mgamma and gamma_C.  The scan walks the
+// chunks of a head in order (forward.rs:1906-1950 unrolled over a chunk):
+//   U_c = Ut_c - W_c S_{c-1}
+//   O_c = Q'_c S_{c-1} + P_c U_c               (the chunk's readouts)
+//   S_c = gamma_C S_{c-1} + K'_c^T U_c
+// It runs them transposed, so that the 128 state columns j are the MMA's 128
+// rows (M = 128) and every product is one tcgen05.mma chain:
+//   U^T[j][t]  = sum_i S^T[j][i] W[t][i]          (A = S^T, B = W, both K-major)
+//   O^T[j][t]  = sum_i S^T[j][i] Q'[t][i] + sum_s U^T[j][s] P[t][s]
+//   S^T[j][i] += sum_t U^T[j][t] K'[t][i]         (B = K', N-major)
+// S^T accumulates in tensor memory in f32 for the whole scan; only its bf16
+// copy for the next chunk's products goes through registers and shared memory.
+//
+// Precision (bf16 operands as pairs x = hi + lo where it matters): W S is one
+// hi*hi term (the delta rule's feedback corrects it: U = Ut - W S feeds S
+// back), O takes the three terms hi*hi + hi*lo + lo*hi of both products, and
+// the state update two, U_hi (K'_hi + K'_lo).  A CPU model of these roundings
+// against the token-sequential recurrence gave 4e-3 of the per-head output
+// at 4096 tokens against 2.7e-3 for f32 products and 1.25e-2 for bf16 pairs
+// in Q K^T (the term the chunk-local kernel now takes at 24 bits).
+//
+// One CTA per value head, ten warps:
+//   warps 0-3  the chain: thread j owns state column j (tensor-memory lane j):
+//              U = Ut - acc into shared memory as a bf16 pair; after the state
+//              update, S_c as a bf16 pair for the next products, gamma S_c
+//              back into tensor memory
+//   warps 4-7  the readout: O^T from tensor memory to the output rows
+//   warp 8     TMA producer, one lane per operand (K' double-buffered; W,
+//              Q', P single, each refilled as soon as the MMAs that read it
+//              are done), and bulk L2 prefetches two chunks ahead
+//   warp 9     tensor-memory owner and MMA issuer (one lane)
+// Every wait is bounded; a wait that gives up flags DEV_TIMEOUT and the roles
+// wind down (copies and MMAs in flight are waited for before the tensor
+// memory and shared memory are released).
+#include "common.cuh"
+#include "kernels.h"
+#include "mma.cuh"
+#include "tc.cuh"
+
+namespace rl {
+namespace sc {
+constexpr int S = 128, C = 64;
+constexpr int THREADS = 320;
+constexpr int PRODUCER_WARP = 8, MMA_WARP = 9;
+constexpr uint32_t BOX64 = 64 * 128;    // 64 rows x 64 bf16 (128-byte rows, swizzled)
+constexpr uint32_t BOX128 = 128 * 128;  // 128 rows x 64 bf16
+// shared-memory byte offsets from a 1024-byte aligned base
+constexpr uint32_t W_OFF = 0;                     // [i box] 64 t x 64 i, hi only
+constexpr uint32_t Q_OFF = W_OFF + 2 * BOX64;     // [hi, lo][i box]
+constexpr uint32_t P_OFF = Q_OFF + 4 * BOX64;     // [hi, lo] 64 t x 64 s
+constexpr uint32_t K_OFF = P_OFF + 2 * BOX64;     // [buffer][hi, lo][i box] 64 t x 64 i
+constexpr uint32_t ST_OFF = K_OFF + 8 * BOX64;    // S^T [hi, lo][i box] 128 j x 64 i
+constexpr uint32_t UT_OFF = ST_OFF + 4 * BOX128;  // U^T [hi, lo] 128 j x 64 t
+constexpr uint32_t SMEM = UT_OFF + 2 * BOX128 + 1024;
+constexpr uint32_t TMEM_COLS = 512, S_COL = 0, U_COL = 128, O_COL = 256;  // O: 2 x 64
+constexpr uint32_t W_BYTES = 2 * BOX64, Q_BYTES = 4 * BOX64, P_BYTES = 2 * BOX64,
+                   K_BYTES = 4 * BOX64;
+}  // namespace sc
+
+// Byte offset of the 16-byte chunk `c` of row `r` in a 128-byte swizzled box.
+__device__ __forceinline__ uint32_t sw(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// 32 f32 values of a row as bf16 (hi) or as the low halves x - bf16(x) (lo),
+// into 4 consecutive 16-byte chunks c0.. of row r of a swizzled box.
+__device__ __forceinline__ void put32(unsigned char *box, int r, int c0, const float *x, bool lo) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float a = x[q * 8 + 2 * e], b = x[q * 8 + 2 * e + 1];
+            w[e] = lo ? pack_bf16(a - bf16_hi(a), b - bf16_hi(b)) : pack_bf16(a, b);
+        }
+        *reinterpret_cast<uint4 *>(box + sw(r, c0 + q)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ __forceinline__ void as_f32(const uint32_t (&r)[32], float *x) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(r[e]);
+}
+
+__global__ void __launch_bounds__(sc::THREADS, 1)
+    dn_scan_tc_kernel(const __grid_constant__ DnChunkArgs a, const __grid_constant__ DnScanMaps m) {
+    using namespace sc;
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t w_full, w_empty, q_full, q_empty, p_full, p_empty,
+        k_full[2], k_empty[2], s_ready, u_done, u_ready, s_done, o_full[2], o_empty[2], fin;
+    __shared__ uint32_t tmem_base;
+    __shared__ int flag_s;
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const uint32_t sbase = smem_u32(smem);
+    const int vh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nc = a.nc;
+    const size_t blk0 = (size_t)vh * nc;
+    float *state = a.ssm_state + (size_t)vh * a.slots * S * S + (size_t)a.live * S * S;
+
+    if (tid == 0) {
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&k_full[b], 1);
+            mbar_init(&k_empty[b], 1);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_empty[b], 128);
+        }
+        mbar_init(&w_full, 1);
+        mbar_init(&w_empty, 1);
+        mbar_init(&q_full, 1);
+        mbar_init(&q_empty, 1);
+        mbar_init(&p_full, 1);
+        mbar_init(&p_empty, 1);
+        mbar_init(&s_ready, 128);
+        mbar_init(&u_done, 1);
+        mbar_init(&u_ready, 128);
+        mbar_init(&s_done, 1);
+        mbar_init(&fin, 1);
+        flag_s = 0;
+        fence_barrier_init();
+    }
+    if (warp == MMA_WARP) {
+        tc::tmem_alloc(&tmem_base, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == PRODUCER_WARP) {
+        // ---------------- TMA producer: lane 0 W, 1 Q', 2 P, 3 K', 4 the L2
+        // prefetch of the chunk after next ----------------
+        if (lane < 5) {
+            const int role = lane;
+            if (role == 0) {
+                prefetch_tensormap(&m.w);
+            } else if (role == 1) {
+                prefetch_tensormap(&m.qh);
+                prefetch_tensormap(&m.ql);
+            } else if (role == 2) {
+                prefetch_tensormap(&m.ph);
+                prefetch_tensormap(&m.pl);
+            } else if (role == 3) {
+                prefetch_tensormap(&m.kh);
+                prefetch_tensormap(&m.kl);
+            }
+            int c = 0;
+            for (; c < nc; ++c) {
+                const int row = (int)(blk0 + c) * C;
+                if (role == 0) {
+                    if (c >= 1 && !mbar_wait(&w_empty, (c - 1) & 1, a.status)) break;
+                    mbar_arrive_expect_tx(&w_full, W_BYTES);
+                    for (int x = 0; x < 2; ++x)
+                        tma_load_2d(smem + W_OFF + x * BOX64, &m.w, 64 * x, row, &w_full);
+                } else if (role == 1) {
+                    if (c >= 1 && !mbar_wait(&q_empty, (c - 1) & 1, a.status)) break;
+                    mbar_arrive_expect_tx(&q_full, Q_BYTES);
+                    for (int x = 0; x < 2; ++x) {
+                        tma_load_2d(smem + Q_OFF + x * BOX64, &m.qh, 64 * x, row, &q_full);
+                        tma_load_2d(smem + Q_OFF + (2 + x) * BOX64, &m.ql, 64 * x, row, &q_full);
+                    }
+                } else if (role == 2) {
+                    if (c >= 1 && !mbar_wait(&p_empty, (c - 1) & 1, a.status)) break;
+                    mbar_arrive_expect_tx(&p_full, P_BYTES);
+                    tma_load_2d(smem + P_OFF, &m.ph, 0, row, &p_full);
+                    tma_load_2d(smem + P_OFF + BOX64, &m.pl, 0, row, &p_full);
+                } else if (role == 3) {
+                    const int b = c & 1;
+                    if (c >= 2 && !mbar_wait(&k_empty[b], ((c >> 1) - 1) & 1, a.status)) break;
+                    mbar_arrive_expect_tx(&k_full[b], K_BYTES);
+                    unsigned char *kd = smem + K_OFF + b * 4 * BOX64;
+                    for (int x = 0; x < 2; ++x) {
+                        tma_load_2d(kd + x * BOX64, &m.kh, 64 * x, row, &k_full[b]);
+                        tma_load_2d(kd + (2 + x) * BOX64, &m.kl, 64 * x, row, &k_full[b]);
+                    }
+                } else {
+                    // the chunk after next into L2, paced by this chunk's W (so
+                    // it runs at most two chunks ahead of the MMAs)
+                    if (c >= 1 && !mbar_wait(&w_empty, (c - 1) & 1, a.status)) break;
+                    const int cn = c + 2;
+                    if (cn < nc) {
+                        const size_t bo = (blk0 + cn) * C;
+                        prefetch_l2_bulk(a.w + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.qp + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.qp_lo + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.kp + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.kp_lo + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.p + bo * C, C * C * 2);
+                        prefetch_l2_bulk(a.p_lo + bo * C, C * C * 2);
+                    }
+                    if (c + 1 < nc) prefetch_l2_bulk(a.ut + (blk0 + c + 1) * C * S, C * S * 4);
+                }
+            }
+            if (c < nc) flag_s = 1;
+            // every copy this lane started lands before the shared memory is
+            // released (bounded: a consumer that gave up leaves a buffer full)
+            const int last = min(c, nc - 1);
+            if (last >= 0) {
+                if (role == 0) mbar_wait(&w_full, last & 1, a.status);
+                if (role == 1) mbar_wait(&q_full, last & 1, a.status);
+                if (role == 2) mbar_wait(&p_full, last & 1, a.status);
+                if (role == 3) {
+                    mbar_wait(&k_full[last & 1], (last >> 1) & 1, a.status);
+                    if (last >= 1) mbar_wait(&k_full[(last - 1) & 1], ((last - 1) >> 1) & 1, a.status);
+                }
+            }
+        }
+    } else if (warp == MMA_WARP) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t id_n64 = tc::idesc_bf16(128, 64, false);
+            constexpr uint32_t id_s = tc::idesc_bf16(128, 128, true);
+            const uint32_t w_s = sbase + W_OFF, q_s = sbase + Q_OFF, p_s = sbase + P_OFF,
+                           k_s = sbase + K_OFF, st_s = sbase + ST_OFF, ut_s = sbase + UT_OFF;
+            bool ok = true;
+            for (int c = 0; c < nc && ok; ++c) {
+                const int b = c & 1;
+                const uint32_t o_acc = tmem + O_COL + b * 64;
+                ok = mbar_wait(&s_ready, c & 1, a.status) && mbar_wait(&w_full, c & 1, a.status);
+                if (!ok) break;
+                tc::fence_after_sync();
+                // U^T = S^T_hi W_hi (K = 128: two boxes of four 16-wide steps)
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * BOX128 + (kk & 3) * 32;
+                    const uint32_t offb = (kk >> 2) * BOX64 + (kk & 3) * 32;
+                    tc::mma_ss(tmem + U_COL, tc::smem_desc(st_s + off, 16, 1024),
+                               tc::smem_desc(w_s + offb, 16, 1024), id_n64, kk > 0);
+                }
+                tc::commit(&u_done);
+                tc::commit(&w_empty);
+                // O^T = S^T Q'^T, three terms
+                ok = (c < 2 || mbar_wait(&o_empty[b], ((c >> 1) - 1) & 1, a.status)) &&
+                     mbar_wait(&q_full, c & 1, a.status);
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int term = 0; term < 3; ++term) {
+                    const uint32_t sa = st_s + (term == 2 ? 2 * BOX128 : 0);  // S lo for term 2
+                    const uint32_t qb = q_s + (term == 1 ? 2 * BOX64 : 0);    // Q' lo for term 1
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * BOX128 + (kk & 3) * 32;
+                        const uint32_t offb = (kk >> 2) * BOX64 + (kk & 3) * 32;
+                        tc::mma_ss(o_acc, tc::smem_desc(sa + off, 16, 1024),
+                                   tc::smem_desc(qb + offb, 16, 1024), id_n64, term > 0 || kk > 0);
+                    }
+                }
+                tc::commit(&q_empty);
+                // the state update as soon as U is in shared memory
+                ok = mbar_wait(&u_ready, c & 1, a.status) &&
+                     mbar_wait(&k_full[b], (c >> 1) & 1, a.status);
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int term = 0; term < 2; ++term) {
+                    const uint32_t kb = k_s + b * 4 * BOX64 + term * 2 * BOX64;  // K' hi, then lo
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc::mma_ss(tmem + S_COL, tc::smem_desc(ut_s + kk * 32, 16, 1024),
+                                   tc::smem_desc(kb + kk * 16 * 128, BOX64, 1024), id_s, true);
+                }
+                tc::commit(&k_empty[b]);
+                tc::commit(&s_done);
+                // O^T += U^T P^T, three terms
+                ok = mbar_wait(&p_full, c & 1, a.status);
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int term = 0; term < 3; ++term) {
+                    const uint32_t ua = ut_s + (term == 2 ? BOX128 : 0);
+                    const uint32_t pb = p_s + (term == 1 ? BOX64 : 0);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc::mma_ss(o_acc, tc::smem_desc(ua + kk * 32, 16, 1024),
+                                   tc::smem_desc(pb + kk * 32, 16, 1024), id_n64, true);
+                }
+                tc::commit(&p_empty);
+                tc::commit(&o_full[b]);
+            }
+            if (!ok) flag_s = 1;
+            // every MMA issued is complete before the tensor memory is freed
+            tc::commit(&fin);
+            mbar_wait(&fin, 0, a.status);
+        }
+    } else if (warp < 4) {
+        // ---------------- the chain: thread j owns state column j ----------------
+        const int j = tid;
+        const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+        unsigned char *st_hi = smem + ST_OFF, *st_lo = smem + ST_OFF + 2 * BOX128;
+        unsigned char *ut_hi = smem + UT_OFF, *ut_lo = smem + UT_OFF + BOX128;
+        bool ok = true;
+        // S_{-1}: its bf16 pair for the first products, gamma_0 S into tensor memory
+        {
+            const float g0 = a.gc[blk0];
+#pragma unroll 1
+            for (int q = 0; q < 4; ++q) {
+                float x[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) x[e] = state[(size_t)(q * 32 + e) * S + j];
+                put32(st_hi + (q >> 1) * BOX128, j, (q & 1) * 4, x, false);
+                put32(st_lo + (q >> 1) * BOX128, j, (q & 1) * 4, x, true);
+                uint32_t r[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(x[e] * g0);
+                tc::st32(tmem + lane_addr + S_COL + q * 32, r);
+            }
+            tc::wait_st();
+            fence_proxy_async_smem();
+            tc::fence_before_sync();
+            mbar_arrive(&s_ready);
+        }
+        for (int c = 0; c < nc && ok; ++c) {
+            const size_t blk = blk0 + c;
+            const float *ut = a.ut + blk * C * S + j;
+            // ---- U = Ut - S W, into shared memory as a bf16 pair (Ut's
+            // column j is read while the MMAs run: 64 loads, coalesced over j)
+            float x[64];
+#pragma unroll
+            for (int e = 0; e < 64; ++e) x[e] = __ldcg(ut + (size_t)e * S);
+            ok = mbar_wait(&u_done, c & 1, a.status);
+            if (!ok) break;
+            tc::fence_after_sync();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[32];
+                tc::ld32(tmem + lane_addr + U_COL + h * 32, r);
+                tc::wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) x[h * 32 + e] -= __uint_as_float(r[e]);
+                put32(ut_hi, j, h * 4, x + h * 32, false);
+                put32(ut_lo, j, h * 4, x + h * 32, true);
+            }
+            fence_proxy_async_smem();
+            tc::fence_before_sync();
+            mbar_arrive(&u_ready);
+            // ---- S_c: its pair for the next chunk, gamma_{c+1} S_c back into
+            // tensor memory, or out to the state after the last chunk
+            ok = mbar_wait(&s_done, c & 1, a.status);
+            if (!ok) break;
+            tc::fence_after_sync();
+            const bool more = c + 1 < nc;
+            const float gn = more ? a.gc[blk + 1] : 1.0f;
+#pragma unroll 1
+            for (int q = 0; q < 4; ++q) {
+                uint32_t r[32];
+                tc::ld32(tmem + lane_addr + S_COL + q * 32, r);
+                tc::wait_ld();
+                float x[32];
+                as_f32(r, x);
+                if (more) {
+                    put32(st_hi + (q >> 1) * BOX128, j, (q & 1) * 4, x, false);
+                    put32(st_lo + (q >> 1) * BOX128, j, (q & 1) * 4, x, true);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(x[e] * gn);
+                    tc::st32(tmem + lane_addr + S_COL + q * 32, r);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) state[(size_t)(q * 32 + e) * S + j] = x[e];
+                }
+            }
+            if (more) {
+                tc::wait_st();
+                fence_proxy_async_smem();
+                tc::fence_before_sync();
+                mbar_arrive(&s_ready);
+            }
+        }
+        if (!ok) flag_s = 1;
+    } else {
+        // ---------------- the readout: O^T rows to the output ----------------
+        const int j = tid - 128, q4 = warp - 4;
+        const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+        const float scale = 1.0f / sqrtf((float)S);
+        for (int c = 0; c < nc; ++c) {
+            const int b = c & 1;
+            if (!mbar_wait(&o_full[b], (c >> 1) & 1, a.status)) {
+                flag_s = 1;
+                break;
+            }
+            tc::fence_after_sync();
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[32];
+                tc::ld32(tmem + lane_addr + O_COL + b * 64 + h * 32, r);
+                tc::wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int tok = c * C + h * 32 + e;
+                    if (tok < a.t)
+                        a.opre[((size_t)tok * a.n_v + vh) * S + j] = __uint_as_float(r[e]) * scale;
+                }
+            }
+            tc::fence_before_sync();
+            mbar_arrive(&o_empty[b]);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0 && flag_s) atomicOr(a.status, DEV_TIMEOUT);
+    if (warp == MMA_WARP) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+cudaError_t init_dn_scan_tc_kernel() {
+    return cudaFuncSetAttribute(dn_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sc::SMEM);
+}
+
+cudaError_t launch_dn_scan_tc(const DnChunkArgs &a, const DnScanMaps &m, cudaStream_t st) {
+    dn_scan_tc_kernel<<<a.n_v, sc::THREADS, sc::SMEM, st>>>(a, m);
+    return cudaGetLastError();
+}
+
+}  // namespace rl

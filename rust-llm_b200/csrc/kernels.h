@@ -66,14 +66,13 @@ struct DecodeArgs {
     // non-null: the merge writes this shard's partial [t*n_head][hd + 2]
     // (unnormalised output, max in log2 units, sum) instead of the output
     float *part_out;
-    // non-null (a split sequence, peer exchange): the merge writes this GPU's
-    // partial into slot (xslot, xrank) of every GPU's exchange buffer and,
-    // once all its CTAs have, sets flag xrank of every GPU to xepoch
+    // non-null (a split sequence, peer exchange): each merge CTA (head, 64-dim
+    // slice) writes its slice of this GPU's partial into slot (epoch & 1,
+    // xrank) of every GPU's exchange buffer, each value beside the epoch, its
+    // own count of steps (xepochs, one word per CTA)
     float *const *xpeers;  // [xworld] exchange buffers, as addressed from this GPU
-    int xrank, xworld, xslot;
-    unsigned xepoch;
-    size_t xflag_off;      // byte offset of the flags in an exchange buffer
-    int *xcount;           // arrival counter, zero between launches
+    int xrank, xworld;
+    unsigned *xepochs;     // [rows_heads * 4] steps published, per merge CTA
     // non-null (bf16 walk, one row per sequence): row r is sequence r, at
     // position batch_pos[r] of its own context, described by rows[r]
     const BatchRow *rows;
@@ -95,21 +94,19 @@ int decode_max_active_clusters(bool kv_bf16, bool fused, int csize);
 cudaError_t init_decode_mma_kernels();
 cudaError_t launch_decode_mma(const DecodeArgs &a, const CUtensorMap &kv_map, cudaStream_t st);
 cudaError_t launch_decode_combine(const DecodeArgs &a, cudaStream_t st);
-// The exchange buffer of one GPU for a split sequence: partials
-// [2 slots][world][rows_heads][hd + 2] f32, then [world] u32 flags at a
-// 128-byte boundary.  Slot = epoch & 1.
-__host__ __device__ inline size_t xbuf_flag_offset(int world, int rows_heads, int hd) {
-    const size_t data = (size_t)2 * world * rows_heads * (hd + 2) * sizeof(float);
-    return (data + 127) / 128 * 128;
-}
+// The exchange buffer of one GPU for a split sequence: [2 slots][world]
+// [rows_heads][hd + 2] 64-bit words, each an f32 value (low half: the
+// unnormalised output, then the max in log2 units and the sum) beside the
+// epoch of the step that stored it (high half).  Slot = epoch & 1.
 __host__ __device__ inline size_t xbuf_bytes(int world, int rows_heads, int hd) {
-    return xbuf_flag_offset(world, rows_heads, hd) + ((size_t)world * 4 + 127) / 128 * 128;
+    return (size_t)2 * world * rows_heads * (hd + 2) * sizeof(unsigned long long);
 }
-// Waits (bounded) until every GPU's flag in this GPU's exchange buffer has
-// reached `epoch`, then merges slot `slot`'s partials and applies the gate:
-// out [rows_heads][hd].  Launched as a programmatic dependent.
-cudaError_t launch_peer_merge(const float *xbuf, int world, int slot, unsigned epoch,
-                              int rows_heads, const float *qg, float *out, int *status,
+// Waits (bounded, limit_ns) until every GPU's values of a head in this GPU's
+// exchange buffer carry the step's epoch (epochs: [rows_heads] steps merged,
+// per CTA), then merges them and applies the gate: out [rows_heads][hd].
+// Launched as a programmatic dependent.
+cudaError_t launch_peer_merge(const unsigned long long *xbuf, int world, int rows_heads,
+                              const float *qg, float *out, int *status, unsigned *epochs,
                               unsigned long long limit_ns, cudaStream_t st);
 // parts [n_parts][rows_heads][hd + 2] -> out [rows_heads][hd], gated
 cudaError_t launch_merge_parts(const float *parts, int n_parts, int rows_heads, const float *qg,
@@ -219,7 +216,18 @@ struct DnChunkArgs {
     float eps;
 };
 cudaError_t init_dn_chunk_kernels();
-cudaError_t launch_dn_chunk(const DnChunkArgs &a, cudaStream_t st);
+// The chunk scan on tcgen05 (dn_scan_tc.cu) reads the chunk-local kernel's
+// outputs through these tensor maps: W (hi), Q' and K' (hi, lo) as
+// [n_v * nc * 64][128] bf16 and P (hi, lo) as [n_v * nc * 64][64] bf16, all in
+// boxes of 64 rows x 64 columns with the 128-byte swizzle.
+struct DnScanMaps {
+    CUtensorMap w, qh, ql, kh, kl, ph, pl;
+};
+cudaError_t init_dn_scan_tc_kernel();
+cudaError_t launch_dn_scan_tc(const DnChunkArgs &a, const DnScanMaps &m, cudaStream_t st);
+// The whole chunked prefill of one call; `scan_maps` non-null selects the
+// tcgen05 chunk scan, null the mma.sync one.
+cudaError_t launch_dn_chunk(const DnChunkArgs &a, const DnScanMaps *scan_maps, cudaStream_t st);
 
 // KV cache fill from f32 (host-visible test and bench helper): positions
 // [p0, p0+n) of every KV head, src [2][n_kv][n][hd] f32 on the device.
@@ -227,6 +235,29 @@ cudaError_t launch_kv_fill(void *k_cache, void *v_cache, const float *src, int n
                            int context, int hd, int p0, int n, bool kv_bf16, cudaStream_t st);
 cudaError_t launch_kv_read(const void *k_cache, const void *v_cache, float *dst, int n_kv,
                            int context, int hd, int p0, int n, bool kv_bf16, cudaStream_t st);
+
+// Projections (proj.cu): t rows of k activations quantized to int8 per
+// 256-value super-block (d [t][nb], qs [t][nb][256], bs [t][nb][16]), then
+// out [t][rows] = W . x for a weight of GGML type 12 (Q4_K), 14 (Q6_K) or
+// 8 (Q8_0) stored as rows of proj_row_bytes(type, k) bytes.
+size_t proj_row_bytes(int ggml_type, int k);
+cudaError_t launch_q8k_quantize(const float *x, int t, int k, float *d, int8_t *qs, int16_t *bs,
+                                cudaStream_t st);
+// A group of up to 8 weights dotted with the same activations, one launch.
+constexpr int kMatvecGroupMax = 8;
+struct MatvecGroup {
+    int n;
+    int type[kMatvecGroupMax], rows[kMatvecGroupMax];
+    size_t stride[kMatvecGroupMax];
+    const void *w[kMatvecGroupMax];
+    float *out[kMatvecGroupMax];
+};
+// A weight row is staged in shared memory: at most this many bytes (k up to
+// 16384 for Q8_0, the largest row of the reference's tests).
+constexpr int kMatvecRowSmemMax = 17456;
+cudaError_t init_matvec_kernel();
+cudaError_t launch_matvec_group(const MatvecGroup &g, int k, const float *d, const int8_t *qs,
+                                const int16_t *bs, int t, cudaStream_t st);
 
 // Sets the calling thread's message for rl_last_error(NULL).
 void set_thread_error(const char *msg);

@@ -1,0 +1,302 @@
+// The projections either side of the attention path on the device, sm_100a:
+// activations quantized to int8 per 256-value super-block, then each weight
+// row (Q4_K, Q6_K or Q8_0 blocks, the GGUF layouts) dotted with them in
+// integer arithmetic and the blocks' scales applied in f32, block by block in
+// order.  This is the reference's scalar kernel tier, value for value:
+//   Activations::quantize_batch   crates/llm-core/src/quant.rs:337-372
+//   q4k_dot_scalar / q6k_dot_scalar / q80_dot_scalar
+//                                 crates/llm-core/src/kernels/mod.rs:245-320
+// The integer sums are exact whatever their order, and every f32 operation
+// is the reference's, in its order and without contraction, so a row's
+// result is the scalar tier's bit for bit.  The rows are HBM-bound at decode
+// sizes: one warp per weight row, the row's blocks streamed once, all of a
+// batch's activation rows dotted against them while they are in registers.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rl {
+namespace pj {
+constexpr int QK = 256;            // super-block
+constexpr int Q4K_BYTES = 144, Q6K_BYTES = 210, Q80_BYTES = 34;
+}  // namespace pj
+
+// ---- activation quantization -------------------------------------------------
+// One warp per (row, super-block); lane l takes values 8l .. 8l+7.  amax is a
+// max (exact in any order); d = amax / 127 and the inverse 127 / amax are the
+// reference's two f32 divisions; q = round(x * inverse), ties away from zero,
+// clamped to +-127; the tail past k is zero; bsums are exact.
+__global__ void __launch_bounds__(256) q8k_quantize_kernel(const float *x, int k, int t, int nb,
+                                                           float *d, int8_t *qs, int16_t *bs) {
+    // x comes from the kernel ahead; the scratch it writes was last read by
+    // the matvecs ahead, which have completed once this wait returns
+    grid_dep_wait();
+    grid_dep_launch();
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (item >= t * nb) return;
+    const int row = item / nb, b = item % nb;
+    const float *src = x + (size_t)row * k + (size_t)b * pj::QK + lane * 8;
+    const int n = min(pj::QK, k - b * pj::QK) - lane * 8;  // this lane's values inside k
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = e < n ? src[e] : 0.0f;
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    amax = warp_max(amax);
+    const float id = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    int q[8];
+    int s = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        float r = roundf(__fmul_rn(v[e], id));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        q[e] = (int)r;
+        s += q[e];
+    }
+    uint2 packed;
+    packed.x = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)q[3] << 24);
+    packed.y = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)q[7] << 24);
+    *reinterpret_cast<uint2 *>(qs + (size_t)item * pj::QK + lane * 8) = packed;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16 values: lanes 2g, 2g + 1
+    if (!(lane & 1)) bs[(size_t)item * 16 + lane / 2] = (int16_t)s;
+    if (lane == 0) d[item] = __fdiv_rn(amax, 127.0f);
+}
+
+// ---- dots ------------------------------------------------------------------------
+__device__ __forceinline__ float f16_at(const uint8_t *p) {
+    const uint16_t h = (uint16_t)(p[0] | (p[1] << 8));
+    return __half2float(__ushort_as_half(h));
+}
+// Sum over the 8 lanes of a group (lane bits 0-2); exact for integers.
+__device__ __forceinline__ int sum8(int v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    return v;
+}
+__device__ __forceinline__ int sum32(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// 32 bytes of int8 activations, as 8 packed words
+__device__ __forceinline__ void act32(const int8_t *p, int (&a)[8]) {
+    const int4 x = *reinterpret_cast<const int4 *>(p), y = *reinterpret_cast<const int4 *>(p + 16);
+    a[0] = x.x, a[1] = x.y, a[2] = x.z, a[3] = x.w, a[4] = y.x, a[5] = y.y, a[6] = y.z, a[7] = y.w;
+}
+
+// Q4_K super-block (d, dmin, 12 bytes of 6-bit scales and mins, 128 bytes of
+// nibbles) at b (shared memory) against activation block ab: lane e of the
+// block's 8-lane group takes sub-block e (32 weights: the low nibbles of
+// bytes (e/2)*32 .. +31 for even e, the high ones for odd).  Returns the
+// term ad * (d * isum - dmin * imin) on every lane of the group.
+__device__ __forceinline__ float q4k_term(const uint8_t *b, float ad, const int8_t *aq,
+                                          const int16_t *bsum, int e) {
+    const uint8_t *scales = b + 4;
+    int sc, m;
+    if (e < 4) {
+        sc = scales[e] & 63;
+        m = scales[e + 4] & 63;
+    } else {
+        sc = (scales[e + 4] & 0xF) | ((scales[e - 4] >> 6) << 4);
+        m = (scales[e + 4] >> 4) | ((scales[e] >> 6) << 4);
+    }
+    const uint4 *wq = reinterpret_cast<const uint4 *>(b + 16 + (e >> 1) * 32);
+    const uint4 w0 = wq[0], w1 = wq[1];
+    const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    int a[8];
+    act32(aq + e * 32, a);
+    const int sh = (e & 1) * 4;
+    int dot = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dot = __dp4a((int)((wv[i] >> sh) & 0x0F0F0F0Fu), a[i], dot);
+    const int isum = sum8(sc * dot);
+    const int imin = sum8(m * ((int)bsum[2 * e] + (int)bsum[2 * e + 1]));
+    const float d = f16_at(b), dmin = f16_at(b + 2);
+    return __fmul_rn(ad, __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dmin, (float)imin)));
+}
+
+// Q6_K super-block (ql 128, qh 64, int8 scales 16, d) at b: lane e of the group
+// takes the 32 values e*32 .. e*32+31 (h = e / 4, g = e % 4), whose scales are
+// sc[h*8 + 2g] for the first 16 and sc[h*8 + 2g + 1] for the rest.
+__device__ __forceinline__ float q6k_term(const uint8_t *b, float ad, const int8_t *aq, int e) {
+    const int h = e >> 2, g = e & 3;
+    const uint8_t *ql = b + h * 64 + (g & 1) * 32, *qh = b + 128 + h * 32;
+    int a[8];
+    act32(aq + e * 32, a);
+    int dot0 = 0, dot1 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t lo = (uint32_t)ql[4 * i] | ((uint32_t)ql[4 * i + 1] << 8) |
+                            ((uint32_t)ql[4 * i + 2] << 16) | ((uint32_t)ql[4 * i + 3] << 24);
+        const uint32_t hi = (uint32_t)qh[4 * i] | ((uint32_t)qh[4 * i + 1] << 8) |
+                            ((uint32_t)qh[4 * i + 2] << 16) | ((uint32_t)qh[4 * i + 3] << 24);
+        const uint32_t low = (lo >> ((g >> 1) * 4)) & 0x0F0F0F0Fu;
+        const uint32_t high = ((hi >> (2 * g)) & 0x03030303u) << 4;
+        const int q = (int)__vsub4(low | high, 0x20202020u);  // (low | high) - 32 per byte
+        if (i < 4) dot0 = __dp4a(q, a[i], dot0);
+        else dot1 = __dp4a(q, a[i], dot1);
+    }
+    const int s0 = (int8_t)b[192 + h * 8 + 2 * g], s1 = (int8_t)b[192 + h * 8 + 2 * g + 1];
+    const int isum = sum8(s0 * dot0 + s1 * dot1);
+    return __fmul_rn(__fmul_rn(ad, f16_at(b + 208)), (float)isum);
+}
+
+// Copies `bytes` from global p (any alignment) into shared s (16-byte
+// aligned) plus p's offset within 16 bytes: whole 16-byte pieces inside the
+// range by vector loads, the ends by bytes.  Returns the row's start in s.
+__device__ __forceinline__ const uint8_t *stage_row(uint8_t *s, const uint8_t *p, size_t bytes,
+                                                    int lane) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + bytes;
+    const uintptr_t v0 = (a0 + 15) & ~(uintptr_t)15, v1 = a1 & ~(uintptr_t)15;
+    const int off = (int)(a0 & 15);
+    if (v0 < v1) {
+        for (uintptr_t a = v0 + 16 * lane; a < v1; a += 16 * 32)
+            *reinterpret_cast<uint4 *>(s + off + (a - a0)) = *reinterpret_cast<const uint4 *>(a);
+    }
+    const uintptr_t head_end = v0 < a1 ? v0 : a1;
+    for (uintptr_t a = a0 + lane; a < head_end; a += 32) s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
+    for (uintptr_t a = (v1 > head_end ? v1 : head_end) + lane; a < a1; a += 32)
+        s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
+    __syncwarp();
+    return s + off;
+}
+
+// One warp per weight row of a group of weights that share the activations
+// (Exec::matmul_group's group).  The warp stages the row in shared memory
+// with wide loads, then its four 8-lane groups take four super-blocks at a
+// time; lane 0 adds their terms to the running f32 sum in block order, for
+// each activation row of the batch.  Launched as a programmatic dependent:
+// the row is staged before the wait for the kernel ahead (the activations'
+// quantization), since the weights do not depend on it.
+constexpr int kMvWarps = 4;
+__global__ void __launch_bounds__(kMvWarps * 32)
+    matvec_group_kernel(const __grid_constant__ MatvecGroup g, int k, int nb, const float *ad,
+                        const int8_t *aq, const int16_t *abs_, int t, int row_smem) {
+    extern __shared__ __align__(16) uint8_t mv_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int r = blockIdx.x * kMvWarps + warp;
+    int p = 0;
+    while (p < g.n && r >= g.rows[p]) r -= g.rows[p++];
+    const bool live = p < g.n;
+    const uint8_t *row = nullptr;
+    if (live)
+        row = stage_row(mv_smem + warp * row_smem,
+                        static_cast<const uint8_t *>(g.w[p]) + (size_t)r * g.stride[p],
+                        g.stride[p], lane);
+    grid_dep_wait();    // the activations are quantized
+    grid_dep_launch();  // the next kernel may start staging its own weights
+    if (!live) return;
+    const int type = g.type[p], rows = g.rows[p];
+    float *out = g.out[p];
+    const int grp = lane >> 3, e = lane & 7;
+    for (int tt = 0; tt < t; ++tt) {
+        const float *adt = ad + (size_t)tt * nb;
+        const int8_t *aqt = aq + (size_t)tt * nb * pj::QK;
+        float sum = 0.0f;
+        if (type == 8) {
+            // Q8_0: lane l takes blocks l, l + 32, ...; each block's term is
+            // independent, the sum over them sequential in block order
+            const int n32 = (k + 31) / 32;
+            for (int i0 = 0; i0 < n32; i0 += 32) {
+                const int ib = i0 + lane;
+                float term = 0.0f;
+                if (ib < n32) {
+                    const uint8_t *b = row + (size_t)ib * pj::Q80_BYTES;
+                    const int blk = ib / 8;
+                    const int8_t *qa = aqt + (size_t)blk * pj::QK + (ib % 8) * 32;
+                    int dot = 0;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int w = (int)((uint32_t)b[2 + 4 * i] | ((uint32_t)b[3 + 4 * i] << 8) |
+                                            ((uint32_t)b[4 + 4 * i] << 16) |
+                                            ((uint32_t)b[5 + 4 * i] << 24));
+                        dot = __dp4a(w, *reinterpret_cast<const int *>(qa + 4 * i), dot);
+                    }
+                    term = __fmul_rn(__fmul_rn(f16_at(b), adt[blk]), (float)dot);
+                }
+                const int n = min(32, n32 - i0);
+                for (int i = 0; i < n; ++i) {
+                    const float v = __shfl_sync(0xffffffffu, term, i);
+                    if (lane == 0) sum = __fadd_rn(sum, v);
+                }
+            }
+        } else {
+            for (int ib0 = 0; ib0 < nb; ib0 += 4) {
+                // every lane runs a block (the group shuffles take all 32
+                // lanes); a group past the row's end repeats the last block
+                // and its term is dropped
+                const int ib = min(ib0 + grp, nb - 1);
+                const size_t ab = (size_t)tt * nb + ib;
+                float term = type == 12 ? q4k_term(row + (size_t)ib * pj::Q4K_BYTES, ad[ab],
+                                                   aq + ab * pj::QK, abs_ + ab * 16, e)
+                                        : q6k_term(row + (size_t)ib * pj::Q6K_BYTES, ad[ab],
+                                                   aq + ab * pj::QK, e);
+                if (ib0 + grp >= nb) term = 0.0f;
+                const int n = min(4, nb - ib0);
+                for (int i = 0; i < n; ++i) {
+                    const float v = __shfl_sync(0xffffffffu, term, 8 * i);
+                    if (lane == 0) sum = __fadd_rn(sum, v);
+                }
+            }
+        }
+        if (lane == 0) out[(size_t)tt * rows + r] = sum;
+    }
+}
+
+size_t proj_row_bytes(int ggml_type, int k) {
+    switch (ggml_type) {
+    case 12: return (size_t)((k + 255) / 256) * pj::Q4K_BYTES;
+    case 14: return (size_t)((k + 255) / 256) * pj::Q6K_BYTES;
+    case 8: return (size_t)((k + 31) / 32) * pj::Q80_BYTES;
+    default: return 0;
+    }
+}
+
+cudaError_t launch_q8k_quantize(const float *x, int t, int k, float *d, int8_t *qs, int16_t *bs,
+                                cudaStream_t st) {
+    const int nb = (k + pj::QK - 1) / pj::QK;
+    const int items = t * nb;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((items + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, q8k_quantize_kernel, x, k, t, nb, d, qs, bs);
+}
+
+cudaError_t init_matvec_kernel() {
+    return cudaFuncSetAttribute(matvec_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kMvWarps * kMatvecRowSmemMax);
+}
+
+cudaError_t launch_matvec_group(const MatvecGroup &g, int k, const float *d, const int8_t *qs,
+                                const int16_t *bs, int t, cudaStream_t st) {
+    const int nb = (k + pj::QK - 1) / pj::QK;
+    int total = 0;
+    size_t stride_max = 0;
+    for (int p = 0; p < g.n; ++p) total += g.rows[p], stride_max = max(stride_max, g.stride[p]);
+    // a row plus its offset within 16 bytes, in whole 16-byte pieces
+    const int row_smem = (int)((stride_max + 15 + 15) / 16 * 16);
+    if (row_smem > kMatvecRowSmemMax) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((total + kMvWarps - 1) / kMvWarps);
+    cfg.blockDim = dim3(kMvWarps * 32);
+    cfg.dynamicSmemBytes = (size_t)kMvWarps * row_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, matvec_group_kernel, g, k, nb, d, qs, bs, t, row_smem);
+}
+
+}  // namespace rl

@@ -48,6 +48,9 @@ struct rl_ctx {
     CUtensorMap gate_map{};
     CUtensorMap ssm_map{};  // every layer's DeltaNet state, rows of d_state f32
     bool ssm_map_ok = false;
+    // the chunk scan's operand maps (the tcgen05 scan runs when set)
+    rl::DnScanMaps dn_scan_maps{};
+    bool dn_scan_maps_ok = false;
     // chunked DeltaNet prefill scratch (slots == 1 and max_batch >= 64)
     __nv_bfloat16 *dn_qn = nullptr, *dn_kn = nullptr, *dn_vn = nullptr;
     __nv_bfloat16 *dn_qn_lo = nullptr, *dn_kn_lo = nullptr, *dn_vn_lo = nullptr;
@@ -71,8 +74,15 @@ struct rl_ctx {
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
     int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1;
     int64_t opt_wait_limit_us = 0;  // 0: rl::PEER_WAIT_LIMIT_NS
+    int64_t opt_dn_scan_tc = 1;
     // RL_OPT_WALK_SPANS: [n_full][4] {first start, CTAs done, span sum, launches}
     unsigned long long *spans = nullptr;
+    // rl_act_quantize's int8 activations (grown on demand) and their shape
+    float *act_d = nullptr;
+    int8_t *act_qs = nullptr;
+    int16_t *act_bs = nullptr;
+    size_t act_cap = 0;  // super-blocks the scratch holds
+    int act_t = 0, act_k = 0;
     // resident clusters of the f32 decode kernel: [fused][log2 cluster size]
     int max_clusters[2][4] = {};
     // resident CTAs per SM of the bf16 walk: [fused]
@@ -95,8 +105,9 @@ struct rl_ctx {
     float **xpeers = nullptr;
     std::vector<void *> xopened;
     int xrank = 0, xworld = 0;
-    unsigned xepoch = 0;
-    int *xcount = nullptr;
+    unsigned xepoch = 0;          // steps published (host side; the kernels keep their own)
+    unsigned *xepochs = nullptr;  // [n_head * 4] publishing CTAs' step counts, then
+                                  // [n_head] merging CTAs' step counts
     bool xpublish = false;  // rl_full_attn_partial called by rl_split_publish
     std::string err;
     // per-kernel timing (rl_profile_*)
@@ -215,6 +226,9 @@ void free_all(rl_ctx *x) {
     for (void *p : ps)
         if (p) cudaFree(p);
     if (x->spans) cudaFree(x->spans);
+    if (x->act_d) cudaFree(x->act_d);
+    if (x->act_qs) cudaFree(x->act_qs);
+    if (x->act_bs) cudaFree(x->act_bs);
     if (x->hpin_base) cudaFreeHost(x->hpin_base);
     if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
 }
@@ -441,6 +455,7 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     if (rl::init_full_attn_kernels() != cudaSuccess || rl::init_dn_kernels() != cudaSuccess ||
         rl::init_decode_kernels() != cudaSuccess || rl::init_decode_mma_kernels() != cudaSuccess ||
         rl::init_prefill_kernels() != cudaSuccess || rl::init_dn_chunk_kernels() != cudaSuccess ||
+        rl::init_matvec_kernel() != cudaSuccess ||
         rl::init_dn_rows_kernel() != cudaSuccess)
         return bail(fail(x, RL_ECUDA, "kernel attribute set-up failed"));
     for (int f = 0; f < 2; ++f) {
@@ -521,6 +536,17 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
             (code = alloc(x, &x->dn_ut, nv * nc * 64 * s)) || (code = alloc(x, &x->dn_gc, nv * nc)) ||
             (code = alloc(x, &x->dn_opre, mb * nv * s)))
             return bail(code);
+        const uint64_t rows = (uint64_t)nv * nc * 64;
+        rl::DnScanMaps &m = x->dn_scan_maps;
+        x->dn_scan_maps_ok =
+            rows < (1ull << 31) &&
+            rl::encode_bf16_2d(&m.w, x->dn_w, rows, s, s * 2, 64, 64) == cudaSuccess &&
+            rl::encode_bf16_2d(&m.qh, x->dn_qp, rows, s, s * 2, 64, 64) == cudaSuccess &&
+            rl::encode_bf16_2d(&m.ql, x->dn_qp_lo, rows, s, s * 2, 64, 64) == cudaSuccess &&
+            rl::encode_bf16_2d(&m.kh, x->dn_kp, rows, s, s * 2, 64, 64) == cudaSuccess &&
+            rl::encode_bf16_2d(&m.kl, x->dn_kp_lo, rows, s, s * 2, 64, 64) == cudaSuccess &&
+            rl::encode_bf16_2d(&m.ph, x->dn_p, rows, 64, 128, 64, 64) == cudaSuccess &&
+            rl::encode_bf16_2d(&m.pl, x->dn_p_lo, rows, 64, 128, 64, 64) == cudaSuccess;
     }
     // staging for the host entry points: the larger of the two paths' in+out
     const size_t full_io = mb * (2 * hd * nh + 2 * hd * c.n_head_kv + hd * nh);
@@ -581,7 +607,7 @@ void rl_ctx_destroy(rl_ctx *ctx) {
     for (void *p : ctx->xopened) cudaIpcCloseMemHandle(p);
     if (ctx->xbuf) cudaFree(ctx->xbuf);
     if (ctx->xpeers) cudaFree(ctx->xpeers);
-    if (ctx->xcount) cudaFree(ctx->xcount);
+    if (ctx->xepochs) cudaFree(ctx->xepochs);
     free_all(ctx);
     delete ctx;
 }
@@ -885,14 +911,11 @@ int rl_full_attn_partial(rl_ctx *ctx, int layer, int pos, const float *qg, const
     d.shard_lo = ctx->shard_lo;
     d.part_out = partial;
     if (ctx->xpublish) {
-        const unsigned epoch = ++ctx->xepoch;
+        ++ctx->xepoch;
         d.xpeers = ctx->xpeers;
         d.xrank = ctx->xrank;
         d.xworld = ctx->xworld;
-        d.xslot = (int)(epoch & 1);
-        d.xepoch = epoch;
-        d.xflag_off = rl::xbuf_flag_offset(ctx->xworld, c.n_head, c.head_dim);
-        d.xcount = ctx->xcount;
+        d.xepochs = ctx->xepochs;
     }
     const int64_t local = std::max<int64_t>(
         0, std::min<int64_t>((int64_t)pos + 1 - ctx->shard_lo, c.context));
@@ -911,8 +934,8 @@ int rl_exchange_init(rl_ctx *ctx, int rank, int world, void *handle_out) {
     // its own allocation, so that its IPC handle names exactly this buffer
     CK(ctx, cudaMalloc(&ctx->xbuf, bytes));
     CK(ctx, cudaMemset(ctx->xbuf, 0, bytes));
-    CK(ctx, cudaMalloc(&ctx->xcount, sizeof(int)));
-    CK(ctx, cudaMemset(ctx->xcount, 0, sizeof(int)));
+    CK(ctx, cudaMalloc(&ctx->xepochs, sizeof(unsigned) * c.n_head * 5));
+    CK(ctx, cudaMemset(ctx->xepochs, 0, sizeof(unsigned) * c.n_head * 5));
     CK(ctx, cudaMalloc(&ctx->xpeers, sizeof(float *) * world));
     ctx->xrank = rank;
     ctx->xworld = world;
@@ -992,9 +1015,10 @@ int rl_split_merge(rl_ctx *ctx, const float *qg, float *out) {
         const unsigned long long limit_ns =
             ctx->opt_wait_limit_us > 0 ? (unsigned long long)ctx->opt_wait_limit_us * 1000ull
                                        : rl::PEER_WAIT_LIMIT_NS;
-        CK(ctx, rl::launch_peer_merge(ctx->xbuf, ctx->xworld, (int)(ctx->xepoch & 1),
-                                      ctx->xepoch, ctx->cfg.n_head, qg, out, ctx->status,
-                                      limit_ns, ctx->stream));
+        CK(ctx, rl::launch_peer_merge(reinterpret_cast<const unsigned long long *>(ctx->xbuf),
+                                      ctx->xworld, ctx->cfg.n_head, qg, out,
+                                      ctx->status, ctx->xepochs + 4 * ctx->cfg.n_head, limit_ns,
+                                      ctx->stream));
     }
     ctx->prev_dn = 0;
     return RL_OK;
@@ -1268,7 +1292,8 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
         d.eps = c.rms_eps;
         {
             ProfScope ps(ctx, RL_PROF_DN_CHUNK);
-            CK(ctx, rl::launch_dn_chunk(d, ctx->stream));
+            const bool tc_scan = ctx->opt_dn_scan_tc && ctx->dn_scan_maps_ok;
+            CK(ctx, rl::launch_dn_chunk(d, tc_scan ? &ctx->dn_scan_maps : nullptr, ctx->stream));
         }
         // a step of this layer right after must not read the state early
         ctx->prev_dn = 1;
@@ -1376,6 +1401,77 @@ int rl_sync(rl_ctx *ctx) {
     return check_status(ctx);
 }
 
+// ---- projections ---------------------------------------------------------------
+
+int rl_act_quantize(rl_ctx *ctx, const float *x, int t, int k) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (!x || t < 1 || k < 1) return fail(ctx, RL_EINVAL, "x, t >= 1 and k >= 1 are required");
+    if (((uintptr_t)x) & 15) return fail(ctx, RL_EINVAL, "x must be 16-byte aligned");
+    CK(ctx, cudaSetDevice(ctx->device));
+    const size_t blocks = (size_t)t * ((k + 255) / 256);
+    if (blocks > ctx->act_cap) {
+        // grows once to the largest batch seen; a call that grows it allocates
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+        if (ctx->act_d) cudaFree(ctx->act_d);
+        if (ctx->act_qs) cudaFree(ctx->act_qs);
+        if (ctx->act_bs) cudaFree(ctx->act_bs);
+        ctx->act_d = nullptr, ctx->act_qs = nullptr, ctx->act_bs = nullptr, ctx->act_cap = 0;
+        CK(ctx, cudaMalloc((void **)&ctx->act_d, blocks * sizeof(float)));
+        CK(ctx, cudaMalloc((void **)&ctx->act_qs, blocks * 256));
+        CK(ctx, cudaMalloc((void **)&ctx->act_bs, blocks * 16 * sizeof(int16_t)));
+        ctx->act_cap = blocks;
+    }
+    CK(ctx, rl::launch_q8k_quantize(x, t, k, ctx->act_d, ctx->act_qs, ctx->act_bs, ctx->stream));
+    ctx->act_t = t;
+    ctx->act_k = k;
+    ctx->early_ok = false;
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
+
+int rl_matvec_group(rl_ctx *ctx, int n, const int *types, const void *const *ws,
+                    const int *rows, float *const *outs) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (ctx->act_k < 1) return fail(ctx, RL_EINVAL, "no activations quantized (rl_act_quantize)");
+    if (n < 1 || n > rl::kMatvecGroupMax || !types || !ws || !rows || !outs)
+        return fail(ctx, RL_EINVAL, "a group of 1 to %d weights", rl::kMatvecGroupMax);
+    rl::MatvecGroup g{};
+    g.n = n;
+    int64_t total = 0;
+    for (int p = 0; p < n; ++p) {
+        const size_t stride = rl::proj_row_bytes(types[p], ctx->act_k);
+        if (stride == 0)
+            return fail(ctx, RL_EUNSUPPORTED,
+                        "weight type %d: Q4_K (12), Q6_K (14) and Q8_0 (8) only", types[p]);
+        if (!ws[p] || !outs[p] || rows[p] < 1)
+            return fail(ctx, RL_EINVAL, "weight %d: w, out and rows >= 1 are required", p);
+        if (((uintptr_t)outs[p] & 3)) return fail(ctx, RL_EINVAL, "out must be 4-byte aligned");
+        if (types[p] == 12 && ((uintptr_t)ws[p] & 15))
+            return fail(ctx, RL_EINVAL,
+                        "Q4_K rows are read in 16-byte pieces: w must be 16-byte aligned");
+        if (stride + 30 > (size_t)rl::kMatvecRowSmemMax)
+            return fail(ctx, RL_EUNSUPPORTED, "rows of %zu bytes: at most %d", stride,
+                        rl::kMatvecRowSmemMax - 30);
+        g.type[p] = types[p];
+        g.rows[p] = rows[p];
+        g.stride[p] = stride;
+        g.w[p] = ws[p];
+        g.out[p] = outs[p];
+        total += rows[p];
+    }
+    if (total > (1 << 30)) return fail(ctx, RL_EINVAL, "too many rows in one group");
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, rl::launch_matvec_group(g, ctx->act_k, ctx->act_d, ctx->act_qs, ctx->act_bs, ctx->act_t,
+                                    ctx->stream));
+    ctx->early_ok = false;
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
+
+int rl_matvec(rl_ctx *ctx, int ggml_type, const void *w, int rows, float *out) {
+    return rl_matvec_group(ctx, 1, &ggml_type, &w, &rows, &out);
+}
+
 int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
     if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
     if (value < 0) return fail(ctx, RL_EINVAL, "option values are >= 0");
@@ -1404,6 +1500,10 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
         if (value > 60000000)
             return fail(ctx, RL_EINVAL, "a wait limit above 60 s is not a limit");
         ctx->opt_wait_limit_us = value;
+        return RL_OK;
+    case RL_OPT_DN_SCAN_TC:
+        if (value > 1) return fail(ctx, RL_EINVAL, "the scan option must be 0 or 1");
+        ctx->opt_dn_scan_tc = value;
         return RL_OK;
     case RL_OPT_WALK_SPANS:
         if (value > 1) return fail(ctx, RL_EINVAL, "the span option must be 0 or 1");
@@ -1436,6 +1536,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_DN_ROWS: return ctx->opt_dn_rows;
     case RL_OPT_WAIT_LIMIT_US: return ctx->opt_wait_limit_us;
     case RL_OPT_WALK_SPANS: return ctx->spans ? 1 : 0;
+    case RL_OPT_DN_SCAN_TC: return ctx->opt_dn_scan_tc;
     default: return -1;
     }
 }

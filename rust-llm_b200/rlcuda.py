@@ -25,7 +25,8 @@ RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED,
     0, -1, -2, -3, -4, -5, -6, -7)
 RL_KV_F32, RL_KV_BF16 = 0, 1
 (RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS, RL_OPT_CLUSTER, RL_OPT_EARLY_TILES,
- RL_OPT_VERIFY_TC, RL_OPT_DN_ROWS, RL_OPT_WAIT_LIMIT_US, RL_OPT_WALK_SPANS) = range(9)
+ RL_OPT_VERIFY_TC, RL_OPT_DN_ROWS, RL_OPT_WAIT_LIMIT_US, RL_OPT_WALK_SPANS,
+ RL_OPT_DN_SCAN_TC) = range(10)
 PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify",
                 "walk_span")
 HOST, DEVICE = 0, 1
@@ -110,6 +111,10 @@ SIGNATURES = {
     "rl_full_attn_noalloc": ([ctypes.POINTER(Config), _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp,
                               _vp, _vp], _i),
     "rl_noalloc_status": ([_vp], _i),
+    "rl_act_quantize": ([_vp, _vp, _i, _i], _i),
+    "rl_matvec": ([_vp, _i, _vp, _i, _vp], _i),
+    "rl_matvec_group": ([_vp, _i, ctypes.POINTER(_i), ctypes.POINTER(_vp), ctypes.POINTER(_i),
+                         ctypes.POINTER(_vp)], _i),
     "rl_set_shard": ([_vp, _i, _i], _i),
     "rl_full_attn_partial": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "rl_merge_partials": ([_vp, _i, _vp, _vp, _vp], _i),
@@ -298,6 +303,25 @@ class Context:
 
     def exchange_buffer(self) -> int:
         return int(self._L.rl_exchange_buffer(self._h))
+
+    # -- projections ----------------------------------------------------
+    def act_quantize(self, x, t: int, k: int):
+        """Activations::quantize_batch on device rows x [t][k]."""
+        self._check(self._L.rl_act_quantize(self._h, _ptr(x), t, k))
+
+    def matvec(self, ggml_type: int, w, rows: int, out):
+        """out [t][rows] = W . x against the last quantized activations."""
+        self._check(self._L.rl_matvec(self._h, ggml_type, _ptr(w), rows, _ptr(out)))
+
+    def matvec_group(self, parts):
+        """parts: [(ggml_type, w, rows, out)] sharing the last quantized
+        activations, one launch."""
+        n = len(parts)
+        types = (_i * n)(*[p[0] for p in parts])
+        ws = (_vp * n)(*[_ptr(p[1]) for p in parts])
+        rows = (_i * n)(*[p[2] for p in parts])
+        outs = (_vp * n)(*[_ptr(p[3]) for p in parts])
+        self._check(self._L.rl_matvec_group(self._h, n, types, ws, rows, outs))
 
     def split_publish(self, layer, pos, qg, k, v):
         self._check(self._L.rl_split_publish(self._h, layer, pos, _ptr(qg), _ptr(k), _ptr(v)))

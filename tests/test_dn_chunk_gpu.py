@@ -20,7 +20,7 @@ COS_MIN = 0.9999
 pytestmark = pytest.mark.gpu
 
 
-def run_chunked(t, seed, unit_norm=True):
+def run_chunked(t, seed, unit_norm=True, scan_tc=1):
     r = orc.Rng(seed)
     rows = cases.lin_rows(r, t)
     w = cases.lin_weights(r, unit_norm=unit_norm)
@@ -30,6 +30,7 @@ def run_chunked(t, seed, unit_norm=True):
     cfg = rlcuda.qwen35_config(n_full=0, n_linear=1, context=max(t, 64), slots=1,
                                max_batch=max(t, 64))
     with rlcuda.Context(cfg) as ctx:
+        ctx.set_option(rlcuda.RL_OPT_DN_SCAN_TC, scan_tc)
         ctx.set_weights_linear(0, w.conv1d, w.ssm_a, w.dt_bias, w.norm)
         ctx.write_conv(0, conv)
         ctx.write_ssm(0, ssm)
@@ -40,12 +41,14 @@ def run_chunked(t, seed, unit_norm=True):
     return got, want, conv_got, conv_w, ssm_got, ssm_w, chunk_launches
 
 
+@pytest.mark.parametrize("scan_tc", [1, 0], ids=["tcgen05_scan", "mma_sync_scan"])
 @pytest.mark.parametrize("t", [64, 100, 257, 1024, 4096])
-def test_chunked_prefill_matches_the_token_sequential_oracle(t):
+def test_chunked_prefill_matches_the_token_sequential_oracle(t, scan_tc):
     """t = 4096 is the benchmarked config-2 DeltaNet layer: the state is
     carried through 64 chunks, where the bf16-pair products' error would
-    grow if it were going to."""
-    got, want, conv_got, conv_w, ssm_got, ssm_w, n = run_chunked(t, 900 + t)
+    grow if it were going to.  Both chunk scans: tcgen05 (the default) and
+    mma.sync."""
+    got, want, conv_got, conv_w, ssm_got, ssm_w, n = run_chunked(t, 900 + t, scan_tc=scan_tc)
     assert n == 1, "the call did not take the chunked kernels"
     assert np.isfinite(got).all()
     err = cases.rel_err_per_head(got, want, cases.S)
