@@ -296,6 +296,12 @@ int rl_matvec(rl_ctx *ctx, int ggml_type, const void *w, int rows, float *out);
  * share the activations, e.g. a layer's qg, k and v (forward.rs:1250). */
 int rl_matvec_group(rl_ctx *ctx, int n, const int *types, const void *const *ws, const int *rows,
                     float *const *outs);
+/* Exec::matmul_group itself (forward.rs:1157-1180): x [t][k] (device)
+ * quantized and dotted with the group's n weights in one launch, the same
+ * bits as rl_act_quantize followed by rl_matvec_group (which it falls back to
+ * when the batch's quantized rows do not fit a CTA's shared memory). */
+int rl_matmul_group(rl_ctx *ctx, const float *x, int t, int k, int n, const int *types,
+                    const void *const *ws, const int *rows, float *const *outs);
 
 /* ---- full attention without allocation ---------------------------------
  * No counterpart in the reference: its runner owns all of its memory, so it

@@ -24,16 +24,21 @@
 // at 4096 tokens against 2.7e-3 for f32 products and 1.25e-2 for bf16 pairs
 // in Q K^T (the term the chunk-local kernel now takes at 24 bits).
 //
-// One CTA per value head, ten warps:
-//   warps 0-3  the chain: thread j owns state column j (tensor-memory lane j):
-//              U = Ut - acc into shared memory as a bf16 pair; after the state
-//              update, S_c as a bf16 pair for the next products, gamma S_c
-//              back into tensor memory
-//   warps 4-7  the readout: O^T from tensor memory to the output rows
-//   warp 8     TMA producer, one lane per operand (K' double-buffered; W,
+// One CTA per value head, fourteen warps:
+//   warps 0-7  the compute warps: warp w owns state column j = 32 (w % 4) +
+//              lane (tensor-memory lane j) and half w / 4 of every row it
+//              touches: U = Ut - acc into shared memory as a bf16 pair; after
+//              the state update, S_c as a bf16 pair for the next products and
+//              gamma S_c back into tensor memory
+//   warps 8-11 the readout: O^T from tensor memory to the output rows, off
+//              the chain's path (the readout accumulator is double-buffered)
+//   warp 12    TMA producer, one lane per operand (K' double-buffered; W,
 //              Q', P single, each refilled as soon as the MMAs that read it
 //              are done), and bulk L2 prefetches two chunks ahead
-//   warp 9     tensor-memory owner and MMA issuer (one lane)
+//   warp 13    tensor-memory owner and MMA issuer (one lane): U, the first
+//              readout product while the compute warps convert U (the tensor
+//              pipe is otherwise idle then), the state update, the second
+//              readout product
 // Every wait is bounded; a wait that gives up flags DEV_TIMEOUT and the roles
 // wind down (copies and MMAs in flight are waited for before the tensor
 // memory and shared memory are released).
@@ -45,8 +50,8 @@
 namespace rl {
 namespace sc {
 constexpr int S = 128, C = 64;
-constexpr int THREADS = 320;
-constexpr int PRODUCER_WARP = 8, MMA_WARP = 9;
+constexpr int THREADS = 448;
+constexpr int READOUT_WARP0 = 8, PRODUCER_WARP = 12, MMA_WARP = 13;
 constexpr uint32_t BOX64 = 64 * 128;    // 64 rows x 64 bf16 (128-byte rows, swizzled)
 constexpr uint32_t BOX128 = 128 * 128;  // 128 rows x 64 bf16
 // shared-memory byte offsets from a 1024-byte aligned base
@@ -113,9 +118,9 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         mbar_init(&q_empty, 1);
         mbar_init(&p_full, 1);
         mbar_init(&p_empty, 1);
-        mbar_init(&s_ready, 128);
+        mbar_init(&s_ready, 256);
         mbar_init(&u_done, 1);
-        mbar_init(&u_ready, 128);
+        mbar_init(&u_ready, 256);
         mbar_init(&s_done, 1);
         mbar_init(&fin, 1);
         flag_s = 0;
@@ -209,60 +214,75 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             }
         }
     } else if (warp == MMA_WARP) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer: U; the first readout while U is
+        // converted; the state update; the second readout ----------------
         if (lane == 0) {
             constexpr uint32_t id_n64 = tc::idesc_bf16(128, 64, false);
             constexpr uint32_t id_s = tc::idesc_bf16(128, 128, true);
-            const uint32_t w_s = sbase + W_OFF, q_s = sbase + Q_OFF, p_s = sbase + P_OFF,
-                           k_s = sbase + K_OFF, st_s = sbase + ST_OFF, ut_s = sbase + UT_OFF;
+            // descriptors of the operands' first 16-wide step; a step is +32 B
+            // (+2 in the descriptor) inside a box, a box +BOX64 or +BOX128
+            const uint64_t st_hi = tc::smem_desc(sbase + ST_OFF, 16, 1024);
+            const uint64_t st_lo = tc::smem_desc(sbase + ST_OFF + 2 * BOX128, 16, 1024);
+            const uint64_t ut_hi = tc::smem_desc(sbase + UT_OFF, 16, 1024);
+            const uint64_t ut_lo = tc::smem_desc(sbase + UT_OFF + BOX128, 16, 1024);
+            const uint64_t w_hi = tc::smem_desc(sbase + W_OFF, 16, 1024);
+            const uint64_t q_hi = tc::smem_desc(sbase + Q_OFF, 16, 1024);
+            const uint64_t q_lo = tc::smem_desc(sbase + Q_OFF + 2 * BOX64, 16, 1024);
+            const uint64_t p_hi = tc::smem_desc(sbase + P_OFF, 16, 1024);
+            const uint64_t p_lo = tc::smem_desc(sbase + P_OFF + BOX64, 16, 1024);
+            // K' is N-major: a 16-row step is +2 KiB; its two 64-column boxes
+            // are BOX64 apart (the leading byte offset)
+            const uint64_t k_d[2][2] = {
+                {tc::smem_desc(sbase + K_OFF, BOX64, 1024),
+                 tc::smem_desc(sbase + K_OFF + 2 * BOX64, BOX64, 1024)},
+                {tc::smem_desc(sbase + K_OFF + 4 * BOX64, BOX64, 1024),
+                 tc::smem_desc(sbase + K_OFF + 6 * BOX64, BOX64, 1024)}};
+            auto kstep = [](int kk, uint32_t box) -> uint64_t {
+                return (uint64_t)(((kk >> 2) * box + (kk & 3) * 32) >> 4);
+            };
             bool ok = true;
             for (int c = 0; c < nc && ok; ++c) {
                 const int b = c & 1;
                 const uint32_t o_acc = tmem + O_COL + b * 64;
+                // U^T = S^T_hi W_hi (K = 128: two boxes of four 16-wide steps)
                 ok = mbar_wait(&s_ready, c & 1, a.status) && mbar_wait(&w_full, c & 1, a.status);
                 if (!ok) break;
                 tc::fence_after_sync();
-                // U^T = S^T_hi W_hi (K = 128: two boxes of four 16-wide steps)
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * BOX128 + (kk & 3) * 32;
-                    const uint32_t offb = (kk >> 2) * BOX64 + (kk & 3) * 32;
-                    tc::mma_ss(tmem + U_COL, tc::smem_desc(st_s + off, 16, 1024),
-                               tc::smem_desc(w_s + offb, 16, 1024), id_n64, kk > 0);
-                }
+                for (int kk = 0; kk < 8; ++kk)
+                    tc::mma_ss(tmem + U_COL, st_hi + kstep(kk, BOX128), w_hi + kstep(kk, BOX64),
+                               id_n64, kk > 0);
                 tc::commit(&u_done);
                 tc::commit(&w_empty);
-                // O^T = S^T Q'^T, three terms
+                // O^T = S^T Q'^T (three terms), in the tensor pipe's idle time
+                // while the compute warps convert U
                 ok = (c < 2 || mbar_wait(&o_empty[b], ((c >> 1) - 1) & 1, a.status)) &&
                      mbar_wait(&q_full, c & 1, a.status);
                 if (!ok) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int term = 0; term < 3; ++term) {
-                    const uint32_t sa = st_s + (term == 2 ? 2 * BOX128 : 0);  // S lo for term 2
-                    const uint32_t qb = q_s + (term == 1 ? 2 * BOX64 : 0);    // Q' lo for term 1
+                    const uint64_t sa = term == 2 ? st_lo : st_hi;
+                    const uint64_t qb = term == 1 ? q_lo : q_hi;
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t off = (kk >> 2) * BOX128 + (kk & 3) * 32;
-                        const uint32_t offb = (kk >> 2) * BOX64 + (kk & 3) * 32;
-                        tc::mma_ss(o_acc, tc::smem_desc(sa + off, 16, 1024),
-                                   tc::smem_desc(qb + offb, 16, 1024), id_n64, term > 0 || kk > 0);
-                    }
+                    for (int kk = 0; kk < 8; ++kk)
+                        tc::mma_ss(o_acc, sa + kstep(kk, BOX128), qb + kstep(kk, BOX64), id_n64,
+                                   term > 0 || kk > 0);
                 }
                 tc::commit(&q_empty);
-                // the state update as soon as U is in shared memory
+                // the state update as soon as U is in shared memory:
+                // S^T += U^T_hi (K'_hi + K'_lo); its completion also covers
+                // everything above, so S^T's shared copy is free then
                 ok = mbar_wait(&u_ready, c & 1, a.status) &&
                      mbar_wait(&k_full[b], (c >> 1) & 1, a.status);
                 if (!ok) break;
                 tc::fence_after_sync();
 #pragma unroll
-                for (int term = 0; term < 2; ++term) {
-                    const uint32_t kb = k_s + b * 4 * BOX64 + term * 2 * BOX64;  // K' hi, then lo
+                for (int term = 0; term < 2; ++term)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        tc::mma_ss(tmem + S_COL, tc::smem_desc(ut_s + kk * 32, 16, 1024),
-                                   tc::smem_desc(kb + kk * 16 * 128, BOX64, 1024), id_s, true);
-                }
+                        tc::mma_ss(tmem + S_COL, ut_hi + kk * 2, k_d[b][term] + kk * 128, id_s,
+                                   true);
                 tc::commit(&k_empty[b]);
                 tc::commit(&s_done);
                 // O^T += U^T P^T, three terms
@@ -271,12 +291,11 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                 tc::fence_after_sync();
 #pragma unroll
                 for (int term = 0; term < 3; ++term) {
-                    const uint32_t ua = ut_s + (term == 2 ? BOX128 : 0);
-                    const uint32_t pb = p_s + (term == 1 ? BOX64 : 0);
+                    const uint64_t ua = term == 2 ? ut_lo : ut_hi;
+                    const uint64_t pb = term == 1 ? p_lo : p_hi;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        tc::mma_ss(o_acc, tc::smem_desc(ua + kk * 32, 16, 1024),
-                                   tc::smem_desc(pb + kk * 32, 16, 1024), id_n64, true);
+                        tc::mma_ss(o_acc, ua + kk * 2, pb + kk * 2, id_n64, true);
                 }
                 tc::commit(&p_empty);
                 tc::commit(&o_full[b]);
@@ -286,27 +305,31 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             tc::commit(&fin);
             mbar_wait(&fin, 0, a.status);
         }
-    } else if (warp < 4) {
-        // ---------------- the chain: thread j owns state column j ----------------
-        const int j = tid;
-        const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-        unsigned char *st_hi = smem + ST_OFF, *st_lo = smem + ST_OFF + 2 * BOX128;
+    } else if (warp < READOUT_WARP0) {
+        // ---------------- the compute warps: warp w owns state column
+        // j = 32 (w % 4) + lane (tensor-memory lane j) and the half w / 4 of
+        // each row it converts or reads out ----------------
+        const int q4 = warp & 3, hf = warp >> 2, j = q4 * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+        unsigned char *st_hi = smem + ST_OFF + hf * BOX128, *st_lo = st_hi + 2 * BOX128;
         unsigned char *ut_hi = smem + UT_OFF, *ut_lo = smem + UT_OFF + BOX128;
         bool ok = true;
-        // S_{-1}: its bf16 pair for the first products, gamma_0 S into tensor memory
+        // S_{-1}: its bf16 pair for the first products, gamma_0 S into tensor
+        // memory (this warp: state rows i of its half)
         {
             const float g0 = a.gc[blk0];
 #pragma unroll 1
-            for (int q = 0; q < 4; ++q) {
+            for (int h = 0; h < 2; ++h) {
+                const int i0 = hf * 64 + h * 32;
                 float x[32];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) x[e] = state[(size_t)(q * 32 + e) * S + j];
-                put32(st_hi + (q >> 1) * BOX128, j, (q & 1) * 4, x, false);
-                put32(st_lo + (q >> 1) * BOX128, j, (q & 1) * 4, x, true);
+                for (int e = 0; e < 32; ++e) x[e] = state[(size_t)(i0 + e) * S + j];
+                put32(st_hi, j, h * 4, x, false);
+                put32(st_lo, j, h * 4, x, true);
                 uint32_t r[32];
 #pragma unroll
                 for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(x[e] * g0);
-                tc::st32(tmem + lane_addr + S_COL + q * 32, r);
+                tc::st32(tmem + lane_addr + S_COL + i0, r);
             }
             tc::wait_st();
             fence_proxy_async_smem();
@@ -315,24 +338,24 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         }
         for (int c = 0; c < nc && ok; ++c) {
             const size_t blk = blk0 + c;
-            const float *ut = a.ut + blk * C * S + j;
-            // ---- U = Ut - S W, into shared memory as a bf16 pair (Ut's
-            // column j is read while the MMAs run: 64 loads, coalesced over j)
-            float x[64];
+            const int b = c & 1;
+            // ---- U = Ut - S W for this warp's 32 tokens, into shared memory
+            // as a bf16 pair (Ut's column j is read while the MMAs run)
+            const float *ut = a.ut + blk * C * S + (size_t)(hf * 32) * S + j;
+            float x[32];
 #pragma unroll
-            for (int e = 0; e < 64; ++e) x[e] = __ldcg(ut + (size_t)e * S);
+            for (int e = 0; e < 32; ++e) x[e] = __ldcg(ut + (size_t)e * S);
             ok = mbar_wait(&u_done, c & 1, a.status);
             if (!ok) break;
             tc::fence_after_sync();
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            {
                 uint32_t r[32];
-                tc::ld32(tmem + lane_addr + U_COL + h * 32, r);
+                tc::ld32(tmem + lane_addr + U_COL + hf * 32, r);
                 tc::wait_ld();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) x[h * 32 + e] -= __uint_as_float(r[e]);
-                put32(ut_hi, j, h * 4, x + h * 32, false);
-                put32(ut_lo, j, h * 4, x + h * 32, true);
+                for (int e = 0; e < 32; ++e) x[e] -= __uint_as_float(r[e]);
+                put32(ut_hi, j, hf * 4, x, false);
+                put32(ut_lo, j, hf * 4, x, true);
             }
             fence_proxy_async_smem();
             tc::fence_before_sync();
@@ -345,21 +368,22 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             const bool more = c + 1 < nc;
             const float gn = more ? a.gc[blk + 1] : 1.0f;
 #pragma unroll 1
-            for (int q = 0; q < 4; ++q) {
+            for (int h = 0; h < 2; ++h) {
+                const int i0 = hf * 64 + h * 32;
                 uint32_t r[32];
-                tc::ld32(tmem + lane_addr + S_COL + q * 32, r);
+                tc::ld32(tmem + lane_addr + S_COL + i0, r);
                 tc::wait_ld();
-                float x[32];
-                as_f32(r, x);
+                float y[32];
+                as_f32(r, y);
                 if (more) {
-                    put32(st_hi + (q >> 1) * BOX128, j, (q & 1) * 4, x, false);
-                    put32(st_lo + (q >> 1) * BOX128, j, (q & 1) * 4, x, true);
+                    put32(st_hi, j, h * 4, y, false);
+                    put32(st_lo, j, h * 4, y, true);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(x[e] * gn);
-                    tc::st32(tmem + lane_addr + S_COL + q * 32, r);
+                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(y[e] * gn);
+                    tc::st32(tmem + lane_addr + S_COL + i0, r);
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) state[(size_t)(q * 32 + e) * S + j] = x[e];
+                    for (int e = 0; e < 32; ++e) state[(size_t)(i0 + e) * S + j] = y[e];
                 }
             }
             if (more) {
@@ -371,8 +395,9 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         }
         if (!ok) flag_s = 1;
     } else {
-        // ---------------- the readout: O^T rows to the output ----------------
-        const int j = tid - 128, q4 = warp - 4;
+        // ---------------- the readout warps: O^T rows to the output, a
+        // chunk behind the chain; warp 8 + q owns state columns 32q .. ----------------
+        const int q4 = warp - READOUT_WARP0, j = q4 * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
         const float scale = 1.0f / sqrtf((float)S);
         for (int c = 0; c < nc; ++c) {

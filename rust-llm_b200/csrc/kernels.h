@@ -256,6 +256,13 @@ struct MatvecGroup {
 // 16384 for Q8_0, the largest row of the reference's tests).
 constexpr int kMatvecRowSmemMax = 17456;
 cudaError_t init_matvec_kernel();
+// Exec::matmul_group in one launch (quantization of x [t][k] included), when
+// its shared memory fits: the quantized rows plus two staged weight rows per
+// warp.
+constexpr int kMatmulSmemMax = 200 * 1024;
+size_t matmul_group_smem(int t, int k, size_t stride_max);
+cudaError_t launch_matmul_group(const MatvecGroup &g, const float *x, int t, int k,
+                                cudaStream_t st);
 cudaError_t launch_matvec_group(const MatvecGroup &g, int k, const float *d, const int8_t *qs,
                                 const int16_t *bs, int t, cudaStream_t st);
 

@@ -145,6 +145,35 @@ __device__ __forceinline__ float q6k_term(const uint8_t *b, float ad, const int8
     return __fmul_rn(__fmul_rn(ad, f16_at(b + 208)), (float)isum);
 }
 
+__device__ __forceinline__ void pj_cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void pj_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void pj_cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// stage_row with the whole 16-byte pieces as asynchronous copies in this
+// lane's current group (commit and wait before reading them); the ends, by
+// bytes, are in place on return.
+__device__ __forceinline__ const uint8_t *stage_row_async(uint8_t *s, const uint8_t *p,
+                                                          size_t bytes, int lane) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + bytes;
+    const uintptr_t v0 = (a0 + 15) & ~(uintptr_t)15, v1 = a1 & ~(uintptr_t)15;
+    const int off = (int)(a0 & 15);
+    if (v0 < v1) {
+        for (uintptr_t a = v0 + 16 * lane; a < v1; a += 16 * 32)
+            pj_cp_async16(s + off + (a - a0), reinterpret_cast<const void *>(a));
+    }
+    const uintptr_t head_end = v0 < a1 ? v0 : a1;
+    for (uintptr_t a = a0 + lane; a < head_end; a += 32) s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
+    for (uintptr_t a = (v1 > head_end ? v1 : head_end) + lane; a < a1; a += 32)
+        s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
+    return s + off;
+}
+
 // Copies `bytes` from global p (any alignment) into shared s (16-byte
 // aligned) plus p's offset within 16 bytes: whole 16-byte pieces inside the
 // range by vector loads, the ends by bytes.  Returns the row's start in s.
@@ -165,33 +194,15 @@ __device__ __forceinline__ const uint8_t *stage_row(uint8_t *s, const uint8_t *p
     return s + off;
 }
 
-// One warp per weight row of a group of weights that share the activations
-// (Exec::matmul_group's group).  The warp stages the row in shared memory
-// with wide loads, then its four 8-lane groups take four super-blocks at a
-// time; lane 0 adds their terms to the running f32 sum in block order, for
-// each activation row of the batch.  Launched as a programmatic dependent:
-// the row is staged before the wait for the kernel ahead (the activations'
-// quantization), since the weights do not depend on it.
-constexpr int kMvWarps = 4;
-__global__ void __launch_bounds__(kMvWarps * 32)
-    matvec_group_kernel(const __grid_constant__ MatvecGroup g, int k, int nb, const float *ad,
-                        const int8_t *aq, const int16_t *abs_, int t, int row_smem) {
-    extern __shared__ __align__(16) uint8_t mv_smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int r = blockIdx.x * kMvWarps + warp;
-    int p = 0;
-    while (p < g.n && r >= g.rows[p]) r -= g.rows[p++];
-    const bool live = p < g.n;
-    const uint8_t *row = nullptr;
-    if (live)
-        row = stage_row(mv_smem + warp * row_smem,
-                        static_cast<const uint8_t *>(g.w[p]) + (size_t)r * g.stride[p],
-                        g.stride[p], lane);
-    grid_dep_wait();    // the activations are quantized
-    grid_dep_launch();  // the next kernel may start staging its own weights
-    if (!live) return;
-    const int type = g.type[p], rows = g.rows[p];
-    float *out = g.out[p];
+// One weight row against t activation rows: the row staged at `row`
+// (shared memory), the activations' d / quants / block sums at ad / aq / abs_
+// (global or shared memory, [t][nb], [t][nb][256], [t][nb][16]).  The warp's
+// four 8-lane groups take four super-blocks at a time (lane e of a group
+// sub-block e); lane 0 adds their terms to the running f32 sum in block
+// order, and writes out[tt * rows + r].
+__device__ __forceinline__ void row_dots(const uint8_t *row, int type, int k, int nb,
+                                         const float *ad, const int8_t *aq, const int16_t *abs_,
+                                         int t, int rows, int r, float *out, int lane) {
     const int grp = lane >> 3, e = lane & 7;
     for (int tt = 0; tt < t; ++tt) {
         const float *adt = ad + (size_t)tt * nb;
@@ -247,6 +258,116 @@ __global__ void __launch_bounds__(kMvWarps * 32)
     }
 }
 
+// Weight row `gr` of the group: its part, its row within the part, its bytes.
+struct GroupRow {
+    int p, r;
+    const uint8_t *bytes;
+};
+__device__ __forceinline__ GroupRow group_row(const MatvecGroup &g, int gr) {
+    int p = 0;
+    while (p < g.n && gr >= g.rows[p]) gr -= g.rows[p++];
+    GroupRow out{p, gr, nullptr};
+    if (p < g.n) out.bytes = static_cast<const uint8_t *>(g.w[p]) + (size_t)gr * g.stride[p];
+    return out;
+}
+
+// One warp per weight row against activations already quantized (by
+// q8k_quantize_kernel).  Launched as a programmatic dependent: the row is
+// staged before the wait for the kernel ahead (the quantization), since the
+// weights do not depend on it.
+constexpr int kMvWarps = 4;
+__global__ void __launch_bounds__(kMvWarps * 32)
+    matvec_group_kernel(const __grid_constant__ MatvecGroup g, int k, int nb, const float *ad,
+                        const int8_t *aq, const int16_t *abs_, int t, int row_smem) {
+    extern __shared__ __align__(16) uint8_t mv_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const GroupRow gr = group_row(g, blockIdx.x * kMvWarps + warp);
+    const bool live = gr.p < g.n;
+    const uint8_t *row = nullptr;
+    if (live) row = stage_row(mv_smem + warp * row_smem, gr.bytes, g.stride[gr.p], lane);
+    grid_dep_wait();    // the activations are quantized
+    grid_dep_launch();  // the next kernel may start staging its own weights
+    if (!live) return;
+    row_dots(row, g.type[gr.p], k, nb, ad, aq, abs_, t, g.rows[gr.p], gr.r, g.out[gr.p], lane);
+}
+
+// Exec::matmul_group in one launch: every CTA quantizes the t activation rows
+// into its shared memory (the same bits in every CTA: the quantization is a
+// function of the values alone), then each warp walks `rpw` weight rows,
+// staging the next row while it dots the current one.  The first rows are
+// staged before the programmatic-dependency wait.
+__global__ void __launch_bounds__(kMvWarps * 32)
+    matmul_group_kernel(const __grid_constant__ MatvecGroup g, const float *x, int k, int nb,
+                        int t, int row_smem, int rpw, int total) {
+    extern __shared__ __align__(16) uint8_t mm_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int items = t * nb;
+    int8_t *aq = reinterpret_cast<int8_t *>(mm_smem);
+    float *ad = reinterpret_cast<float *>(mm_smem + (size_t)items * pj::QK);
+    int16_t *abs_ = reinterpret_cast<int16_t *>(mm_smem + (size_t)items * (pj::QK + 4));
+    uint8_t *rows_s = mm_smem + (((size_t)items * (pj::QK + 4 + 32) + 15) / 16 * 16) +
+                      (size_t)warp * 2 * row_smem;
+    const int r0 = (blockIdx.x * kMvWarps + warp) * rpw;
+    GroupRow cur = group_row(g, min(r0, total - 1));
+    const uint8_t *row = nullptr;
+    if (r0 < total) row = stage_row_async(rows_s, cur.bytes, g.stride[cur.p], lane);
+    pj_cp_commit();
+    grid_dep_wait();    // x comes from the kernel ahead
+    grid_dep_launch();
+    // the activations, as q8k_quantize_kernel quantizes them
+    for (int item = warp; item < items; item += kMvWarps) {
+        const int rr = item / nb, b = item % nb;
+        const float *src = x + (size_t)rr * k + (size_t)b * pj::QK + lane * 8;
+        const int n = min(pj::QK, k - b * pj::QK) - lane * 8;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = i < n ? src[i] : 0.0f;
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = warp_max(amax);
+        const float id = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        int q[8], sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float f = roundf(__fmul_rn(v[i], id));
+            f = fminf(fmaxf(f, -127.0f), 127.0f);
+            q[i] = (int)f;
+            sum += q[i];
+        }
+        uint2 packed;
+        packed.x = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)q[3] << 24);
+        packed.y = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)q[7] << 24);
+        *reinterpret_cast<uint2 *>(aq + (size_t)item * pj::QK + lane * 8) = packed;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (!(lane & 1)) abs_[(size_t)item * 16 + lane / 2] = (int16_t)sum;
+        if (lane == 0) ad[item] = __fdiv_rn(amax, 127.0f);
+    }
+    __syncthreads();
+    for (int i = 0; i < rpw; ++i) {
+        const int gr_i = r0 + i;
+        if (gr_i >= total) break;
+        // stage the next row into the other buffer while this one is dotted
+        GroupRow nxt{};
+        const uint8_t *row_n = nullptr;
+        const bool more = gr_i + 1 < total && i + 1 < rpw;
+        if (more) {
+            nxt = group_row(g, gr_i + 1);
+            row_n = stage_row_async(rows_s + ((i + 1) & 1) * row_smem, nxt.bytes,
+                                    g.stride[nxt.p], lane);
+        }
+        pj_cp_commit();
+        pj_cp_wait<1>();  // this row's copies (the next row's may be in flight)
+        __syncwarp();
+        row_dots(row, g.type[cur.p], k, nb, ad, aq, abs_, t, g.rows[cur.p], cur.r, g.out[cur.p],
+                 lane);
+        __syncwarp();
+        cur = nxt;
+        row = row_n;
+    }
+    pj_cp_wait<0>();  // nothing in flight when the CTA's memory is released
+}
+
 size_t proj_row_bytes(int ggml_type, int k) {
     switch (ggml_type) {
     case 12: return (size_t)((k + 255) / 256) * pj::Q4K_BYTES;
@@ -273,8 +394,48 @@ cudaError_t launch_q8k_quantize(const float *x, int t, int k, float *d, int8_t *
 }
 
 cudaError_t init_matvec_kernel() {
-    return cudaFuncSetAttribute(matvec_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kMvWarps * kMatvecRowSmemMax);
+    cudaError_t e = cudaFuncSetAttribute(matvec_group_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kMvWarps * kMatvecRowSmemMax);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(matmul_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMatmulSmemMax);
+    return e;
+}
+
+size_t matmul_group_smem(int t, int k, size_t stride_max) {
+    const size_t items = (size_t)t * ((k + pj::QK - 1) / pj::QK);
+    const size_t row_smem = (stride_max + 15 + 15) / 16 * 16;
+    return (items * (pj::QK + 4 + 32) + 15) / 16 * 16 + (size_t)kMvWarps * 2 * row_smem;
+}
+
+cudaError_t launch_matmul_group(const MatvecGroup &g, const float *x, int t, int k,
+                                cudaStream_t st) {
+    const int nb = (k + pj::QK - 1) / pj::QK;
+    int total = 0;
+    size_t stride_max = 0;
+    for (int p = 0; p < g.n; ++p) total += g.rows[p], stride_max = max(stride_max, g.stride[p]);
+    const size_t smem = matmul_group_smem(t, k, stride_max);
+    if (smem > (size_t)kMatmulSmemMax) return cudaErrorInvalidValue;
+    const int row_smem = (int)((stride_max + 15 + 15) / 16 * 16);
+    // rows per warp: about two waves of 16 four-warp CTAs per SM
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int warps_wanted = sms * 16 * kMvWarps;
+    const int rpw = max(1, min(8, (total + warps_wanted - 1) / warps_wanted));
+    const int warps = (total + rpw - 1) / rpw;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((warps + kMvWarps - 1) / kMvWarps);
+    cfg.blockDim = dim3(kMvWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, matmul_group_kernel, g, x, k, nb, t, row_smem, rpw, total);
 }
 
 cudaError_t launch_matvec_group(const MatvecGroup &g, int k, const float *d, const int8_t *qs,

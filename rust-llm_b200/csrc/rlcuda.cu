@@ -59,6 +59,7 @@ struct rl_ctx {
     float *dn_lg = nullptr, *dn_bt = nullptr;
     __nv_bfloat16 *dn_w = nullptr, *dn_qp = nullptr, *dn_kp = nullptr, *dn_p = nullptr;
     float *dn_ut = nullptr, *dn_gc = nullptr, *dn_opre = nullptr;
+    float *stage_raw = nullptr;  // the status word (64 B), then the staging
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
     // pinned host staging for the *_host entry points (calls of up to
@@ -220,7 +221,7 @@ void free_all(rl_ctx *x) {
     x->ev_pool.clear();
     void *ps[] = {x->kv, x->conv, x->ssm, x->q_norm, x->k_norm, x->conv1d, x->ssm_a,
                   x->dt_bias, x->ssm_norm, x->q_f32, x->q_bf16, x->gate_bf16, x->part_o, x->part_ml,
-                  x->counters, x->rope_cs, x->rope_sn, x->stage, x->status,
+                  x->counters, x->rope_cs, x->rope_sn, x->stage_raw,
                   x->dn_qn, x->dn_kn, x->dn_vn, x->dn_qn_lo, x->dn_kn_lo, x->dn_vn_lo, x->dn_qn_l2, x->dn_kn_l2, x->dn_w_lo, x->dn_qp_lo, x->dn_kp_lo, x->dn_p_lo, x->dn_lg, x->dn_bt, x->dn_w, x->dn_qp, x->dn_kp,
                   x->dn_p, x->dn_ut, x->dn_gc, x->dn_opre};
     for (void *p : ps)
@@ -291,6 +292,22 @@ int reset_spans(rl_ctx *x) {
     for (int l = 0; l < x->cfg.n_full; ++l) h[4 * l] = ~0ull;
     CK(x, cudaStreamSynchronize(x->stream));
     CK(x, cudaMemcpy(x->spans, h.data(), h.size() * sizeof(h[0]), cudaMemcpyHostToDevice));
+    return RL_OK;
+}
+
+// The end of a pinned host call: the status word and the output that follows
+// it in the staging, back in one copy and one wait.
+int finish_host_call(rl_ctx *x, size_t out_floats) {
+    CK(x, cudaMemcpyAsync(x->hpin_base, x->stage_raw, 64 + out_floats * sizeof(float),
+                          cudaMemcpyDeviceToHost, x->stream));
+    CK(x, cudaStreamSynchronize(x->stream));
+    const int st = *x->hstatus;
+    if (st) {
+        CK(x, cudaMemsetAsync(x->status, 0, sizeof(int), x->stream));
+        if (st & rl::DEV_TIMEOUT)
+            return fail(x, RL_ETIMEOUT, "a kernel's bounded wait gave up (status %d)", st);
+        return fail(x, RL_EINVAL, "a kernel flagged a bad argument (status %d)", st);
+    }
     return RL_OK;
 }
 
@@ -473,8 +490,7 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         (code = alloc(x, &x->conv1d, (size_t)c.n_linear * cd * c.conv_kernel)) ||
         (code = alloc(x, &x->ssm_a, (size_t)c.n_linear * c.n_v_heads)) ||
         (code = alloc(x, &x->dt_bias, (size_t)c.n_linear * c.n_v_heads)) ||
-        (code = alloc(x, &x->ssm_norm, (size_t)c.n_linear * s)) ||
-        (code = alloc(x, &x->status, 1)))
+        (code = alloc(x, &x->ssm_norm, (size_t)c.n_linear * s)))
         return bail(code);
     if (c.n_full > 0) {
         x->part_rows = std::max<int64_t>(mb, 4 * (int64_t)x->num_sms);
@@ -552,7 +568,12 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
     const size_t full_io = mb * (2 * hd * nh + 2 * hd * c.n_head_kv + hd * nh);
     const size_t lin_io = mb * (cd + 2 * s * c.n_v_heads + 2 * c.n_v_heads);
     x->stage_floats = std::max(c.n_full ? full_io : 0, c.n_linear ? lin_io : 0);
-    if ((code = alloc(x, &x->stage, x->stage_floats))) return bail(code);
+    // the status word heads the staging, so that a host call's output and the
+    // status behind it come back in one copy: [status, 64 B][output][inputs]
+    if ((code = alloc(x, &x->stage_raw, x->stage_floats + 16))) return bail(code);
+    x->status = reinterpret_cast<int *>(x->stage_raw);
+    x->stage = x->stage_raw + 16;
+    CK(x, cudaMemsetAsync(x->status, 0, sizeof(int), x->stream));
     {
         // pinned staging for calls of up to 64 rows (without it, the host
         // entry points copy from and to the callers' buffers directly)
@@ -1205,12 +1226,12 @@ int rl_full_attn_host(rl_ctx *ctx, int layer, int pos, int t, const float *qg, c
     const size_t nqg = (size_t)t * 2 * c.head_dim * c.n_head;
     const size_t nk = (size_t)t * c.head_dim * c.n_head_kv;
     const size_t no = (size_t)t * c.head_dim * c.n_head;
-    float *dq = ctx->stage, *dk = dq + nqg, *dv = dk + nk, *dout = dv + nk;
+    float *dout = ctx->stage, *dq = dout + no, *dk = dq + nqg, *dv = dk + nk;
     if (ctx->hpin && t <= ctx->hpin_rows) {
         // the inputs packed in the pinned staging in the device staging's
         // order (the previous call's copies have completed: every call ends
-        // in a wait), one copy in, one out
-        float *hp = ctx->hpin, *hout = hp + nqg + 2 * nk;
+        // in a wait), one copy in; the status word and the output, one copy out
+        float *hout = ctx->hpin, *hp = hout + no;
         std::memcpy(hp, qg, nqg * 4);
         std::memcpy(hp + nqg, k, nk * 4);
         std::memcpy(hp + nqg + nk, v, nk * 4);
@@ -1220,8 +1241,7 @@ int rl_full_attn_host(rl_ctx *ctx, int layer, int pos, int t, const float *qg, c
             cudaStreamSynchronize(ctx->stream);  // the staging's copy is done before reuse
             return code;
         }
-        CK(ctx, cudaMemcpyAsync(hout, dout, no * 4, cudaMemcpyDeviceToHost, ctx->stream));
-        code = check_status(ctx);
+        code = finish_host_call(ctx, no);
         std::memcpy(out, hout, no * 4);
         return code;
     }
@@ -1346,10 +1366,10 @@ int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qk
     CK(ctx, cudaSetDevice(ctx->device));
     const size_t nx = (size_t)t * conv_dim(c), nz = (size_t)t * c.n_v_heads * c.d_state;
     const size_t ng = (size_t)t * c.n_v_heads;
-    float *dx = ctx->stage, *dz = dx + nx, *da = dz + nz, *db = da + ng, *dout = db + ng;
+    float *dout = ctx->stage, *dx = dout + nz, *dz = dx + nx, *da = dz + nz, *db = da + ng;
     if (ctx->hpin && t <= ctx->hpin_rows) {
         // as rl_full_attn_host: packed pinned inputs, one copy in, one out
-        float *hp = ctx->hpin, *hout = hp + nx + nz + 2 * ng;
+        float *hout = ctx->hpin, *hp = hout + nz;
         std::memcpy(hp, qkv, nx * 4);
         std::memcpy(hp + nx, z, nz * 4);
         std::memcpy(hp + nx + nz, alpha, ng * 4);
@@ -1361,8 +1381,7 @@ int rl_linear_attn_host(rl_ctx *ctx, int layer, int live, int t, const float *qk
             cudaStreamSynchronize(ctx->stream);  // the staging's copy is done before reuse
             return code;
         }
-        CK(ctx, cudaMemcpyAsync(hout, dout, nz * 4, cudaMemcpyDeviceToHost, ctx->stream));
-        code = check_status(ctx);
+        code = finish_host_call(ctx, nz);
         std::memcpy(out, hout, nz * 4);
         return code;
     }
@@ -1429,17 +1448,17 @@ int rl_act_quantize(rl_ctx *ctx, const float *x, int t, int k) {
     return RL_OK;
 }
 
-int rl_matvec_group(rl_ctx *ctx, int n, const int *types, const void *const *ws,
-                    const int *rows, float *const *outs) {
-    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
-    if (ctx->act_k < 1) return fail(ctx, RL_EINVAL, "no activations quantized (rl_act_quantize)");
+namespace {
+// The group's parts checked and packed (rows of k values each).
+int make_group(rl_ctx *ctx, int k, int n, const int *types, const void *const *ws,
+               const int *rows, float *const *outs, rl::MatvecGroup *g) {
     if (n < 1 || n > rl::kMatvecGroupMax || !types || !ws || !rows || !outs)
         return fail(ctx, RL_EINVAL, "a group of 1 to %d weights", rl::kMatvecGroupMax);
-    rl::MatvecGroup g{};
-    g.n = n;
+    *g = rl::MatvecGroup{};
+    g->n = n;
     int64_t total = 0;
     for (int p = 0; p < n; ++p) {
-        const size_t stride = rl::proj_row_bytes(types[p], ctx->act_k);
+        const size_t stride = rl::proj_row_bytes(types[p], k);
         if (stride == 0)
             return fail(ctx, RL_EUNSUPPORTED,
                         "weight type %d: Q4_K (12), Q6_K (14) and Q8_0 (8) only", types[p]);
@@ -1452,17 +1471,50 @@ int rl_matvec_group(rl_ctx *ctx, int n, const int *types, const void *const *ws,
         if (stride + 30 > (size_t)rl::kMatvecRowSmemMax)
             return fail(ctx, RL_EUNSUPPORTED, "rows of %zu bytes: at most %d", stride,
                         rl::kMatvecRowSmemMax - 30);
-        g.type[p] = types[p];
-        g.rows[p] = rows[p];
-        g.stride[p] = stride;
-        g.w[p] = ws[p];
-        g.out[p] = outs[p];
+        g->type[p] = types[p];
+        g->rows[p] = rows[p];
+        g->stride[p] = stride;
+        g->w[p] = ws[p];
+        g->out[p] = outs[p];
         total += rows[p];
     }
     if (total > (1 << 30)) return fail(ctx, RL_EINVAL, "too many rows in one group");
+    return RL_OK;
+}
+}  // namespace
+
+int rl_matvec_group(rl_ctx *ctx, int n, const int *types, const void *const *ws,
+                    const int *rows, float *const *outs) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (ctx->act_k < 1) return fail(ctx, RL_EINVAL, "no activations quantized (rl_act_quantize)");
+    rl::MatvecGroup g;
+    const int code = make_group(ctx, ctx->act_k, n, types, ws, rows, outs, &g);
+    if (code) return code;
     CK(ctx, cudaSetDevice(ctx->device));
     CK(ctx, rl::launch_matvec_group(g, ctx->act_k, ctx->act_d, ctx->act_qs, ctx->act_bs, ctx->act_t,
                                     ctx->stream));
+    ctx->early_ok = false;
+    ctx->prev_dn = 0;
+    return RL_OK;
+}
+
+int rl_matmul_group(rl_ctx *ctx, const float *x, int t, int k, int n, const int *types,
+                    const void *const *ws, const int *rows, float *const *outs) {
+    if (!ctx) return fail(nullptr, RL_EINVAL, "NULL context");
+    if (!x || t < 1 || k < 1) return fail(ctx, RL_EINVAL, "x, t >= 1 and k >= 1 are required");
+    if (((uintptr_t)x) & 15) return fail(ctx, RL_EINVAL, "x must be 16-byte aligned");
+    rl::MatvecGroup g;
+    int code = make_group(ctx, k, n, types, ws, rows, outs, &g);
+    if (code) return code;
+    size_t stride_max = 0;
+    for (int p = 0; p < n; ++p) stride_max = std::max(stride_max, g.stride[p]);
+    if (rl::matmul_group_smem(t, k, stride_max) > (size_t)rl::kMatmulSmemMax) {
+        // too many activation rows to quantize in every CTA: two launches
+        if ((code = rl_act_quantize(ctx, x, t, k))) return code;
+        return rl_matvec_group(ctx, n, types, ws, rows, outs);
+    }
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, rl::launch_matmul_group(g, x, t, k, ctx->stream));
     ctx->early_ok = false;
     ctx->prev_dn = 0;
     return RL_OK;

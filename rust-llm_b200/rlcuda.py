@@ -115,6 +115,8 @@ SIGNATURES = {
     "rl_matvec": ([_vp, _i, _vp, _i, _vp], _i),
     "rl_matvec_group": ([_vp, _i, ctypes.POINTER(_i), ctypes.POINTER(_vp), ctypes.POINTER(_i),
                          ctypes.POINTER(_vp)], _i),
+    "rl_matmul_group": ([_vp, _vp, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_vp),
+                         ctypes.POINTER(_i), ctypes.POINTER(_vp)], _i),
     "rl_set_shard": ([_vp, _i, _i], _i),
     "rl_full_attn_partial": ([_vp, _i, _i, _vp, _vp, _vp, _vp], _i),
     "rl_merge_partials": ([_vp, _i, _vp, _vp, _vp], _i),
@@ -322,6 +324,16 @@ class Context:
         rows = (_i * n)(*[p[2] for p in parts])
         outs = (_vp * n)(*[_ptr(p[3]) for p in parts])
         self._check(self._L.rl_matvec_group(self._h, n, types, ws, rows, outs))
+
+    def matmul_group(self, x, t: int, k: int, parts):
+        """Exec::matmul_group: x [t][k] quantized and dotted with every
+        (ggml_type, w, rows, out) of parts, one launch."""
+        n = len(parts)
+        types = (_i * n)(*[p[0] for p in parts])
+        ws = (_vp * n)(*[_ptr(p[1]) for p in parts])
+        rows = (_i * n)(*[p[2] for p in parts])
+        outs = (_vp * n)(*[_ptr(p[3]) for p in parts])
+        self._check(self._L.rl_matmul_group(self._h, _ptr(x), t, k, n, types, ws, rows, outs))
 
     def split_publish(self, layer, pos, qg, k, v):
         self._check(self._L.rl_split_publish(self._h, layer, pos, _ptr(qg), _ptr(k), _ptr(v)))

@@ -88,6 +88,27 @@ def test_a_group_gives_each_weight_its_own_result(ctx):
         assert np.array_equal(out.cpu().numpy(), orc.matvec(ty, w, rows, k, xs)), ty
 
 
+@pytest.mark.parametrize("t", [1, 3])
+def test_the_one_launch_group_matches_the_two_launch_path(ctx, t):
+    """rl_matmul_group (quantization inside the launch) gives the bits of
+    rl_act_quantize + rl_matvec_group, over groups of mixed types and row
+    counts that leave warps with partial row runs."""
+    dev = torch.device("cuda", 0)
+    for k in (2560, 4096, 300):
+        parts = []
+        for i, (ty, rows) in enumerate([(pc.Q4_K, 2051), (pc.Q6_K, 130), (pc.Q8_0, 33)]):
+            w, _ = pc.shape_case(ty, k, rows, 0x900 + i + k)
+            parts.append((ty, torch.from_numpy(w).to(dev), rows,
+                          torch.full((t, rows), float("nan"), device=dev), w))
+        rng = pc.XorShift(k + t)
+        xs = (rng.signed_n(t * k) * np.float32(3.0)).reshape(t, k)
+        ctx.matmul_group(torch.from_numpy(xs).to(dev), t, k, [p[:4] for p in parts])
+        ctx.sync()
+        for ty, _, rows, out, w in parts:
+            assert np.array_equal(out.cpu().numpy(), orc.matvec(ty, w, rows, k, xs, threads=8)), \
+                (ty, k, t)
+
+
 def test_zero_inputs_give_zero(ctx):
     k = 512
     for ty in pc.TYPES:
