@@ -652,14 +652,12 @@ __global__ void __launch_bounds__(256) peer_merge_kernel(const unsigned long lon
                                                          unsigned long long limit_ns) {
     grid_dep_launch();  // the next layer's walk may start streaming meanwhile
     __shared__ float m_s[RL_EXCHANGE_MAX_GPUS], l_s[RL_EXCHANGE_MAX_GPUS];
-    __shared__ int late_s;
     const int hh = blockIdx.x, d = threadIdx.x;
     const unsigned E = epochs[hh] + 1;  // written last by this CTA's previous step
     const size_t stride = (size_t)rows_heads * (dm::HD + 2);
     const unsigned long long *p0 = xbuf + (size_t)(E & 1) * world * stride + (size_t)hh * (dm::HD + 2);
     const unsigned long long start = globaltimer_ns();
     bool late = false;
-    if (d == 0) late_s = 0;
     if ((d & 31) < world && d < 64) {
         const int g = d & 31;
         const float v = xload(p0 + g * stride + dm::HD + (d >> 5), E, start, limit_ns, late);
@@ -669,9 +667,7 @@ __global__ void __launch_bounds__(256) peer_merge_kernel(const unsigned long lon
 #pragma unroll
     for (int g = 0; g < RL_EXCHANGE_MAX_GPUS; ++g)
         if (g < world) vals[g] = xload(p0 + g * stride + d, E, start, limit_ns, late);
-    if (late) late_s = 1;
-    __syncthreads();
-    if (d == 0 && late_s) atomicOr(status, DEV_TIMEOUT);
+    if (__syncthreads_or(late) && d == 0) atomicOr(status, DEV_TIMEOUT);
     float M = -INFINITY;
     for (int g = 0; g < world; ++g) M = fmaxf(M, m_s[g]);
     float L = 0.0f, o = 0.0f;

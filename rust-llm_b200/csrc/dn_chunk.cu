@@ -266,21 +266,28 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     const int t0 = ck * C, rows = min(C, a.t - t0);
 
     // ---- operands of the chunk (rows past the batch are zero): every copy
-    // in flight at once
+    // in flight at once, in two groups: q and k (the first products) and v
+    // (needed only for Ut, after T)
 #pragma unroll 2
     for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
         const bool ok = r < rows;
         const size_t ko = ((size_t)(t0 + (ok ? r : 0)) * a.n_k + kh) * S + c8;
-        const size_t vo = ((size_t)(t0 + (ok ? r : 0)) * a.n_v + vh) * S + c8;
         cp_async16_zfill(&sm.k[r][c8], a.kn + ko, ok);
         cp_async16_zfill(&sm.q[r][c8], a.qn + ko, ok);
         cp_async16_zfill(&sm.kl[r][c8], a.kn_lo + ko, ok);
         cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
-        cp_async16_zfill(&sm.v[r][c8], a.vn + vo, ok);
-        cp_async16_zfill(&sm.vl[r][c8], a.vn_lo + vo, ok);
         cp_async16_zfill(&sm.k2[r][c8], a.kn_l2 + ko, ok);
         cp_async16_zfill(&sm.q2[r][c8], a.qn_l2 + ko, ok);
+    }
+    cp_async_commit();
+#pragma unroll 2
+    for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
+        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+        const bool ok = r < rows;
+        const size_t vo = ((size_t)(t0 + (ok ? r : 0)) * a.n_v + vh) * S + c8;
+        cp_async16_zfill(&sm.v[r][c8], a.vn + vo, ok);
+        cp_async16_zfill(&sm.vl[r][c8], a.vn_lo + vo, ok);
     }
     cp_async_commit();
     if (warp == 0) {
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
         sm.beta[ta] = ta < rows ? a.bt[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
         sm.beta[tb] = tb < rows ? a.bt[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
     }
-    cp_async_wait<0>();
+    cp_async_wait<1>();  // q and k (v may still be in flight)
     __syncthreads();
     // ---- K K^T as hi*hi + hi*lo + lo*hi of the bf16 pairs, and Q K^T of
     // the bf16 triples (hi*hi + hi*lo + lo*hi + lo*lo + hi*l2 + l2*hi): the
@@ -358,6 +365,61 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
         }
     }
     __syncthreads();
+    const size_t blk = (size_t)vh * a.nc + ck;
+    // ---- P = Q K^T o Mgamma (s <= t), Q' = gamma Q, K' = gamma_C / gamma K:
+    // written now, so that the stores drain while T is built
+    // (8 consecutive elements a thread: 16-byte stores)
+    __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
+#pragma unroll 2
+    for (int e8 = tid; e8 < C * C / 8; e8 += LOCAL_THREADS) {
+        const int r = e8 / (C / 8), s0 = (e8 % (C / 8)) * 8;
+        const float cr = sm.cum[r];
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int sa = s0 + 2 * k, sb = sa + 1;
+            const float x0 = sa <= r ? sm.qk[r][sa] * __expf(cr - sm.cum[sa]) : 0.0f;
+            const float x1 = sb <= r ? sm.qk[r][sb] * __expf(cr - sm.cum[sb]) : 0.0f;
+            hi[k] = pack_bf16(x0, x1);
+            lo[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+        }
+        *reinterpret_cast<uint4 *>(p_out + r * C + s0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(pl_out + r * C + s0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    const float cum_c = sm.cum[C - 1];
+    __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
+    __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
+#pragma unroll 2
+    for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
+        const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
+        const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
+        const uint4 qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
+        const uint4 ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
+        const uint4 kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
+        const uint4 kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
+        const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
+        const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
+        const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
+        const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
+        uint32_t xh[4], xl[4], yh[4], yl[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
+            const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
+            const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
+            const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
+            xh[k] = pack_bf16(x0, x1);
+            xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+            yh[k] = pack_bf16(y0, y1);
+            yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
+        }
+        const size_t o = (size_t)r * S + c0;
+        *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+        *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+        *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+        *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
+    }
+    if (tid == 0) a.gc[blk] = __expf(cum_c);
     // ---- L (in place over kk) and T = (I + L)^-1, one column per thread
     {
         // this thread's column s is fixed (the CTA is a multiple of C)
@@ -448,9 +510,9 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
             sm.tb_lo[r][s] = __float2bfloat16_rn(y - yh);
         }
     }
+    cp_async_wait<0>();  // v
     __syncthreads();
     // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows, 64 cols)
-    const size_t blk = (size_t)vh * a.nc + ck;
     float *ut_out = a.ut + blk * C * S;
     __nv_bfloat16 *w_out = a.w + blk * C * S, *wl_out = a.w_lo + blk * C * S;
     const int r0 = (warp & 3) * 16 + (lane >> 2), c0 = (lane & 3) * 2;
@@ -497,63 +559,13 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
                 const float x0 = dw[n][2 * e2], x1 = dw[n][2 * e2 + 1];
                 const size_t o = (size_t)(r0 + 8 * e2) * S + col;
                 *reinterpret_cast<uint32_t *>(w_out + o) = pack_bf16(x0, x1);
-                *reinterpret_cast<uint32_t *>(wl_out + o) = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+                if (a.w_lo_out)  // only the mma.sync scan reads W's low half
+                    *reinterpret_cast<uint32_t *>(wl_out + o) =
+                        pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
             }
         }
     }
-    // ---- P = Q K^T o Mgamma (s <= t), Q' = gamma Q, K' = gamma_C / gamma K
-    // (8 consecutive elements a thread: 16-byte stores)
-    __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
-#pragma unroll 2
-    for (int e8 = tid; e8 < C * C / 8; e8 += LOCAL_THREADS) {
-        const int r = e8 / (C / 8), s0 = (e8 % (C / 8)) * 8;
-        const float cr = sm.cum[r];
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int sa = s0 + 2 * k, sb = sa + 1;
-            const float x0 = sa <= r ? sm.qk[r][sa] * __expf(cr - sm.cum[sa]) : 0.0f;
-            const float x1 = sb <= r ? sm.qk[r][sb] * __expf(cr - sm.cum[sb]) : 0.0f;
-            hi[k] = pack_bf16(x0, x1);
-            lo[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
-        }
-        *reinterpret_cast<uint4 *>(p_out + r * C + s0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4 *>(pl_out + r * C + s0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    }
-    const float cum_c = sm.cum[C - 1];
-    __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
-    __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
-#pragma unroll 2
-    for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
-        const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
-        const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
-        const uint4 qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
-        const uint4 ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
-        const uint4 kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
-        const uint4 kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
-        const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
-        const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
-        const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
-        const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
-        uint32_t xh[4], xl[4], yh[4], yl[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
-            const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
-            const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
-            const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
-            xh[k] = pack_bf16(x0, x1);
-            xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
-            yh[k] = pack_bf16(y0, y1);
-            yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
-        }
-        const size_t o = (size_t)r * S + c0;
-        *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
-        *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
-        *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
-        *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
-    }
-    if (tid == 0) a.gc[blk] = __expf(cum_c);
+
 }
 
 // ---------------------------------------------------------------------------
@@ -856,8 +868,10 @@ cudaError_t init_dn_chunk_kernels() {
     return e;
 }
 
-cudaError_t launch_dn_chunk(const DnChunkArgs &a, const DnScanMaps *scan_maps, cudaStream_t st) {
+cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps, cudaStream_t st) {
     using namespace dc;
+    DnChunkArgs a = a_in;
+    a.w_lo_out = scan_maps == nullptr;
     dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
                      st>>>(a);
     dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);

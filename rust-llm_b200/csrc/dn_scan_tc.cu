@@ -13,8 +13,9 @@
 //   U^T[j][t]  = sum_i S^T[j][i] W[t][i]          (A = S^T, B = W, both K-major)
 //   O^T[j][t]  = sum_i S^T[j][i] Q'[t][i] + sum_s U^T[j][s] P[t][s]
 //   S^T[j][i] += sum_t U^T[j][t] K'[t][i]         (B = K', N-major)
-// S^T accumulates in tensor memory in f32 for the whole scan; only its bf16
-// copy for the next chunk's products goes through registers and shared memory.
+// The state stays in the compute threads' registers in f32 for the whole scan
+// (S_c = gamma_C S_{c-1} + D with D = K'^T U from tensor memory); its bf16
+// copy for the next chunk's products goes through shared memory.
 //
 // Precision (bf16 operands as pairs x = hi + lo where it matters): W S is one
 // hi*hi term (the delta rule's feedback corrects it: U = Ut - W S feeds S
@@ -27,9 +28,9 @@
 // One CTA per value head, fourteen warps:
 //   warps 0-7  the compute warps: warp w owns state column j = 32 (w % 4) +
 //              lane (tensor-memory lane j) and half w / 4 of every row it
-//              touches: U = Ut - acc into shared memory as a bf16 pair; after
-//              the state update, S_c as a bf16 pair for the next products and
-//              gamma S_c back into tensor memory
+//              touches: U = Ut - acc into shared memory as a bf16 pair; then
+//              S_c = gamma_C S_{c-1} + D in registers, and S_c as a bf16 pair
+//              for the next products
 //   warps 8-11 the readout: O^T from tensor memory to the output rows, off
 //              the chain's path (the readout accumulator is double-buffered)
 //   warp 12    TMA producer, one lane per operand (K' double-buffered; W,
@@ -270,9 +271,10 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                                    term > 0 || kk > 0);
                 }
                 tc::commit(&q_empty);
-                // the state update as soon as U is in shared memory:
-                // S^T += U^T_hi (K'_hi + K'_lo); its completion also covers
-                // everything above, so S^T's shared copy is free then
+                // the state update's product as soon as U is in shared memory:
+                // D = U^T_hi (K'_hi + K'_lo) (the compute warps add gamma_C S);
+                // its completion also covers everything above, so S^T's
+                // shared copy is free then
                 ok = mbar_wait(&u_ready, c & 1, a.status) &&
                      mbar_wait(&k_full[b], (c >> 1) & 1, a.status);
                 if (!ok) break;
@@ -282,7 +284,7 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         tc::mma_ss(tmem + S_COL, ut_hi + kk * 2, k_d[b][term] + kk * 128, id_s,
-                                   true);
+                                   term > 0 || kk > 0);
                 tc::commit(&k_empty[b]);
                 tc::commit(&s_done);
                 // O^T += U^T P^T, three terms
@@ -314,37 +316,27 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         unsigned char *st_hi = smem + ST_OFF + hf * BOX128, *st_lo = st_hi + 2 * BOX128;
         unsigned char *ut_hi = smem + UT_OFF, *ut_lo = smem + UT_OFF + BOX128;
         bool ok = true;
-        // S_{-1}: its bf16 pair for the first products, gamma_0 S into tensor
-        // memory (this warp: state rows i of its half)
-        {
-            const float g0 = a.gc[blk0];
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-                const int i0 = hf * 64 + h * 32;
-                float x[32];
+        // the state in registers, f32: this thread's 64 values S[i][j] of its
+        // half; S_{-1} from the slot, its bf16 pair for the first products
+        float sv[64];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) x[e] = state[(size_t)(i0 + e) * S + j];
-                put32(st_hi, j, h * 4, x, false);
-                put32(st_lo, j, h * 4, x, true);
-                uint32_t r[32];
-#pragma unroll
-                for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(x[e] * g0);
-                tc::st32(tmem + lane_addr + S_COL + i0, r);
-            }
-            tc::wait_st();
-            fence_proxy_async_smem();
-            tc::fence_before_sync();
-            mbar_arrive(&s_ready);
-        }
+        for (int e = 0; e < 64; ++e) sv[e] = state[(size_t)(hf * 64 + e) * S + j];
+        put32(st_hi, j, 0, sv, false);
+        put32(st_lo, j, 0, sv, true);
+        put32(st_hi, j, 4, sv + 32, false);
+        put32(st_lo, j, 4, sv + 32, true);
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        mbar_arrive(&s_ready);
         for (int c = 0; c < nc && ok; ++c) {
             const size_t blk = blk0 + c;
-            const int b = c & 1;
             // ---- U = Ut - S W for this warp's 32 tokens, into shared memory
             // as a bf16 pair (Ut's column j is read while the MMAs run)
             const float *ut = a.ut + blk * C * S + (size_t)(hf * 32) * S + j;
             float x[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) x[e] = __ldcg(ut + (size_t)e * S);
+            const float gc = a.gc[blk];
             ok = mbar_wait(&u_done, c & 1, a.status);
             if (!ok) break;
             tc::fence_after_sync();
@@ -360,37 +352,33 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             fence_proxy_async_smem();
             tc::fence_before_sync();
             mbar_arrive(&u_ready);
-            // ---- S_c: its pair for the next chunk, gamma_{c+1} S_c back into
-            // tensor memory, or out to the state after the last chunk
+            // ---- S_c = gamma_C S_{c-1} + D, D = K'^T U from tensor memory; its
+            // pair for the next chunk, or the state after the last chunk
             ok = mbar_wait(&s_done, c & 1, a.status);
             if (!ok) break;
             tc::fence_after_sync();
-            const bool more = c + 1 < nc;
-            const float gn = more ? a.gc[blk + 1] : 1.0f;
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-                const int i0 = hf * 64 + h * 32;
-                uint32_t r[32];
-                tc::ld32(tmem + lane_addr + S_COL + i0, r);
+            {
+                uint32_t r0[32], r1[32];
+                tc::ld32(tmem + lane_addr + S_COL + hf * 64, r0);
+                tc::ld32(tmem + lane_addr + S_COL + hf * 64 + 32, r1);
                 tc::wait_ld();
-                float y[32];
-                as_f32(r, y);
-                if (more) {
-                    put32(st_hi, j, h * 4, y, false);
-                    put32(st_lo, j, h * 4, y, true);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(y[e] * gn);
-                    tc::st32(tmem + lane_addr + S_COL + i0, r);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) state[(size_t)(i0 + e) * S + j] = y[e];
+                for (int e = 0; e < 32; ++e) {
+                    sv[e] = fmaf(gc, sv[e], __uint_as_float(r0[e]));
+                    sv[32 + e] = fmaf(gc, sv[32 + e], __uint_as_float(r1[e]));
                 }
             }
-            if (more) {
-                tc::wait_st();
+            tc::fence_before_sync();  // D is read: the next update may overwrite it
+            if (c + 1 < nc) {
+                put32(st_hi, j, 0, sv, false);
+                put32(st_lo, j, 0, sv, true);
+                put32(st_hi, j, 4, sv + 32, false);
+                put32(st_lo, j, 4, sv + 32, true);
                 fence_proxy_async_smem();
-                tc::fence_before_sync();
                 mbar_arrive(&s_ready);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 64; ++e) state[(size_t)(hf * 64 + e) * S + j] = sv[e];
             }
         }
         if (!ok) flag_s = 1;

@@ -214,6 +214,7 @@ struct DnChunkArgs {
     int *status;
     int t, nc, n_k, n_v, live, slots;
     float eps;
+    bool w_lo_out;  // write W's low half (the mma.sync scan reads it)
 };
 cudaError_t init_dn_chunk_kernels();
 // The chunk scan on tcgen05 (dn_scan_tc.cu) reads the chunk-local kernel's
