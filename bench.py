@@ -29,6 +29,7 @@ runs it.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import subprocess
@@ -305,15 +306,28 @@ def dn_step_bench(args, dev, stream, rlcuda, torch):
     h_al.copy_(al.cpu().view(DN_LAYERS, 1, -1))
     h_be.copy_(be.cpu().view(DN_LAYERS, 1, -1))
     nq, nz, na, nb = h_qkv.numpy(), h_z.numpy(), h_al.numpy(), h_be.numpy()
+    h_o = torch.empty((DN_LAYERS, 1, 4096), pin_memory=True)
+    no = h_o.numpy()
+    # the C ABI's host entry point itself, pointers made once
+    host_call = rlcuda.lib().rl_linear_attn_host
+    f32p = ctypes.POINTER(ctypes.c_float)
+    host_args = [tuple(a[layer].ctypes.data_as(f32p) for a in (nq, nz, na, nb, no))
+                 for layer in range(DN_LAYERS)]
+
+    def e2e_layer(layer):
+        code = host_call(ctx.handle, layer, 0, 1, *host_args[layer])
+        if code:
+            raise rlcuda.RlError(code, "rl_linear_attn_host")
+
     for layer in range(DN_LAYERS):  # warm
-        ctx.linear_attn_host(layer, 0, nq[layer], nz[layer], na[layer], nb[layer])
+        e2e_layer(layer)
     e2e_steps = max(3, min(args.steps // 50, 50))
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         for layer in range(DN_LAYERS):
-            last = ctx.linear_attn_host(layer, 0, nq[layer], nz[layer], na[layer], nb[layer])
+            e2e_layer(layer)
     e2e_us = (time.perf_counter() - t0) * 1e6 / (e2e_steps * DN_LAYERS)
-    assert np.isfinite(last).all()
+    assert np.isfinite(no).all()
     ctx.close()
     peak, _ = peaks()
     gbs = DN_BYTES_PER_LAYER / (us * 1e-6) / 1e9
@@ -325,7 +339,7 @@ def dn_step_bench(args, dev, stream, rlcuda, torch):
             "e2e": {"value": e2e_us, "unit": "us/layer",
                     "h2d_bytes_per_layer": 4 * (8192 + 4096 + 64),
                     "d2h_bytes_per_layer": 4 * 4096,
-                    "how": "rl_linear_attn_host per layer, pinned host buffers, host clock"}}
+                    "how": "rl_linear_attn_host (the C ABI) per layer, pinned host buffers, host clock"}}
 
 
 PF_T = 4096
@@ -703,8 +717,8 @@ def split_kv_bench(args, world, rank, dev, stream, rlcuda, torch, dist):
     us = ms * 1e3 / (reps * N_LAYERS)
     local_bytes = 2 * N_KV * n * HD * 2
     return {"workload": "config 4a: 1 sequence x 131072 positions, 8 layers, bf16 cache split "
-                        f"across {world} GPU(s); partials exchanged through peer memory (NVLink "
-                        "stores + flags, merged on every GPU)",
+                        f"across {world} GPU(s); partials exchanged through peer memory (64-bit "
+                        "value+epoch stores over NVLink, merged on every GPU)",
             "scaling": "strong", "us_per_layer": us,
             "nccl_us_per_layer": nccl_ms * 1e3 / (reps * N_LAYERS) if nccl_ms else None,
             "walk_us_per_layer": walk_ms * 1e3 / (reps * N_LAYERS),
@@ -958,11 +972,20 @@ def run_ours(args):
     h_qg.copy_(qg.cpu())
     h_k.copy_(kk.cpu())
     h_v.copy_(vv.cpu())
-    n_qg, n_k, n_v = h_qg.numpy(), h_k.numpy(), h_v.numpy()
+    n_qg, n_k, n_v, n_out = h_qg.numpy(), h_k.numpy(), h_v.numpy(), h_out.numpy()
+    # N = 1: the C ABI's host entry point itself, as the reference's Runner
+    # would call it (pointers made once; no per-call Python marshalling)
+    host_call = rlcuda.lib().rl_full_attn_host
+    f32p = ctypes.POINTER(ctypes.c_float)
+    host_args = [tuple(a[layer].ctypes.data_as(f32p) for a in (n_qg, n_k, n_v, n_out))
+                 for layer in range(N_LAYERS)]
 
     def e2e_layer(layer):
         if world == 1:
-            return ctx.full_attn_host(layer, pos, n_qg[layer], n_k[layer], n_v[layer])
+            code = host_call(ctx.handle, layer, pos, 1, *host_args[layer])
+            if code:
+                raise rlcuda.RlError(code, "rl_full_attn_host")
+            return n_out[layer]
         with torch.cuda.stream(stream):
             qg[layer].copy_(h_qg[layer], non_blocking=True)
             kk[layer].copy_(h_k[layer], non_blocking=True)
@@ -1040,8 +1063,11 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "how": "host clock around every layer's pinned copy in, the call and the copy "
-                       "of its output back"},
+                "how": "host clock around every layer's call of rl_full_attn_host (the C ABI: "
+                       "pinned host inputs copied in, the kernels, the output copied back)"
+                       if world == 1 else
+                       "host clock around every layer's pinned copies in, the split call and "
+                       "the copy of its output back"},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "prefill_tflops": pf["tflops_layer"] if pf else None,

@@ -155,9 +155,11 @@ __device__ __forceinline__ void pj_cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// stage_row with the whole 16-byte pieces as asynchronous copies in this
-// lane's current group (commit and wait before reading them); the ends, by
-// bytes, are in place on return.
+// Copies `bytes` from global p (any alignment) into shared s (16-byte
+// aligned) plus p's offset within 16 bytes: the whole 16-byte pieces inside
+// the range as asynchronous copies in this lane's current group (commit and
+// wait before reading them), the ends by bytes, in place on return.  Returns
+// the row's start in s.
 __device__ __forceinline__ const uint8_t *stage_row_async(uint8_t *s, const uint8_t *p,
                                                           size_t bytes, int lane) {
     const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + bytes;
@@ -171,26 +173,6 @@ __device__ __forceinline__ const uint8_t *stage_row_async(uint8_t *s, const uint
     for (uintptr_t a = a0 + lane; a < head_end; a += 32) s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
     for (uintptr_t a = (v1 > head_end ? v1 : head_end) + lane; a < a1; a += 32)
         s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
-    return s + off;
-}
-
-// Copies `bytes` from global p (any alignment) into shared s (16-byte
-// aligned) plus p's offset within 16 bytes: whole 16-byte pieces inside the
-// range by vector loads, the ends by bytes.  Returns the row's start in s.
-__device__ __forceinline__ const uint8_t *stage_row(uint8_t *s, const uint8_t *p, size_t bytes,
-                                                    int lane) {
-    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + bytes;
-    const uintptr_t v0 = (a0 + 15) & ~(uintptr_t)15, v1 = a1 & ~(uintptr_t)15;
-    const int off = (int)(a0 & 15);
-    if (v0 < v1) {
-        for (uintptr_t a = v0 + 16 * lane; a < v1; a += 16 * 32)
-            *reinterpret_cast<uint4 *>(s + off + (a - a0)) = *reinterpret_cast<const uint4 *>(a);
-    }
-    const uintptr_t head_end = v0 < a1 ? v0 : a1;
-    for (uintptr_t a = a0 + lane; a < head_end; a += 32) s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
-    for (uintptr_t a = (v1 > head_end ? v1 : head_end) + lane; a < a1; a += 32)
-        s[off + (a - a0)] = *reinterpret_cast<const uint8_t *>(a);
-    __syncwarp();
     return s + off;
 }
 
@@ -284,9 +266,13 @@ __global__ void __launch_bounds__(kMvWarps * 32)
     const GroupRow gr = group_row(g, blockIdx.x * kMvWarps + warp);
     const bool live = gr.p < g.n;
     const uint8_t *row = nullptr;
-    if (live) row = stage_row(mv_smem + warp * row_smem, gr.bytes, g.stride[gr.p], lane);
+    // asynchronous copies: every piece of the row in flight at once
+    if (live) row = stage_row_async(mv_smem + warp * row_smem, gr.bytes, g.stride[gr.p], lane);
+    pj_cp_commit();
     grid_dep_wait();    // the activations are quantized
     grid_dep_launch();  // the next kernel may start staging its own weights
+    pj_cp_wait<0>();
+    __syncwarp();
     if (!live) return;
     row_dots(row, g.type[gr.p], k, nb, ad, aq, abs_, t, g.rows[gr.p], gr.r, g.out[gr.p], lane);
 }
