@@ -252,6 +252,9 @@ struct MatvecGroup {
     size_t stride[kMatvecGroupMax];
     const void *w[kMatvecGroupMax];
     float *out[kMatvecGroupMax];
+    // set by the one-launch kernel's launcher: rows per warp of each part and
+    // the first warp of each part (wfirst[n] = the warps in all)
+    int rpw[kMatvecGroupMax], wfirst[kMatvecGroupMax + 1];
 };
 // A weight row is staged in shared memory: at most this many bytes (k up to
 // 16384 for Q8_0, the largest row of the reference's tests).

@@ -13,6 +13,8 @@
 // batch's activation rows dotted against them while they are in registers.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -94,7 +96,7 @@ __device__ __forceinline__ void act32(const int8_t *p, int (&a)[8]) {
 // bytes (e/2)*32 .. +31 for even e, the high ones for odd).  Returns the
 // term ad * (d * isum - dmin * imin) on every lane of the group.
 __device__ __forceinline__ float q4k_term(const uint8_t *b, float ad, const int8_t *aq,
-                                          const int16_t *bsum, int e) {
+                                          const int16_t *bsum, int e, int swz) {
     const uint8_t *scales = b + 4;
     int sc, m;
     if (e < 4) {
@@ -108,7 +110,7 @@ __device__ __forceinline__ float q4k_term(const uint8_t *b, float ad, const int8
     const uint4 w0 = wq[0], w1 = wq[1];
     const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     int a[8];
-    act32(aq + e * 32, a);
+    act32(aq + (e ^ swz) * 32, a);
     const int sh = (e & 1) * 4;
     int dot = 0;
 #pragma unroll
@@ -122,11 +124,12 @@ __device__ __forceinline__ float q4k_term(const uint8_t *b, float ad, const int8
 // Q6_K super-block (ql 128, qh 64, int8 scales 16, d) at b: lane e of the group
 // takes the 32 values e*32 .. e*32+31 (h = e / 4, g = e % 4), whose scales are
 // sc[h*8 + 2g] for the first 16 and sc[h*8 + 2g + 1] for the rest.
-__device__ __forceinline__ float q6k_term(const uint8_t *b, float ad, const int8_t *aq, int e) {
+__device__ __forceinline__ float q6k_term(const uint8_t *b, float ad, const int8_t *aq, int e,
+                                          int swz) {
     const int h = e >> 2, g = e & 3;
     const uint8_t *ql = b + h * 64 + (g & 1) * 32, *qh = b + 128 + h * 32;
     int a[8];
-    act32(aq + e * 32, a);
+    act32(aq + (e ^ swz) * 32, a);
     int dot0 = 0, dot1 = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -181,7 +184,10 @@ __device__ __forceinline__ const uint8_t *stage_row_async(uint8_t *s, const uint
 // (global or shared memory, [t][nb], [t][nb][256], [t][nb][16]).  The warp's
 // four 8-lane groups take four super-blocks at a time (lane e of a group
 // sub-block e); lane 0 adds their terms to the running f32 sum in block
-// order, and writes out[tt * rows + r].
+// order, and writes out[tt * rows + r].  SWZ: the activations sit in the
+// one-launch kernel's shared memory, where 32-byte unit u of block b is
+// stored at unit u ^ (b & 7).
+template <bool SWZ>
 __device__ __forceinline__ void row_dots(const uint8_t *row, int type, int k, int nb,
                                          const float *ad, const int8_t *aq, const int16_t *abs_,
                                          int t, int rows, int r, float *out, int lane) {
@@ -200,7 +206,8 @@ __device__ __forceinline__ void row_dots(const uint8_t *row, int type, int k, in
                 if (ib < n32) {
                     const uint8_t *b = row + (size_t)ib * pj::Q80_BYTES;
                     const int blk = ib / 8;
-                    const int8_t *qa = aqt + (size_t)blk * pj::QK + (ib % 8) * 32;
+                    const int8_t *qa =
+                        aqt + (size_t)blk * pj::QK + ((ib % 8) ^ (SWZ ? blk & 7 : 0)) * 32;
                     int dot = 0;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -224,10 +231,11 @@ __device__ __forceinline__ void row_dots(const uint8_t *row, int type, int k, in
                 // and its term is dropped
                 const int ib = min(ib0 + grp, nb - 1);
                 const size_t ab = (size_t)tt * nb + ib;
+                const int swz = SWZ ? ib & 7 : 0;
                 float term = type == 12 ? q4k_term(row + (size_t)ib * pj::Q4K_BYTES, ad[ab],
-                                                   aq + ab * pj::QK, abs_ + ab * 16, e)
+                                                   aq + ab * pj::QK, abs_ + ab * 16, e, swz)
                                         : q6k_term(row + (size_t)ib * pj::Q6K_BYTES, ad[ab],
-                                                   aq + ab * pj::QK, e);
+                                                   aq + ab * pj::QK, e, swz);
                 if (ib0 + grp >= nb) term = 0.0f;
                 const int n = min(4, nb - ib0);
                 for (int i = 0; i < n; ++i) {
@@ -237,6 +245,103 @@ __device__ __forceinline__ void row_dots(const uint8_t *row, int type, int k, in
             }
         }
         if (lane == 0) out[(size_t)tt * rows + r] = sum;
+    }
+}
+
+// Q4_K rows with one lane per super-block: lane l takes block b = l % nb of
+// row j = l / nb (32 / nb rows a warp) when nb <= 32, else blocks l, l + 32,
+// ... of one row.  The lane runs the whole block's integer dot (eight
+// sub-blocks of 32 weights, dp4a) and its f32 term alone, so no shuffle
+// reduction is spent on a block; the row's terms are then added in block
+// order by the row's first lane, as the reference adds them.  The rows are
+// staged contiguously at `span` (shared memory, 16-byte aligned, `stride`
+// bytes apart); the activations sit in shared memory in the swizzled layout
+// (32-byte unit u of block b at unit u ^ (b & 7)).
+__device__ __forceinline__ float q4k_block(const uint8_t *blk, int ab, int bsw, const float *ad,
+                                           const int8_t *aq, const int16_t *abs_) {
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);  // d, dmin, 12 scale bytes
+    const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+    auto byte_at = [](uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFF); };
+    const int8_t *a = aq + (size_t)ab * pj::QK;
+    const uint32_t *bs = reinterpret_cast<const uint32_t *>(abs_ + (size_t)ab * 16);
+    int isum = 0, imin = 0;
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) {
+        // the 32 nibble bytes that sub-blocks 2pr (low nibbles) and 2pr + 1
+        // (high nibbles) share
+        const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + pr * 32);
+        const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + pr * 32);
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int e = 2 * pr + h;
+            int sc, m;
+            if (e < 4) {
+                sc = byte_at(e < 4 ? s0 : s1, e & 3) & 63;
+                m = byte_at(s1, e & 3) & 63;
+            } else {
+                sc = (byte_at(s2, e & 3) & 0xF) | ((byte_at(s0, e & 3) >> 6) << 4);
+                m = (byte_at(s2, e & 3) >> 4) | ((byte_at(s1, e & 3) >> 6) << 4);
+            }
+            const int8_t *au = a + ((e ^ bsw) * 32);
+            const int4 x = *reinterpret_cast<const int4 *>(au), y = *reinterpret_cast<const int4 *>(au + 16);
+            const int av[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+            int dot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dot = __dp4a((int)((wv[i] >> (4 * h)) & 0x0F0F0F0Fu), av[i], dot);
+            isum += sc * dot;
+            const uint32_t pair = bs[e];  // block sums 2e and 2e + 1 (int16 each)
+            imin += m * ((int)(int16_t)(pair & 0xFFFF) + (int)(int16_t)(pair >> 16));
+        }
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+    return __fmul_rn(ad[ab], __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dmin, (float)imin)));
+}
+
+__device__ __forceinline__ void q4k_lane_rows(const uint8_t *span, size_t stride, int nr, int nb,
+                                              const float *ad, const int8_t *aq,
+                                              const int16_t *abs_, int t, int rows, int r0,
+                                              float *out, int lane) {
+    if (nb <= 32) {
+        const int j = lane / nb, b = lane - j * nb;
+        const bool live = j < nr;
+        const int first = j * nb;  // the row's first lane
+        const uint8_t *blk = span + (size_t)(live ? j : 0) * stride + (size_t)b * pj::Q4K_BYTES;
+        for (int tt = 0; tt < t; ++tt) {
+            float term = 0.0f;
+            if (live) term = q4k_block(blk, tt * nb + b, b & 7, ad, aq, abs_);
+            float sum = 0.0f;
+            for (int i = 0; i < nb; ++i) {
+                const float v = __shfl_sync(0xffffffffu, term, min(first + i, 31));
+                if (live && b == 0) sum = __fadd_rn(sum, v);
+            }
+            if (live && b == 0) out[(size_t)tt * rows + r0 + j] = sum;
+        }
+    } else {
+        // one row (nr == 1): lane l takes blocks l + 32 i, lane 0 adds them
+        // in block order
+        constexpr int kMaxPasses = 8;  // nb <= 256: k <= 65536
+        for (int tt = 0; tt < t; ++tt) {
+            float term[kMaxPasses];
+#pragma unroll
+            for (int i = 0; i < kMaxPasses; ++i) {
+                const int b = lane + 32 * i;
+                term[i] = b < nb ? q4k_block(span + (size_t)b * pj::Q4K_BYTES, tt * nb + b, b & 7,
+                                             ad, aq, abs_)
+                                 : 0.0f;
+            }
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kMaxPasses; ++i) {
+                const int n = min(32, nb - 32 * i);
+                for (int l = 0; l < n; ++l) {
+                    const float v = __shfl_sync(0xffffffffu, term[i], l);
+                    if (lane == 0) sum = __fadd_rn(sum, v);
+                }
+            }
+            if (lane == 0) out[(size_t)tt * rows + r0] = sum;
+        }
     }
 }
 
@@ -274,34 +379,50 @@ __global__ void __launch_bounds__(kMvWarps * 32)
     pj_cp_wait<0>();
     __syncwarp();
     if (!live) return;
-    row_dots(row, g.type[gr.p], k, nb, ad, aq, abs_, t, g.rows[gr.p], gr.r, g.out[gr.p], lane);
+    row_dots<false>(row, g.type[gr.p], k, nb, ad, aq, abs_, t, g.rows[gr.p], gr.r, g.out[gr.p],
+                    lane);
 }
 
-// Exec::matmul_group in one launch: every CTA quantizes the t activation rows
-// into its shared memory (the same bits in every CTA: the quantization is a
-// function of the values alone), then each warp walks `rpw` weight rows,
-// staging the next row while it dots the current one.  The first rows are
-// staged before the programmatic-dependency wait.
-__global__ void __launch_bounds__(kMvWarps * 32)
+// Exec::matmul_group in one launch.  Each warp owns a span of consecutive
+// rows of one part of the group (rpw rows: 32 / nb of them for Q4_K, whose
+// lanes take one super-block each; one row for the other types) and stages
+// the span in shared memory by asynchronous copies before the programmatic-
+// dependency wait, since the weights do not depend on the kernel ahead, so
+// the grid streams its weights while that kernel finishes.  After the wait
+// every CTA quantizes the t activation rows into its shared memory (the same
+// bits in every CTA: the quantization is a function of the values alone), in
+// the swizzled layout the block lanes read without bank conflicts.
+constexpr int kMmWarps = 8;
+__global__ void __launch_bounds__(kMmWarps * 32)
     matmul_group_kernel(const __grid_constant__ MatvecGroup g, const float *x, int k, int nb,
-                        int t, int row_smem, int rpw, int total) {
+                        int t, int span_smem) {
     extern __shared__ __align__(16) uint8_t mm_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int items = t * nb;
     int8_t *aq = reinterpret_cast<int8_t *>(mm_smem);
     float *ad = reinterpret_cast<float *>(mm_smem + (size_t)items * pj::QK);
     int16_t *abs_ = reinterpret_cast<int16_t *>(mm_smem + (size_t)items * (pj::QK + 4));
-    uint8_t *rows_s = mm_smem + (((size_t)items * (pj::QK + 4 + 32) + 15) / 16 * 16) +
-                      (size_t)warp * 2 * row_smem;
-    const int r0 = (blockIdx.x * kMvWarps + warp) * rpw;
-    GroupRow cur = group_row(g, min(r0, total - 1));
-    const uint8_t *row = nullptr;
-    if (r0 < total) row = stage_row_async(rows_s, cur.bytes, g.stride[cur.p], lane);
+    uint8_t *span_s = mm_smem + (((size_t)items * (pj::QK + 4 + 32) + 15) / 16 * 16) +
+                      (size_t)warp * span_smem;
+    // this warp's part and rows
+    const int gw = (int)blockIdx.x * kMmWarps + warp;
+    int p = 0;
+    while (p < g.n && gw >= g.wfirst[p + 1]) ++p;
+    const bool live = p < g.n;
+    int r0 = 0, nr = 0;
+    const uint8_t *span = nullptr;
+    if (live) {
+        r0 = (gw - g.wfirst[p]) * g.rpw[p];
+        nr = min(g.rpw[p], g.rows[p] - r0);
+        span = stage_row_async(span_s, static_cast<const uint8_t *>(g.w[p]) + (size_t)r0 * g.stride[p],
+                               (size_t)nr * g.stride[p], lane);
+    }
     pj_cp_commit();
     grid_dep_wait();    // x comes from the kernel ahead
-    grid_dep_launch();
-    // the activations, as q8k_quantize_kernel quantizes them
-    for (int item = warp; item < items; item += kMvWarps) {
+    grid_dep_launch();  // the next kernel may start staging its own weights
+    // the activations, as q8k_quantize_kernel quantizes them, 32-byte unit u
+    // of block b stored at unit u ^ (b & 7)
+    for (int item = warp; item < items; item += kMmWarps) {
         const int rr = item / nb, b = item % nb;
         const float *src = x + (size_t)rr * k + (size_t)b * pj::QK + lane * 8;
         const int n = min(pj::QK, k - b * pj::QK) - lane * 8;
@@ -324,34 +445,23 @@ __global__ void __launch_bounds__(kMvWarps * 32)
         uint2 packed;
         packed.x = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)q[3] << 24);
         packed.y = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)q[7] << 24);
-        *reinterpret_cast<uint2 *>(aq + (size_t)item * pj::QK + lane * 8) = packed;
+        const int unit = (lane >> 2) ^ (b & 7);
+        *reinterpret_cast<uint2 *>(aq + (size_t)item * pj::QK + unit * 32 + (lane & 3) * 8) = packed;
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         if (!(lane & 1)) abs_[(size_t)item * 16 + lane / 2] = (int16_t)sum;
         if (lane == 0) ad[item] = __fdiv_rn(amax, 127.0f);
     }
     __syncthreads();
-    for (int i = 0; i < rpw; ++i) {
-        const int gr_i = r0 + i;
-        if (gr_i >= total) break;
-        // stage the next row into the other buffer while this one is dotted
-        GroupRow nxt{};
-        const uint8_t *row_n = nullptr;
-        const bool more = gr_i + 1 < total && i + 1 < rpw;
-        if (more) {
-            nxt = group_row(g, gr_i + 1);
-            row_n = stage_row_async(rows_s + ((i + 1) & 1) * row_smem, nxt.bytes,
-                                    g.stride[nxt.p], lane);
-        }
-        pj_cp_commit();
-        pj_cp_wait<1>();  // this row's copies (the next row's may be in flight)
-        __syncwarp();
-        row_dots(row, g.type[cur.p], k, nb, ad, aq, abs_, t, g.rows[cur.p], cur.r, g.out[cur.p],
-                 lane);
-        __syncwarp();
-        cur = nxt;
-        row = row_n;
+    pj_cp_wait<0>();  // this warp's rows
+    __syncwarp();
+    if (!live) return;
+    if (g.type[p] == 12) {
+        q4k_lane_rows(span, g.stride[p], nr, nb, ad, aq, abs_, t, g.rows[p], r0, g.out[p], lane);
+    } else {
+        for (int j = 0; j < nr; ++j)
+            row_dots<true>(span + (size_t)j * g.stride[p], g.type[p], k, nb, ad, aq, abs_, t,
+                           g.rows[p], r0 + j, g.out[p], lane);
     }
-    pj_cp_wait<0>();  // nothing in flight when the CTA's memory is released
 }
 
 size_t proj_row_bytes(int ggml_type, int k) {
@@ -389,31 +499,40 @@ cudaError_t init_matvec_kernel() {
     return e;
 }
 
-size_t matmul_group_smem(int t, int k, size_t stride_max) {
+// Rows per warp of a part in the one-launch kernel: as many Q4_K rows as
+// give every lane a super-block, one row of the other types.
+static int rows_per_warp(int type, int nb) { return type == 12 && nb <= 32 ? 32 / nb : 1; }
+// A warp's span in shared memory: its rows plus the first one's offset
+// within 16 bytes, in whole 16-byte pieces.
+static size_t span_bytes(size_t bytes) { return (bytes + 15 + 15) / 16 * 16; }
+static size_t act_smem(int t, int k) {
     const size_t items = (size_t)t * ((k + pj::QK - 1) / pj::QK);
-    const size_t row_smem = (stride_max + 15 + 15) / 16 * 16;
-    return (items * (pj::QK + 4 + 32) + 15) / 16 * 16 + (size_t)kMvWarps * 2 * row_smem;
+    return (items * (pj::QK + 4 + 32) + 15) / 16 * 16;
+}
+// The most shared memory a one-launch group of rows up to stride_max bytes
+// may need (a Q4_K span holds at most 32 super-blocks).
+size_t matmul_group_smem(int t, int k, size_t stride_max) {
+    const size_t span = span_bytes(std::max(stride_max, (size_t)32 * pj::Q4K_BYTES));
+    return act_smem(t, k) + (size_t)kMmWarps * span;
 }
 
-cudaError_t launch_matmul_group(const MatvecGroup &g, const float *x, int t, int k,
+cudaError_t launch_matmul_group(const MatvecGroup &g_in, const float *x, int t, int k,
                                 cudaStream_t st) {
     const int nb = (k + pj::QK - 1) / pj::QK;
-    int total = 0;
-    size_t stride_max = 0;
-    for (int p = 0; p < g.n; ++p) total += g.rows[p], stride_max = max(stride_max, g.stride[p]);
-    const size_t smem = matmul_group_smem(t, k, stride_max);
+    MatvecGroup g = g_in;
+    size_t span_max = 0;
+    g.wfirst[0] = 0;
+    for (int p = 0; p < g.n; ++p) {
+        g.rpw[p] = rows_per_warp(g.type[p], nb);
+        g.wfirst[p + 1] = g.wfirst[p] + (g.rows[p] + g.rpw[p] - 1) / g.rpw[p];
+        span_max = std::max(span_max, span_bytes((size_t)g.rpw[p] * g.stride[p]));
+    }
+    const size_t smem = act_smem(t, k) + (size_t)kMmWarps * span_max;
     if (smem > (size_t)kMatmulSmemMax) return cudaErrorInvalidValue;
-    const int row_smem = (int)((stride_max + 15 + 15) / 16 * 16);
-    // rows per warp: about two waves of 16 four-warp CTAs per SM
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int warps_wanted = sms * 16 * kMvWarps;
-    const int rpw = max(1, min(8, (total + warps_wanted - 1) / warps_wanted));
-    const int warps = (total + rpw - 1) / rpw;
+    const int warps = g.wfirst[g.n];
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((warps + kMvWarps - 1) / kMvWarps);
-    cfg.blockDim = dim3(kMvWarps * 32);
+    cfg.gridDim = dim3((unsigned)std::max(1, (warps + kMmWarps - 1) / kMmWarps));
+    cfg.blockDim = dim3(kMmWarps * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -421,7 +540,7 @@ cudaError_t launch_matmul_group(const MatvecGroup &g, const float *x, int t, int
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, matmul_group_kernel, g, x, k, nb, t, row_smem, rpw, total);
+    return cudaLaunchKernelEx(&cfg, matmul_group_kernel, g, x, k, nb, t, (int)span_max);
 }
 
 cudaError_t launch_matvec_group(const MatvecGroup &g, int k, const float *d, const int8_t *qs,

@@ -109,6 +109,25 @@ def test_the_one_launch_group_matches_the_two_launch_path(ctx, t):
                 (ty, k, t)
 
 
+@pytest.mark.parametrize("ty", pc.TYPES)
+def test_the_one_launch_group_on_awkward_and_long_rows(ctx, ty):
+    """rl_matmul_group alone, bit for bit against the oracle: the awkward
+    shapes (a Q4_K warp then holds 32 / nb rows, one super-block a lane) and
+    rows of more than 32 super-blocks (one Q4_K row a warp, blocks l, l + 32,
+    ... a lane)."""
+    dev = torch.device("cuda", 0)
+    for i, (k, rows) in enumerate(pc.AWKWARD_SHAPES + [(9216, 40), (12800, 7)]):
+        w, x = pc.shape_case(ty, k, rows, 0x1AE + i)
+        x = np.ascontiguousarray(x, np.float32).reshape(1, k)
+        out = torch.full((1, rows), float("nan"), device=dev)
+        ctx.matmul_group(torch.from_numpy(x).to(dev), 1, k,
+                         [(ty, torch.from_numpy(np.ascontiguousarray(w)).to(dev), rows, out)])
+        ctx.sync()
+        want = orc.matvec(ty, w, rows, k, x, threads=8)
+        got = out.cpu().numpy()
+        assert np.array_equal(got, want), (ty, k, rows, np.abs(got - want).max())
+
+
 def test_zero_inputs_give_zero(ctx):
     k = 512
     for ty in pc.TYPES:
