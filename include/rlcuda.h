@@ -231,9 +231,15 @@ typedef enum {
     RL_OPT_WALK_SPANS = 8,    /* 1: every bf16 decode walk records its span on the
                                  global timer (RL_PROF_WALK_SPAN); 0 (default): off.
                                  Costs two atomics per CTA. */
-    RL_OPT_DN_SCAN_TC = 9     /* 1 (default): the chunked DeltaNet prefill walks its
+    RL_OPT_DN_SCAN_TC = 9,    /* 1 (default): the chunked DeltaNet prefill walks its
                                  chunks with the tcgen05 scan (one CTA per value head,
                                  the state in tensor memory); 0: the mma.sync scan */
+    RL_OPT_DN_OVERLAP = 10    /* 1 (default): the tcgen05 chunk scan runs on a second,
+                                 high-priority stream beside the chunk-local kernel,
+                                 taking each chunk as its ready flag goes up (forked
+                                 from and joined back into the context's stream, so a
+                                 CUDA-graph capture of that stream takes both); 0: one
+                                 after the other */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);

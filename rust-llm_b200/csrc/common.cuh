@@ -296,3 +296,31 @@ __device__ __forceinline__ float xload(const unsigned long long *src, unsigned e
     return __uint_as_float((unsigned)w);
 }
 }  // namespace rl
+
+namespace rl {
+// A flag another CTA of the same GPU publishes once its global writes are
+// done: st.release.gpu after every writer's fence and a CTA barrier on the
+// writing side; ld.acquire.gpu here.  Waits until the flag holds `value`,
+// for PEER_WAIT_LIMIT_NS at most on the global timer; a wait that gives up
+// flags DEV_TIMEOUT and returns false.
+__device__ __forceinline__ void st_release_gpu(int *p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool wait_flag_gpu(const int *flag, int value, int *status) {
+    if (ld_acquire_gpu(flag) == value) return true;
+    const unsigned long long start = globaltimer_ns();
+    while (ld_acquire_gpu(flag) != value) {
+        if (globaltimer_ns() - start > PEER_WAIT_LIMIT_NS) {
+            atomicOr(status, DEV_TIMEOUT);
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
+}
+}  // namespace rl

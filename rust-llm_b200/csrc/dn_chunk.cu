@@ -261,7 +261,11 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     using namespace dc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     LocalSmem &sm = *reinterpret_cast<LocalSmem *>(smem_raw);
-    const int ck = blockIdx.x, vh = blockIdx.y, kh = vh % a.n_k;
+    // grid (n_v, n_chunks): the CTAs of a chunk are dispatched together and
+    // the chunks in order (an overlapped scan waits for them in that order)
+    const int vh = blockIdx.x, ck = blockIdx.y, kh = vh % a.n_k;
+    // the epoch this call's scan waits for (read before anything is written)
+    const int ready_value = a.ready ? a.ready_epoch[vh] + 1 : 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = ck * C, rows = min(C, a.t - t0);
 
@@ -565,7 +569,12 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
             }
         }
     }
-
+    if (a.ready) {
+        // every thread's stores are visible GPU-wide before the flag goes up
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) st_release_gpu(a.ready + (size_t)vh * a.nc + ck, ready_value);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -868,17 +877,32 @@ cudaError_t init_dn_chunk_kernels() {
     return e;
 }
 
-cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps, cudaStream_t st) {
+cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps, cudaStream_t st,
+                            const DnOverlap *overlap) {
     using namespace dc;
     DnChunkArgs a = a_in;
     a.w_lo_out = scan_maps == nullptr;
     dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
                      st>>>(a);
-    dn_chunk_local_kernel<<<dim3(a.nc, a.n_v), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
-    if (scan_maps) {
+    if (scan_maps && overlap && a.ready) {
+        // the scan beside the chunk-local kernel: it starts once the prep
+        // kernel is done and walks each head's chunks as their flags go up
+        cudaError_t e = cudaEventRecord(overlap->fork, st);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(overlap->scan_stream, overlap->fork, 0);
+        if (e == cudaSuccess) e = launch_dn_scan_tc(a, *scan_maps, overlap->scan_stream);
+        if (e != cudaSuccess) return e;
+        dn_chunk_local_kernel<<<dim3(a.n_v, a.nc), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
+        e = cudaEventRecord(overlap->join, overlap->scan_stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, overlap->join, 0);
+        if (e != cudaSuccess) return e;
+    } else if (scan_maps) {
+        a.ready = nullptr;
+        dn_chunk_local_kernel<<<dim3(a.n_v, a.nc), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
         const cudaError_t e = launch_dn_scan_tc(a, *scan_maps, st);
         if (e != cudaSuccess) return e;
     } else {
+        a.ready = nullptr;
+        dn_chunk_local_kernel<<<dim3(a.n_v, a.nc), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
         dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
     }
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);

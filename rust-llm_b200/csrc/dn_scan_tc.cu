@@ -105,6 +105,16 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
     const int nc = a.nc;
     const size_t blk0 = (size_t)vh * nc;
     float *state = a.ssm_state + (size_t)vh * a.slots * S * S + (size_t)a.live * S * S;
+    // beside the chunk-local kernel: chunk c of this head may be read once
+    // ready[vh * nc + c] holds this value
+    const int ready_value = a.ready ? a.ready_epoch[vh] + 1 : 0;
+    auto chunk_ready = [&](int c) {
+        if (!a.ready) return true;
+        const bool ok = wait_flag_gpu(a.ready + blk0 + c, ready_value, a.status);
+        // the tensor copies that follow read what the flag published
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        return ok;
+    };
 
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
@@ -154,8 +164,12 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                 prefetch_tensormap(&m.kl);
             }
             int c = 0;
+            // beside the chunk-local kernel the chunks are fresh in L2 when
+            // their flags go up: no prefetch
+            if (role == 4 && a.ready) c = nc;
             for (; c < nc; ++c) {
                 const int row = (int)(blk0 + c) * C;
+                if (role < 4 && !chunk_ready(c)) break;
                 if (role == 0) {
                     if (c >= 1 && !mbar_wait(&w_empty, (c - 1) & 1, a.status)) break;
                     mbar_arrive_expect_tx(&w_full, W_BYTES);
@@ -330,6 +344,7 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         mbar_arrive(&s_ready);
         for (int c = 0; c < nc && ok; ++c) {
             const size_t blk = blk0 + c;
+            if (!(ok = chunk_ready(c))) break;
             // ---- U = Ut - S W for this warp's 32 tokens, into shared memory
             // as a bf16 pair (Ut's column j is read while the MMAs run)
             const float *ut = a.ut + blk * C * S + (size_t)(hf * 32) * S + j;
@@ -414,6 +429,9 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
     tc::fence_before_sync();
     __syncthreads();
     if (tid == 0 && flag_s) atomicOr(a.status, DEV_TIMEOUT);
+    // every chunk of this call is consumed: the next call's flags take the
+    // next value
+    if (tid == 0 && a.ready) a.ready_epoch[vh] = ready_value;
     if (warp == MMA_WARP) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, TMEM_COLS);

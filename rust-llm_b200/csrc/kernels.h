@@ -215,6 +215,16 @@ struct DnChunkArgs {
     int t, nc, n_k, n_v, live, slots;
     float eps;
     bool w_lo_out;  // write W's low half (the mma.sync scan reads it)
+    // overlapped chunk-local and tcgen05 scan (null: one after the other):
+    // the chunk-local CTA of (value head, chunk) stores ready[head * nc +
+    // chunk] = ready_epoch[head] + 1 once its outputs are written; the scan
+    // waits for that value and, done, advances ready_epoch[head]
+    int *ready, *ready_epoch;
+};
+// The second stream and events of an overlapped chunked prefill.
+struct DnOverlap {
+    cudaStream_t scan_stream;
+    cudaEvent_t fork, join;
 };
 cudaError_t init_dn_chunk_kernels();
 // The chunk scan on tcgen05 (dn_scan_tc.cu) reads the chunk-local kernel's
@@ -227,8 +237,12 @@ struct DnScanMaps {
 cudaError_t init_dn_scan_tc_kernel();
 cudaError_t launch_dn_scan_tc(const DnChunkArgs &a, const DnScanMaps &m, cudaStream_t st);
 // The whole chunked prefill of one call; `scan_maps` non-null selects the
-// tcgen05 chunk scan, null the mma.sync one.
-cudaError_t launch_dn_chunk(const DnChunkArgs &a, const DnScanMaps *scan_maps, cudaStream_t st);
+// tcgen05 chunk scan, null the mma.sync one.  With `overlap` (and the tcgen05
+// scan, and a.ready set) the scan runs on overlap->scan_stream beside the
+// chunk-local kernel, forked after the prep kernel and joined before the
+// output kernel.
+cudaError_t launch_dn_chunk(const DnChunkArgs &a, const DnScanMaps *scan_maps, cudaStream_t st,
+                            const DnOverlap *overlap = nullptr);
 
 // KV cache fill from f32 (host-visible test and bench helper): positions
 // [p0, p0+n) of every KV head, src [2][n_kv][n][hd] f32 on the device.

@@ -59,6 +59,12 @@ struct rl_ctx {
     float *dn_lg = nullptr, *dn_bt = nullptr;
     __nv_bfloat16 *dn_w = nullptr, *dn_qp = nullptr, *dn_kp = nullptr, *dn_p = nullptr;
     float *dn_ut = nullptr, *dn_gc = nullptr, *dn_opre = nullptr;
+    // the chunk scan beside the chunk-local kernel: per (value head, chunk)
+    // ready flags, per head the epoch the flags count, the scan's stream and
+    // the fork and join events
+    int *dn_ready = nullptr, *dn_ready_epoch = nullptr;
+    cudaStream_t dn_scan_stream = nullptr;
+    cudaEvent_t dn_fork = nullptr, dn_join = nullptr;
     float *stage_raw = nullptr;  // the status word (64 B), then the staging
     float *stage = nullptr;   // staging for the *_host entry points
     size_t stage_floats = 0;
@@ -73,7 +79,7 @@ struct rl_ctx {
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
-    int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1;
+    int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1, opt_dn_overlap = 1;
     int64_t opt_wait_limit_us = 0;  // 0: rl::PEER_WAIT_LIMIT_NS
     int64_t opt_dn_scan_tc = 1;
     // RL_OPT_WALK_SPANS: [n_full][4] {first start, CTAs done, span sum, launches}
@@ -231,6 +237,11 @@ void free_all(rl_ctx *x) {
     if (x->act_qs) cudaFree(x->act_qs);
     if (x->act_bs) cudaFree(x->act_bs);
     if (x->hpin_base) cudaFreeHost(x->hpin_base);
+    if (x->dn_ready) cudaFree(x->dn_ready);
+    if (x->dn_ready_epoch) cudaFree(x->dn_ready_epoch);
+    if (x->dn_fork) cudaEventDestroy(x->dn_fork);
+    if (x->dn_join) cudaEventDestroy(x->dn_join);
+    if (x->dn_scan_stream) cudaStreamDestroy(x->dn_scan_stream);
     if (x->own_stream && x->stream) cudaStreamDestroy(x->stream);
 }
 
@@ -563,6 +574,20 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
             rl::encode_bf16_2d(&m.kl, x->dn_kp_lo, rows, s, s * 2, 64, 64) == cudaSuccess &&
             rl::encode_bf16_2d(&m.ph, x->dn_p, rows, 64, 128, 64, 64) == cudaSuccess &&
             rl::encode_bf16_2d(&m.pl, x->dn_p_lo, rows, 64, 128, 64, 64) == cudaSuccess;
+        // the scan beside the chunk-local kernel, on a stream of the highest
+        // priority so that its CTAs are placed ahead of the chunk-local ones
+        int lo_prio = 0, hi_prio = 0;
+        cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
+        if ((code = alloc(x, &x->dn_ready, nv * nc)) ||
+            (code = alloc(x, &x->dn_ready_epoch, nv)))
+            return bail(code);
+        if (cudaMemset(x->dn_ready, 0, nv * nc * sizeof(int)) != cudaSuccess ||
+            cudaMemset(x->dn_ready_epoch, 0, nv * sizeof(int)) != cudaSuccess ||
+            cudaStreamCreateWithPriority(&x->dn_scan_stream, cudaStreamNonBlocking, hi_prio) !=
+                cudaSuccess ||
+            cudaEventCreateWithFlags(&x->dn_fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x->dn_join, cudaEventDisableTiming) != cudaSuccess)
+            return bail(fail(x, RL_ECUDA, "the chunk scan's stream or events"));
     }
     // staging for the host entry points: the larger of the two paths' in+out
     const size_t full_io = mb * (2 * hd * nh + 2 * hd * c.n_head_kv + hd * nh);
@@ -1313,7 +1338,12 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
         {
             ProfScope ps(ctx, RL_PROF_DN_CHUNK);
             const bool tc_scan = ctx->opt_dn_scan_tc && ctx->dn_scan_maps_ok;
-            CK(ctx, rl::launch_dn_chunk(d, tc_scan ? &ctx->dn_scan_maps : nullptr, ctx->stream));
+            // the tcgen05 scan runs beside the chunk-local kernel
+            const rl::DnOverlap ov{ctx->dn_scan_stream, ctx->dn_fork, ctx->dn_join};
+            d.ready = tc_scan && ctx->opt_dn_overlap ? ctx->dn_ready : nullptr;
+            d.ready_epoch = ctx->dn_ready_epoch;
+            CK(ctx, rl::launch_dn_chunk(d, tc_scan ? &ctx->dn_scan_maps : nullptr, ctx->stream,
+                                        tc_scan && ctx->opt_dn_overlap ? &ov : nullptr));
         }
         // a step of this layer right after must not read the state early
         ctx->prev_dn = 1;
@@ -1557,6 +1587,10 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
         if (value > 1) return fail(ctx, RL_EINVAL, "the scan option must be 0 or 1");
         ctx->opt_dn_scan_tc = value;
         return RL_OK;
+    case RL_OPT_DN_OVERLAP:
+        if (value > 1) return fail(ctx, RL_EINVAL, "the overlap option must be 0 or 1");
+        ctx->opt_dn_overlap = value;
+        return RL_OK;
     case RL_OPT_WALK_SPANS:
         if (value > 1) return fail(ctx, RL_EINVAL, "the span option must be 0 or 1");
         CK(ctx, cudaSetDevice(ctx->device));
@@ -1589,6 +1623,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_WAIT_LIMIT_US: return ctx->opt_wait_limit_us;
     case RL_OPT_WALK_SPANS: return ctx->spans ? 1 : 0;
     case RL_OPT_DN_SCAN_TC: return ctx->opt_dn_scan_tc;
+    case RL_OPT_DN_OVERLAP: return ctx->opt_dn_overlap;
     default: return -1;
     }
 }

@@ -20,7 +20,7 @@ COS_MIN = 0.9999
 pytestmark = pytest.mark.gpu
 
 
-def run_chunked(t, seed, unit_norm=True, scan_tc=1):
+def run_chunked(t, seed, unit_norm=True, scan_tc=1, overlap=1):
     r = orc.Rng(seed)
     rows = cases.lin_rows(r, t)
     w = cases.lin_weights(r, unit_norm=unit_norm)
@@ -31,6 +31,7 @@ def run_chunked(t, seed, unit_norm=True, scan_tc=1):
                                max_batch=max(t, 64))
     with rlcuda.Context(cfg) as ctx:
         ctx.set_option(rlcuda.RL_OPT_DN_SCAN_TC, scan_tc)
+        ctx.set_option(rlcuda.RL_OPT_DN_OVERLAP, overlap)
         ctx.set_weights_linear(0, w.conv1d, w.ssm_a, w.dt_bias, w.norm)
         ctx.write_conv(0, conv)
         ctx.write_ssm(0, ssm)
@@ -41,14 +42,16 @@ def run_chunked(t, seed, unit_norm=True, scan_tc=1):
     return got, want, conv_got, conv_w, ssm_got, ssm_w, chunk_launches
 
 
-@pytest.mark.parametrize("scan_tc", [1, 0], ids=["tcgen05_scan", "mma_sync_scan"])
+@pytest.mark.parametrize("scan_tc,overlap", [(1, 1), (1, 0), (0, 0)],
+                         ids=["tcgen05_scan_overlapped", "tcgen05_scan", "mma_sync_scan"])
 @pytest.mark.parametrize("t", [64, 100, 257, 1024, 4096])
-def test_chunked_prefill_matches_the_token_sequential_oracle(t, scan_tc):
+def test_chunked_prefill_matches_the_token_sequential_oracle(t, scan_tc, overlap):
     """t = 4096 is the benchmarked config-2 DeltaNet layer: the state is
     carried through 64 chunks, where the bf16-pair products' error would
-    grow if it were going to.  Both chunk scans: tcgen05 (the default) and
-    mma.sync."""
-    got, want, conv_got, conv_w, ssm_got, ssm_w, n = run_chunked(t, 900 + t, scan_tc=scan_tc)
+    grow if it were going to.  Both chunk scans: tcgen05 (the default, beside
+    the chunk-local kernel or after it) and mma.sync."""
+    got, want, conv_got, conv_w, ssm_got, ssm_w, n = run_chunked(t, 900 + t, scan_tc=scan_tc,
+                                                                 overlap=overlap)
     assert n == 1, "the call did not take the chunked kernels"
     assert np.isfinite(got).all()
     err = cases.rel_err_per_head(got, want, cases.S)
@@ -58,6 +61,38 @@ def test_chunked_prefill_matches_the_token_sequential_oracle(t, scan_tc):
     scos = cases.cosine_per_head(ssm_got, ssm_w, cases.S * cases.S)
     assert serr <= REL_TOL and scos >= COS_MIN, (serr, scos)
     assert np.array_equal(conv_got, conv_w)
+
+
+def test_consecutive_chunked_calls_over_two_layers():
+    """Three chunked calls on one context (layer 0, layer 1, layer 0 again):
+    each overlapped scan waits for its own call's chunk flags, whatever the
+    calls before it left in them."""
+    r = orc.Rng(57)
+    rows = cases.lin_rows(r, 384)
+    w0, w1 = cases.lin_weights(r), cases.lin_weights(r)
+    conv, ssm = cases.lin_state(r, 1)
+    c0, s0 = conv.copy(), ssm.copy()
+    c1, s1 = conv.copy(), ssm.copy()
+    half = [slice(0, 192), slice(192, 384)]
+    pick = lambda sl: cases.LinRows(rows.qkv[sl], rows.z[sl], rows.alpha[sl], rows.beta[sl])
+    want = [cases.oracle_linear(w0, pick(half[0]), c0, s0, 1, 0),
+            cases.oracle_linear(w1, pick(half[0]), c1, s1, 1, 0),
+            cases.oracle_linear(w0, pick(half[1]), c0, s0, 1, 0)]
+    cfg = rlcuda.qwen35_config(n_full=0, n_linear=2, context=256, slots=1, max_batch=192)
+    with rlcuda.Context(cfg) as ctx:
+        for layer, w in ((0, w0), (1, w1)):
+            ctx.set_weights_linear(layer, w.conv1d, w.ssm_a, w.dt_bias, w.norm)
+            ctx.write_conv(layer, conv)
+            ctx.write_ssm(layer, ssm)
+        got = []
+        for layer, sl in ((0, half[0]), (1, half[0]), (0, half[1])):
+            x = pick(sl)
+            got.append(ctx.linear_attn_host(layer, 0, x.qkv, x.z, x.alpha, x.beta))
+        ssm0 = ctx.read_ssm(0)
+    for g_, w_ in zip(got, want):
+        assert cases.rel_err_per_head(g_, w_, cases.S) <= REL_TOL
+        assert cases.cosine_per_head(g_, w_, cases.S) >= COS_MIN
+    assert cases.cosine_per_head(ssm0, s0, cases.S * cases.S) >= COS_MIN
 
 
 def test_chunked_prefill_with_norm_weights():
