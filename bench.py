@@ -417,6 +417,8 @@ def dn_prefill_bench(args, dev, stream, rlcuda, torch):
                                max_batch=PF_T)
     ctx = rlcuda.Context(cfg, device=dev.index)
     ctx.set_stream(stream.cuda_stream)
+    if args.dn_serial:
+        ctx.set_option(rlcuda.RL_OPT_DN_OVERLAP, 0)
     import numpy as np
     r = np.random.default_rng(2)
     for layer in range(DN_PF_LAYERS):
@@ -1101,6 +1103,10 @@ def main():
                     help="skip the full-attention prefill section")
     ap.add_argument("--no-dn-prefill", action="store_true",
                     help="skip the DeltaNet chunked-prefill section")
+    ap.add_argument("--dn-serial", action="store_true",
+                    help="run the chunk scan after the chunk-local kernel rather than beside it "
+                         "(for profilers that serialise kernels, under which the overlapped "
+                         "scan waits for chunks that cannot arrive and gives up)")
     ap.add_argument("--no-verify", action="store_true", help="skip the speculative-verify section")
     ap.add_argument("--no-batch", action="store_true",
                     help="skip the config-4b batched multi-sequence section")

@@ -239,7 +239,9 @@ typedef enum {
                                  taking each chunk as its ready flag goes up (forked
                                  from and joined back into the context's stream, so a
                                  CUDA-graph capture of that stream takes both); 0: one
-                                 after the other */
+                                 after the other (for a profiler that serialises
+                                 kernels, under which the overlapped scan waits in vain
+                                 and gives up) */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);

@@ -82,8 +82,8 @@ __device__ __forceinline__ void store_triple4(__nv_bfloat16 *hi, __nv_bfloat16 *
 // One warp per (8 consecutive tokens, group of 128 channels): the group's
 // conv weights are loaded once and the three-token history slides along in
 // registers.
-constexpr int PREP_TOKENS = 8;
-__global__ void __launch_bounds__(256) dn_prep_kernel(const DnChunkArgs a) {
+constexpr int PREP_TOKENS = 4;
+__global__ void __launch_bounds__(256, 4) dn_prep_kernel(const DnChunkArgs a) {
     using namespace dc;
     const int lane = threadIdx.x & 31;
     const int i0 = blockIdx.x * PREP_TOKENS, g = blockIdx.y * 8 + (threadIdx.x >> 5);

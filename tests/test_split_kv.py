@@ -106,7 +106,7 @@ def _free_port():
 
 @pytest.mark.parametrize("world,seq,pos", [(2, 300, 299), (2, 300, 40), (3, 200, 199)])
 def test_gloo_ranks_merge_to_the_single_pass_row(world, seq, pos):
-    res = mp.Manager().dict()
+    res = mp.get_context("spawn").Manager().dict()  # no fork of a threaded process
     mp.spawn(_rank, args=(world, _free_port(), seq, pos, res), nprocs=world, join=True)
     rng = np.random.default_rng(7)
     K = rng.standard_normal((NKV, seq, HD))
