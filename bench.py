@@ -459,8 +459,11 @@ def dn_prefill_bench(args, dev, stream, rlcuda, torch):
                         "f32 state between chunks",
             "us_per_layer": us, "flop_per_layer": DN_PF_FLOP_PER_LAYER,
             "tflops_algorithmic": tf, "frac_of_measured_bf16": tf / peak,
-            "note": "every product is three bf16 mma.sync terms (hi*hi + hi*lo + lo*hi), so "
-                    "the tensor pipes execute about 3x the algorithmic FLOP"}
+            "note": "operands as bf16 pairs (q, k in Q K^T as triples), most products three "
+                    "bf16 terms (hi*hi + hi*lo + lo*hi), so the tensor pipes execute 2-6x the "
+                    "algorithmic FLOP; chunk-local products on mma.sync, the chunk scan on "
+                    "tcgen05 beside the chunk-local kernel (off with --dn-serial)",
+            "overlapped": not args.dn_serial}
 
 
 VERIFY_POS, VERIFY_K = 16384, 8
