@@ -43,7 +43,12 @@ constexpr int LDF = 65;    // padded f32 row of a 64-wide matrix
 constexpr int JC = 32;     // state columns per scan CTA
 constexpr int SCAN_THREADS = 512;  // chunk scan: 8 chain warps + 8 output warps
 constexpr int GROUP_THREADS = 256;
-constexpr int LOCAL_THREADS = 256;  // chunk-local CTA: 8 warps
+constexpr int LOCAL_THREADS = 512;  // chunk-local CTA: 16 warps
+constexpr int LOCAL_WARPS = LOCAL_THREADS / 32;
+// the chunk-local products are cut into 4 row blocks of 16 times
+// LOCAL_WARPS / 4 column blocks, one per warp
+constexpr int QK_COLS = C * 4 / LOCAL_WARPS;  // K K^T, Q K^T columns per warp
+constexpr int UW_COLS = S * 4 / LOCAL_WARPS;  // Ut, W columns per warp
 }  // namespace dc
 
 // ---------------------------------------------------------------------------
@@ -238,8 +243,9 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ---------------------------------------------------------------------------
-// dn_chunk_local_kernel: grid (n_chunks, n_v), 256 threads (8 warps: row block
-// warp % 4 of 16 rows, column half warp / 4 in the two product phases).
+// dn_chunk_local_kernel: grid (n_v, n_chunks), LOCAL_THREADS threads (16
+// warps: row block warp % 4 of 16 rows, column block warp / 4 in the
+// product phases).
 struct LocalSmem {
     __nv_bfloat16 k[dc::C][dc::LDB], q[dc::C][dc::LDB], v[dc::C][dc::LDB];
     __nv_bfloat16 kl[dc::C][dc::LDB], ql[dc::C][dc::LDB], vl[dc::C][dc::LDB];  // low halves
@@ -320,11 +326,12 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     // that follows magnifies their error; pairs (16 bits) measured 1.3e-2 of
     // such a head's output at 4096 tokens, triples stay at the f32 level
     {
-        // warp: rows 16 * (warp % 4), columns 32 * (warp / 4) .. + 31
-        const int rw = (warp & 3) * 16, cn = (warp >> 2) * 32;
-        float dk[4][4], dq[4][4];
+        // warp: rows 16 * (warp % 4), columns QK_COLS * (warp / 4) ..
+        constexpr int NT = QK_COLS / 8;
+        const int rw = (warp & 3) * 16, cn = (warp >> 2) * QK_COLS;
+        float dk[NT][4], dq[NT][4];
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
+        for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int e = 0; e < 4; ++e) dk[n][e] = dq[n][e] = 0.0f;
 #pragma unroll
@@ -336,7 +343,7 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
             ld_a(&sm.ql[0][0], LDB, rw, ks * 16, lane, aql);
             ld_a(&sm.q2[0][0], LDB, rw, ks * 16, lane, aq2);
 #pragma unroll
-            for (int np = 0; np < 2; ++np) {
+            for (int np = 0; np < NT / 2; ++np) {
                 uint32_t b[4], bl[4], b2[4];
                 ld_b2(&sm.k[0][0], LDB, cn + np * 16, ks * 16, lane, b);
                 ld_b2(&sm.kl[0][0], LDB, cn + np * 16, ks * 16, lane, bl);
@@ -357,7 +364,7 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
         }
         const int r0 = rw + (lane >> 2), c0 = cn + (lane & 3) * 2;
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
+        for (int n = 0; n < NT; ++n) {
             sm.kk[r0][n * 8 + c0] = dk[n][0];
             sm.kk[r0][n * 8 + c0 + 1] = dk[n][1];
             sm.kk[r0 + 8][n * 8 + c0] = dk[n][2];
@@ -516,15 +523,17 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     }
     cp_async_wait<0>();  // v
     __syncthreads();
-    // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows, 64 cols)
+    // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows,
+    // UW_COLS columns)
     float *ut_out = a.ut + blk * C * S;
     __nv_bfloat16 *w_out = a.w + blk * C * S, *wl_out = a.w_lo + blk * C * S;
     const int r0 = (warp & 3) * 16 + (lane >> 2), c0 = (lane & 3) * 2;
     {
-        const int half = warp >> 2;  // this warp's 64 output columns
-        float du[8][4], dw[8][4];
+        constexpr int NT = UW_COLS / 8;
+        const int cb = (warp >> 2) * UW_COLS;  // this warp's first output column
+        float du[NT][4], dw[NT][4];
 #pragma unroll
-        for (int n = 0; n < 8; ++n)
+        for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int e = 0; e < 4; ++e) du[n][e] = dw[n][e] = 0.0f;
 #pragma unroll
@@ -535,8 +544,8 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
             ld_a(&sm.tb_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bh);
             ld_a(&sm.tb_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bl);
 #pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                const int n0 = half * 64 + np * 16;
+            for (int np = 0; np < NT / 2; ++np) {
+                const int n0 = cb + np * 16;
                 uint32_t vh_[4], vl_[4], kh_[4], kl_[4];
                 ld_b2_t(&sm.v[0][0], LDB, n0, ks * 16, lane, vh_);
                 ld_b2_t(&sm.vl[0][0], LDB, n0, ks * 16, lane, vl_);
@@ -554,8 +563,8 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
             }
         }
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-            const int col = half * 64 + n * 8 + c0;
+        for (int n = 0; n < NT; ++n) {
+            const int col = cb + n * 8 + c0;
             *reinterpret_cast<float2 *>(ut_out + r0 * S + col) = make_float2(du[n][0], du[n][1]);
             *reinterpret_cast<float2 *>(ut_out + (r0 + 8) * S + col) = make_float2(du[n][2], du[n][3]);
 #pragma unroll
