@@ -234,7 +234,7 @@ typedef enum {
     RL_OPT_DN_SCAN_TC = 9,    /* 1 (default): the chunked DeltaNet prefill walks its
                                  chunks with the tcgen05 scan (one CTA per value head,
                                  the state in tensor memory); 0: the mma.sync scan */
-    RL_OPT_DN_OVERLAP = 10    /* 1 (default): the tcgen05 chunk scan runs on a second,
+    RL_OPT_DN_OVERLAP = 10,   /* 1 (default): the tcgen05 chunk scan runs on a second,
                                  high-priority stream beside the chunk-local kernel,
                                  taking each chunk as its ready flag goes up (forked
                                  from and joined back into the context's stream, so a
@@ -242,6 +242,9 @@ typedef enum {
                                  after the other (for a profiler that serialises
                                  kernels, under which the overlapped scan waits in vain
                                  and gives up) */
+    RL_OPT_DN_LOCAL_TC = 11   /* 1 (default): the chunked prefill's chunk-local kernel
+                                 takes K K^T and Q K^T on tcgen05 (q and k by TMA, one
+                                 M = 128 product of [K; Q] against K); 0: on mma.sync */
 } rl_option;
 int rl_set_option(rl_ctx *ctx, int option, int64_t value);
 int64_t rl_get_option(const rl_ctx *ctx, int option);

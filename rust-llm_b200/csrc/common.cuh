@@ -324,3 +324,15 @@ __device__ __forceinline__ bool wait_flag_gpu(const int *flag, int value, int *s
     return true;
 }
 }  // namespace rl
+
+namespace rl {
+// A tiled TMA load of a 3-D box at (x, y, z), completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y,
+                                            int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+}  // namespace rl

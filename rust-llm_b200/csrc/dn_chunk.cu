@@ -29,9 +29,12 @@
 //                         conv history (the reference's history after the batch)
 // The state columns are independent of each other in the recurrence, so the
 // scan splits each head's 128 x 128 state over 4 CTAs.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "mma.cuh"
+#include "tc.cuh"
 
 namespace rl {
 namespace dc {
@@ -263,10 +266,55 @@ struct LocalSmem {
     float cum[dc::C], beta[dc::C];
 };
 
-__global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const DnChunkArgs a) {
+// The tcgen05 form's layout (1024-byte aligned).  q and k arrive by TMA as
+// 64-token x 64-channel boxes with the 128-byte swizzle, in 16 KiB blocks of
+// (plane, channel box): K's 64 rows, then Q's, so that a block is the
+// 128-row A operand [K; Q] of K K^T and Q K^T stacked, and its first half
+// the B operand K.  The planes' third terms are read by that product only,
+// so T's pairs and the T inversion's scratch reuse their space.
+struct LocalSmemTc {
+    unsigned char hl[2][2][16384];  // [hi, lo][channel box]
+    union {
+        unsigned char l2[2][16384];  // [channel box], the third terms
+        float x[dc::C][dc::LDF];
+        struct {
+            __nv_bfloat16 ta_hi[dc::C][dc::LDP], ta_lo[dc::C][dc::LDP];  // T diag(beta)
+            __nv_bfloat16 tb_hi[dc::C][dc::LDP], tb_lo[dc::C][dc::LDP];  // T diag(beta gamma)
+        };
+    };
+    __nv_bfloat16 v[dc::C][dc::LDB], vl[dc::C][dc::LDB];
+    float kk[dc::C][dc::LDF], qk[dc::C][dc::LDF], t[dc::C][dc::LDF];
+    float cum[dc::C], beta[dc::C];
+    uint64_t qk_full, mma_done;
+    uint32_t tmem_base;
+};
+static_assert(sizeof(LocalSmemTc) + 1024 <= 227 * 1024, "the tcgen05 chunk-local layout fits");
+constexpr uint32_t QK_BLOCK = 16384, Q_HALF = 8192;
+
+// The tcgen05 form's plane x (0 hi, 1 lo, 2 third term) of k (q: + Q_HALF),
+// channel box cb
+template <typename Sm>
+__device__ __forceinline__ unsigned char *qk_block(Sm &sm, int x, int cb) {
+    return x < 2 ? sm.hl[x][cb] : sm.l2[cb];
+}
+// B fragments of two n-tiles (channels n0, n0 + 8) from a swizzled plane
+// stored as rows k (tokens) with n (channels) contiguous, as ld_b2_t reads a
+// padded one
+__device__ __forceinline__ void ld_b2_t_swz(const unsigned char *box0, int n0, int k0, int lane,
+                                            uint32_t (&b)[4]) {
+    const int r = k0 + (lane & 7) + ((lane >> 3) & 1) * 8, c = n0 + (lane >> 4) * 8;
+    ldsm_x4_t(smem_u32(box0 + (c >> 6) * QK_BLOCK + swz128(r, (c & 63) >> 3)), b);
+}
+
+template <bool TC>
+__global__ void __launch_bounds__(dc::LOCAL_THREADS)
+    dn_chunk_local_kernel(const DnChunkArgs a, const __grid_constant__ DnPlaneMaps pm) {
     using namespace dc;
+    using Sm = std::conditional_t<TC, LocalSmemTc, LocalSmem>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    LocalSmem &sm = *reinterpret_cast<LocalSmem *>(smem_raw);
+    unsigned char *base =
+        TC ? smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023) : smem_raw;
+    Sm &sm = *reinterpret_cast<Sm *>(base);
     // grid (n_v, n_chunks): the CTAs of a chunk are dispatched together and
     // the chunks in order (an overlapped scan waits for them in that order)
     const int vh = blockIdx.x, ck = blockIdx.y, kh = vh % a.n_k;
@@ -276,21 +324,49 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     const int t0 = ck * C, rows = min(C, a.t - t0);
 
     // ---- operands of the chunk (rows past the batch are zero): every copy
-    // in flight at once, in two groups: q and k (the first products) and v
+    // in flight at once, q and k first (the first products), v after them
     // (needed only for Ut, after T)
+    if constexpr (TC) {
+        // q and k by TMA (the maps end at the call's rows, so the rows past
+        // them read as zero), into the stacked blocks
+        if (tid == 0) {
+            mbar_init(&sm.qk_full, 1);
+            mbar_init(&sm.mma_done, 1);
+            fence_barrier_init();
+        }
+        if (warp == 0) {
+            tc::tmem_alloc(&sm.tmem_base, 64);
+            tc::tmem_relinquish();
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (tid == 0) {
+            mbar_arrive_expect_tx(&sm.qk_full, 12 * Q_HALF);
+#pragma unroll 1
+            for (int x = 0; x < 3; ++x)
+#pragma unroll 1
+                for (int cb = 0; cb < 2; ++cb) {
+                    unsigned char *blk = qk_block(sm, x, cb);
+                    tma_load_3d(blk, &pm.k[x], cb * 64, kh, t0, &sm.qk_full);
+                    tma_load_3d(blk + Q_HALF, &pm.q[x], cb * 64, kh, t0, &sm.qk_full);
+                }
+        }
+    } else {
 #pragma unroll 2
-    for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
-        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
-        const bool ok = r < rows;
-        const size_t ko = ((size_t)(t0 + (ok ? r : 0)) * a.n_k + kh) * S + c8;
-        cp_async16_zfill(&sm.k[r][c8], a.kn + ko, ok);
-        cp_async16_zfill(&sm.q[r][c8], a.qn + ko, ok);
-        cp_async16_zfill(&sm.kl[r][c8], a.kn_lo + ko, ok);
-        cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
-        cp_async16_zfill(&sm.k2[r][c8], a.kn_l2 + ko, ok);
-        cp_async16_zfill(&sm.q2[r][c8], a.qn_l2 + ko, ok);
+        for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
+            const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+            const bool ok = r < rows;
+            const size_t ko = ((size_t)(t0 + (ok ? r : 0)) * a.n_k + kh) * S + c8;
+            cp_async16_zfill(&sm.k[r][c8], a.kn + ko, ok);
+            cp_async16_zfill(&sm.q[r][c8], a.qn + ko, ok);
+            cp_async16_zfill(&sm.kl[r][c8], a.kn_lo + ko, ok);
+            cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
+            cp_async16_zfill(&sm.k2[r][c8], a.kn_l2 + ko, ok);
+            cp_async16_zfill(&sm.q2[r][c8], a.qn_l2 + ko, ok);
+        }
+        cp_async_commit();
     }
-    cp_async_commit();
 #pragma unroll 2
     for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
         const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
@@ -317,15 +393,62 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
         sm.beta[ta] = ta < rows ? a.bt[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
         sm.beta[tb] = tb < rows ? a.bt[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
     }
-    cp_async_wait<1>();  // q and k (v may still be in flight)
-    __syncthreads();
+    if constexpr (!TC) {
+        cp_async_wait<1>();  // q and k (v may still be in flight)
+        __syncthreads();
+    }
     // ---- K K^T as hi*hi + hi*lo + lo*hi of the bf16 pairs, and Q K^T of
     // the bf16 triples (hi*hi + hi*lo + lo*hi + lo*lo + hi*l2 + l2*hi): the
     // readout P U of a token whose state has all but decayed away cancels
     // down to the q.k products of its own chunk, and the per-head gated norm
     // that follows magnifies their error; pairs (16 bits) measured 1.3e-2 of
     // such a head's output at 4096 tokens, triples stay at the f32 level
-    {
+    if constexpr (TC) {
+        // one tcgen05 chain: [K; Q]_xa K_xb^T over the six (xa, xb) plane
+        // pairs Q K^T takes (hi hi, hi lo, hi l2, lo hi, lo lo, l2 hi); the
+        // accumulator's rows 0-63 are K K^T (to six terms), 64-127 Q K^T
+        if (tid == 0) {
+            const bool okq = mbar_wait(&sm.qk_full, 0, a.status);
+            if (okq) {
+                tc::fence_after_sync();
+                constexpr uint32_t id = tc::idesc_bf16(128, 64, false);
+                const int xa[6] = {0, 0, 0, 1, 1, 2}, xb[6] = {0, 1, 2, 0, 1, 0};
+#pragma unroll
+                for (int p = 0; p < 6; ++p) {
+                    const uint64_t ad = tc::smem_desc(smem_u32(qk_block(sm, xa[p], 0)), 16, 1024);
+                    const uint64_t bd = tc::smem_desc(smem_u32(qk_block(sm, xb[p], 0)), 16, 1024);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        // a 16-channel step is 32 bytes inside a box, the next
+                        // box the next block
+                        const uint64_t step = ((kk >> 2) * QK_BLOCK + (kk & 3) * 32) >> 4;
+                        tc::mma_ss(sm.tmem_base, ad + step, bd + step, id, p > 0 || kk > 0);
+                    }
+                }
+                tc::commit(&sm.mma_done);
+            } else {
+                mbar_arrive(&sm.mma_done);  // flagged; the readers go on
+            }
+        }
+        if (warp < 4) {
+            // warp w reads tensor-memory lanes 32w .. 32w + 31: rows of K K^T
+            // (w < 2) or of Q K^T
+            mbar_wait(&sm.mma_done, 0, a.status);
+            tc::fence_after_sync();
+            uint32_t r0[32], r1[32];
+            const uint32_t taddr = sm.tmem_base + ((uint32_t)(warp * 32) << 16);
+            tc::ld32(taddr, r0);
+            tc::ld32(taddr + 32, r1);
+            tc::wait_ld();
+            const int row = warp * 32 + lane;
+            float *dst = row < C ? &sm.kk[row][0] : &sm.qk[row - C][0];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                dst[c] = __uint_as_float(r0[c]);
+                dst[32 + c] = __uint_as_float(r1[c]);
+            }
+        }
+    } else {
         // warp: rows 16 * (warp % 4), columns QK_COLS * (warp / 4) ..
         constexpr int NT = QK_COLS / 8;
         const int rw = (warp & 3) * 16, cn = (warp >> 2) * QK_COLS;
@@ -404,10 +527,19 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
     for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
         const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
         const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
-        const uint4 qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
-        const uint4 ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
-        const uint4 kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
-        const uint4 kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
+        uint4 qh, ql, kh4, kl4;
+        if constexpr (TC) {
+            const uint32_t so = (c0 >> 6) * QK_BLOCK + swz128(r, (c0 & 63) >> 3);
+            qh = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so + Q_HALF);
+            ql = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so + Q_HALF);
+            kh4 = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so);
+            kl4 = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so);
+        } else {
+            qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
+            ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
+            kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
+            kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
+        }
         const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
         const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
         const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
@@ -549,8 +681,13 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
                 uint32_t vh_[4], vl_[4], kh_[4], kl_[4];
                 ld_b2_t(&sm.v[0][0], LDB, n0, ks * 16, lane, vh_);
                 ld_b2_t(&sm.vl[0][0], LDB, n0, ks * 16, lane, vl_);
-                ld_b2_t(&sm.k[0][0], LDB, n0, ks * 16, lane, kh_);
-                ld_b2_t(&sm.kl[0][0], LDB, n0, ks * 16, lane, kl_);
+                if constexpr (TC) {
+                    ld_b2_t_swz(sm.hl[0][0], n0, ks * 16, lane, kh_);
+                    ld_b2_t_swz(sm.hl[1][0], n0, ks * 16, lane, kl_);
+                } else {
+                    ld_b2_t(&sm.k[0][0], LDB, n0, ks * 16, lane, kh_);
+                    ld_b2_t(&sm.kl[0][0], LDB, n0, ks * 16, lane, kl_);
+                }
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     mma_16816(du[2 * np + h], ah, vh_[2 * h], vh_[2 * h + 1]);
@@ -583,6 +720,14 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS) dn_chunk_local_kernel(const
         __threadfence();
         __syncthreads();
         if (tid == 0) st_release_gpu(a.ready + (size_t)vh * a.nc + ck, ready_value);
+    }
+    if constexpr (TC) {
+        tc::fence_before_sync();
+        __syncthreads();
+        if (warp == 0) {
+            tc::fence_after_sync();
+            tc::tmem_dealloc(sm.tmem_base, 64);
+        }
     }
 }
 
@@ -876,9 +1021,13 @@ __global__ void dn_hist_kernel(const DnChunkArgs a) {
 }
 
 cudaError_t init_dn_chunk_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(dn_chunk_local_kernel,
+    cudaError_t e = cudaFuncSetAttribute(dn_chunk_local_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(LocalSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(dn_chunk_local_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(LocalSmemTc) + 1024));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(ScanSmem));
@@ -887,10 +1036,18 @@ cudaError_t init_dn_chunk_kernels() {
 }
 
 cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps, cudaStream_t st,
-                            const DnOverlap *overlap) {
+                            const DnOverlap *overlap, const DnPlaneMaps *planes) {
     using namespace dc;
     DnChunkArgs a = a_in;
     a.w_lo_out = scan_maps == nullptr;
+    auto launch_local = [&](const DnChunkArgs &la) {
+        if (planes)
+            dn_chunk_local_kernel<true>
+                <<<dim3(la.n_v, la.nc), LOCAL_THREADS, sizeof(LocalSmemTc) + 1024, st>>>(la, *planes);
+        else
+            dn_chunk_local_kernel<false>
+                <<<dim3(la.n_v, la.nc), LOCAL_THREADS, sizeof(LocalSmem), st>>>(la, DnPlaneMaps{});
+    };
     dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
                      st>>>(a);
     if (scan_maps && overlap && a.ready) {
@@ -900,18 +1057,18 @@ cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps
         if (e == cudaSuccess) e = cudaStreamWaitEvent(overlap->scan_stream, overlap->fork, 0);
         if (e == cudaSuccess) e = launch_dn_scan_tc(a, *scan_maps, overlap->scan_stream);
         if (e != cudaSuccess) return e;
-        dn_chunk_local_kernel<<<dim3(a.n_v, a.nc), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
+        launch_local(a);
         e = cudaEventRecord(overlap->join, overlap->scan_stream);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(st, overlap->join, 0);
         if (e != cudaSuccess) return e;
     } else if (scan_maps) {
         a.ready = nullptr;
-        dn_chunk_local_kernel<<<dim3(a.n_v, a.nc), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
+        launch_local(a);
         const cudaError_t e = launch_dn_scan_tc(a, *scan_maps, st);
         if (e != cudaSuccess) return e;
     } else {
         a.ready = nullptr;
-        dn_chunk_local_kernel<<<dim3(a.n_v, a.nc), dc::LOCAL_THREADS, sizeof(LocalSmem), st>>>(a);
+        launch_local(a);
         dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
     }
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);

@@ -221,6 +221,12 @@ struct DnChunkArgs {
     // waits for that value and, done, advances ready_epoch[head]
     int *ready, *ready_epoch;
 };
+// The prep kernel's q and k planes (hi, lo, third term) as [t][n_k][128]
+// bf16 with t the call's rows, boxes of 64 channels x 1 head x 64 tokens, the
+// 128-byte swizzle: the chunk-local kernel's tcgen05 form loads them by TMA.
+struct DnPlaneMaps {
+    CUtensorMap q[3], k[3];
+};
 // The second stream and events of an overlapped chunked prefill.
 struct DnOverlap {
     cudaStream_t scan_stream;
@@ -240,9 +246,11 @@ cudaError_t launch_dn_scan_tc(const DnChunkArgs &a, const DnScanMaps &m, cudaStr
 // tcgen05 chunk scan, null the mma.sync one.  With `overlap` (and the tcgen05
 // scan, and a.ready set) the scan runs on overlap->scan_stream beside the
 // chunk-local kernel, forked after the prep kernel and joined before the
-// output kernel.
+// output kernel.  With `planes` the chunk-local kernel takes K K^T and
+// Q K^T on tcgen05 (its tcgen05 form), else on mma.sync.
 cudaError_t launch_dn_chunk(const DnChunkArgs &a, const DnScanMaps *scan_maps, cudaStream_t st,
-                            const DnOverlap *overlap = nullptr);
+                            const DnOverlap *overlap = nullptr,
+                            const DnPlaneMaps *planes = nullptr);
 
 // KV cache fill from f32 (host-visible test and bench helper): positions
 // [p0, p0+n) of every KV head, src [2][n_kv][n][hd] f32 on the device.

@@ -86,14 +86,6 @@ __device__ __forceinline__ void bulk_commit_and_wait() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y,
-                                            int z, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // VERIFY: the multi-row verify form.  The CTA is (key split, KV head); tile
 // row r is draft row r % 32 of query head 4 * kv_head + r / 32, so the four

@@ -79,7 +79,8 @@ struct rl_ctx {
     int *status = nullptr;    // device status word (rl::DEV_*)
     int pos = 0, live = 0;
     int64_t opt_splits = 0, opt_prefill_rows = 64, opt_chunk_rows = 64, opt_cluster = 0;
-    int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1, opt_dn_overlap = 1;
+    int64_t opt_early_tiles = 2, opt_verify_tc = 1, opt_dn_rows = 1, opt_dn_overlap = 1,
+            opt_dn_local_tc = 1;
     int64_t opt_wait_limit_us = 0;  // 0: rl::PEER_WAIT_LIMIT_NS
     int64_t opt_dn_scan_tc = 1;
     // RL_OPT_WALK_SPANS: [n_full][4] {first start, CTAs done, span sum, launches}
@@ -1342,8 +1343,21 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
             const rl::DnOverlap ov{ctx->dn_scan_stream, ctx->dn_fork, ctx->dn_join};
             d.ready = tc_scan && ctx->opt_dn_overlap ? ctx->dn_ready : nullptr;
             d.ready_epoch = ctx->dn_ready_epoch;
+            // the chunk-local kernel's tcgen05 form reads q and k by TMA, through
+            // maps that end at this call's rows (the rows past them read as 0)
+            rl::DnPlaneMaps pm;
+            bool planes_ok = ctx->opt_dn_local_tc != 0;
+            const uint64_t nk = c.n_k_heads, s = c.d_state;
+            const __nv_bfloat16 *qp[3] = {ctx->dn_qn, ctx->dn_qn_lo, ctx->dn_qn_l2};
+            const __nv_bfloat16 *kp[3] = {ctx->dn_kn, ctx->dn_kn_lo, ctx->dn_kn_l2};
+            for (int x = 0; x < 3 && planes_ok; ++x)
+                planes_ok = rl::encode_bf16_3d(&pm.q[x], qp[x], s, nk, (uint64_t)t, s * 2,
+                                               nk * s * 2, 64, 1, 64) == cudaSuccess &&
+                            rl::encode_bf16_3d(&pm.k[x], kp[x], s, nk, (uint64_t)t, s * 2,
+                                               nk * s * 2, 64, 1, 64) == cudaSuccess;
             CK(ctx, rl::launch_dn_chunk(d, tc_scan ? &ctx->dn_scan_maps : nullptr, ctx->stream,
-                                        tc_scan && ctx->opt_dn_overlap ? &ov : nullptr));
+                                        tc_scan && ctx->opt_dn_overlap ? &ov : nullptr,
+                                        planes_ok ? &pm : nullptr));
         }
         // a step of this layer right after must not read the state early
         ctx->prev_dn = 1;
@@ -1591,6 +1605,10 @@ int rl_set_option(rl_ctx *ctx, int option, int64_t value) {
         if (value > 1) return fail(ctx, RL_EINVAL, "the overlap option must be 0 or 1");
         ctx->opt_dn_overlap = value;
         return RL_OK;
+    case RL_OPT_DN_LOCAL_TC:
+        if (value > 1) return fail(ctx, RL_EINVAL, "the chunk-local option must be 0 or 1");
+        ctx->opt_dn_local_tc = value;
+        return RL_OK;
     case RL_OPT_WALK_SPANS:
         if (value > 1) return fail(ctx, RL_EINVAL, "the span option must be 0 or 1");
         CK(ctx, cudaSetDevice(ctx->device));
@@ -1624,6 +1642,7 @@ int64_t rl_get_option(const rl_ctx *ctx, int option) {
     case RL_OPT_WALK_SPANS: return ctx->spans ? 1 : 0;
     case RL_OPT_DN_SCAN_TC: return ctx->opt_dn_scan_tc;
     case RL_OPT_DN_OVERLAP: return ctx->opt_dn_overlap;
+    case RL_OPT_DN_LOCAL_TC: return ctx->opt_dn_local_tc;
     default: return -1;
     }
 }

@@ -26,7 +26,7 @@ RL_OK, RL_EINVAL, RL_ECONTEXT, RL_ECUDA, RL_ENCCL, RL_ETIMEOUT, RL_EUNSUPPORTED,
 RL_KV_F32, RL_KV_BF16 = 0, 1
 (RL_OPT_SPLITS, RL_OPT_PREFILL_ROWS, RL_OPT_CHUNK_ROWS, RL_OPT_CLUSTER, RL_OPT_EARLY_TILES,
  RL_OPT_VERIFY_TC, RL_OPT_DN_ROWS, RL_OPT_WAIT_LIMIT_US, RL_OPT_WALK_SPANS,
- RL_OPT_DN_SCAN_TC, RL_OPT_DN_OVERLAP) = range(11)
+ RL_OPT_DN_SCAN_TC, RL_OPT_DN_OVERLAP, RL_OPT_DN_LOCAL_TC) = range(12)
 PROF_KERNELS = ("prologue", "decode", "merge", "dn_step", "prefill", "dn_chunk", "verify",
                 "walk_span")
 HOST, DEVICE = 0, 1

@@ -20,7 +20,7 @@ COS_MIN = 0.9999
 pytestmark = pytest.mark.gpu
 
 
-def run_chunked(t, seed, unit_norm=True, scan_tc=1, overlap=1):
+def run_chunked(t, seed, unit_norm=True, scan_tc=1, overlap=1, local_tc=1):
     r = orc.Rng(seed)
     rows = cases.lin_rows(r, t)
     w = cases.lin_weights(r, unit_norm=unit_norm)
@@ -32,6 +32,7 @@ def run_chunked(t, seed, unit_norm=True, scan_tc=1, overlap=1):
     with rlcuda.Context(cfg) as ctx:
         ctx.set_option(rlcuda.RL_OPT_DN_SCAN_TC, scan_tc)
         ctx.set_option(rlcuda.RL_OPT_DN_OVERLAP, overlap)
+        ctx.set_option(rlcuda.RL_OPT_DN_LOCAL_TC, local_tc)
         ctx.set_weights_linear(0, w.conv1d, w.ssm_a, w.dt_bias, w.norm)
         ctx.write_conv(0, conv)
         ctx.write_ssm(0, ssm)
@@ -42,16 +43,20 @@ def run_chunked(t, seed, unit_norm=True, scan_tc=1, overlap=1):
     return got, want, conv_got, conv_w, ssm_got, ssm_w, chunk_launches
 
 
-@pytest.mark.parametrize("scan_tc,overlap", [(1, 1), (1, 0), (0, 0)],
-                         ids=["tcgen05_scan_overlapped", "tcgen05_scan", "mma_sync_scan"])
+@pytest.mark.parametrize("scan_tc,overlap,local_tc",
+                         [(1, 1, 1), (1, 0, 1), (1, 1, 0), (0, 0, 0)],
+                         ids=["tcgen05_scan_overlapped", "tcgen05_scan", "mma_sync_local",
+                              "mma_sync_scan"])
 @pytest.mark.parametrize("t", [64, 100, 257, 1024, 4096])
-def test_chunked_prefill_matches_the_token_sequential_oracle(t, scan_tc, overlap):
+def test_chunked_prefill_matches_the_token_sequential_oracle(t, scan_tc, overlap, local_tc):
     """t = 4096 is the benchmarked config-2 DeltaNet layer: the state is
     carried through 64 chunks, where the bf16-pair products' error would
     grow if it were going to.  Both chunk scans: tcgen05 (the default, beside
-    the chunk-local kernel or after it) and mma.sync."""
+    the chunk-local kernel or after it) and mma.sync; the chunk-local kernel's
+    K K^T and Q K^T on tcgen05 (the default) and on mma.sync."""
     got, want, conv_got, conv_w, ssm_got, ssm_w, n = run_chunked(t, 900 + t, scan_tc=scan_tc,
-                                                                 overlap=overlap)
+                                                                 overlap=overlap,
+                                                                 local_tc=local_tc)
     assert n == 1, "the call did not take the chunked kernels"
     assert np.isfinite(got).all()
     err = cases.rel_err_per_head(got, want, cases.S)
