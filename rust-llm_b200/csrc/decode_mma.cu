@@ -663,10 +663,24 @@ __global__ void __launch_bounds__(256) peer_merge_kernel(const unsigned long lon
         const float v = xload(p0 + g * stride + dm::HD + (d >> 5), E, start, limit_ns, late);
         (d < 32 ? m_s : l_s)[g] = v;
     }
+    // every GPU's value d in flight at once (one round trip for all of them,
+    // where polling them in turn took one each), then a bounded wait for any
+    // that did not yet carry the step's epoch
+    unsigned long long w[RL_EXCHANGE_MAX_GPUS];
+#pragma unroll
+    for (int g = 0; g < RL_EXCHANGE_MAX_GPUS; ++g)
+        if (g < world)
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
+                         : "=l"(w[g])
+                         : "l"(p0 + g * stride + d)
+                         : "memory");
     float vals[RL_EXCHANGE_MAX_GPUS];
 #pragma unroll
     for (int g = 0; g < RL_EXCHANGE_MAX_GPUS; ++g)
-        if (g < world) vals[g] = xload(p0 + g * stride + d, E, start, limit_ns, late);
+        if (g < world)
+            vals[g] = (unsigned)(w[g] >> 32) == E
+                          ? __uint_as_float((unsigned)w[g])
+                          : xload(p0 + g * stride + d, E, start, limit_ns, late);
     if (__syncthreads_or(late) && d == 0) atomicOr(status, DEV_TIMEOUT);
     float M = -INFINITY;
     for (int g = 0; g < world; ++g) M = fmaxf(M, m_s[g]);

@@ -1050,17 +1050,24 @@ cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps
     };
     dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
                      st>>>(a);
+    const int conv_dim = 2 * a.n_k * S + a.n_v * S;
     if (scan_maps && overlap && a.ready) {
         // the scan beside the chunk-local kernel: it starts once the prep
-        // kernel is done and walks each head's chunks as their flags go up
+        // kernel is done and walks each head's chunks as their flags go up;
+        // the output and history kernels follow it on its stream, and the
+        // context's stream joins it after them
+        cudaStream_t ss = overlap->scan_stream;
         cudaError_t e = cudaEventRecord(overlap->fork, st);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(overlap->scan_stream, overlap->fork, 0);
-        if (e == cudaSuccess) e = launch_dn_scan_tc(a, *scan_maps, overlap->scan_stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ss, overlap->fork, 0);
+        if (e == cudaSuccess) e = launch_dn_scan_tc(a, *scan_maps, ss);
         if (e != cudaSuccess) return e;
         launch_local(a);
-        e = cudaEventRecord(overlap->join, overlap->scan_stream);
+        dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, ss>>>(a);
+        dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, ss>>>(a);
+        e = cudaEventRecord(overlap->join, ss);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(st, overlap->join, 0);
         if (e != cudaSuccess) return e;
+        return cudaGetLastError();
     } else if (scan_maps) {
         a.ready = nullptr;
         launch_local(a);
@@ -1072,7 +1079,6 @@ cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps
         dn_chunk_scan_kernel<<<dim3(S / JC, a.n_v), SCAN_THREADS, sizeof(ScanSmem), st>>>(a);
     }
     dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
-    const int conv_dim = 2 * a.n_k * S + a.n_v * S;
     dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, st>>>(a);
     return cudaGetLastError();
 }
