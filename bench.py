@@ -461,8 +461,9 @@ def dn_prefill_bench(args, dev, stream, rlcuda, torch):
             "tflops_algorithmic": tf, "frac_of_measured_bf16": tf / peak,
             "note": "operands as bf16 pairs (q, k in Q K^T as triples), most products three "
                     "bf16 terms (hi*hi + hi*lo + lo*hi), so the tensor pipes execute 2-6x the "
-                    "algorithmic FLOP; chunk-local products on mma.sync, the chunk scan on "
-                    "tcgen05 beside the chunk-local kernel (off with --dn-serial)",
+                    "algorithmic FLOP; the chunk-local Q K^T and K K^T on tcgen05 (the rest of "
+                    "that kernel on mma.sync), the chunk scan on tcgen05 beside the chunk-local "
+                    "kernel (off with --dn-serial)",
             "overlapped": not args.dn_serial}
 
 

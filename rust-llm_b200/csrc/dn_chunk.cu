@@ -1032,6 +1032,17 @@ cudaError_t init_dn_chunk_kernels() {
         e = cudaFuncSetAttribute(dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(ScanSmem));
     if (e == cudaSuccess) e = init_dn_scan_tc_kernel();
+    // With lazy module loading a kernel is loaded at its first launch, and
+    // loading waits for the device.  The overlapped prefill launches the
+    // chunk-local, output and history kernels while the scan spins on the
+    // chunks' ready flags, so a first launch there would wait for a scan that
+    // waits for it: load every kernel of the path here, before any scan runs.
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, dn_prep_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, dn_out_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, dn_hist_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, dn_chunk_local_kernel<false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, dn_chunk_local_kernel<true>);
     return e;
 }
 
