@@ -716,8 +716,10 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
         }
     }
     if (a.ready) {
-        // every thread's stores are visible GPU-wide before the flag goes up
-        __threadfence();
+        // the barrier orders every thread's stores before thread 0's, and a
+        // release is cumulative: once the flag is seen at GPU scope, so is
+        // everything its writer had seen (the semaphore pattern; a fence in
+        // every thread would hold each warp until its own stores land)
         __syncthreads();
         if (tid == 0) st_release_gpu(a.ready + (size_t)vh * a.nc + ck, ready_value);
     }
