@@ -397,6 +397,53 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
         cp_async_wait<1>();  // q and k (v may still be in flight)
         __syncthreads();
     }
+    // Q' = gamma Q and K' = gamma_C / gamma K as bf16 pairs, 8 consecutive
+    // elements a thread (16-byte stores); needs cum and the q/k planes
+    const size_t blk = (size_t)vh * a.nc + ck;
+    auto write_qk_prime = [&]() {
+        const float cum_c = sm.cum[C - 1];
+        __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
+        __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
+#pragma unroll 2
+        for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
+            const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
+            const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
+            uint4 qh, ql, kh4, kl4;
+            if constexpr (TC) {
+                const uint32_t so = (c0 >> 6) * QK_BLOCK + swz128(r, (c0 & 63) >> 3);
+                qh = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so + Q_HALF);
+                ql = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so + Q_HALF);
+                kh4 = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so);
+                kl4 = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so);
+            } else {
+                qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
+                ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
+                kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
+                kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
+            }
+            const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
+            const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
+            const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
+            const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
+            uint32_t xh[4], xl[4], yh[4], yl[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
+                const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
+                const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
+                const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
+                xh[k] = pack_bf16(x0, x1);
+                xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+                yh[k] = pack_bf16(y0, y1);
+                yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
+            }
+            const size_t o = (size_t)r * S + c0;
+            *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+            *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+            *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+            *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
+        }
+    };
     // ---- K K^T as hi*hi + hi*lo + lo*hi of the bf16 pairs, and Q K^T of
     // the bf16 triples (hi*hi + hi*lo + lo*hi + lo*lo + hi*l2 + l2*hi): the
     // readout P U of a token whose state has all but decayed away cancels
@@ -406,9 +453,14 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
     if constexpr (TC) {
         // one tcgen05 chain: [K; Q]_xa K_xb^T over the six (xa, xb) plane
         // pairs Q K^T takes (hi hi, hi lo, hi l2, lo hi, lo lo, l2 hi); the
-        // accumulator's rows 0-63 are K K^T (to six terms), 64-127 Q K^T
-        if (tid == 0) {
-            const bool okq = mbar_wait(&sm.qk_full, 0, a.status);
+        // accumulator's rows 0-63 are K K^T (to six terms), 64-127 Q K^T.
+        // The chain keeps the tensor pipe busy for ~2,400 cycles: warp 15
+        // issues it while every warp writes Q' and K' from the same planes,
+        // then warps 0-3 read the products back.  The barrier after the
+        // planes land also publishes cum and beta.
+        const bool okq = mbar_wait(&sm.qk_full, 0, a.status);
+        __syncthreads();
+        if (tid == LOCAL_THREADS - 32) {
             if (okq) {
                 tc::fence_after_sync();
                 constexpr uint32_t id = tc::idesc_bf16(128, 64, false);
@@ -430,6 +482,7 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
                 mbar_arrive(&sm.mma_done);  // flagged; the readers go on
             }
         }
+        write_qk_prime();
         if (warp < 4) {
             // warp w reads tensor-memory lanes 32w .. 32w + 31: rows of K K^T
             // (w < 2) or of Q K^T
@@ -499,10 +552,10 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
         }
     }
     __syncthreads();
-    const size_t blk = (size_t)vh * a.nc + ck;
-    // ---- P = Q K^T o Mgamma (s <= t), Q' = gamma Q, K' = gamma_C / gamma K:
-    // written now, so that the stores drain while T is built
-    // (8 consecutive elements a thread: 16-byte stores)
+    // ---- P = Q K^T o Mgamma (s <= t), and in the mma.sync form Q' and K'
+    // (the tcgen05 form wrote them beside its products): written now, so
+    // that the stores drain while T is built (8 consecutive elements a
+    // thread: 16-byte stores)
     __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
 #pragma unroll 2
     for (int e8 = tid; e8 < C * C / 8; e8 += LOCAL_THREADS) {
@@ -521,47 +574,7 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
         *reinterpret_cast<uint4 *>(pl_out + r * C + s0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     const float cum_c = sm.cum[C - 1];
-    __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
-    __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
-#pragma unroll 2
-    for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
-        const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
-        const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
-        uint4 qh, ql, kh4, kl4;
-        if constexpr (TC) {
-            const uint32_t so = (c0 >> 6) * QK_BLOCK + swz128(r, (c0 & 63) >> 3);
-            qh = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so + Q_HALF);
-            ql = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so + Q_HALF);
-            kh4 = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so);
-            kl4 = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so);
-        } else {
-            qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
-            ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
-            kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
-            kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
-        }
-        const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
-        const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
-        const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
-        const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
-        uint32_t xh[4], xl[4], yh[4], yl[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
-            const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
-            const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
-            const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
-            xh[k] = pack_bf16(x0, x1);
-            xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
-            yh[k] = pack_bf16(y0, y1);
-            yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
-        }
-        const size_t o = (size_t)r * S + c0;
-        *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
-        *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
-        *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
-        *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
-    }
+    if constexpr (!TC) write_qk_prime();
     if (tid == 0) a.gc[blk] = __expf(cum_c);
     // ---- L (in place over kk) and T = (I + L)^-1, one column per thread
     {
