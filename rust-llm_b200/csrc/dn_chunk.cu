@@ -95,6 +95,11 @@ __global__ void __launch_bounds__(256, 4) dn_prep_kernel(const DnChunkArgs a) {
     using namespace dc;
     const int lane = threadIdx.x & 31;
     const int i0 = blockIdx.x * PREP_TOKENS, g = blockIdx.y * 8 + (threadIdx.x >> 5);
+    if (a.out_ready && blockIdx.y == 0) {
+        // the output kernel of this call waits for the scan to count these up
+        const int f = blockIdx.x * blockDim.x + threadIdx.x;
+        if (f < a.n_v * a.nc) a.out_ready[f] = 0;
+    }
     const int n_groups = 2 * a.n_k + a.n_v;
     if (g >= n_groups) return;
     const int key_dim = a.n_k * S, conv_dim = 2 * key_dim + a.n_v * S;
@@ -1001,9 +1006,15 @@ __global__ void __launch_bounds__(128) dn_out_kernel(const DnChunkArgs a) {
     const int i = blockIdx.x, vh = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (vh >= a.n_v) return;
     const size_t off = ((size_t)i * a.n_v + vh) * S + lane * 4;
-    const float4 o = *reinterpret_cast<const float4 *>(a.opre + off);
     const float4 z = *reinterpret_cast<const float4 *>(a.z + off);
     const float4 w = *reinterpret_cast<const float4 *>(a.norm + lane * 4);
+    if (a.out_ready) {
+        // beside the scan: its rows of this chunk are stored once its four
+        // readout warps have counted in
+        if (lane == 0) wait_flag_gpu(a.out_ready + (size_t)vh * a.nc + i / C, 4, a.status);
+        __syncwarp();
+    }
+    const float4 o = *reinterpret_cast<const float4 *>(a.opre + off);
     double sq = (double)__fmul_rn(o.x, o.x) + (double)__fmul_rn(o.y, o.y) +
                 (double)__fmul_rn(o.z, o.z) + (double)__fmul_rn(o.w, o.w);
     sq = warp_sum_d(sq);
@@ -1079,17 +1090,19 @@ cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps
     const int conv_dim = 2 * a.n_k * S + a.n_v * S;
     if (scan_maps && overlap && a.ready) {
         // the scan beside the chunk-local kernel: it starts once the prep
-        // kernel is done and walks each head's chunks as their flags go up;
-        // the output and history kernels follow it on its stream, and the
-        // context's stream joins it after them
+        // kernel is done and walks each head's chunks as their flags go up.
+        // The history and output kernels follow the chunk-local kernel on the
+        // context's stream, beside the scan's last chunks: an output warp
+        // waits for its chunk's rows of the scan (out_ready).  The context's
+        // stream then joins the scan.
         cudaStream_t ss = overlap->scan_stream;
         cudaError_t e = cudaEventRecord(overlap->fork, st);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(ss, overlap->fork, 0);
         if (e == cudaSuccess) e = launch_dn_scan_tc(a, *scan_maps, ss);
         if (e != cudaSuccess) return e;
         launch_local(a);
-        dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, ss>>>(a);
-        dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, ss>>>(a);
+        dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, st>>>(a);
+        dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
         e = cudaEventRecord(overlap->join, ss);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(st, overlap->join, 0);
         if (e != cudaSuccess) return e;

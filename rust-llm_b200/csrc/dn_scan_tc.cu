@@ -424,6 +424,13 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             }
             tc::fence_before_sync();
             mbar_arrive(&o_empty[b]);
+            if (a.out_ready) {
+                // this warp's rows of the chunk are stored: each of the four
+                // readout warps adds 1 with release semantics (cumulative over
+                // the lanes' stores, which the warp barrier orders first)
+                __syncwarp();
+                if (lane == 0) red_release_add_gpu(a.out_ready + (size_t)vh * a.nc + c, 1);
+            }
         }
     }
     tc::fence_before_sync();

@@ -220,6 +220,11 @@ struct DnChunkArgs {
     // chunk] = ready_epoch[head] + 1 once its outputs are written; the scan
     // waits for that value and, done, advances ready_epoch[head]
     int *ready, *ready_epoch;
+    // out_ready[head * nc + chunk]: zeroed by the prep kernel; each of the
+    // tcgen05 scan's four readout warps adds 1 once its pre-norm rows of the
+    // chunk are stored; the output kernel waits for 4 (null: it runs after
+    // the scan)
+    int *out_ready;
 };
 // The prep kernel's q and k planes (hi, lo, third term) as [t][n_k][128]
 // bf16 with t the call's rows, boxes of 64 channels x 1 head x 64 tokens, the

@@ -63,6 +63,7 @@ struct rl_ctx {
     // ready flags, per head the epoch the flags count, the scan's stream and
     // the fork and join events
     int *dn_ready = nullptr, *dn_ready_epoch = nullptr;
+    int *dn_out_ready = nullptr;
     cudaStream_t dn_scan_stream = nullptr;
     cudaEvent_t dn_fork = nullptr, dn_join = nullptr;
     float *stage_raw = nullptr;  // the status word (64 B), then the staging
@@ -240,6 +241,7 @@ void free_all(rl_ctx *x) {
     if (x->hpin_base) cudaFreeHost(x->hpin_base);
     if (x->dn_ready) cudaFree(x->dn_ready);
     if (x->dn_ready_epoch) cudaFree(x->dn_ready_epoch);
+    if (x->dn_out_ready) cudaFree(x->dn_out_ready);
     if (x->dn_fork) cudaEventDestroy(x->dn_fork);
     if (x->dn_join) cudaEventDestroy(x->dn_join);
     if (x->dn_scan_stream) cudaStreamDestroy(x->dn_scan_stream);
@@ -580,7 +582,8 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         int lo_prio = 0, hi_prio = 0;
         cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
         if ((code = alloc(x, &x->dn_ready, nv * nc)) ||
-            (code = alloc(x, &x->dn_ready_epoch, nv)))
+            (code = alloc(x, &x->dn_ready_epoch, nv)) ||
+            (code = alloc(x, &x->dn_out_ready, nv * nc)))
             return bail(code);
         if (cudaMemset(x->dn_ready, 0, nv * nc * sizeof(int)) != cudaSuccess ||
             cudaMemset(x->dn_ready_epoch, 0, nv * sizeof(int)) != cudaSuccess ||
@@ -1343,6 +1346,7 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
             const rl::DnOverlap ov{ctx->dn_scan_stream, ctx->dn_fork, ctx->dn_join};
             d.ready = tc_scan && ctx->opt_dn_overlap ? ctx->dn_ready : nullptr;
             d.ready_epoch = ctx->dn_ready_epoch;
+            d.out_ready = d.ready ? ctx->dn_out_ready : nullptr;
             // the chunk-local kernel's tcgen05 form reads q and k by TMA, through
             // maps that end at this call's rows (the rows past them read as 0)
             rl::DnPlaneMaps pm;
