@@ -120,18 +120,26 @@ __global__ void __launch_bounds__(256, 4) dn_prep_kernel(const DnChunkArgs a) {
             for (int e = 0; e < 4; ++e) h[j][e] = a.conv_state[(size_t)(ch + e) * 3 + (src + 3)];
         }
     }
+    // a v head's gates, one token a lane: their loads go out with the rows'
+    const bool is_v = g >= 2 * a.n_k;
+    const int vh = g - 2 * a.n_k;
+    float gx = 0.0f, gb = 0.0f;
+    if (is_v && lane < PREP_TOKENS && i0 + lane < a.t) {
+        gx = __fadd_rn(a.alpha[(size_t)(i0 + lane) * a.n_v + vh], a.dt_bias[vh]);
+        gb = a.beta[(size_t)(i0 + lane) * a.n_v + vh];
+    }
     float4 xin[PREP_TOKENS];
 #pragma unroll
     for (int tt = 0; tt < PREP_TOKENS; ++tt)
         xin[tt] = i0 + tt < a.t
                       ? *reinterpret_cast<const float4 *>(a.qkv + (size_t)(i0 + tt) * conv_dim + ch)
                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    // the causal conv and SiLU of every token first, so that the q/k heads'
+    // norm reductions below run side by side
+    float y[PREP_TOKENS][4];
 #pragma unroll
     for (int tt = 0; tt < PREP_TOKENS; ++tt) {
-        const int i = i0 + tt;
-        if (i >= a.t) break;  // warp-uniform
         const float xs[4] = {xin[tt].x, xin[tt].y, xin[tt].z, xin[tt].w};
-        float y[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             // forward.rs:2018-2031: x * w[3] first, then the history taps in order
@@ -139,38 +147,55 @@ __global__ void __launch_bounds__(256, 4) dn_prep_kernel(const DnChunkArgs a) {
             c = __fadd_rn(c, __fmul_rn(h[0][e], w[e].x));
             c = __fadd_rn(c, __fmul_rn(h[1][e], w[e].y));
             c = __fadd_rn(c, __fmul_rn(h[2][e], w[e].z));
-            y[e] = silu_fast(c);
+            y[tt][e] = silu_fast(c);
             h[0][e] = h[1][e];
             h[1][e] = h[2][e];
             h[2][e] = xs[e];
         }
-        if (g < 2 * a.n_k) {
-            // L2 norm: rms_scale with eps/n, then 1/sqrt(n) (forward.rs:1720-1727)
-            double sq = 0.0;
+    }
+    const int n_tok = min(PREP_TOKENS, a.t - i0);
+    if (!is_v) {
+        // L2 norm: rms_scale with eps/n, then 1/sqrt(n) (forward.rs:1720-1727);
+        // each token's sum is the same butterfly, the tokens' interleaved
+        double sq[PREP_TOKENS];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) sq += (double)__fmul_rn(y[e], y[e]);
-            sq = warp_sum_d(sq);
-            const float sc = rms_scale_fast(sq, S, a.eps / (float)S);
-            const float shrink = 1.0f / sqrtf((float)S);
+        for (int tt = 0; tt < PREP_TOKENS; ++tt) {
+            sq[tt] = 0.0;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], sc), shrink);
-            const bool is_q = g < a.n_k;
-            const size_t o = ((size_t)i * a.n_k + (is_q ? g : g - a.n_k)) * S + lane * 4;
+            for (int e = 0; e < 4; ++e) sq[tt] += (double)__fmul_rn(y[tt][e], y[tt][e]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int tt = 0; tt < PREP_TOKENS; ++tt)
+                sq[tt] += __shfl_xor_sync(0xffffffffu, sq[tt], o);
+        const float shrink = 1.0f / sqrtf((float)S);
+        const bool is_q = g < a.n_k;
+#pragma unroll
+        for (int tt = 0; tt < PREP_TOKENS; ++tt) {
+            if (tt >= n_tok) break;  // warp-uniform
+            const float sc = rms_scale_fast(sq[tt], S, a.eps / (float)S);
+            float yn[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) yn[e] = __fmul_rn(__fmul_rn(y[tt][e], sc), shrink);
+            const size_t o = ((size_t)(i0 + tt) * a.n_k + (is_q ? g : g - a.n_k)) * S + lane * 4;
             store_triple4((is_q ? a.qn : a.kn) + o, (is_q ? a.qn_lo : a.kn_lo) + o,
-                          (is_q ? a.qn_l2 : a.kn_l2) + o, y);
-        } else {
-            const int vh = g - 2 * a.n_k;
-            const size_t o = ((size_t)i * a.n_v + vh) * S + lane * 4;
-            store_pair4(a.vn + o, a.vn_lo + o, y);
-            if (lane == 0) {
-                // gates (forward.rs:1530-1546): log decay and beta
-                // (hardware exp2 / log2: one lane runs these while the warp waits)
-                const float x = __fadd_rn(a.alpha[(size_t)i * a.n_v + vh], a.dt_bias[vh]);
-                const float sp = x > 20.0f ? x : __logf(1.0f + __expf(x));
-                a.lg[(size_t)i * a.n_v + vh] = __fmul_rn(sp, a.ssm_a[vh]);
-                a.bt[(size_t)i * a.n_v + vh] =
-                    __fdividef(1.0f, 1.0f + __expf(-a.beta[(size_t)i * a.n_v + vh]));
-            }
+                          (is_q ? a.qn_l2 : a.kn_l2) + o, yn);
+        }
+    } else {
+#pragma unroll
+        for (int tt = 0; tt < PREP_TOKENS; ++tt) {
+            if (tt >= n_tok) break;  // warp-uniform
+            const size_t o = ((size_t)(i0 + tt) * a.n_v + vh) * S + lane * 4;
+            store_pair4(a.vn + o, a.vn_lo + o, y[tt]);
+        }
+        if (lane < n_tok) {
+            // gates (forward.rs:1530-1546): log decay and beta, token i0 + lane
+            // (hardware exp2 / log2)
+            const size_t o = (size_t)(i0 + lane) * a.n_v + vh;
+            const float sp = gx > 20.0f ? gx : __logf(1.0f + __expf(gx));
+            a.lg[o] = __fmul_rn(sp, a.ssm_a[vh]);
+            a.bt[o] = __fdividef(1.0f, 1.0f + __expf(-gb));
         }
     }
 }
