@@ -60,8 +60,9 @@ constexpr int UW_COLS = S * 4 / LOCAL_WARPS;  // Ut, W columns per warp
 // (the accurate library forms made the prep and output kernels issue-bound).
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// dn_prep_kernel: grid (t, groups / 8), 8 warps; one warp per (token, group
-// of 128 channels: a q head, a k head or a v head), 4 channels per lane.
+// dn_prep_kernel: grid (t / PREP_TOKENS, groups / 8), 8 warps; one warp per
+// (PREP_TOKENS tokens, group of 128 channels: a q head, a k head or a v
+// head), 4 channels per lane.
 __device__ __forceinline__ void store_pair4(__nv_bfloat16 *hi, __nv_bfloat16 *lo, const float *y) {
     uint2 h, l;
     h.x = pack_bf16(y[0], y[1]);
@@ -90,8 +91,8 @@ __device__ __forceinline__ void store_triple4(__nv_bfloat16 *hi, __nv_bfloat16 *
 // One warp per (8 consecutive tokens, group of 128 channels): the group's
 // conv weights are loaded once and the three-token history slides along in
 // registers.
-constexpr int PREP_TOKENS = 4;
-__global__ void __launch_bounds__(256, 4) dn_prep_kernel(const DnChunkArgs a) {
+constexpr int PREP_TOKENS = 8;
+__global__ void __launch_bounds__(256, 3) dn_prep_kernel(const DnChunkArgs a) {
     using namespace dc;
     const int lane = threadIdx.x & 31;
     const int i0 = blockIdx.x * PREP_TOKENS, g = blockIdx.y * 8 + (threadIdx.x >> 5);
