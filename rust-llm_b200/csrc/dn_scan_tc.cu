@@ -33,9 +33,11 @@
 //              for the next products
 //   warps 8-11 the readout: O^T from tensor memory to the output rows, off
 //              the chain's path (the readout accumulator is double-buffered)
-//   warp 12    TMA producer, one lane per operand (K' double-buffered; W,
-//              Q', P single, each refilled as soon as the MMAs that read it
-//              are done), and bulk L2 prefetches two chunks ahead
+//   warp 12    TMA producer, one lane per operand (W, Q', P, K', each
+//              refilled as soon as the MMAs that read it are done), bulk L2
+//              prefetches two chunks ahead, and a lane that waits for each
+//              chunk's flag and stages its Ut (f32) and gamma_C in shared
+//              memory for the compute warps (no global load on the chain)
 //   warp 13    tensor-memory owner and MMA issuer (one lane): U, the first
 //              readout product while the compute warps convert U (the tensor
 //              pipe is otherwise idle then), the state update, the second
@@ -59,13 +61,14 @@ constexpr uint32_t BOX128 = 128 * 128;  // 128 rows x 64 bf16
 constexpr uint32_t W_OFF = 0;                     // [i box] 64 t x 64 i, hi only
 constexpr uint32_t Q_OFF = W_OFF + 2 * BOX64;     // [hi, lo][i box]
 constexpr uint32_t P_OFF = Q_OFF + 4 * BOX64;     // [hi, lo] 64 t x 64 s
-constexpr uint32_t K_OFF = P_OFF + 2 * BOX64;     // [buffer][hi, lo][i box] 64 t x 64 i
-constexpr uint32_t ST_OFF = K_OFF + 8 * BOX64;    // S^T [hi, lo][i box] 128 j x 64 i
+constexpr uint32_t K_OFF = P_OFF + 2 * BOX64;     // [hi, lo][i box] 64 t x 64 i
+constexpr uint32_t UTS_OFF = K_OFF + 4 * BOX64;   // Ut, f32 64 t x 128 j (plain rows)
+constexpr uint32_t ST_OFF = UTS_OFF + 4 * BOX64;  // S^T [hi, lo][i box] 128 j x 64 i
 constexpr uint32_t UT_OFF = ST_OFF + 4 * BOX128;  // U^T [hi, lo] 128 j x 64 t
 constexpr uint32_t SMEM = UT_OFF + 2 * BOX128 + 1024;
 constexpr uint32_t TMEM_COLS = 512, S_COL = 0, U_COL = 128, O_COL = 256;  // O: 2 x 64
 constexpr uint32_t W_BYTES = 2 * BOX64, Q_BYTES = 4 * BOX64, P_BYTES = 2 * BOX64,
-                   K_BYTES = 4 * BOX64;
+                   K_BYTES = 4 * BOX64, UT_BYTES = C * S * 4;
 }  // namespace sc
 
 // Byte offset of the 16-byte chunk `c` of row `r` in a 128-byte swizzled box.
@@ -96,7 +99,9 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
     using namespace sc;
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t w_full, w_empty, q_full, q_empty, p_full, p_empty,
-        k_full[2], k_empty[2], s_ready, u_done, u_ready, s_done, o_full[2], o_empty[2], fin;
+        k_full, k_empty, ut_full, ut_empty, s_ready, u_done, u_ready, s_done, o_full[2], o_empty[2],
+        fin;
+    __shared__ float gc_s;  // gamma_C of the chunk whose Ut is staged
     __shared__ uint32_t tmem_base;
     __shared__ int flag_s;
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -118,11 +123,13 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
 
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&k_full[b], 1);
-            mbar_init(&k_empty[b], 1);
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 128);
         }
+        mbar_init(&k_full, 1);
+        mbar_init(&k_empty, 1);
+        mbar_init(&ut_full, 1);
+        mbar_init(&ut_empty, 8);
         mbar_init(&w_full, 1);
         mbar_init(&w_empty, 1);
         mbar_init(&q_full, 1);
@@ -147,8 +154,11 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
     const uint32_t tmem = tmem_base;
 
     if (warp == PRODUCER_WARP) {
-        // ---------------- TMA producer: lane 0 W, 1 Q', 2 P, 3 K', 4 the L2
-        // prefetch of the chunk after next ----------------
+        // ---------------- TMA producer: lane 0 W (and, after the chunk-local
+        // kernel, the L2 prefetch of the chunk after next), 1 Q', 2 P, 3 K',
+        // 4 Ut (a bulk copy) and gamma_C for the compute warps.  Each lane
+        // waits only on the barrier that gates its own refill, so none can
+        // fall two phases behind one. ----------------
         if (lane < 5) {
             const int role = lane;
             if (role == 0) {
@@ -164,17 +174,29 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                 prefetch_tensormap(&m.kl);
             }
             int c = 0;
-            // beside the chunk-local kernel the chunks are fresh in L2 when
-            // their flags go up: no prefetch
-            if (role == 4 && a.ready) c = nc;
             for (; c < nc; ++c) {
                 const int row = (int)(blk0 + c) * C;
-                if (role < 4 && !chunk_ready(c)) break;
+                if (!chunk_ready(c)) break;
                 if (role == 0) {
                     if (c >= 1 && !mbar_wait(&w_empty, (c - 1) & 1, a.status)) break;
                     mbar_arrive_expect_tx(&w_full, W_BYTES);
                     for (int x = 0; x < 2; ++x)
                         tma_load_2d(smem + W_OFF + x * BOX64, &m.w, 64 * x, row, &w_full);
+                    // after the chunk-local kernel the chunk after next into L2,
+                    // paced by this chunk's W (beside it the chunks are fresh
+                    // in L2 when their flags go up)
+                    const int cn = c + 2;
+                    if (!a.ready && cn < nc) {
+                        const size_t bo = (blk0 + cn) * C;
+                        prefetch_l2_bulk(a.w + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.qp + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.qp_lo + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.kp + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.kp_lo + bo * S, C * S * 2);
+                        prefetch_l2_bulk(a.p + bo * C, C * C * 2);
+                        prefetch_l2_bulk(a.p_lo + bo * C, C * C * 2);
+                        prefetch_l2_bulk(a.ut + bo * S, C * S * 4);
+                    }
                 } else if (role == 1) {
                     if (c >= 1 && !mbar_wait(&q_empty, (c - 1) & 1, a.status)) break;
                     mbar_arrive_expect_tx(&q_full, Q_BYTES);
@@ -188,30 +210,21 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                     tma_load_2d(smem + P_OFF, &m.ph, 0, row, &p_full);
                     tma_load_2d(smem + P_OFF + BOX64, &m.pl, 0, row, &p_full);
                 } else if (role == 3) {
-                    const int b = c & 1;
-                    if (c >= 2 && !mbar_wait(&k_empty[b], ((c >> 1) - 1) & 1, a.status)) break;
-                    mbar_arrive_expect_tx(&k_full[b], K_BYTES);
-                    unsigned char *kd = smem + K_OFF + b * 4 * BOX64;
+                    // one buffer: the next K' has a whole chain step to land
+                    if (c >= 1 && !mbar_wait(&k_empty, (c - 1) & 1, a.status)) break;
+                    mbar_arrive_expect_tx(&k_full, K_BYTES);
+                    unsigned char *kd = smem + K_OFF;
                     for (int x = 0; x < 2; ++x) {
-                        tma_load_2d(kd + x * BOX64, &m.kh, 64 * x, row, &k_full[b]);
-                        tma_load_2d(kd + (2 + x) * BOX64, &m.kl, 64 * x, row, &k_full[b]);
+                        tma_load_2d(kd + x * BOX64, &m.kh, 64 * x, row, &k_full);
+                        tma_load_2d(kd + (2 + x) * BOX64, &m.kl, 64 * x, row, &k_full);
                     }
                 } else {
-                    // the chunk after next into L2, paced by this chunk's W (so
-                    // it runs at most two chunks ahead of the MMAs)
-                    if (c >= 1 && !mbar_wait(&w_empty, (c - 1) & 1, a.status)) break;
-                    const int cn = c + 2;
-                    if (cn < nc) {
-                        const size_t bo = (blk0 + cn) * C;
-                        prefetch_l2_bulk(a.w + bo * S, C * S * 2);
-                        prefetch_l2_bulk(a.qp + bo * S, C * S * 2);
-                        prefetch_l2_bulk(a.qp_lo + bo * S, C * S * 2);
-                        prefetch_l2_bulk(a.kp + bo * S, C * S * 2);
-                        prefetch_l2_bulk(a.kp_lo + bo * S, C * S * 2);
-                        prefetch_l2_bulk(a.p + bo * C, C * C * 2);
-                        prefetch_l2_bulk(a.p_lo + bo * C, C * C * 2);
-                    }
-                    if (c + 1 < nc) prefetch_l2_bulk(a.ut + (blk0 + c + 1) * C * S, C * S * 4);
+                    // the compute warps read this chunk's Ut and gamma_C from
+                    // shared memory once they have converted the previous U
+                    if (c >= 1 && !mbar_wait(&ut_empty, (c - 1) & 1, a.status)) break;
+                    gc_s = a.gc[blk0 + c];
+                    mbar_arrive_expect_tx(&ut_full, UT_BYTES);
+                    bulk_g2s(smem + UTS_OFF, a.ut + (blk0 + c) * C * S, UT_BYTES, &ut_full);
                 }
             }
             if (c < nc) flag_s = 1;
@@ -222,10 +235,8 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                 if (role == 0) mbar_wait(&w_full, last & 1, a.status);
                 if (role == 1) mbar_wait(&q_full, last & 1, a.status);
                 if (role == 2) mbar_wait(&p_full, last & 1, a.status);
-                if (role == 3) {
-                    mbar_wait(&k_full[last & 1], (last >> 1) & 1, a.status);
-                    if (last >= 1) mbar_wait(&k_full[(last - 1) & 1], ((last - 1) >> 1) & 1, a.status);
-                }
+                if (role == 3) mbar_wait(&k_full, last & 1, a.status);
+                if (role == 4) mbar_wait(&ut_full, last & 1, a.status);
             }
         }
     } else if (warp == MMA_WARP) {
@@ -247,11 +258,8 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             const uint64_t p_lo = tc::smem_desc(sbase + P_OFF + BOX64, 16, 1024);
             // K' is N-major: a 16-row step is +2 KiB; its two 64-column boxes
             // are BOX64 apart (the leading byte offset)
-            const uint64_t k_d[2][2] = {
-                {tc::smem_desc(sbase + K_OFF, BOX64, 1024),
-                 tc::smem_desc(sbase + K_OFF + 2 * BOX64, BOX64, 1024)},
-                {tc::smem_desc(sbase + K_OFF + 4 * BOX64, BOX64, 1024),
-                 tc::smem_desc(sbase + K_OFF + 6 * BOX64, BOX64, 1024)}};
+            const uint64_t k_d[2] = {tc::smem_desc(sbase + K_OFF, BOX64, 1024),
+                                     tc::smem_desc(sbase + K_OFF + 2 * BOX64, BOX64, 1024)};
             auto kstep = [](int kk, uint32_t box) -> uint64_t {
                 return (uint64_t)(((kk >> 2) * box + (kk & 3) * 32) >> 4);
             };
@@ -290,16 +298,16 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                 // its completion also covers everything above, so S^T's
                 // shared copy is free then
                 ok = mbar_wait(&u_ready, c & 1, a.status) &&
-                     mbar_wait(&k_full[b], (c >> 1) & 1, a.status);
+                     mbar_wait(&k_full, c & 1, a.status);
                 if (!ok) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int term = 0; term < 2; ++term)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        tc::mma_ss(tmem + S_COL, ut_hi + kk * 2, k_d[b][term] + kk * 128, id_s,
+                        tc::mma_ss(tmem + S_COL, ut_hi + kk * 2, k_d[term] + kk * 128, id_s,
                                    term > 0 || kk > 0);
-                tc::commit(&k_empty[b]);
+                tc::commit(&k_empty);
                 tc::commit(&s_done);
                 // O^T += U^T P^T, three terms
                 ok = mbar_wait(&p_full, c & 1, a.status);
@@ -342,16 +350,18 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         fence_proxy_async_smem();
         tc::fence_before_sync();
         mbar_arrive(&s_ready);
+        const float *uts = reinterpret_cast<const float *>(smem + UTS_OFF) + (hf * 32) * S + j;
         for (int c = 0; c < nc && ok; ++c) {
-            const size_t blk = blk0 + c;
-            if (!(ok = chunk_ready(c))) break;
             // ---- U = Ut - S W for this warp's 32 tokens, into shared memory
-            // as a bf16 pair (Ut's column j is read while the MMAs run)
-            const float *ut = a.ut + blk * C * S + (size_t)(hf * 32) * S + j;
+            // as a bf16 pair (Ut's column j, staged by the producer, is read
+            // while the MMAs run)
+            if (!(ok = mbar_wait(&ut_full, c & 1, a.status))) break;
             float x[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) x[e] = __ldcg(ut + (size_t)e * S);
-            const float gc = a.gc[blk];
+            for (int e = 0; e < 32; ++e) x[e] = uts[e * S];
+            const float gc = gc_s;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ut_empty);
             ok = mbar_wait(&u_done, c & 1, a.status);
             if (!ok) break;
             tc::fence_after_sync();
