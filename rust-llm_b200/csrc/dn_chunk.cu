@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(256, 3) dn_prep_kernel(const DnChunkArgs a) {
         const int f = blockIdx.x * blockDim.x + threadIdx.x;
         if (f < a.n_v * a.nc) a.out_ready[f] = 0;
     }
+    // the chunk-local kernel after this one claims its items from zero
+    if (a.local_next && blockIdx.x == 0 && threadIdx.x == 0 && blockIdx.y == 0) *a.local_next = 0;
     const int n_groups = 2 * a.n_k + a.n_v;
     if (g >= n_groups) return;
     const int key_dim = a.n_k * S, conv_dim = 2 * key_dim + a.n_v * S;
@@ -277,9 +279,9 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ---------------------------------------------------------------------------
-// dn_chunk_local_kernel: grid (n_v, n_chunks), LOCAL_THREADS threads (16
-// warps: row block warp % 4 of 16 rows, column block warp / 4 in the
-// product phases).
+// dn_chunk_local_kernel: items (value head, chunk), LOCAL_THREADS threads
+// (16 warps: row block warp % 4 of 16 rows, column block warp / 4 in the
+// product phases); a CTA per item, or (the tcgen05 form) one per SM looping.
 struct LocalSmem {
     __nv_bfloat16 k[dc::C][dc::LDB], q[dc::C][dc::LDB], v[dc::C][dc::LDB];
     __nv_bfloat16 kl[dc::C][dc::LDB], ql[dc::C][dc::LDB], vl[dc::C][dc::LDB];  // low halves
@@ -295,6 +297,7 @@ struct LocalSmem {
         };
     };
     float cum[dc::C], beta[dc::C];
+    int next[2];  // the item after this one, by the item's parity
 };
 
 // The tcgen05 form's layout (1024-byte aligned).  q and k arrive by TMA as
@@ -318,6 +321,7 @@ struct LocalSmemTc {
     float cum[dc::C], beta[dc::C];
     uint64_t qk_full, mma_done;
     uint32_t tmem_base;
+    int next[2];  // the item after this one, by the item's parity
 };
 static_assert(sizeof(LocalSmemTc) + 1024 <= 227 * 1024, "the tcgen05 chunk-local layout fits");
 constexpr uint32_t QK_BLOCK = 16384, Q_HALF = 8192;
@@ -346,20 +350,8 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
     unsigned char *base =
         TC ? smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023) : smem_raw;
     Sm &sm = *reinterpret_cast<Sm *>(base);
-    // grid (n_v, n_chunks): the CTAs of a chunk are dispatched together and
-    // the chunks in order (an overlapped scan waits for them in that order)
-    const int vh = blockIdx.x, ck = blockIdx.y, kh = vh % a.n_k;
-    // the epoch this call's scan waits for (read before anything is written)
-    const int ready_value = a.ready ? a.ready_epoch[vh] + 1 : 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int t0 = ck * C, rows = min(C, a.t - t0);
-
-    // ---- operands of the chunk (rows past the batch are zero): every copy
-    // in flight at once, q and k first (the first products), v after them
-    // (needed only for Ut, after T)
     if constexpr (TC) {
-        // q and k by TMA (the maps end at the call's rows, so the rows past
-        // them read as zero), into the stacked blocks
         if (tid == 0) {
             mbar_init(&sm.qk_full, 1);
             mbar_init(&sm.mma_done, 1);
@@ -372,408 +364,440 @@ __global__ void __launch_bounds__(dc::LOCAL_THREADS)
         tc::fence_before_sync();
         __syncthreads();
         tc::fence_after_sync();
-        if (tid == 0) {
-            mbar_arrive_expect_tx(&sm.qk_full, 12 * Q_HALF);
+    }
+    // The items (value head, chunk) in chunk-major order.  The tcgen05 form
+    // runs one CTA per SM the kernel gets, each looping with no launch
+    // between items: its first item is its block index, each later one is
+    // claimed from a counter while the one before runs, so that the chunks
+    // finish in order (an overlapped scan waits for them in that order) and a
+    // CTA that falls behind takes fewer.
+    const int n_items = a.n_v * a.nc;
+    int item = blockIdx.x;
 #pragma unroll 1
-            for (int x = 0; x < 3; ++x)
+    for (int it = 0; item < n_items; ++it) {
+        const int vh = item % a.n_v, ck = item / a.n_v, kh = vh % a.n_k;
+        const uint32_t par = it & 1;  // the mbarriers' phase of this item
+        // the epoch this call's scan waits for (its scan advances it only after
+        // this item's flag is up)
+        const int ready_value = a.ready ? a.ready_epoch[vh] + 1 : 0;
+        const int t0 = ck * C, rows = min(C, a.t - t0);
+
+        // ---- operands of the chunk (rows past the batch are zero): every copy
+        // in flight at once, q and k first (the first products), v after them
+        // (needed only for Ut, after T)
+        if constexpr (TC) {
+            // q and k by TMA (the maps end at the call's rows, so the rows past
+            // them read as zero), into the stacked blocks
+            if (tid == 0) {
+                mbar_arrive_expect_tx(&sm.qk_full, 12 * Q_HALF);
 #pragma unroll 1
-                for (int cb = 0; cb < 2; ++cb) {
-                    unsigned char *blk = qk_block(sm, x, cb);
-                    tma_load_3d(blk, &pm.k[x], cb * 64, kh, t0, &sm.qk_full);
-                    tma_load_3d(blk + Q_HALF, &pm.q[x], cb * 64, kh, t0, &sm.qk_full);
-                }
+                for (int x = 0; x < 3; ++x)
+#pragma unroll 1
+                    for (int cb = 0; cb < 2; ++cb) {
+                        unsigned char *blk = qk_block(sm, x, cb);
+                        tma_load_3d(blk, &pm.k[x], cb * 64, kh, t0, &sm.qk_full);
+                        tma_load_3d(blk + Q_HALF, &pm.q[x], cb * 64, kh, t0, &sm.qk_full);
+                    }
+            }
+        } else {
+#pragma unroll 2
+            for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
+                const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
+                const bool ok = r < rows;
+                const size_t ko = ((size_t)(t0 + (ok ? r : 0)) * a.n_k + kh) * S + c8;
+                cp_async16_zfill(&sm.k[r][c8], a.kn + ko, ok);
+                cp_async16_zfill(&sm.q[r][c8], a.qn + ko, ok);
+                cp_async16_zfill(&sm.kl[r][c8], a.kn_lo + ko, ok);
+                cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
+                cp_async16_zfill(&sm.k2[r][c8], a.kn_l2 + ko, ok);
+                cp_async16_zfill(&sm.q2[r][c8], a.qn_l2 + ko, ok);
+            }
+            cp_async_commit();
         }
-    } else {
 #pragma unroll 2
         for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
             const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
             const bool ok = r < rows;
-            const size_t ko = ((size_t)(t0 + (ok ? r : 0)) * a.n_k + kh) * S + c8;
-            cp_async16_zfill(&sm.k[r][c8], a.kn + ko, ok);
-            cp_async16_zfill(&sm.q[r][c8], a.qn + ko, ok);
-            cp_async16_zfill(&sm.kl[r][c8], a.kn_lo + ko, ok);
-            cp_async16_zfill(&sm.ql[r][c8], a.qn_lo + ko, ok);
-            cp_async16_zfill(&sm.k2[r][c8], a.kn_l2 + ko, ok);
-            cp_async16_zfill(&sm.q2[r][c8], a.qn_l2 + ko, ok);
+            const size_t vo = ((size_t)(t0 + (ok ? r : 0)) * a.n_v + vh) * S + c8;
+            cp_async16_zfill(&sm.v[r][c8], a.vn + vo, ok);
+            cp_async16_zfill(&sm.vl[r][c8], a.vn_lo + vo, ok);
         }
         cp_async_commit();
-    }
-#pragma unroll 2
-    for (int e = tid; e < C * (S / 8); e += LOCAL_THREADS) {
-        const int r = e / (S / 8), c8 = (e % (S / 8)) * 8;
-        const bool ok = r < rows;
-        const size_t vo = ((size_t)(t0 + (ok ? r : 0)) * a.n_v + vh) * S + c8;
-        cp_async16_zfill(&sm.v[r][c8], a.vn + vo, ok);
-        cp_async16_zfill(&sm.vl[r][c8], a.vn_lo + vo, ok);
-    }
-    cp_async_commit();
-    if (warp == 0) {
-        // cumulative log decay, gamma_t = exp(cum[t]): lane l holds tokens
-        // 2l and 2l + 1, an inclusive scan over the pairs' sums
-        const int ta = 2 * lane, tb = ta + 1;
-        const float la = ta < rows ? a.lg[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
-        const float lb = tb < rows ? a.lg[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
-        float inc = la + lb;
+        if (tid == 64)  // a warp with nothing else waiting on it here
+            sm.next[(it + 1) & 1] = a.local_next ? (int)gridDim.x + atomicAdd(a.local_next, 1)
+                                                 : item + (int)gridDim.x;
+        if (warp == 0) {
+            // cumulative log decay, gamma_t = exp(cum[t]): lane l holds tokens
+            // 2l and 2l + 1, an inclusive scan over the pairs' sums
+            const int ta = 2 * lane, tb = ta + 1;
+            const float la = ta < rows ? a.lg[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
+            const float lb = tb < rows ? a.lg[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
+            float inc = la + lb;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += y;
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += y;
+            }
+            sm.cum[tb] = inc;
+            sm.cum[ta] = inc - lb;
+            sm.beta[ta] = ta < rows ? a.bt[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
+            sm.beta[tb] = tb < rows ? a.bt[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
         }
-        sm.cum[tb] = inc;
-        sm.cum[ta] = inc - lb;
-        sm.beta[ta] = ta < rows ? a.bt[(size_t)(t0 + ta) * a.n_v + vh] : 0.0f;
-        sm.beta[tb] = tb < rows ? a.bt[(size_t)(t0 + tb) * a.n_v + vh] : 0.0f;
-    }
-    if constexpr (!TC) {
-        cp_async_wait<1>();  // q and k (v may still be in flight)
-        __syncthreads();
-    }
-    // Q' = gamma Q and K' = gamma_C / gamma K as bf16 pairs, 8 consecutive
-    // elements a thread (16-byte stores); needs cum and the q/k planes
-    const size_t blk = (size_t)vh * a.nc + ck;
-    auto write_qk_prime = [&]() {
-        const float cum_c = sm.cum[C - 1];
-        __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
-        __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
+        if constexpr (!TC) {
+            cp_async_wait<1>();  // q and k (v may still be in flight)
+            __syncthreads();
+        }
+        // Q' = gamma Q and K' = gamma_C / gamma K as bf16 pairs, 8 consecutive
+        // elements a thread (16-byte stores); needs cum and the q/k planes
+        const size_t blk = (size_t)vh * a.nc + ck;
+        auto write_qk_prime = [&]() {
+            const float cum_c = sm.cum[C - 1];
+            __nv_bfloat16 *qp_out = a.qp + blk * C * S, *kp_out = a.kp + blk * C * S;
+            __nv_bfloat16 *qpl_out = a.qp_lo + blk * C * S, *kpl_out = a.kp_lo + blk * C * S;
 #pragma unroll 2
-        for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
-            const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
-            const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
-            uint4 qh, ql, kh4, kl4;
-            if constexpr (TC) {
-                const uint32_t so = (c0 >> 6) * QK_BLOCK + swz128(r, (c0 & 63) >> 3);
-                qh = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so + Q_HALF);
-                ql = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so + Q_HALF);
-                kh4 = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so);
-                kl4 = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so);
-            } else {
-                qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
-                ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
-                kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
-                kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
-            }
-            const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
-            const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
-            const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
-            const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
-            uint32_t xh[4], xl[4], yh[4], yl[4];
+            for (int e8 = tid; e8 < C * S / 8; e8 += LOCAL_THREADS) {
+                const int r = e8 / (S / 8), c0 = (e8 % (S / 8)) * 8;
+                const float gq = __expf(sm.cum[r]), gk = __expf(cum_c - sm.cum[r]);
+                uint4 qh, ql, kh4, kl4;
+                if constexpr (TC) {
+                    const uint32_t so = (c0 >> 6) * QK_BLOCK + swz128(r, (c0 & 63) >> 3);
+                    qh = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so + Q_HALF);
+                    ql = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so + Q_HALF);
+                    kh4 = *reinterpret_cast<const uint4 *>(sm.hl[0][0] + so);
+                    kl4 = *reinterpret_cast<const uint4 *>(sm.hl[1][0] + so);
+                } else {
+                    qh = *reinterpret_cast<const uint4 *>(&sm.q[r][c0]);
+                    ql = *reinterpret_cast<const uint4 *>(&sm.ql[r][c0]);
+                    kh4 = *reinterpret_cast<const uint4 *>(&sm.k[r][c0]);
+                    kl4 = *reinterpret_cast<const uint4 *>(&sm.kl[r][c0]);
+                }
+                const __nv_bfloat162 *qh2 = reinterpret_cast<const __nv_bfloat162 *>(&qh);
+                const __nv_bfloat162 *ql2 = reinterpret_cast<const __nv_bfloat162 *>(&ql);
+                const __nv_bfloat162 *kh2 = reinterpret_cast<const __nv_bfloat162 *>(&kh4);
+                const __nv_bfloat162 *kl2 = reinterpret_cast<const __nv_bfloat162 *>(&kl4);
+                uint32_t xh[4], xl[4], yh[4], yl[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
-                const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
-                const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
-                const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
-                xh[k] = pack_bf16(x0, x1);
-                xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
-                yh[k] = pack_bf16(y0, y1);
-                yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
+                for (int k = 0; k < 4; ++k) {
+                    const float2 qa = __bfloat1622float2(qh2[k]), qb = __bfloat1622float2(ql2[k]);
+                    const float2 ka = __bfloat1622float2(kh2[k]), kb = __bfloat1622float2(kl2[k]);
+                    const float x0 = (qa.x + qb.x) * gq, x1 = (qa.y + qb.y) * gq;
+                    const float y0 = (ka.x + kb.x) * gk, y1 = (ka.y + kb.y) * gk;
+                    xh[k] = pack_bf16(x0, x1);
+                    xl[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+                    yh[k] = pack_bf16(y0, y1);
+                    yl[k] = pack_bf16(y0 - bf16_hi(y0), y1 - bf16_hi(y1));
+                }
+                const size_t o = (size_t)r * S + c0;
+                *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+                *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+                *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+                *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
             }
-            const size_t o = (size_t)r * S + c0;
-            *reinterpret_cast<uint4 *>(qp_out + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
-            *reinterpret_cast<uint4 *>(qpl_out + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
-            *reinterpret_cast<uint4 *>(kp_out + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
-            *reinterpret_cast<uint4 *>(kpl_out + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
-        }
-    };
-    // ---- K K^T as hi*hi + hi*lo + lo*hi of the bf16 pairs, and Q K^T of
-    // the bf16 triples (hi*hi + hi*lo + lo*hi + lo*lo + hi*l2 + l2*hi): the
-    // readout P U of a token whose state has all but decayed away cancels
-    // down to the q.k products of its own chunk, and the per-head gated norm
-    // that follows magnifies their error; pairs (16 bits) measured 1.3e-2 of
-    // such a head's output at 4096 tokens, triples stay at the f32 level
-    if constexpr (TC) {
-        // one tcgen05 chain: [K; Q]_xa K_xb^T over the six (xa, xb) plane
-        // pairs Q K^T takes (hi hi, hi lo, hi l2, lo hi, lo lo, l2 hi); the
-        // accumulator's rows 0-63 are K K^T (to six terms), 64-127 Q K^T.
-        // The chain keeps the tensor pipe busy for ~2,400 cycles: warp 15
-        // issues it while every warp writes Q' and K' from the same planes,
-        // then warps 0-3 read the products back.  The barrier after the
-        // planes land also publishes cum and beta.
-        const bool okq = mbar_wait(&sm.qk_full, 0, a.status);
-        __syncthreads();
-        if (tid == LOCAL_THREADS - 32) {
-            if (okq) {
+        };
+        // ---- K K^T as hi*hi + hi*lo + lo*hi of the bf16 pairs, and Q K^T of
+        // the bf16 triples (hi*hi + hi*lo + lo*hi + lo*lo + hi*l2 + l2*hi): the
+        // readout P U of a token whose state has all but decayed away cancels
+        // down to the q.k products of its own chunk, and the per-head gated norm
+        // that follows magnifies their error; pairs (16 bits) measured 1.3e-2 of
+        // such a head's output at 4096 tokens, triples stay at the f32 level
+        if constexpr (TC) {
+            // one tcgen05 chain: [K; Q]_xa K_xb^T over the six (xa, xb) plane
+            // pairs Q K^T takes (hi hi, hi lo, hi l2, lo hi, lo lo, l2 hi); the
+            // accumulator's rows 0-63 are K K^T (to six terms), 64-127 Q K^T.
+            // The chain keeps the tensor pipe busy for ~2,400 cycles: warp 15
+            // issues it while every warp writes Q' and K' from the same planes,
+            // then warps 0-3 read the products back.  The barrier after the
+            // planes land also publishes cum and beta.
+            const bool okq = mbar_wait(&sm.qk_full, par, a.status);
+            __syncthreads();
+            if (tid == LOCAL_THREADS - 32) {
+                if (okq) {
+                    tc::fence_after_sync();
+                    constexpr uint32_t id = tc::idesc_bf16(128, 64, false);
+                    const int xa[6] = {0, 0, 0, 1, 1, 2}, xb[6] = {0, 1, 2, 0, 1, 0};
+#pragma unroll
+                    for (int p = 0; p < 6; ++p) {
+                        const uint64_t ad =
+                            tc::smem_desc(smem_u32(qk_block(sm, xa[p], 0)), 16, 1024);
+                        const uint64_t bd =
+                            tc::smem_desc(smem_u32(qk_block(sm, xb[p], 0)), 16, 1024);
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            // a 16-channel step is 32 bytes inside a box, the next
+                            // box the next block
+                            const uint64_t step = ((kk >> 2) * QK_BLOCK + (kk & 3) * 32) >> 4;
+                            tc::mma_ss(sm.tmem_base, ad + step, bd + step, id, p > 0 || kk > 0);
+                        }
+                    }
+                    tc::commit(&sm.mma_done);
+                } else {
+                    mbar_arrive(&sm.mma_done);  // flagged; the readers go on
+                }
+            }
+            write_qk_prime();
+            if (warp < 4) {
+                // warp w reads tensor-memory lanes 32w .. 32w + 31: rows of K K^T
+                // (w < 2) or of Q K^T
+                mbar_wait(&sm.mma_done, par, a.status);
                 tc::fence_after_sync();
-                constexpr uint32_t id = tc::idesc_bf16(128, 64, false);
-                const int xa[6] = {0, 0, 0, 1, 1, 2}, xb[6] = {0, 1, 2, 0, 1, 0};
+                uint32_t r0[32], r1[32];
+                const uint32_t taddr = sm.tmem_base + ((uint32_t)(warp * 32) << 16);
+                tc::ld32(taddr, r0);
+                tc::ld32(taddr + 32, r1);
+                tc::wait_ld();
+                const int row = warp * 32 + lane;
+                float *dst = row < C ? &sm.kk[row][0] : &sm.qk[row - C][0];
 #pragma unroll
-                for (int p = 0; p < 6; ++p) {
-                    const uint64_t ad = tc::smem_desc(smem_u32(qk_block(sm, xa[p], 0)), 16, 1024);
-                    const uint64_t bd = tc::smem_desc(smem_u32(qk_block(sm, xb[p], 0)), 16, 1024);
+                for (int c = 0; c < 32; ++c) {
+                    dst[c] = __uint_as_float(r0[c]);
+                    dst[32 + c] = __uint_as_float(r1[c]);
+                }
+            }
+        } else {
+            // warp: rows 16 * (warp % 4), columns QK_COLS * (warp / 4) ..
+            constexpr int NT = QK_COLS / 8;
+            const int rw = (warp & 3) * 16, cn = (warp >> 2) * QK_COLS;
+            float dk[NT][4], dq[NT][4];
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        // a 16-channel step is 32 bytes inside a box, the next
-                        // box the next block
-                        const uint64_t step = ((kk >> 2) * QK_BLOCK + (kk & 3) * 32) >> 4;
-                        tc::mma_ss(sm.tmem_base, ad + step, bd + step, id, p > 0 || kk > 0);
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dk[n][e] = dq[n][e] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < S / 16; ++ks) {
+                uint32_t ak[4], aq[4], akl[4], aql[4], aq2[4];
+                ld_a(&sm.k[0][0], LDB, rw, ks * 16, lane, ak);
+                ld_a(&sm.q[0][0], LDB, rw, ks * 16, lane, aq);
+                ld_a(&sm.kl[0][0], LDB, rw, ks * 16, lane, akl);
+                ld_a(&sm.ql[0][0], LDB, rw, ks * 16, lane, aql);
+                ld_a(&sm.q2[0][0], LDB, rw, ks * 16, lane, aq2);
+#pragma unroll
+                for (int np = 0; np < NT / 2; ++np) {
+                    uint32_t b[4], bl[4], b2[4];
+                    ld_b2(&sm.k[0][0], LDB, cn + np * 16, ks * 16, lane, b);
+                    ld_b2(&sm.kl[0][0], LDB, cn + np * 16, ks * 16, lane, bl);
+                    ld_b2(&sm.k2[0][0], LDB, cn + np * 16, ks * 16, lane, b2);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        mma_16816(dk[2 * np + h], ak, b[2 * h], b[2 * h + 1]);
+                        mma_16816(dk[2 * np + h], ak, bl[2 * h], bl[2 * h + 1]);
+                        mma_16816(dk[2 * np + h], akl, b[2 * h], b[2 * h + 1]);
+                        mma_16816(dq[2 * np + h], aq, b[2 * h], b[2 * h + 1]);
+                        mma_16816(dq[2 * np + h], aq, bl[2 * h], bl[2 * h + 1]);
+                        mma_16816(dq[2 * np + h], aql, b[2 * h], b[2 * h + 1]);
+                        mma_16816(dq[2 * np + h], aql, bl[2 * h], bl[2 * h + 1]);
+                        mma_16816(dq[2 * np + h], aq, b2[2 * h], b2[2 * h + 1]);
+                        mma_16816(dq[2 * np + h], aq2, b[2 * h], b[2 * h + 1]);
                     }
                 }
-                tc::commit(&sm.mma_done);
-            } else {
-                mbar_arrive(&sm.mma_done);  // flagged; the readers go on
+            }
+            const int r0 = rw + (lane >> 2), c0 = cn + (lane & 3) * 2;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                sm.kk[r0][n * 8 + c0] = dk[n][0];
+                sm.kk[r0][n * 8 + c0 + 1] = dk[n][1];
+                sm.kk[r0 + 8][n * 8 + c0] = dk[n][2];
+                sm.kk[r0 + 8][n * 8 + c0 + 1] = dk[n][3];
+                sm.qk[r0][n * 8 + c0] = dq[n][0];
+                sm.qk[r0][n * 8 + c0 + 1] = dq[n][1];
+                sm.qk[r0 + 8][n * 8 + c0] = dq[n][2];
+                sm.qk[r0 + 8][n * 8 + c0 + 1] = dq[n][3];
             }
         }
-        write_qk_prime();
-        if (warp < 4) {
-            // warp w reads tensor-memory lanes 32w .. 32w + 31: rows of K K^T
-            // (w < 2) or of Q K^T
-            mbar_wait(&sm.mma_done, 0, a.status);
-            tc::fence_after_sync();
-            uint32_t r0[32], r1[32];
-            const uint32_t taddr = sm.tmem_base + ((uint32_t)(warp * 32) << 16);
-            tc::ld32(taddr, r0);
-            tc::ld32(taddr + 32, r1);
-            tc::wait_ld();
-            const int row = warp * 32 + lane;
-            float *dst = row < C ? &sm.kk[row][0] : &sm.qk[row - C][0];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                dst[c] = __uint_as_float(r0[c]);
-                dst[32 + c] = __uint_as_float(r1[c]);
-            }
-        }
-    } else {
-        // warp: rows 16 * (warp % 4), columns QK_COLS * (warp / 4) ..
-        constexpr int NT = QK_COLS / 8;
-        const int rw = (warp & 3) * 16, cn = (warp >> 2) * QK_COLS;
-        float dk[NT][4], dq[NT][4];
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) dk[n][e] = dq[n][e] = 0.0f;
-#pragma unroll
-        for (int ks = 0; ks < S / 16; ++ks) {
-            uint32_t ak[4], aq[4], akl[4], aql[4], aq2[4];
-            ld_a(&sm.k[0][0], LDB, rw, ks * 16, lane, ak);
-            ld_a(&sm.q[0][0], LDB, rw, ks * 16, lane, aq);
-            ld_a(&sm.kl[0][0], LDB, rw, ks * 16, lane, akl);
-            ld_a(&sm.ql[0][0], LDB, rw, ks * 16, lane, aql);
-            ld_a(&sm.q2[0][0], LDB, rw, ks * 16, lane, aq2);
-#pragma unroll
-            for (int np = 0; np < NT / 2; ++np) {
-                uint32_t b[4], bl[4], b2[4];
-                ld_b2(&sm.k[0][0], LDB, cn + np * 16, ks * 16, lane, b);
-                ld_b2(&sm.kl[0][0], LDB, cn + np * 16, ks * 16, lane, bl);
-                ld_b2(&sm.k2[0][0], LDB, cn + np * 16, ks * 16, lane, b2);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    mma_16816(dk[2 * np + h], ak, b[2 * h], b[2 * h + 1]);
-                    mma_16816(dk[2 * np + h], ak, bl[2 * h], bl[2 * h + 1]);
-                    mma_16816(dk[2 * np + h], akl, b[2 * h], b[2 * h + 1]);
-                    mma_16816(dq[2 * np + h], aq, b[2 * h], b[2 * h + 1]);
-                    mma_16816(dq[2 * np + h], aq, bl[2 * h], bl[2 * h + 1]);
-                    mma_16816(dq[2 * np + h], aql, b[2 * h], b[2 * h + 1]);
-                    mma_16816(dq[2 * np + h], aql, bl[2 * h], bl[2 * h + 1]);
-                    mma_16816(dq[2 * np + h], aq, b2[2 * h], b2[2 * h + 1]);
-                    mma_16816(dq[2 * np + h], aq2, b[2 * h], b[2 * h + 1]);
-                }
-            }
-        }
-        const int r0 = rw + (lane >> 2), c0 = cn + (lane & 3) * 2;
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            sm.kk[r0][n * 8 + c0] = dk[n][0];
-            sm.kk[r0][n * 8 + c0 + 1] = dk[n][1];
-            sm.kk[r0 + 8][n * 8 + c0] = dk[n][2];
-            sm.kk[r0 + 8][n * 8 + c0 + 1] = dk[n][3];
-            sm.qk[r0][n * 8 + c0] = dq[n][0];
-            sm.qk[r0][n * 8 + c0 + 1] = dq[n][1];
-            sm.qk[r0 + 8][n * 8 + c0] = dq[n][2];
-            sm.qk[r0 + 8][n * 8 + c0 + 1] = dq[n][3];
-        }
-    }
-    __syncthreads();
-    // ---- P = Q K^T o Mgamma (s <= t), and in the mma.sync form Q' and K'
-    // (the tcgen05 form wrote them beside its products): written now, so
-    // that the stores drain while T is built (8 consecutive elements a
-    // thread: 16-byte stores)
-    __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
+        __syncthreads();
+        // ---- P = Q K^T o Mgamma (s <= t), and in the mma.sync form Q' and K'
+        // (the tcgen05 form wrote them beside its products): written now, so
+        // that the stores drain while T is built (8 consecutive elements a
+        // thread: 16-byte stores)
+        __nv_bfloat16 *p_out = a.p + blk * C * C, *pl_out = a.p_lo + blk * C * C;
 #pragma unroll 2
-    for (int e8 = tid; e8 < C * C / 8; e8 += LOCAL_THREADS) {
-        const int r = e8 / (C / 8), s0 = (e8 % (C / 8)) * 8;
-        const float cr = sm.cum[r];
-        uint32_t hi[4], lo[4];
+        for (int e8 = tid; e8 < C * C / 8; e8 += LOCAL_THREADS) {
+            const int r = e8 / (C / 8), s0 = (e8 % (C / 8)) * 8;
+            const float cr = sm.cum[r];
+            uint32_t hi[4], lo[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int sa = s0 + 2 * k, sb = sa + 1;
-            const float x0 = sa <= r ? sm.qk[r][sa] * __expf(cr - sm.cum[sa]) : 0.0f;
-            const float x1 = sb <= r ? sm.qk[r][sb] * __expf(cr - sm.cum[sb]) : 0.0f;
-            hi[k] = pack_bf16(x0, x1);
-            lo[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+            for (int k = 0; k < 4; ++k) {
+                const int sa = s0 + 2 * k, sb = sa + 1;
+                const float x0 = sa <= r ? sm.qk[r][sa] * __expf(cr - sm.cum[sa]) : 0.0f;
+                const float x1 = sb <= r ? sm.qk[r][sb] * __expf(cr - sm.cum[sb]) : 0.0f;
+                hi[k] = pack_bf16(x0, x1);
+                lo[k] = pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+            }
+            *reinterpret_cast<uint4 *>(p_out + r * C + s0) =
+                make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(pl_out + r * C + s0) =
+                make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
-        *reinterpret_cast<uint4 *>(p_out + r * C + s0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4 *>(pl_out + r * C + s0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    }
-    const float cum_c = sm.cum[C - 1];
-    if constexpr (!TC) write_qk_prime();
-    if (tid == 0) a.gc[blk] = __expf(cum_c);
-    // ---- L (in place over kk) and T = (I + L)^-1, one column per thread
-    {
-        // this thread's column s is fixed (the CTA is a multiple of C)
-        const int s = tid & (C - 1);
-        const float cs = sm.cum[s];
+        const float cum_c = sm.cum[C - 1];
+        if constexpr (!TC) write_qk_prime();
+        if (tid == 0) a.gc[blk] = __expf(cum_c);
+        // ---- L (in place over kk) and T = (I + L)^-1, one column per thread
+        {
+            // this thread's column s is fixed (the CTA is a multiple of C)
+            const int s = tid & (C - 1);
+            const float cs = sm.cum[s];
 #pragma unroll 4
-        for (int r = tid / C; r < C; r += LOCAL_THREADS / C) {
-            sm.kk[r][s] = s < r ? sm.beta[r] * __expf(sm.cum[r] - cs) * sm.kk[r][s] : 0.0f;
-            sm.t[r][s] = 0.0f;
+            for (int r = tid / C; r < C; r += LOCAL_THREADS / C) {
+                sm.kk[r][s] = s < r ? sm.beta[r] * __expf(sm.cum[r] - cs) * sm.kk[r][s] : 0.0f;
+                sm.t[r][s] = 0.0f;
+            }
         }
-    }
-    __syncthreads();
-    // T = (I + L)^-1 in 16 x 16 blocks: the four diagonal blocks by forward
-    // substitution (one column per thread), then the blocks below the
-    // diagonal, one diagonal at a time: T_ij = -T_ii sum_{j<=k<i} L_ik T_kj
-    if (tid < C) {
-        // column s of diagonal block b0, in registers (entries above the
-        // diagonal are zero, so the sums may run over every m < r)
-        const int b0 = (tid >> 4) * 16, s = tid & 15;
-        float tc[16];
+        __syncthreads();
+        // T = (I + L)^-1 in 16 x 16 blocks: the four diagonal blocks by forward
+        // substitution (one column per thread), then the blocks below the
+        // diagonal, one diagonal at a time: T_ij = -T_ii sum_{j<=k<i} L_ik T_kj
+        if (tid < C) {
+            // column s of diagonal block b0, in registers (entries above the
+            // diagonal are zero, so the sums may run over every m < r)
+            const int b0 = (tid >> 4) * 16, s = tid & 15;
+            float tc[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            float acc = 0.0f;
+            for (int r = 0; r < 16; ++r) {
+                float acc = 0.0f;
 #pragma unroll
-            for (int m = 0; m < r; ++m) acc = fmaf(sm.kk[b0 + r][b0 + m], tc[m], acc);
-            tc[r] = r == s ? 1.0f : (r > s ? -acc : 0.0f);
+                for (int m = 0; m < r; ++m) acc = fmaf(sm.kk[b0 + r][b0 + m], tc[m], acc);
+                tc[r] = r == s ? 1.0f : (r > s ? -acc : 0.0f);
+            }
+#pragma unroll
+            for (int r = 0; r < 16; ++r) sm.t[b0 + r][b0 + s] = tc[r];
         }
-#pragma unroll
-        for (int r = 0; r < 16; ++r) sm.t[b0 + r][b0 + s] = tc[r];
-    }
-    __syncthreads();
-    // the blocks below the diagonal, one diagonal dg at a time: warp j < 4 -
-    // dg takes block (i, j) = (j + dg, j), X = sum_{j <= k < i} L_ik T_kj and
-    // then T_ij = -T_ii X, both on the tensor cores as bf16 pairs
+        __syncthreads();
+        // the blocks below the diagonal, one diagonal dg at a time: warp j < 4 -
+        // dg takes block (i, j) = (j + dg, j), X = sum_{j <= k < i} L_ik T_kj and
+        // then T_ij = -T_ii X, both on the tensor cores as bf16 pairs
 #pragma unroll 1
-    for (int dg = 1; dg < 4; ++dg) {
-        if (warp < 4 - dg) {
-            const int bj = warp, bi = warp + dg;
-            const int g = lane >> 2, t2 = (lane & 3) * 2;
-            float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            for (int kb = bj; kb < bi; ++kb) {
+        for (int dg = 1; dg < 4; ++dg) {
+            if (warp < 4 - dg) {
+                const int bj = warp, bi = warp + dg;
+                const int g = lane >> 2, t2 = (lane & 3) * 2;
+                float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                for (int kb = bj; kb < bi; ++kb) {
+                    uint32_t ah[4], al[4];
+                    frag_a_f32(&sm.kk[0][0], LDF, 16 * bi, 16 * kb, lane, ah, al);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        uint32_t bh[2], bl[2];
+                        frag_b_f32(&sm.t[0][0], LDF, 16 * kb, 16 * bj + 8 * nt, lane, bh, bl);
+                        mma3(x[nt], ah, al, bh, bl);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    sm.x[16 * bi + g][16 * bj + 8 * nt + t2] = x[nt][0];
+                    sm.x[16 * bi + g][16 * bj + 8 * nt + t2 + 1] = x[nt][1];
+                    sm.x[16 * bi + g + 8][16 * bj + 8 * nt + t2] = x[nt][2];
+                    sm.x[16 * bi + g + 8][16 * bj + 8 * nt + t2 + 1] = x[nt][3];
+                }
+                __syncwarp();
                 uint32_t ah[4], al[4];
-                frag_a_f32(&sm.kk[0][0], LDF, 16 * bi, 16 * kb, lane, ah, al);
+                frag_a_f32(&sm.t[0][0], LDF, 16 * bi, 16 * bi, lane, ah, al);
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
                     uint32_t bh[2], bl[2];
-                    frag_b_f32(&sm.t[0][0], LDF, 16 * kb, 16 * bj + 8 * nt, lane, bh, bl);
-                    mma3(x[nt], ah, al, bh, bl);
+                    frag_b_f32(&sm.x[0][0], LDF, 16 * bi, 16 * bj + 8 * nt, lane, bh, bl);
+                    float y[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma3(y, ah, al, bh, bl);
+                    sm.t[16 * bi + g][16 * bj + 8 * nt + t2] = -y[0];
+                    sm.t[16 * bi + g][16 * bj + 8 * nt + t2 + 1] = -y[1];
+                    sm.t[16 * bi + g + 8][16 * bj + 8 * nt + t2] = -y[2];
+                    sm.t[16 * bi + g + 8][16 * bj + 8 * nt + t2 + 1] = -y[3];
                 }
             }
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                sm.x[16 * bi + g][16 * bj + 8 * nt + t2] = x[nt][0];
-                sm.x[16 * bi + g][16 * bj + 8 * nt + t2 + 1] = x[nt][1];
-                sm.x[16 * bi + g + 8][16 * bj + 8 * nt + t2] = x[nt][2];
-                sm.x[16 * bi + g + 8][16 * bj + 8 * nt + t2 + 1] = x[nt][3];
-            }
-            __syncwarp();
-            uint32_t ah[4], al[4];
-            frag_a_f32(&sm.t[0][0], LDF, 16 * bi, 16 * bi, lane, ah, al);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                uint32_t bh[2], bl[2];
-                frag_b_f32(&sm.x[0][0], LDF, 16 * bi, 16 * bj + 8 * nt, lane, bh, bl);
-                float y[4] = {0.f, 0.f, 0.f, 0.f};
-                mma3(y, ah, al, bh, bl);
-                sm.t[16 * bi + g][16 * bj + 8 * nt + t2] = -y[0];
-                sm.t[16 * bi + g][16 * bj + 8 * nt + t2 + 1] = -y[1];
-                sm.t[16 * bi + g + 8][16 * bj + 8 * nt + t2] = -y[2];
-                sm.t[16 * bi + g + 8][16 * bj + 8 * nt + t2 + 1] = -y[3];
-            }
+            __syncthreads();
         }
-        __syncthreads();
-    }
-    // ---- T diag(beta) and T diag(beta gamma) as bf16 pairs
-    {
-        // this thread's column s is fixed (the CTA is a multiple of C)
-        const int s = tid & (C - 1);
-        const float bs = sm.beta[s], gs = __expf(sm.cum[s]);
+        // ---- T diag(beta) and T diag(beta gamma) as bf16 pairs
+        {
+            // this thread's column s is fixed (the CTA is a multiple of C)
+            const int s = tid & (C - 1);
+            const float bs = sm.beta[s], gs = __expf(sm.cum[s]);
 #pragma unroll 4
-        for (int r = tid / C; r < C; r += LOCAL_THREADS / C) {
-            const float x = sm.t[r][s] * bs;
-            const float y = x * gs;
-            const float xh = bf16_hi(x), yh = bf16_hi(y);
-            sm.ta_hi[r][s] = __float2bfloat16_rn(x);
-            sm.ta_lo[r][s] = __float2bfloat16_rn(x - xh);
-            sm.tb_hi[r][s] = __float2bfloat16_rn(y);
-            sm.tb_lo[r][s] = __float2bfloat16_rn(y - yh);
-        }
-    }
-    cp_async_wait<0>();  // v
-    __syncthreads();
-    // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows,
-    // UW_COLS columns)
-    float *ut_out = a.ut + blk * C * S;
-    __nv_bfloat16 *w_out = a.w + blk * C * S, *wl_out = a.w_lo + blk * C * S;
-    const int r0 = (warp & 3) * 16 + (lane >> 2), c0 = (lane & 3) * 2;
-    {
-        constexpr int NT = UW_COLS / 8;
-        const int cb = (warp >> 2) * UW_COLS;  // this warp's first output column
-        float du[NT][4], dw[NT][4];
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) du[n][e] = dw[n][e] = 0.0f;
-#pragma unroll
-        for (int ks = 0; ks < C / 16; ++ks) {
-            uint32_t ah[4], al[4], bh[4], bl[4];
-            ld_a(&sm.ta_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, ah);
-            ld_a(&sm.ta_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, al);
-            ld_a(&sm.tb_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bh);
-            ld_a(&sm.tb_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bl);
-#pragma unroll
-            for (int np = 0; np < NT / 2; ++np) {
-                const int n0 = cb + np * 16;
-                uint32_t vh_[4], vl_[4], kh_[4], kl_[4];
-                ld_b2_t(&sm.v[0][0], LDB, n0, ks * 16, lane, vh_);
-                ld_b2_t(&sm.vl[0][0], LDB, n0, ks * 16, lane, vl_);
-                if constexpr (TC) {
-                    ld_b2_t_swz(sm.hl[0][0], n0, ks * 16, lane, kh_);
-                    ld_b2_t_swz(sm.hl[1][0], n0, ks * 16, lane, kl_);
-                } else {
-                    ld_b2_t(&sm.k[0][0], LDB, n0, ks * 16, lane, kh_);
-                    ld_b2_t(&sm.kl[0][0], LDB, n0, ks * 16, lane, kl_);
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    mma_16816(du[2 * np + h], ah, vh_[2 * h], vh_[2 * h + 1]);
-                    mma_16816(du[2 * np + h], ah, vl_[2 * h], vl_[2 * h + 1]);
-                    mma_16816(du[2 * np + h], al, vh_[2 * h], vh_[2 * h + 1]);
-                    mma_16816(dw[2 * np + h], bh, kh_[2 * h], kh_[2 * h + 1]);
-                    mma_16816(dw[2 * np + h], bh, kl_[2 * h], kl_[2 * h + 1]);
-                    mma_16816(dw[2 * np + h], bl, kh_[2 * h], kh_[2 * h + 1]);
-                }
+            for (int r = tid / C; r < C; r += LOCAL_THREADS / C) {
+                const float x = sm.t[r][s] * bs;
+                const float y = x * gs;
+                const float xh = bf16_hi(x), yh = bf16_hi(y);
+                sm.ta_hi[r][s] = __float2bfloat16_rn(x);
+                sm.ta_lo[r][s] = __float2bfloat16_rn(x - xh);
+                sm.tb_hi[r][s] = __float2bfloat16_rn(y);
+                sm.tb_lo[r][s] = __float2bfloat16_rn(y - yh);
             }
         }
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            const int col = cb + n * 8 + c0;
-            *reinterpret_cast<float2 *>(ut_out + r0 * S + col) = make_float2(du[n][0], du[n][1]);
-            *reinterpret_cast<float2 *>(ut_out + (r0 + 8) * S + col) = make_float2(du[n][2], du[n][3]);
-#pragma unroll
-            for (int e2 = 0; e2 < 2; ++e2) {
-                const float x0 = dw[n][2 * e2], x1 = dw[n][2 * e2 + 1];
-                const size_t o = (size_t)(r0 + 8 * e2) * S + col;
-                *reinterpret_cast<uint32_t *>(w_out + o) = pack_bf16(x0, x1);
-                if (a.w_lo_out)  // only the mma.sync scan reads W's low half
-                    *reinterpret_cast<uint32_t *>(wl_out + o) =
-                        pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
-            }
-        }
-    }
-    if (a.ready) {
-        // the barrier orders every thread's stores before thread 0's, and a
-        // release is cumulative: once the flag is seen at GPU scope, so is
-        // everything its writer had seen (the semaphore pattern; a fence in
-        // every thread would hold each warp until its own stores land)
+        cp_async_wait<0>();  // v
         __syncthreads();
-        if (tid == 0) st_release_gpu(a.ready + (size_t)vh * a.nc + ck, ready_value);
+        // ---- Ut = T diag(beta) V and W = T diag(beta gamma) K (warp: 16 rows,
+        // UW_COLS columns)
+        float *ut_out = a.ut + blk * C * S;
+        __nv_bfloat16 *w_out = a.w + blk * C * S, *wl_out = a.w_lo + blk * C * S;
+        const int r0 = (warp & 3) * 16 + (lane >> 2), c0 = (lane & 3) * 2;
+        {
+            constexpr int NT = UW_COLS / 8;
+            const int cb = (warp >> 2) * UW_COLS;  // this warp's first output column
+            float du[NT][4], dw[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) du[n][e] = dw[n][e] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < C / 16; ++ks) {
+                uint32_t ah[4], al[4], bh[4], bl[4];
+                ld_a(&sm.ta_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, ah);
+                ld_a(&sm.ta_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, al);
+                ld_a(&sm.tb_hi[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bh);
+                ld_a(&sm.tb_lo[0][0], LDP, (warp & 3) * 16, ks * 16, lane, bl);
+#pragma unroll
+                for (int np = 0; np < NT / 2; ++np) {
+                    const int n0 = cb + np * 16;
+                    uint32_t vh_[4], vl_[4], kh_[4], kl_[4];
+                    ld_b2_t(&sm.v[0][0], LDB, n0, ks * 16, lane, vh_);
+                    ld_b2_t(&sm.vl[0][0], LDB, n0, ks * 16, lane, vl_);
+                    if constexpr (TC) {
+                        ld_b2_t_swz(sm.hl[0][0], n0, ks * 16, lane, kh_);
+                        ld_b2_t_swz(sm.hl[1][0], n0, ks * 16, lane, kl_);
+                    } else {
+                        ld_b2_t(&sm.k[0][0], LDB, n0, ks * 16, lane, kh_);
+                        ld_b2_t(&sm.kl[0][0], LDB, n0, ks * 16, lane, kl_);
+                    }
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        mma_16816(du[2 * np + h], ah, vh_[2 * h], vh_[2 * h + 1]);
+                        mma_16816(du[2 * np + h], ah, vl_[2 * h], vl_[2 * h + 1]);
+                        mma_16816(du[2 * np + h], al, vh_[2 * h], vh_[2 * h + 1]);
+                        mma_16816(dw[2 * np + h], bh, kh_[2 * h], kh_[2 * h + 1]);
+                        mma_16816(dw[2 * np + h], bh, kl_[2 * h], kl_[2 * h + 1]);
+                        mma_16816(dw[2 * np + h], bl, kh_[2 * h], kh_[2 * h + 1]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const int col = cb + n * 8 + c0;
+                *reinterpret_cast<float2 *>(ut_out + r0 * S + col) =
+                    make_float2(du[n][0], du[n][1]);
+                *reinterpret_cast<float2 *>(ut_out + (r0 + 8) * S + col) =
+                    make_float2(du[n][2], du[n][3]);
+#pragma unroll
+                for (int e2 = 0; e2 < 2; ++e2) {
+                    const float x0 = dw[n][2 * e2], x1 = dw[n][2 * e2 + 1];
+                    const size_t o = (size_t)(r0 + 8 * e2) * S + col;
+                    *reinterpret_cast<uint32_t *>(w_out + o) = pack_bf16(x0, x1);
+                    if (a.w_lo_out)  // only the mma.sync scan reads W's low half
+                        *reinterpret_cast<uint32_t *>(wl_out + o) =
+                            pack_bf16(x0 - bf16_hi(x0), x1 - bf16_hi(x1));
+                }
+            }
+        }
+        // every thread is done with this item's shared memory and tensor memory
+        // (the next item's copies overwrite them) and has stored its outputs
+        if constexpr (TC) tc::fence_before_sync();
+        __syncthreads();
+        if constexpr (TC) tc::fence_after_sync();
+        // The barrier orders every thread's stores before warp 1's, and a
+        // release is cumulative: once the flag is seen at GPU scope, so is
+        // everything its writer had seen (the semaphore pattern).  Warp 1 waits
+        // for the stores to land while thread 0 sends the next item's loads.
+        if (a.ready && tid == 32) st_release_gpu(a.ready + (size_t)vh * a.nc + ck, ready_value);
+        item = sm.next[(it + 1) & 1];
     }
     if constexpr (TC) {
-        tc::fence_before_sync();
-        __syncthreads();
-        if (warp == 0) {
-            tc::fence_after_sync();
-            tc::tmem_dealloc(sm.tmem_base, 64);
-        }
+        if (warp == 0) tc::tmem_dealloc(sm.tmem_base, 64);
     }
 }
 
@@ -1103,13 +1127,18 @@ cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps
     using namespace dc;
     DnChunkArgs a = a_in;
     a.w_lo_out = scan_maps == nullptr;
+    // the tcgen05 form: one CTA per SM it gets, looping over the items; the
+    // mma.sync form: a CTA per item
+    const int n_items = a.n_v * a.nc;
     auto launch_local = [&](const DnChunkArgs &la) {
-        if (planes)
+        if (planes) {
+            const int grid = la.local_ctas > 0 && la.local_ctas < n_items ? la.local_ctas : n_items;
             dn_chunk_local_kernel<true>
-                <<<dim3(la.n_v, la.nc), LOCAL_THREADS, sizeof(LocalSmemTc) + 1024, st>>>(la, *planes);
-        else
+                <<<grid, LOCAL_THREADS, sizeof(LocalSmemTc) + 1024, st>>>(la, *planes);
+        } else {
             dn_chunk_local_kernel<false>
-                <<<dim3(la.n_v, la.nc), LOCAL_THREADS, sizeof(LocalSmem), st>>>(la, DnPlaneMaps{});
+                <<<n_items, LOCAL_THREADS, sizeof(LocalSmem), st>>>(la, DnPlaneMaps{});
+        }
     };
     dn_prep_kernel<<<dim3((a.t + PREP_TOKENS - 1) / PREP_TOKENS, (2 * a.n_k + a.n_v + 7) / 8), 256, 0,
                      st>>>(a);

@@ -220,6 +220,11 @@ struct DnChunkArgs {
     // chunk] = ready_epoch[head] + 1 once its outputs are written; the scan
     // waits for that value and, done, advances ready_epoch[head]
     int *ready, *ready_epoch;
+    // CTAs of the tcgen05 chunk-local kernel, one per SM it gets (0: one per
+    // item), and the item counter they claim from (zeroed by the prep kernel;
+    // null: a CTA takes every gridDim.x-th item)
+    int local_ctas;
+    int *local_next;
     // out_ready[head * nc + chunk]: zeroed by the prep kernel; each of the
     // tcgen05 scan's four readout warps adds 1 once its pre-norm rows of the
     // chunk are stored; the output kernel waits for 4 (null: it runs after

@@ -63,6 +63,7 @@ struct rl_ctx {
     // ready flags, per head the epoch the flags count, the scan's stream and
     // the fork and join events
     int *dn_ready = nullptr, *dn_ready_epoch = nullptr;
+    int *dn_local_next = nullptr;  // the chunk-local kernel's item counter
     int *dn_out_ready = nullptr;
     cudaStream_t dn_scan_stream = nullptr;
     cudaEvent_t dn_fork = nullptr, dn_join = nullptr;
@@ -241,6 +242,7 @@ void free_all(rl_ctx *x) {
     if (x->hpin_base) cudaFreeHost(x->hpin_base);
     if (x->dn_ready) cudaFree(x->dn_ready);
     if (x->dn_ready_epoch) cudaFree(x->dn_ready_epoch);
+    if (x->dn_local_next) cudaFree(x->dn_local_next);
     if (x->dn_out_ready) cudaFree(x->dn_out_ready);
     if (x->dn_fork) cudaEventDestroy(x->dn_fork);
     if (x->dn_join) cudaEventDestroy(x->dn_join);
@@ -583,6 +585,7 @@ int rl_ctx_create(int device, const rl_config *cfg, rl_ctx **out) {
         cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
         if ((code = alloc(x, &x->dn_ready, nv * nc)) ||
             (code = alloc(x, &x->dn_ready_epoch, nv)) ||
+            (code = alloc(x, &x->dn_local_next, 1)) ||
             (code = alloc(x, &x->dn_out_ready, nv * nc)))
             return bail(code);
         if (cudaMemset(x->dn_ready, 0, nv * nc * sizeof(int)) != cudaSuccess ||
@@ -1346,6 +1349,10 @@ int rl_linear_attn(rl_ctx *ctx, int layer, int live, int t, const float *qkv, co
             const rl::DnOverlap ov{ctx->dn_scan_stream, ctx->dn_fork, ctx->dn_join};
             d.ready = tc_scan && ctx->opt_dn_overlap ? ctx->dn_ready : nullptr;
             d.ready_epoch = ctx->dn_ready_epoch;
+            // beside the scan the chunk-local kernel gets the SMs the scan's n_v
+            // CTAs leave
+            d.local_ctas = std::max(1, ctx->num_sms - (d.ready ? c.n_v_heads : 0));
+            d.local_next = ctx->dn_local_next;
             d.out_ready = d.ready ? ctx->dn_out_ready : nullptr;
             // the chunk-local kernel's tcgen05 form reads q and k by TMA, through
             // maps that end at this call's rows (the rows past them read as 0)
