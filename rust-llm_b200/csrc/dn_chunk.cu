@@ -1146,18 +1146,19 @@ cudaError_t launch_dn_chunk(const DnChunkArgs &a_in, const DnScanMaps *scan_maps
     if (scan_maps && overlap && a.ready) {
         // the scan beside the chunk-local kernel: it starts once the prep
         // kernel is done and walks each head's chunks as their flags go up.
-        // The history and output kernels follow the chunk-local kernel on the
-        // context's stream, beside the scan's last chunks: an output warp
-        // waits for its chunk's rows of the scan (out_ready).  The context's
-        // stream then joins the scan.
+        // The output kernel follows the chunk-local kernel on the context's
+        // stream, beside the scan's last chunks: an output warp waits for its
+        // chunk's rows of the scan (out_ready).  The history kernel (it reads
+        // only the raw rows) follows the scan on its stream, and the
+        // context's stream then joins the scan's.
         cudaStream_t ss = overlap->scan_stream;
         cudaError_t e = cudaEventRecord(overlap->fork, st);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(ss, overlap->fork, 0);
         if (e == cudaSuccess) e = launch_dn_scan_tc(a, *scan_maps, ss);
         if (e != cudaSuccess) return e;
         launch_local(a);
-        dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, st>>>(a);
         dn_out_kernel<<<dim3(a.t, (a.n_v + 3) / 4), 128, 0, st>>>(a);
+        dn_hist_kernel<<<(conv_dim + 255) / 256, 256, 0, ss>>>(a);
         e = cudaEventRecord(overlap->join, ss);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(st, overlap->join, 0);
         if (e != cudaSuccess) return e;
