@@ -32,7 +32,7 @@
 //              S_c = gamma_C S_{c-1} + D in registers, and S_c as a bf16 pair
 //              for the next products
 //   warps 8-11 the readout: O^T from tensor memory to the output rows, off
-//              the chain's path (the readout accumulator is double-buffered)
+//              the chain's path (the readout accumulator has NO buffers)
 //   warp 12    TMA producer, one lane per operand (W, Q', P, K', each
 //              refilled as soon as the MMAs that read it are done), bulk L2
 //              prefetches two chunks ahead, and a lane that waits for each
@@ -66,7 +66,11 @@ constexpr uint32_t UTS_OFF = K_OFF + 4 * BOX64;   // Ut, f32 64 t x 128 j (plain
 constexpr uint32_t ST_OFF = UTS_OFF + 4 * BOX64;  // S^T [hi, lo][i box] 128 j x 64 i
 constexpr uint32_t UT_OFF = ST_OFF + 4 * BOX128;  // U^T [hi, lo] 128 j x 64 t
 constexpr uint32_t SMEM = UT_OFF + 2 * BOX128 + 1024;
-constexpr uint32_t TMEM_COLS = 512, S_COL = 0, U_COL = 128, O_COL = 256;  // O: 2 x 64
+constexpr uint32_t TMEM_COLS = 512, S_COL = 0, U_COL = 128, O_COL = 256;  // O: NO x 64
+// O accumulator buffers: the readout warps' output stores slow down beside
+// the chunk-local kernel's traffic, and the chain's first readout product
+// waits for a free buffer, so they get NO - 1 chain steps of slack
+constexpr int NO = 4;
 constexpr uint32_t W_BYTES = 2 * BOX64, Q_BYTES = 4 * BOX64, P_BYTES = 2 * BOX64,
                    K_BYTES = 4 * BOX64, UT_BYTES = C * S * 4;
 }  // namespace sc
@@ -99,7 +103,7 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
     using namespace sc;
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t w_full, w_empty, q_full, q_empty, p_full, p_empty,
-        k_full, k_empty, ut_full, ut_empty, s_ready, u_done, u_ready, s_done, o_full[2], o_empty[2],
+        k_full, k_empty, ut_full, ut_empty, s_ready, u_done, u_ready, s_done, o_full[NO], o_empty[NO],
         fin;
     __shared__ float gc_s;  // gamma_C of the chunk whose Ut is staged
     __shared__ uint32_t tmem_base;
@@ -122,7 +126,7 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
     };
 
     if (tid == 0) {
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NO; ++b) {
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 128);
         }
@@ -265,7 +269,7 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
             };
             bool ok = true;
             for (int c = 0; c < nc && ok; ++c) {
-                const int b = c & 1;
+                const int b = c % NO;
                 const uint32_t o_acc = tmem + O_COL + b * 64;
                 // U^T = S^T_hi W_hi (K = 128: two boxes of four 16-wide steps)
                 ok = mbar_wait(&s_ready, c & 1, a.status) && mbar_wait(&w_full, c & 1, a.status);
@@ -279,7 +283,7 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
                 tc::commit(&w_empty);
                 // O^T = S^T Q'^T (three terms), in the tensor pipe's idle time
                 // while the compute warps convert U
-                ok = (c < 2 || mbar_wait(&o_empty[b], ((c >> 1) - 1) & 1, a.status)) &&
+                ok = (c < NO || mbar_wait(&o_empty[b], ((c / NO) - 1) & 1, a.status)) &&
                      mbar_wait(&q_full, c & 1, a.status);
                 if (!ok) break;
                 tc::fence_after_sync();
@@ -414,8 +418,8 @@ __global__ void __launch_bounds__(sc::THREADS, 1)
         const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
         const float scale = 1.0f / sqrtf((float)S);
         for (int c = 0; c < nc; ++c) {
-            const int b = c & 1;
-            if (!mbar_wait(&o_full[b], (c >> 1) & 1, a.status)) {
+            const int b = c % NO;
+            if (!mbar_wait(&o_full[b], (c / NO) & 1, a.status)) {
                 flag_s = 1;
                 break;
             }
